@@ -1,0 +1,653 @@
+#!/usr/bin/env python3
+"""Benchmark of the MLz src/simd hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1..c5] [--n N]
+                    [--impl mlz|reference]
+
+Workloads (synthetic seeded inputs of the named shapes; random-init weights):
+  c1  F16 mul_mat, Llama-3.2-3B FFN up-proj: W 8192x3072 f16, X 3072xN f32, N in {1,8,32}
+  c2  prefill GEMM of one Llama-3.2-3B layer: 7 F16 projections (Q 3072^2, K/V 1024x3072,
+      O 3072^2, gate/up 8192x3072, down 3072x8192) over M tokens, M in {512, 2048}
+      (default workload: c2, M = 2048)
+  c3  Q4_K decode mul_mat on Llama-3.1-8B shapes 4096x4096, 14336x4096, 4096x14336, batch N
+  c4  flash-attention decode, 16 sequences, L ~ U{512..8192}, 32 q / 8 kv heads, D = 128
+  c5  Llama-3-70B FFN (gate/up 28672x8192, down 8192x28672) row-sharded over the ranks with
+      NCCL all-gather of the output slices, N in {1, 256}
+
+A step is one pass of the hot path over one batch.  `value` is whole-job throughput with
+inputs resident in HBM; `e2e` is the same metric through the reference-facing plugin
+(mlzc_try_mul_mat / mlzc_try_flash_attn) with pinned host buffers, copies included.
+The reference arm (--impl reference) times the CPU restatement of the reference kernels
+(oracle/) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--n", type=int, default=None, help="activation columns / tokens / batch")
+    ap.add_argument("--impl", default="mlz", choices=["mlz", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU sample length")
+    return ap.parse_args()
+
+
+DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 256}
+
+
+def load_peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# --------------------------------------------------------------------------- workloads
+
+class Workload:
+    """A configuration: device operands, one step, and its algorithmic work."""
+    metric = ""
+    unit = ""
+    bound = "hbm"
+    scaling = "weak"
+    dtype = "f16"
+
+    def work_units(self) -> float:        # bytes (GB/s metrics) or flops (TFLOP/s) per step per rank
+        raise NotImplementedError
+
+    def unit_scale(self) -> float:        # units/s -> metric unit
+        return 1e-9 if self.unit == "GB/s" else 1e-12
+
+
+def _rot_copies(nbytes: int) -> int:
+    return max(1, math.ceil(4 * L2_BYTES / max(nbytes, 1)))
+
+
+class C1(Workload):
+    unit = "GB/s"
+    bound = "hbm"
+
+    def __init__(self, n, dev, gen):
+        import torch
+        from mlz_b200 import synth
+        self.M, self.K, self.N = 8192, 3072, n
+        self.metric = f"decode mul_mat GB/s (F16 W 8192x3072 . X 3072x{n}, fp32 acc)"
+        self.R = _rot_copies(2 * self.M * self.K)
+        self.W = [synth.f16_weights_dev(gen, self.M, self.K, dev) for _ in range(self.R)]
+        self.X = synth.f32_acts_dev(gen, n, self.K, dev)
+        self.Y = torch.empty((n, self.M), dtype=torch.float32, device=dev)
+        import mlz_b200
+        wsb = mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, self.M, self.K, n)
+        self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        self.config = {"workload": f"c1 F16 mul_mat Llama-3.2-3B up-proj 8192x3072, N={n}",
+                       "M": self.M, "K": self.K, "N": n,
+                       "l2": f"rotates {self.R} weight copies ({self.R * 2 * self.M * self.K / 1e6:.0f} MB >= 4x L2)"}
+
+    def work_units(self):
+        return 2 * self.M * self.K + 4 * self.K * self.N + 4 * self.M * self.N
+
+    def launches(self, i):
+        import mlz_b200
+        W = self.W[i % self.R]
+        return [(lambda W=W: mlz_b200.mul_mat(W, self.X, out=self.Y, workspace=self.ws), self.work_units())]
+
+    def host_weights(self):
+        import numpy as np
+        self.hW = self.W[0].cpu().numpy()
+        return [(self.hW, 1, self.K)]
+
+    def e2e_calls(self, pinned):
+        import torch
+        x = self.X.cpu().pin_memory()
+        y = torch.empty((self.N, self.M), dtype=torch.float32).pin_memory()
+        pinned.extend([x, y])
+        return [(0, x, y)], x.numel() * 4, y.numel() * 4
+
+
+class C2(Workload):
+    unit = "TFLOP/s"
+    bound = "tensor"
+    PROJ = [("q", 3072, 3072, 0), ("k", 1024, 3072, 0), ("v", 1024, 3072, 0), ("o", 3072, 3072, 1),
+            ("gate", 8192, 3072, 2), ("up", 8192, 3072, 2), ("down", 3072, 8192, 3)]
+
+    def __init__(self, n, dev, gen):
+        import torch
+        import mlz_b200
+        from mlz_b200 import synth
+        self.Mtok = n
+        self.metric = f"prefill mul_mat TFLOP/s (Llama-3.2-3B layer, 7 F16 projections, M={n} tokens, fp32 acc)"
+        self.W = [synth.f16_weights_dev(gen, o, i, dev) for (_, o, i, _) in self.PROJ]
+        ins = [3072, 3072, 3072, 8192]
+        self.X = [synth.f32_acts_dev(gen, n, k, dev) for k in ins]
+        self.Y = [torch.empty((n, o), dtype=torch.float32, device=dev) for (_, o, _, _) in self.PROJ]
+        wsb = max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, o, i, n) for (_, o, i, _) in self.PROJ)
+        self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        self.config = {"workload": f"c2 Llama-3.2-3B layer prefill, 7 F16 projections, M={n} tokens",
+                       "tokens": n, "projections": "q,k,v,o 3072/1024x3072; gate,up 8192x3072; down 3072x8192",
+                       "l2": "inputs larger than L2 (201 MB of weights per step)"}
+
+    def work_units(self):
+        return sum(2.0 * self.Mtok * o * i for (_, o, i, _) in self.PROJ)
+
+    def launches(self, i):
+        import mlz_b200
+        out = []
+        for j, (_, o, k, xi) in enumerate(self.PROJ):
+            out.append((lambda j=j, xi=xi: mlz_b200.mul_mat(self.W[j], self.X[xi], out=self.Y[j], workspace=self.ws),
+                        2.0 * self.Mtok * o * k))
+        return out
+
+    def host_weights(self):
+        self.hW = [w.cpu().numpy() for w in self.W]
+        return [(w, 1, w.shape[1]) for w in self.hW]
+
+    def e2e_calls(self, pinned):
+        import torch
+        xs = [x.cpu().pin_memory() for x in self.X]
+        ys = [torch.empty(y.shape, dtype=torch.float32).pin_memory() for y in self.Y]
+        pinned.extend(xs + ys)
+        calls = [(j, xs[xi], ys[j]) for j, (_, _, _, xi) in enumerate(self.PROJ)]
+        h2d = sum(xs[xi].numel() * 4 for (_, _, _, xi) in self.PROJ)
+        d2h = sum(y.numel() * 4 for y in ys)
+        return calls, h2d, d2h
+
+
+class C3(Workload):
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = "q4_k/f32"
+    SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
+
+    def __init__(self, n, dev, gen):
+        import torch
+        from mlz_b200 import synth
+        self.N = n
+        self.metric = f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
+        per_step = sum(m * k // 256 * 144 for m, k in self.SHAPES)
+        self.R = _rot_copies(per_step)
+        self.W = [[synth.q4k_blocks_dev(gen, m, k, dev) for (m, k) in self.SHAPES] for _ in range(self.R)]
+        self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, k) in self.SHAPES]
+        self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (m, _) in self.SHAPES]
+        self.config = {"workload": f"c3 Q4_K mul_mat Llama-3.1-8B shapes, batch {n}", "batch": n,
+                       "shapes": "4096x4096, 14336x4096, 4096x14336",
+                       "l2": f"rotates {self.R} weight sets ({self.R * per_step / 1e6:.0f} MB >= 4x L2)"}
+
+    def _bytes(self, m, k):
+        return m * k // 256 * 144 + 4 * k * self.N + 4 * m * self.N
+
+    def work_units(self):
+        return sum(self._bytes(m, k) for m, k in self.SHAPES)
+
+    def launches(self, i):
+        import mlz_b200
+        Ws = self.W[i % self.R]
+        return [(lambda j=j: mlz_b200.mul_mat(Ws[j], self.X[j], out=self.Y[j]), self._bytes(m, k))
+                for j, (m, k) in enumerate(self.SHAPES)]
+
+    def host_weights(self):
+        self.hW = [w.cpu().numpy() for w in self.W[0]]
+        return [(w, 12, k) for w, (_, k) in zip(self.hW, self.SHAPES)]
+
+    def e2e_calls(self, pinned):
+        import torch
+        xs = [x.cpu().pin_memory() for x in self.X]
+        ys = [torch.empty(y.shape, dtype=torch.float32).pin_memory() for y in self.Y]
+        pinned.extend(xs + ys)
+        return ([(j, xs[j], ys[j]) for j in range(3)], sum(x.numel() * 4 for x in xs),
+                sum(y.numel() * 4 for y in ys))
+
+
+class C4(Workload):
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = "f16 kv / f32"
+
+    def __init__(self, n, dev, gen):
+        import numpy as np
+        import torch
+        import mlz_b200
+        from mlz_b200 import synth
+        self.B, self.Hq, self.Hkv, self.D = n, 32, 8, 128
+        g = synth.rng(synth.seed_for(4, n))
+        self.kv_len_np = synth.kv_lengths(g, n, 512, 8192)
+        self.L = 8192
+        s = 1.0 / math.sqrt(self.D)
+        self.q = torch.randn((n, self.Hq, 1, self.D), generator=gen, device=dev) * s
+        self.k = (torch.randn((n, self.Hkv, self.L, self.D), generator=gen, device=dev) * s).half()
+        self.v = (torch.randn((n, self.Hkv, self.L, self.D), generator=gen, device=dev) * s).half()
+        self.kv_len = torch.from_numpy(self.kv_len_np).to(dev)
+        self.out = torch.empty((n, self.Hq, 1, self.D), dtype=torch.float32, device=dev)
+        from mlz_b200.ops import _nb
+        desc = mlz_b200.make_fa_desc(self.q.data_ptr(), _nb(self.q, 4), self.k.data_ptr(), _nb(self.k, 2),
+                                     self.v.data_ptr(), _nb(self.v, 2), self.out.data_ptr(), _nb(self.out, 4),
+                                     (n, self.Hq, 1, self.Hkv, self.L, self.D), s,
+                                     kv_len_ptr=self.kv_len.data_ptr())
+        self.ws = torch.empty(max(mlz_b200.flash_attn_workspace_bytes(desc), 1), dtype=torch.uint8, device=dev)
+        self.metric = (f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)")
+        tot = int(self.kv_len_np.sum())
+        self.config = {"workload": f"c4 FA decode GQA, {n} sequences, sum L = {tot}", "batch": n,
+                       "sum_kv_len": tot, "l2": "inputs larger than L2 (KV cache 537 MB)"}
+
+    def work_units(self):
+        return 4096 * float(self.kv_len_np.sum()) + 2 * self.B * self.Hq * self.D * 4
+
+    def launches(self, i):
+        import mlz_b200
+        return [(lambda: mlz_b200.flash_attn_dispatch(self.q, self.k, self.v, 1.0 / math.sqrt(self.D),
+                                                      kv_len=self.kv_len, out=self.out, workspace=self.ws),
+                 self.work_units())]
+
+
+class C5(Workload):
+    scaling = "strong"
+
+    def __init__(self, n, dev, gen, rank, world, comm):
+        import torch
+        from mlz_b200 import synth
+        self.N, self.rank, self.world, self.comm = n, rank, world, comm
+        self.unit = "GB/s" if n == 1 else "TFLOP/s"
+        self.bound = "hbm" if n == 1 else "tensor"
+        self.mats = [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]
+        self.metric = (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
+                       f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, NCCL all-gather)")
+        self.W = [synth.f16_weights_dev(gen, m // world, k, dev) for (_, m, k) in self.mats]
+        self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, _, k) in self.mats]
+        self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (_, m, _) in self.mats]
+        self.ws = torch.empty(max(comm.workspace_bytes(1, m, k, n) for (_, m, k) in self.mats) if comm else 1,
+                              dtype=torch.uint8, device=dev)
+        self.config = {"workload": f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}", "N": n,
+                       "parallelism": f"row-shard x{world} + all-gather", "l2": "inputs larger than L2"}
+
+    def work_units(self):  # whole-job units (all ranks together), reported once
+        if self.N == 1:
+            return sum(2.0 * m * k + 4 * k + 4 * m for (_, m, k) in self.mats)
+        return sum(2.0 * self.N * m * k for (_, m, k) in self.mats)
+
+    def launches(self, i):
+        import mlz_b200
+        out = []
+        for j, (_, m, k) in enumerate(self.mats):
+            u = (2.0 * m * k + 4 * k + 4 * m) if self.N == 1 else 2.0 * self.N * m * k
+            if self.comm is not None:
+                f = (lambda j=j, m=m: self.comm.mul_mat_sharded(self.W[j], self.X[j], m, out=self.Y[j], workspace=self.ws))
+            else:
+                f = (lambda j=j: mlz_b200.mul_mat(self.W[j], self.X[j], out=self.Y[j], workspace=self.ws))
+            out.append((f, u))
+        return out
+
+
+# --------------------------------------------------------------------------- helpers
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        for line in out.splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = float(p[2])
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" else torch.device("cpu")
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_sample(cfg: str, n: int, target_s: float):
+    """Times the reference's loop structure (oracle port, all host threads) on a bounded
+    sample of the workload; returns (value in the metric's unit, description, threads)."""
+    import numpy as np
+    import oracle
+    from mlz_b200 import synth
+    nth = oracle.host_threads()
+    g = synth.rng(77)
+
+    def grow(run, units_of):
+        rows = 1
+        while True:
+            t0 = time.perf_counter()
+            run(rows)
+            dt = time.perf_counter() - t0
+            if dt >= target_s or rows >= 1 << 20:
+                return units_of(rows) / dt, rows, dt
+            rows = max(rows * 2, int(rows * target_s / max(dt, 1e-3) * 1.1))
+
+    if cfg in ("c1", "c2", "c5"):
+        M, K = {"c1": (8192, 3072), "c2": (3072, 3072), "c5": (28672, 8192)}[cfg]
+        N = n
+        w = synth.f16_weights(g, min(M, 4096), K)
+        x = synth.f32_acts(g, N, K)
+
+        def run(rows):
+            reps, r = divmod(rows, w.shape[0])
+            for _ in range(reps):
+                oracle.base_mul_mat_f16(w, x, nth)
+            if r:
+                oracle.base_mul_mat_f16(w[:r], x, nth)
+
+        if cfg == "c1" or (cfg == "c5" and n == 1):
+            per_row = 2 * K + (4 * K * N) / M + 4 * N
+            v, rows, dt = grow(run, lambda r: per_row * r)
+            return v * 1e-9, f"{rows} weight rows of {M}x{K} x N={N} in {dt:.1f}s", nth
+        v, rows, dt = grow(run, lambda r: 2.0 * r * K * N)
+        return v * 1e-12, f"{rows} weight rows of the {M}x{K} projection x {N} tokens in {dt:.1f}s", nth
+    if cfg == "c3":
+        M, K = 14336, 4096
+        w = synth.q4k_blocks(g, 2048, K)
+        x = synth.f32_acts(g, n, K)
+
+        def run(rows):
+            reps, r = divmod(rows, w.shape[0])
+            for _ in range(reps):
+                oracle.base_mul_mat_q4k(w, x, nth)
+            if r:
+                oracle.base_mul_mat_q4k(w[:r], x, nth)
+        v, rows, dt = grow(run, lambda r: r * (K // 256 * 144 + 4 * n) + 4 * K * n * r / M)
+        return v * 1e-9, f"{rows} Q4_K rows of 14336x4096 x batch {n} in {dt:.1f}s", nth
+    if cfg == "c4":
+        B, Hq, Hkv, D = n, 32, 8, 128
+        kl = synth.kv_lengths(synth.rng(synth.seed_for(4, n)), B, 512, 8192)
+        L = int(kl.max())
+        Lc = min(L, 2048)
+        q, k, v = synth.fa_inputs(g, 1, Hq, Hkv, Lc, D)
+
+        def run(seqs):
+            for _ in range(seqs):
+                oracle.base_flash_attn(q, k, v, 1 / math.sqrt(D), nth=nth)
+        vv, seqs, dt = grow(run, lambda s: s * 4096.0 * Lc)
+        return vv * 1e-9, f"{seqs} sequences of L={Lc} (32q/8kv heads, D=128) in {dt:.1f}s", nth
+    raise ValueError(cfg)
+
+
+# --------------------------------------------------------------------------- arms
+
+def reference_arm(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    n = a.n or DEFAULT_N[a.config]
+    unit = {"c1": "GB/s", "c2": "TFLOP/s", "c3": "GB/s", "c4": "GB/s", "c5": "GB/s" if n == 1 else "TFLOP/s"}[a.config]
+    import oracle
+    oracle.build()
+    per_step = max(a.cpu_seconds / max(a.steps, 1), 0.5)
+    for _ in range(a.warmup):
+        cpu_sample(a.config, n, min(per_step, 0.5))
+    vals, desc, nth = [], "", 1
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        v, desc, nth = cpu_sample(a.config, n, per_step)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    metric = {"c1": f"decode mul_mat GB/s (F16 W 8192x3072 . X 3072x{n}, fp32 acc)",
+              "c2": f"prefill mul_mat TFLOP/s (Llama-3.2-3B layer, 7 F16 projections, M={n} tokens, fp32 acc)",
+              "c3": f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})",
+              "c4": f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)",
+              "c5": f"sharded FFN mul_mat {unit} (Llama-3-70B, F16, N={n})"}[a.config]
+    line = {
+        "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * wall / max(a.steps, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{a.config} N={n} (CPU restatement of the reference kernels)"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": nth, "kind": "port",
+                         "sample": desc + f"; host {oracle.host_cpu_model()}"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def mlz_arm(a):
+    import torch
+    import mlz_b200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    mlz_b200.init(local)
+    n = a.n or DEFAULT_N[a.config]
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    comm = None
+    if a.config == "c5" and world > 1:
+        import torch.distributed as dist
+        obj = [mlz_b200.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = mlz_b200.Comm(world, rank, local, obj[0], timeout_ms=60000)
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + 100 * int(a.config[1]) + n + rank)
+    wl = {"c1": C1, "c2": C2, "c3": C3, "c4": C4}.get(a.config)
+    w = wl(n, dev, gen) if wl else C5(n, dev, gen, rank, world, comm)
+    peaks = load_peaks()
+    stream = torch.cuda.current_stream()
+
+    # warm-up (first calls also create contexts / workspaces outside the timed region)
+    for i in range(max(a.warmup, 3)):
+        for f, _ in w.launches(i):
+            f()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_load = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t_load < 1.0:  # load for the clock sampler before timing
+        for f, _ in w.launches(i):
+            f()
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+    K = a.steps
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in w.launches(0)]
+          for _ in range(K)]
+    units_l = [u for _, u in w.launches(0)]
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = mlz_b200.launch_count()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s in range(K):
+        for j, (f, _) in enumerate(w.launches(s)):
+            ev[s][j][0].record(stream)
+            f()
+            ev[s][j][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    n_launch = mlz_b200.launch_count() - n0
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    per_launch_ms = [sum(ev[s][j][0].elapsed_time(ev[s][j][1]) for s in range(K)) / K for j in range(len(units_l))]
+
+    units = w.work_units()
+    job_units = units if isinstance(w, C5) else units * world
+    value = job_units * K / (ms * 1e-3) * w.unit_scale()
+
+    # roofline of the dominant launch (largest average device time)
+    jdom = max(range(len(units_l)), key=lambda j: per_launch_ms[j])
+    if isinstance(w, C2):  # all 7 projections run the same GEMM kernel: pool them
+        ach = sum(units_l) / (sum(per_launch_ms) * 1e-3) * 1e-12
+    else:
+        ach = units_l[jdom] / (per_launch_ms[jdom] * 1e-3) * w.unit_scale()
+    long_run = ms * 1e-3 > 1.0
+    if w.bound == "hbm":
+        peak, peak_name = peaks["hbm_gbs"], "hbm_gbs"
+    else:
+        peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
+        peak_name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
+    roofline = {"bound": w.bound, "achieved": ach, "peak": peak,
+                "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s", "frac": ach / peak, "traffic": None,
+                "peak_source": f"{peaks['source']} {peak_name}",
+                "kernel": "mul_mat (all projections)" if isinstance(w, C2) else f"launch {jdom} of the step"}
+
+    # end to end through the plugin entry point with pinned host buffers
+    e2e = None
+    if not a.no_e2e and not isinstance(w, C5) and world >= 1:
+        e2e = run_e2e(w, a, world, value)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        try:
+            v, desc, nth = cpu_sample(a.config, n, a.cpu_seconds)
+            import oracle
+            cpu = {"value": v, "unit": w.unit, "cores": nth, "kind": "port",
+                   "sample": desc + f"; host {oracle.host_cpu_model()}"}
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": w.unit, "cores": None, "kind": "port", "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        cfg = dict(w.config)
+        cfg["parallelism"] = cfg.get("parallelism", f"replicas x{world}" if world > 1 else "single GPU")
+        line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world, "steps": K,
+                "warmup": a.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": w.scaling,
+                "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded), random-init weights",
+                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": n_launch, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.destroy()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_e2e(w, a, world, value_dev):
+    """Same metric through mlzc_try_mul_mat / mlzc_try_flash_attn with host buffers."""
+    import numpy as np
+    import torch
+    import mlz_b200
+    pinned = []
+    if isinstance(w, C4):
+        q = w.q.cpu().pin_memory()
+        k = w.k.cpu().pin_memory()
+        v = w.v.cpu().pin_memory()
+        kl = torch.from_numpy(w.kv_len_np).pin_memory()
+        o = torch.empty(w.out.shape, dtype=torch.float32).pin_memory()
+        nb = lambda t, e: tuple(s * e for s in t.stride()[::-1])
+        desc = mlz_b200.make_fa_desc(q.data_ptr(), nb(q, 4), k.data_ptr(), nb(k, 2), v.data_ptr(), nb(v, 2),
+                                     o.data_ptr(), nb(o, 4), (w.B, w.Hq, 1, w.Hkv, w.L, w.D),
+                                     1.0 / math.sqrt(w.D), kv_len_ptr=kl.data_ptr())
+        # the hook copies the whole cache view it is given: here only the live keys count
+        h2d = q.numel() * 4 + (k.numel() + v.numel()) * 2 + kl.numel() * 4
+        d2h = o.numel() * 4
+        step = lambda: mlz_b200.ggml_simd_try_flash_attn(desc)
+    else:
+        hws = w.host_weights()
+        calls, h2d, d2h = w.e2e_calls(pinned)
+        views = []
+        for (j, x, y) in calls:
+            hw, t, K = hws[j]
+            views.append((mlz_b200.tensor_view(hw if t != 1 else hw.view(np.uint16), t, ne0=K),
+                          mlz_b200.TensorView(), mlz_b200.TensorView()))
+            sv = views[-1]
+            for tv, arr in ((sv[1], x), (sv[2], y)):
+                tv.type = 0
+                tv.ne[:] = [arr.shape[1], arr.shape[0], 1, 1]
+                tv.nb[:] = [4, arr.stride(0) * 4, arr.stride(0) * 4 * arr.shape[0], arr.stride(0) * 4 * arr.shape[0]]
+                tv.data = arr.data_ptr()
+
+        def step():
+            r = 1
+            for (s0, s1, d) in views:
+                r &= mlz_b200.ggml_simd_try_mul_mat(s0, s1, d)
+            return r
+    for _ in range(max(a.warmup, 2)):
+        if step() != 1:
+            raise RuntimeError("plugin entry point declined the workload: " + mlz_b200.last_error())
+    torch.cuda.synchronize()
+    K = max(3, min(a.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = max_over_ranks(time.perf_counter() - t0, world)
+    units = w.work_units() * world
+    return {"value": units * K / dt * w.unit_scale(), "unit": w.unit, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "path": "mlzc_try_flash_attn" if isinstance(w, C4) else "mlzc_try_mul_mat",
+            "ms_per_step": 1e3 * dt / K}
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        reference_arm(a)
+    else:
+        mlz_arm(a)
+
+
+if __name__ == "__main__":
+    main()

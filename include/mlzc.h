@@ -1,0 +1,206 @@
+/*
+ * mlzc.h -- C ABI of the B200 (sm_100a) implementation of MLz's src/simd hot path.
+ *
+ * The library (mlz_b200/libmlzc.so) replaces the CPU kernels behind MLz's ggml hook:
+ *   - F16 / F32 weight x F32 activation mul_mat (decode GEMV and prefill GEMM),
+ *   - Q4_K super-block weight x F32 activation mul_mat (dequant-dot),
+ *   - F16-KV flash-attention decode with grouped-query heads,
+ *   - row-sharded mul_mat over several GPUs of one node (NCCL all-gather of slices).
+ *
+ * Conventions (all entry points):
+ *   - Every function returns an int status: MLZC_OK (0) on success, a negative
+ *     MLZC_ERR_* on failure.  Nothing aborts or traps; mlzc_last_error() gives a
+ *     human-readable message for the calling thread's last failure.
+ *   - Plain pointers and sizes only.  "stream" is a cudaStream_t passed as void*
+ *     (NULL = the legacy default stream).  "_dev" functions take device pointers and
+ *     are asynchronous on that stream; the others take host pointers and return when
+ *     the result is in host memory.
+ *   - Tensors use ggml's layout: ne[0] is the contiguous axis, nb[] are byte strides.
+ *     For mul_mat: W has ne = [K, M] (row m at w + m*w_row_bytes), X has ne = [K, N]
+ *     (column n at x + n*x_col_bytes), Y has ne = [M, N] (element (m, n) at
+ *     y + n*y_col_bytes + 4*m).  This is the contract ggml_compute_forward_mul_mat
+ *     asserts (src/simd/ggml-cpu-simd.c:1273-1288 in the MLz tree).
+ *   - Type ids are ggml_type values: F32 = 0, F16 = 1, Q4_K = 12.
+ *   - F16 weights: activations are narrowed to f16 (round-to-nearest-even) and the
+ *     products are accumulated in fp32, which is the contract of the reference's
+ *     F16 path (type_traits_cpu[F16].vec_dot_type = F16, ggml-cpu-simd.c:215-220).
+ *     F32 and Q4_K weights: activations stay f32, fp32 accumulation.
+ *   - The first call that touches a device creates its context (a small device
+ *     allocation); make that call, or mlzc_init(), before any stream capture.
+ */
+#ifndef MLZC_H
+#define MLZC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLZC_VERSION 1
+
+enum mlzc_status {
+    MLZC_OK = 0,
+    MLZC_ERR_INVALID = -1,      /* bad pointer, size, stride or alignment */
+    MLZC_ERR_UNSUPPORTED = -2,  /* type / shape combination this library does not take */
+    MLZC_ERR_CUDA = -3,         /* a CUDA runtime call failed */
+    MLZC_ERR_NOMEM = -4,        /* device or pinned allocation failed, or workspace too small */
+    MLZC_ERR_DEVICE = -5,       /* a kernel reported an error (see mlzc_device_errors) */
+    MLZC_ERR_COMM = -6          /* NCCL failure or timeout */
+};
+
+enum mlzc_type { MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_K = 12 };
+
+/* Attention mode bits; same values as FA_MODE_* (src/simd/flash_attention.h:43-49). */
+#define MLZC_FA_MODE_GQA_BATCH 0x04u
+#define MLZC_FA_MODE_ALIBI 0x08u
+#define MLZC_FA_MODE_SOFTCAP 0x10u
+
+/* Kernel error bits reported by mlzc_device_errors(). */
+#define MLZC_DEVERR_WAIT_TIMEOUT 0x1u  /* a bounded mbarrier / flag wait gave up */
+#define MLZC_DEVERR_BAD_SHAPE 0x2u     /* a kernel saw a shape its launch did not promise */
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Number of kernels this library has launched in this process (all devices).  A
+ * diagnostics counter with no counterpart in the reference; benchmarks read it around a
+ * timed region. */
+int mlzc_launch_count(uint64_t* out_count);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* mlzc_last_error(void);
+int mlzc_version(void);
+/* Create the context of CUDA device `device` (idempotent). */
+int mlzc_init(int device);
+/* Release every context, cached weight and workspace this library holds. */
+int mlzc_shutdown(void);
+/* Read and clear the kernel error word of `device` (MLZC_DEVERR_* bits).  Synchronises
+ * the device. */
+int mlzc_device_errors(int device, uint32_t* out_bits);
+
+/* --------------------------------------------------- device-pointer kernels */
+
+/* Workspace (device bytes) that mlzc_mul_mat_dev needs for this shape; 0 if none. */
+int mlzc_mul_mat_workspace_bytes(int w_type, int64_t M, int64_t K, int64_t N, size_t* out_bytes);
+
+/* Y = W . X in ggml layout (see the header comment), on `stream`.
+ * Replaces: ggml_simd_try_mul_mat's compute branches (src/simd/ggml_simd_hook.cpp:188-311),
+ * simd_matmul_f32 (src/simd/simd_matmul.cpp:214-251), simd_matmul_f16 (:428-480), and the
+ * upstream F16 vec_dot path the hook falls back to (src/simd/ggml-cpu-simd.c:1314-1465).
+ * Pointers and strides need only their element alignment; 16-byte aligned W and X with
+ * 16-byte multiple strides take the vectorised kernels, anything else a slower exact
+ * path.  Q4_K needs K % 256 == 0 and 16-byte aligned blocks and activation columns.
+ * `workspace` may be NULL when the query above returned 0. */
+int mlzc_mul_mat_dev(int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                     const float* x, size_t x_col_bytes, int64_t N,
+                     float* y, size_t y_col_bytes,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* One flash-attention call.  Field names and meaning follow flash_attn_config_t
+ * (src/simd/flash_attention.h:65-114); pointers are DEVICE pointers for
+ * mlzc_flash_attn_dev and HOST pointers for mlzc_try_flash_attn.
+ * Q: f32, ne = [DK, n_queries, n_head_q, batch]; K/V: f16, ne = [DK|DV, n_kv,
+ * n_head_kv, batch]; mask: f32 [n_kv, n_queries] added to the scaled scores (NULL =
+ * none); dst: f32, element (d, iq, ihq, ib) at d*4 + iq*dst_nb[1] + ihq*dst_nb[2] +
+ * ib*dst_nb[3].  kv_len (extension): int32 per batch element, keys at positions
+ * >= kv_len[ib] are not read (NULL = n_kv for every element); this is how a ragged
+ * batch of sequences is expressed without a mask.
+ * Score of key j for query iq of head ihq: s = scale * <q, k_j>; s += mask(iq, j);
+ * if MLZC_FA_MODE_SOFTCAP: s = softcap * tanh(s / softcap); if MLZC_FA_MODE_ALIBI:
+ * s += slope(ihq) * (j - iq) with slope = 2^(-8/P)^(ihq+1), P = n_head_q rounded up to a
+ * power of two (the order and slope of flash_attention.cpp:339-363).  KV head of query
+ * head ihq: ihq * n_head_kv / n_head_q.  Rows with no visible key produce zeros. */
+typedef struct {
+    int64_t head_dim_k, head_dim_v, n_queries, n_kv, n_head_q, n_head_kv, batch_size;
+    float scale, logit_softcap, max_bias;
+    uint32_t mode;
+    const float* q;
+    const void* k;
+    const void* v;
+    const float* mask;
+    float* dst;
+    size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
+    int32_t k_type, v_type;   /* both must be MLZC_TYPE_F16 */
+    const int32_t* kv_len;    /* NULL or batch_size entries (device memory for _dev) */
+} mlzc_fa_desc;
+
+/* Workspace (device bytes) mlzc_flash_attn_dev needs for this call. */
+int mlzc_flash_attn_workspace_bytes(const mlzc_fa_desc* desc, size_t* out_bytes);
+
+/* Flash-attention on device pointers.
+ * Replaces: flash_attn_dispatch's F16/F16 branch (src/simd/flash_attention.cpp:143-150)
+ * -> simd_flash_attn_f16_avx512 (kernels/x86/flash/flash_attn_f16_avx512.asm + the FA2
+ * skeleton flash_attn_fa2_skeleton_avx512.inc:394-842).
+ * Requirements: DK == DV in {64, 128, 256}; contiguous f16 K/V rows whose strides
+ * (nb[1..3]) are multiples of 16 bytes; contiguous, 16-byte aligned f32 q rows. */
+int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* ------------------------------------------------ host-pointer (hook) level */
+
+/* The subset of struct ggml_tensor the hook reads. */
+typedef struct {
+    int32_t type;
+    int64_t ne[4];
+    size_t nb[4];
+    void* data;
+} mlzc_tensor;
+
+/* Drop-in body for ggml_simd_try_mul_mat (src/simd/ggml_simd_hook.cpp:153-315): called by
+ * every ggml threadpool thread (ith of nth) for the same MUL_MAT node.  Returns 1 when the
+ * node was computed on the GPU (dst written) and 0 when the caller must fall back to the
+ * CPU path.  All nth threads of a node receive the same answer, so a fallback is taken by
+ * all of them together (the upstream path has barriers inside).  Thread 0 does the GPU
+ * work: weights are uploaded on first use and cached on the device keyed by
+ * (src0->data, type, ne, nb); X is copied in and Y copied out on every call.
+ * ne[2] / ne[3] broadcast of ggml is not taken (returns 0 when ne[2] or ne[3] != 1). */
+int mlzc_try_mul_mat(const mlzc_tensor* src0, const mlzc_tensor* src1, mlzc_tensor* dst,
+                     int ith, int nth);
+
+/* Drop-in body for ggml_simd_try_flash_attn (src/simd/ggml_simd_hook.cpp:317-375) with
+ * host pointers in `desc`; same 1 / 0 contract and thread rule as mlzc_try_mul_mat. */
+int mlzc_try_flash_attn(const mlzc_fa_desc* desc, int ith, int nth);
+
+/* Device-resident weights for callers that manage their own tensors (the engine). */
+typedef struct mlzc_weight_s* mlzc_weight;
+int mlzc_weight_upload(int device, int w_type, const void* host, size_t row_bytes,
+                       int64_t M, int64_t K, mlzc_weight* out);
+int mlzc_weight_free(mlzc_weight w);
+/* Y = W . X with X, Y in HOST memory (pinned or pageable).  Synchronous. */
+int mlzc_mul_mat(mlzc_weight w, const float* x, size_t x_col_bytes, int64_t N,
+                 float* y, size_t y_col_bytes);
+/* Drop every weight cached by mlzc_try_mul_mat (e.g. when a model is unloaded). */
+int mlzc_weight_cache_clear(void);
+
+/* ---------------------------------------------------- multi-GPU (one node) */
+
+typedef struct mlzc_comm_s* mlzc_comm;
+#define MLZC_UNIQUE_ID_BYTES 128
+/* Rank 0 creates the id and the caller distributes it to every rank. */
+int mlzc_comm_unique_id(void* out_id);
+/* Collective over `nranks` processes, one GPU each; `timeout_ms` bounds every wait. */
+int mlzc_comm_init(int nranks, int rank, int device, const void* unique_id, int timeout_ms,
+                   mlzc_comm* out);
+int mlzc_comm_destroy(mlzc_comm comm);
+
+/* Workspace for mlzc_mul_mat_sharded_dev. */
+int mlzc_mul_mat_sharded_workspace_bytes(mlzc_comm comm, int w_type, int64_t M_total,
+                                         int64_t K, int64_t N, size_t* out_bytes);
+
+/* Row-sharded mul_mat: this rank holds rows [r*M_total/G, (r+1)*M_total/G) of W
+ * (w_shard, M_total % G == 0) and computes that slice of Y; the slices are all-gathered
+ * so that every rank ends with the full Y (ggml layout, M_total rows).  No counterpart
+ * in the reference (it has no multi-GPU path); it composes mlzc_mul_mat_dev with an
+ * NCCL all-gather on `stream`. */
+int mlzc_mul_mat_sharded_dev(mlzc_comm comm, int w_type, const void* w_shard,
+                             size_t w_row_bytes, int64_t M_total, int64_t K,
+                             const float* x, size_t x_col_bytes, int64_t N,
+                             float* y, size_t y_col_bytes,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLZC_H */

@@ -1,0 +1,24 @@
+"""B200-native (sm_100a) implementation of MLz's src/simd hot path.
+
+The compute lives in ``libmlzc.so`` (CUDA kernels + C ABI, see include/mlzc.h); this
+package is the host-side mirror of the reference's dispatch interface over that ABI.
+Importing it loads the library and fails if it has not been built -- there is no CPU
+fallback.
+"""
+from ._lib import (EXPORTS, FA_MODE_ALIBI, FA_MODE_GQA_BATCH, FA_MODE_SOFTCAP, LIB_PATH,
+                   TYPE_F16, TYPE_F32, TYPE_Q4_K, UNIQUE_ID_BYTES, FaDesc, MlzcError,
+                   TensorView, check, last_error, launch_count, lib)
+from .ops import (Comm, Weight, device_errors, flash_attn_dispatch, flash_attn_workspace_bytes,
+                  ggml_simd_try_flash_attn, ggml_simd_try_mul_mat, init, make_fa_desc, mul_mat,
+                  mul_mat_workspace_bytes, shutdown, tensor_view, weight_type_of)
+
+lib()  # load now: a missing or broken build is an import error, not a silent fallback
+
+__all__ = [
+    "EXPORTS", "FA_MODE_ALIBI", "FA_MODE_GQA_BATCH", "FA_MODE_SOFTCAP", "LIB_PATH", "TYPE_F16",
+    "TYPE_F32", "TYPE_Q4_K", "UNIQUE_ID_BYTES", "FaDesc", "MlzcError", "TensorView", "check",
+    "last_error", "launch_count", "lib", "Comm", "Weight", "device_errors", "flash_attn_dispatch",
+    "flash_attn_workspace_bytes", "ggml_simd_try_flash_attn", "ggml_simd_try_mul_mat", "init",
+    "make_fa_desc", "mul_mat", "mul_mat_workspace_bytes", "shutdown", "tensor_view",
+    "weight_type_of",
+]

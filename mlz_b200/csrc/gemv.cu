@@ -1,0 +1,387 @@
+// gemv.cu -- decode-shaped mul_mat (few activation columns) on the CUDA cores.
+//
+// Replaces the per-row dot products of the reference: matrix_mult_avx512's k-loop
+// (kernels/x86/matrix_mult_avx512.asm:165-181) reached through simd_matmul_f32
+// (src/simd/simd_matmul.cpp:214-251), the upstream F16 vec_dot path the hook falls back
+// to (src/simd/ggml-cpu-simd.c:1145-1244), and the per-(m, n) Q4_K x Q8_K vec_dot loop of
+// ggml_simd_try_mul_mat (src/simd/ggml_simd_hook.cpp:254-299).
+//
+// Design (HBM-bound: every weight byte is read exactly once):
+//   - one warp owns ROWS consecutive weight rows; its 32 lanes stride over K in 16-byte
+//     chunks, so every load instruction of the warp reads 512 contiguous bytes per row;
+//   - weights are read with ld.global.nc.L1::no_allocate (streamed, never re-read),
+//     activations through the read-only path (they are re-read by every warp and stay
+//     in L1/L2);
+//   - fp32 accumulation per lane, butterfly shuffle reduction at the end;
+//   - the ROWS rows of a warp share each activation load, which keeps the L1 traffic
+//     per FMA at or below one byte.
+// Q4_K: each lane decodes a 64-value chunk (one 32-byte qs run, sub-blocks 2c and 2c+1
+// of its super-block) with the 6-bit scale/min unpack of GGUF, folds the minimum into
+// the weight (w = d*sc*q - dmin*m, exact nibble-to-float via a float bit trick) and
+// accumulates w*x in fp32 -- no activation quantisation (the reference's Q8_K step,
+// ggml_simd_hook.cpp:109-148, is what the parity gate excludes).
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "internal.h"
+
+namespace mlzc {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t u) {
+    __half2 h = *reinterpret_cast<__half2*>(&u);
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ float round_to_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Unpacks 8 weights of one 16-byte chunk to f32 (F16 weights: 8 values per chunk).
+struct WF16 {
+    static constexpr int kPerChunk = 8;
+    static constexpr bool kRoundX = true;
+    __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
+        float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+        w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
+        w[4] = c.x; w[5] = c.y; w[6] = d.x; w[7] = d.y;
+    }
+    __device__ __forceinline__ static float scalar(const char* row, int64_t k) {
+        return __half2float(reinterpret_cast<const __half*>(row)[k]);
+    }
+};
+
+// F32 weights: 4 values per chunk, activations used as they are.
+struct WF32 {
+    static constexpr int kPerChunk = 4;
+    static constexpr bool kRoundX = false;
+    __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
+        w[0] = __uint_as_float(v.x); w[1] = __uint_as_float(v.y);
+        w[2] = __uint_as_float(v.z); w[3] = __uint_as_float(v.w);
+    }
+    __device__ __forceinline__ static float scalar(const char* row, int64_t k) {
+        return reinterpret_cast<const float*>(row)[k];
+    }
+};
+
+// Vectorised kernel: requires 16-byte aligned rows/columns and K % kPerChunk == 0.
+template <class WT, int NB, int ROWS>
+__global__ void __launch_bounds__(kThreads)
+gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
+                const char* __restrict__ X, size_t x_cs, int ncols,
+                char* __restrict__ Y, size_t y_cs) {
+    constexpr int CH = WT::kPerChunk;
+    const int lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
+    if (row0 >= M) return;
+
+    const char* wrow[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) wrow[r] = W + (size_t)min(row0 + r, M - 1) * w_rs;
+
+    float acc[ROWS][NB];
+#pragma unroll
+    for (int r = 0; r < ROWS; r++)
+#pragma unroll
+        for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
+
+    const int64_t nchunk = K / CH;
+    for (int64_t c = lane; c < nchunk; c += 32) {
+        uint4 wv[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) wv[r] = ld_stream16(wrow[r] + (size_t)c * 16);
+        float wf[ROWS][CH];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) WT::unpack(wv[r], wf[r]);
+#pragma unroll
+        for (int n = 0; n < NB; n++) {
+            if (n < ncols) {
+                const float4* xp = reinterpret_cast<const float4*>(X + (size_t)n * x_cs) + c * (CH / 4);
+                float xf[CH];
+#pragma unroll
+                for (int q = 0; q < CH / 4; q++) {
+                    const float4 t = __ldg(xp + q);
+                    xf[4 * q + 0] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+                }
+                if (WT::kRoundX) {
+#pragma unroll
+                    for (int i = 0; i < CH; i++) xf[i] = round_to_f16(xf[i]);
+                }
+#pragma unroll
+                for (int r = 0; r < ROWS; r++)
+#pragma unroll
+                    for (int i = 0; i < CH; i++) acc[r][n] = fmaf(wf[r][i], xf[i], acc[r][n]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; r++)
+#pragma unroll
+        for (int n = 0; n < NB; n++) {
+            const float v = warp_sum(acc[r][n]);
+            if (lane == 0 && n < ncols && row0 + r < M)
+                reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row0 + r] = v;
+        }
+}
+
+// Scalar kernel for any alignment / K: one warp per row, columns in sequence.
+template <class WT>
+__global__ void __launch_bounds__(kThreads)
+gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
+                   const char* __restrict__ X, size_t x_cs, int64_t N,
+                   char* __restrict__ Y, size_t y_cs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const char* wr = W + (size_t)row * w_rs;
+    for (int64_t n = 0; n < N; n++) {
+        const float* xc = reinterpret_cast<const float*>(X + (size_t)n * x_cs);
+        float acc = 0.0f;
+        for (int64_t k = lane; k < K; k += 32) {
+            float xv = xc[k];
+            if (WT::kRoundX) xv = round_to_f16(xv);
+            acc = fmaf(WT::scalar(wr, k), xv, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row] = acc;
+    }
+}
+
+template <class WT, int NB>
+void launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
+                int ncols, char* y, size_t y_cs, cudaStream_t s) {
+    constexpr int ROWS = 4;
+    const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
+    const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
+    gemv_vec_kernel<WT, NB, ROWS><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
+    count_launch();
+}
+
+template <class WT>
+int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, size_t x_cs,
+             int64_t N, float* y, size_t y_cs, cudaStream_t s) {
+    const char* wc = static_cast<const char*>(w);
+    const char* xc = reinterpret_cast<const char*>(x);
+    char* yc = reinterpret_cast<char*>(y);
+    const bool aligned = ((uintptr_t)w % 16 == 0) && ((uintptr_t)x % 16 == 0) && (w_rs % 16 == 0) &&
+                         (x_cs % 16 == 0) && (K % WT::kPerChunk == 0);
+    if (!aligned) {
+        const unsigned grid = (unsigned)((M + kWarps - 1) / kWarps);
+        gemv_scalar_kernel<WT><<<grid, kThreads, 0, s>>>(wc, w_rs, M, K, xc, x_cs, N, yc, y_cs);
+        count_launch();
+        MLZC_CUDA_TRY(cudaGetLastError());
+        return MLZC_OK;
+    }
+    for (int64_t n0 = 0; n0 < N; n0 += 8) {
+        const int nc = (int)std::min<int64_t>(8, N - n0);
+        const char* xn = xc + (size_t)n0 * x_cs;
+        char* yn = yc + (size_t)n0 * y_cs;
+        if (nc == 1) launch_vec<WT, 1>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else if (nc == 2) launch_vec<WT, 2>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else if (nc <= 4) launch_vec<WT, 4>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else launch_vec<WT, 8>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        MLZC_CUDA_TRY(cudaGetLastError());
+    }
+    return MLZC_OK;
+}
+
+// ---------------------------------------------------------------- Q4_K
+
+constexpr int kQK = 256;
+constexpr int kQ4KBytes = 144;
+
+// 6-bit scale / min of sub-block j from the 12 packed scale bytes (GGUF order; the
+// unpack of vec_dot_q4_k_q8_k_avx2.asm:101-150).
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, float& sc, float& mn) {
+    int a, b;
+    if (j < 4) {
+        a = s[j] & 63;
+        b = s[j + 4] & 63;
+    } else {
+        a = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        b = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+    sc = (float)a;
+    mn = (float)b;
+}
+
+// Exact nibble -> float: 0x4B000000 | q is the float 2^23 + q.
+__device__ __forceinline__ float nib_f(uint32_t word, int shift) {
+    return __uint_as_float(0x4B000000u | ((word >> shift) & 0xFu)) - 8388608.0f;
+}
+
+template <int NB, int ROWS>
+__global__ void __launch_bounds__(kThreads)
+q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
+                const char* __restrict__ X, size_t x_cs, int ncols,
+                char* __restrict__ Y, size_t y_cs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
+    if (row0 >= M) return;
+    const char* wrow[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) wrow[r] = W + (size_t)min(row0 + r, M - 1) * w_rs;
+
+    float acc[ROWS][NB];
+#pragma unroll
+    for (int r = 0; r < ROWS; r++)
+#pragma unroll
+        for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
+
+    const int64_t nchunk = K / 64;   // 64-value chunks, 4 per super-block
+    for (int64_t ch = lane; ch < nchunk; ch += 32) {
+        const int64_t b = ch >> 2;
+        const int c = (int)(ch & 3);
+        uint4 hdr[ROWS], qa[ROWS], qb[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) {
+            const char* blk = wrow[r] + (size_t)b * kQ4KBytes;
+            hdr[r] = ld_stream16(blk);
+            qa[r] = ld_stream16(blk + 16 + 32 * c);
+            qb[r] = ld_stream16(blk + 32 + 32 * c);
+        }
+        float ds0[ROWS], dm0[ROWS], ds1[ROWS], dm1[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++) {
+            const float d = __half2float(__ushort_as_half((unsigned short)(hdr[r].x & 0xFFFFu)));
+            const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[r].x >> 16)));
+            uint8_t sb[12];
+            *reinterpret_cast<uint32_t*>(sb + 0) = hdr[r].y;
+            *reinterpret_cast<uint32_t*>(sb + 4) = hdr[r].z;
+            *reinterpret_cast<uint32_t*>(sb + 8) = hdr[r].w;
+            float sc, mn;
+            q4k_scale_min(sb, 2 * c, sc, mn);
+            ds0[r] = d * sc;
+            dm0[r] = dmin * mn;
+            q4k_scale_min(sb, 2 * c + 1, sc, mn);
+            ds1[r] = d * sc;
+            dm1[r] = dmin * mn;
+        }
+        const int64_t kbase = ch * 64;
+        // 8 words of 4 qs bytes: word i covers values kbase+4i..+4 (low nibbles) and
+        // kbase+32+4i..+4 (high nibbles).
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float wl[ROWS][4], wh[ROWS][4];
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) {
+                const uint32_t word = (i < 4) ? (&qa[r].x)[i] : (&qb[r].x)[i - 4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    wl[r][e] = fmaf(ds0[r], nib_f(word, 8 * e), -dm0[r]);
+                    wh[r][e] = fmaf(ds1[r], nib_f(word, 8 * e + 4), -dm1[r]);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < NB; n++) {
+                if (n < ncols) {
+                    const float* xc = reinterpret_cast<const float*>(X + (size_t)n * x_cs);
+                    const float4 xl = __ldg(reinterpret_cast<const float4*>(xc + kbase + 4 * i));
+                    const float4 xh = __ldg(reinterpret_cast<const float4*>(xc + kbase + 32 + 4 * i));
+#pragma unroll
+                    for (int r = 0; r < ROWS; r++) {
+                        float a = acc[r][n];
+                        a = fmaf(wl[r][0], xl.x, a); a = fmaf(wl[r][1], xl.y, a);
+                        a = fmaf(wl[r][2], xl.z, a); a = fmaf(wl[r][3], xl.w, a);
+                        a = fmaf(wh[r][0], xh.x, a); a = fmaf(wh[r][1], xh.y, a);
+                        a = fmaf(wh[r][2], xh.z, a); a = fmaf(wh[r][3], xh.w, a);
+                        acc[r][n] = a;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < ROWS; r++)
+#pragma unroll
+        for (int n = 0; n < NB; n++) {
+            const float v = warp_sum(acc[r][n]);
+            if (lane == 0 && n < ncols && row0 + r < M)
+                reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row0 + r] = v;
+        }
+}
+
+template <int NB>
+void launch_q4k(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
+                int ncols, char* y, size_t y_cs, cudaStream_t s) {
+    constexpr int ROWS = 2;
+    const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
+    const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
+    q4k_gemv_kernel<NB, ROWS><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
+    count_launch();
+}
+
+__global__ void gather_permute_kernel(const float* __restrict__ src, char* __restrict__ dst,
+                                      size_t dst_cs, int G, int64_t N, int64_t m_loc) {
+    const int64_t total = (int64_t)G * N * m_loc;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i % m_loc;
+        const int64_t n = (i / m_loc) % N;
+        const int64_t r = i / (m_loc * N);
+        reinterpret_cast<float*>(dst + (size_t)n * dst_cs)[r * m_loc + m] = src[i];
+    }
+}
+
+}  // namespace
+
+int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,
+                          int64_t m_loc, cudaStream_t s) {
+    const int64_t total = (int64_t)G * N * m_loc;
+    if (total == 0) return MLZC_OK;
+    const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    gather_permute_kernel<<<grid, 256, 0, s>>>(src, reinterpret_cast<char*>(dst), dst_col_bytes, G, N, m_loc);
+    count_launch();
+    MLZC_CUDA_TRY(cudaGetLastError());
+    return MLZC_OK;
+}
+
+int launch_gemv(const DeviceCtx*, int w_type, const void* w, size_t w_row_bytes, int64_t M,
+                int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
+                size_t y_col_bytes, cudaStream_t s) {
+    if (w_type == MLZC_TYPE_F16)
+        return run_gemv<WF16>(w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
+    if (w_type == MLZC_TYPE_F32)
+        return run_gemv<WF32>(w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
+    return fail(MLZC_ERR_UNSUPPORTED, "gemv: weight type %d", w_type);
+}
+
+int launch_q4k_gemv(const DeviceCtx*, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
+                    cudaStream_t s) {
+    if (K % kQK != 0) return fail(MLZC_ERR_INVALID, "Q4_K: K=%lld is not a multiple of 256", (long long)K);
+    if ((uintptr_t)w % 16 || w_row_bytes % 16 || (uintptr_t)x % 16 || x_col_bytes % 16)
+        return fail(MLZC_ERR_INVALID, "Q4_K: weights and activations must be 16-byte aligned");
+    const char* wc = static_cast<const char*>(w);
+    const char* xc = reinterpret_cast<const char*>(x);
+    char* yc = reinterpret_cast<char*>(y);
+    for (int64_t n0 = 0; n0 < N; n0 += 16) {
+        const int nc = (int)std::min<int64_t>(16, N - n0);
+        const char* xn = xc + (size_t)n0 * x_col_bytes;
+        char* yn = yc + (size_t)n0 * y_col_bytes;
+        if (nc == 1) launch_q4k<1>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        else if (nc <= 2) launch_q4k<2>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        else if (nc <= 4) launch_q4k<4>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        else if (nc <= 8) launch_q4k<8>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        else launch_q4k<16>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        MLZC_CUDA_TRY(cudaGetLastError());
+    }
+    return MLZC_OK;
+}
+
+}  // namespace mlzc

@@ -1,0 +1,87 @@
+// internal.h -- shared declarations of the mlzc library (host and device side).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/mlzc.h"
+
+namespace mlzc {
+
+// Records `status` and a printf-style message as the calling thread's last error and
+// returns `status`, so call sites read `return fail(MLZC_ERR_INVALID, "...")`.
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Maps a CUDA error to MLZC_ERR_CUDA with the failing call's name.
+int cuda_fail(cudaError_t e, const char* what);
+
+#define MLZC_CUDA_TRY(call)                                  \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return ::mlzc::cuda_fail(e_, #call); \
+    } while (0)
+
+// Per-device state, created on first use of the device.
+struct DeviceCtx {
+    int device = -1;
+    int sm_count = 0;
+    unsigned int* err = nullptr;      // kernel error word (MLZC_DEVERR_* bits)
+    cudaStream_t stream = nullptr;    // stream of the host-pointer entry points
+};
+
+// Context of `device` (creating it if needed); nullptr + last error on failure.
+DeviceCtx* device_ctx(int device);
+// Context of the calling thread's current device.
+DeviceCtx* current_ctx();
+
+// Counts one kernel launch (read by mlzc_launch_count).
+void count_launch(int n = 1);
+
+// Bounded-wait budget for every spin loop in the kernels (mbarrier polls).
+constexpr long long kSpinLimit = 1ll << 26;
+
+// ---- launchers (asynchronous; return MLZC_OK or a status with the message set) ----
+
+// CUDA-core GEMV/skinny GEMM for F16 or F32 weights, any N (column chunks).
+int launch_gemv(const DeviceCtx* c, int w_type, const void* w, size_t w_row_bytes,
+                int64_t M, int64_t K, const float* x, size_t x_col_bytes, int64_t N,
+                float* y, size_t y_col_bytes, cudaStream_t s);
+
+// Q4_K dequant-dot on CUDA cores, any N.
+int launch_q4k_gemv(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M,
+                    int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
+                    size_t y_col_bytes, cudaStream_t s);
+
+// tcgen05/TMEM GEMM for F16 weights (activations narrowed to f16 in the workspace).
+size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N);
+bool gemm_f16_applicable(int64_t M, int64_t K, int64_t N, const void* w, size_t w_row_bytes,
+                         const float* x, size_t x_col_bytes, const float* y, size_t y_col_bytes);
+int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M,
+                    int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
+                    size_t y_col_bytes, void* ws, size_t ws_bytes, cudaStream_t s);
+
+// Flash-attention decode (split-K over keys + combine).
+size_t fa_workspace_bytes(const mlzc_fa_desc* d);
+int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
+                      cudaStream_t s);
+
+// Dispatch of one validated mul_mat to the kernel that fits its shape (GEMV, Q4_K,
+// tensor-core GEMM); asynchronous on `s`.
+int mul_mat_run(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64_t M, int64_t K,
+                const float* x, size_t x_cs, int64_t N, float* y, size_t y_cs, void* ws,
+                size_t ws_bytes, cudaStream_t s);
+size_t mul_mat_workspace(int w_type, int64_t M, int64_t K, int64_t N);
+
+// dst[n][r*m_loc + m] = src[r][n][m] for r < G: reorders all-gathered row slices into the
+// ggml [N][M] layout.
+int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,
+                          int64_t m_loc, cudaStream_t s);
+
+// Shape / type gate shared by the device entry point and the hook.
+int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                       const float* x, size_t x_col_bytes, int64_t N, const float* y,
+                       size_t y_col_bytes);
+int check_fa_args(const mlzc_fa_desc* d);
+
+}  // namespace mlzc

@@ -1,0 +1,80 @@
+"""Seeded synthetic operands in the shapes and value distributions of the benchmarked
+workloads (no model files are involved: weights are random-init of the named shapes).
+
+Host generators (numpy PCG64) feed the parity tests; the ``*_dev`` generators build the
+large benchmark operands directly in device memory with torch's seeded CUDA generator.
+
+Distributions:
+  F16 weights  N(0, 0.02) rounded to f16;  activations N(0, 1) f32.
+  Q4_K blocks  d, dmin = f16(|N(0, 0.01)|); 12 random scale bytes (every bit pattern is a
+               valid set of 6-bit scales/mins); qs uniform nibbles 0..15.
+  FA decode    q, k, v ~ N(0, 1)/sqrt(D) (k, v stored f16); kv lengths U{lo..hi}.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+QK_K = 256
+Q4K_BYTES = 144
+
+
+def seed_for(config: int, n: int) -> int:
+    """Per-row seed: 1000 + config*100 + N."""
+    return 1000 + 100 * config + n
+
+
+def rng(seed: int) -> np.random.Generator:
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+def f16_weights(g: np.random.Generator, M: int, K: int, std: float = 0.02) -> np.ndarray:
+    """(M, K) float16."""
+    return (g.standard_normal((M, K), dtype=np.float32) * std).astype(np.float16)
+
+
+def f32_acts(g: np.random.Generator, N: int, K: int) -> np.ndarray:
+    return g.standard_normal((N, K), dtype=np.float32)
+
+
+def q4k_blocks(g: np.random.Generator, M: int, K: int) -> np.ndarray:
+    """(M, K/256*144) uint8 Q4_K super-blocks."""
+    assert K % QK_K == 0
+    nb = K // QK_K
+    blk = g.integers(0, 256, size=(M, nb, Q4K_BYTES), dtype=np.uint8)
+    d = np.abs(g.standard_normal((M, nb, 2), dtype=np.float32) * 0.01).astype(np.float16)
+    blk[:, :, 0:4] = d.view(np.uint8).reshape(M, nb, 4)
+    return blk.reshape(M, nb * Q4K_BYTES)
+
+
+def fa_inputs(g: np.random.Generator, B: int, Hq: int, Hkv: int, L: int, D: int, NQ: int = 1):
+    """q (B, Hq, NQ, D) f32; k, v (B, Hkv, L, D) f16."""
+    s = 1.0 / np.sqrt(D)
+    q = (g.standard_normal((B, Hq, NQ, D), dtype=np.float32) * s).astype(np.float32)
+    k = (g.standard_normal((B, Hkv, L, D), dtype=np.float32) * s).astype(np.float16)
+    v = (g.standard_normal((B, Hkv, L, D), dtype=np.float32) * s).astype(np.float16)
+    return q, k, v
+
+
+def kv_lengths(g: np.random.Generator, B: int, lo: int, hi: int) -> np.ndarray:
+    return g.integers(lo, hi + 1, size=B, dtype=np.int64).astype(np.int32)
+
+
+# ---------------------------------------------------------------- device side
+
+def f16_weights_dev(gen, M: int, K: int, device, std: float = 0.02):
+    import torch
+    return (torch.randn((M, K), generator=gen, device=device, dtype=torch.float32) * std).to(torch.float16)
+
+
+def f32_acts_dev(gen, N: int, K: int, device):
+    import torch
+    return torch.randn((N, K), generator=gen, device=device, dtype=torch.float32)
+
+
+def q4k_blocks_dev(gen, M: int, K: int, device):
+    import torch
+    nb = K // QK_K
+    blk = torch.randint(0, 256, (M, nb, Q4K_BYTES), generator=gen, device=device, dtype=torch.uint8)
+    d = (torch.randn((M, nb, 2), generator=gen, device=device) * 0.01).abs().to(torch.float16)
+    blk[:, :, 0:4] = d.view(torch.uint8).reshape(M, nb, 4)
+    return blk.reshape(M, nb * Q4K_BYTES)

@@ -1,0 +1,104 @@
+"""Generates the golden fixtures of tests/golden/ (run in a checkout that has the
+reference tree and the gguf package; the fixtures are committed, this script is how
+they were made).
+
+* q4k_gguf.npz      -- Q4_K super-blocks and their dequantisation by the gguf 0.19.0
+                       Python decoder (gguf.quants.dequantize), the published GGUF
+                       algorithm the reference's Q4_K kernels implement.
+* fa_reference.npz  -- flash-attention decode cases and the outputs of the reference's
+                       own flash_attn_quantized (src/simd/flash_attention.cpp:291-410),
+                       compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
+* matmul_reference.npz -- tiny row-major matmuls through the reference's simd_matmul_f32
+                       scalar path (src/simd/simd_matmul.cpp:196-223).
+
+Usage: python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+import oracle  # noqa: E402
+
+
+def q4k_fixture() -> None:
+    from gguf import GGMLQuantizationType, quants
+    g = np.random.Generator(np.random.PCG64(7))
+    M, K = 6, 512
+    nb = K // 256
+    blk = g.integers(0, 256, size=(M, nb, 144), dtype=np.uint8)
+    d = np.abs(g.standard_normal((M, nb, 2)) * 0.01).astype(np.float16)
+    # edge values for d/dmin: zero, a subnormal, the largest finite half, negative
+    d[0, 0, 0] = np.float16(0.0)
+    d[1, 0, 1] = np.float16(6e-8)
+    d[2, 1, 0] = np.float16(65504.0)
+    d[3, 1, 1] = np.float16(-0.5)
+    blk[:, :, 0:4] = d.view(np.uint8).reshape(M, nb, 4)
+    blk[4, 0, 4:16] = 0xFF   # all scale/min bits set
+    blk[5, 1, 4:16] = 0x00   # all zero scales
+    blk = blk.reshape(M, nb * 144)
+    deq = quants.dequantize(blk, GGMLQuantizationType.Q4_K).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "q4k_gguf.npz"), blocks=blk, dequant=deq, K=K)
+
+
+def fa_fixture() -> None:
+    g = np.random.Generator(np.random.PCG64(11))
+    cases = {}
+    # (B, Hq, Hkv, L, D, NQ, mask, softcap, alibi)
+    specs = [
+        ("gqa4_l70_d64", 2, 8, 2, 70, 64, 1, False, 0.0, False),
+        ("mha_l1_d128", 1, 4, 4, 1, 128, 1, False, 0.0, False),
+        ("gqa4_l65_d128_mask", 2, 8, 2, 65, 128, 1, True, 0.0, False),
+        ("gqa2_l64_d64_softcap", 1, 4, 2, 64, 64, 1, False, 30.0, False),
+        ("gqa4_l63_d64_alibi", 1, 8, 2, 63, 64, 1, False, 0.0, True),
+        ("gqa4_nq3_l40_d64", 1, 8, 2, 40, 64, 3, True, 0.0, False),
+    ]
+    for name, B, Hq, Hkv, L, D, NQ, use_mask, softcap, alibi in specs:
+        s = 1.0 / np.sqrt(D)
+        q = (g.standard_normal((B, Hq, NQ, D)) * s * 4).astype(np.float32)
+        k = (g.standard_normal((B, Hkv, L, D)) * s * 4).astype(np.float16)
+        v = (g.standard_normal((B, Hkv, L, D)) * s).astype(np.float16)
+        mask = None
+        if use_mask:
+            mask = (g.standard_normal((NQ, L)) * 0.5).astype(np.float32)
+            mask[:, ::7] = -np.inf
+        mode = (oracle.FA_MODE_SOFTCAP if softcap else 0) | (oracle.FA_MODE_ALIBI if alibi else 0)
+        out = oracle.ref_flash_attn(q, k.view(np.uint16), v.view(np.uint16), float(s), mask=mask,
+                                    softcap=softcap, mode=mode)
+        assert oracle.ref_stub_hits() == 0
+        cases[name + "__q"] = q
+        cases[name + "__k"] = k.view(np.uint16)
+        cases[name + "__v"] = v.view(np.uint16)
+        if mask is not None:
+            cases[name + "__mask"] = mask
+        cases[name + "__meta"] = np.array([softcap, 1.0 if alibi else 0.0, s], dtype=np.float64)
+        cases[name + "__out"] = out
+    np.savez_compressed(os.path.join(HERE, "fa_reference.npz"), **cases)
+
+
+def matmul_fixture() -> None:
+    g = np.random.Generator(np.random.PCG64(13))
+    cases = {}
+    for i, (M, N, K) in enumerate([(4, 3, 8), (1, 1, 511), (7, 5, 14), (3, 1, 100)]):
+        a = g.standard_normal((M, K)).astype(np.float32)
+        b = g.standard_normal((K, N)).astype(np.float32)
+        cases[f"a{i}"] = a
+        cases[f"b{i}"] = b
+        cases[f"c{i}"] = oracle.ref_matmul_f32_small(a, b)
+    assert oracle.ref_stub_hits() == 0
+    np.savez_compressed(os.path.join(HERE, "matmul_reference.npz"), **cases)
+
+
+if __name__ == "__main__":
+    oracle.build()
+    if not oracle.ref_available():
+        sys.exit("oracle/_ref/libmlzref.so is missing: run `make -C oracle` where the reference tree exists")
+    q4k_fixture()
+    fa_fixture()
+    matmul_fixture()
+    print("fixtures written to", HERE)
