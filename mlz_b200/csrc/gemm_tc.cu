@@ -1,19 +1,588 @@
-// gemm_tc.cu -- tensor-core (tcgen05 / TMEM) GEMM for F16 weights.  Placeholder until
-// the kernel lands: reports "not applicable" so every F16 shape takes the CUDA-core path.
+// gemm_tc.cu -- F16-weight mul_mat on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces the prefill-shaped mul_mat of the reference: matrix_mult_avx512
+// (kernels/x86/matrix_mult_avx512.asm:118-282) behind simd_matmul_f16's convert-then-GEMM
+// (src/simd/simd_matmul.cpp:428-480), and the upstream F16 path the hook actually falls back
+// to for F16 weights (src/simd/ggml-cpu-simd.c:1314-1465: src1 narrowed to f16, then
+// ggml_vec_dot_f16 with fp32 accumulation).
+//
+// Y[n][m] = sum_k W[m][k] * f16(X[n][k]) with W: M x K f16 (K contiguous), X: N x K f32,
+// Y: N x M f32 (ggml dst layout).  Two launches per call:
+//   1. narrow X to f16 into the workspace (the same round-to-nearest-even the reference's
+//      F16 path applies to src1);
+//   2. a persistent warp-specialised GEMM, one CTA per SM:
+//        warp 0   TMA producer: 128x64 W tile + BNx64 X tile per stage (128-byte swizzle,
+//                 K-major), STAGES-deep mbarrier ring;
+//        warp 1   MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, M = 128,
+//                 N = BN, K = 16 per instruction, fp32 accumulator in TMEM; commits free
+//                 smem stages and publish finished accumulators;
+//        warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns, coalesced stores of
+//                 Y[n][m] (32 consecutive m per warp store).
+//      TMEM holds two accumulators (2*BN columns), so the epilogue of tile t overlaps the
+//      MMAs of tile t+1.  Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
+// Small tile counts split K across CTAs: each split stores its partial tile to the
+// workspace and the split that finishes a tile last sums the partials in split order, so
+// results are bitwise reproducible.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "internal.h"
 
 namespace mlzc {
+namespace {
 
-size_t gemm_f16_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
+constexpr int BM = 128;
+constexpr int BK = 64;                       // one 128-byte swizzle atom of f16
+constexpr int kEpiWarps = 4;
+constexpr int kGemmThreads = 64 + kEpiWarps * 32;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any single mbarrier wait
+constexpr int kSmemBudget = 200 * 1024;
 
-bool gemm_f16_applicable(int64_t, int64_t, int64_t, const void*, size_t, const float*, size_t,
-                         const float*, size_t) {
-    return false;
+// ------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-int launch_gemm_f16(const DeviceCtx*, const void*, size_t, int64_t, int64_t, const float*, size_t,
-                    int64_t, float*, size_t, void*, size_t, cudaStream_t) {
-    return fail(MLZC_ERR_UNSUPPORTED, "tensor-core GEMM not built");
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase of parity `parity` of `bar`; gives up after kWaitNs (setting the
+// error word and the CTA's abort flag) or when another role of the CTA already aborted.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitNs) {
+                atomicOr(err, MLZC_DEVERR_WAIT_TIMEOUT);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Shared-memory word next to the abort flag: "this CTA reduces the current tile".
+__device__ __forceinline__ volatile int* abort_flag_or_last(volatile int* abort_flag) { return abort_flag + 1; }
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// UMMA shared-memory descriptor of a K-major tile written by TMA with 128-byte swizzle:
+// rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked along M/N.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);   // start address        [0, 14)
+    d |= (uint64_t)1 << 16;                     // leading byte offset  [16, 30) (unused: swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset   [32, 46): 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                     // descriptor version   [46, 48) = 1 on sm_100
+    d |= (uint64_t)2 << 61;                     // layout: SWIZZLE_128B [61, 64)
+    return d;
+}
+
+// Instruction descriptor, kind::f16: A = B = f16, D = f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+    return (1u << 4)                             // D format f32        [4, 6)
+           | (0u << 7) | (0u << 10)              // A, B format f16     [7, 10), [10, 13)
+           | (0u << 15) | (0u << 16)             // A, B K-major        15, 16
+           | ((uint32_t)(N >> 3) << 17)          // N / 8               [17, 23)
+           | ((uint32_t)(M >> 4) << 24);         // M / 16              [24, 29)
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// --------------------------------------------------------------------- kernels
+
+template <int BN>
+struct TileCfg {
+    static constexpr uint32_t kABytes = BM * BK * 2;
+    static constexpr uint32_t kBBytes = BN * BK * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (kSmemBudget - 2048) / kStageBytes > 12 ? 12 : (kSmemBudget - 2048) / kStageBytes;
+    static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct GemmArgs {
+    float* y;
+    size_t y_cs;          // bytes between output columns (tokens)
+    int M, N, K;
+    int num_m, num_n;     // tiles
+    int kblocks;          // BK blocks of the whole K
+    int splits;           // K splits; > 1: partial tiles in `part`, the last split to finish sums them
+    int num_work;         // num_m * num_n * splits
+    float* part;          // [splits][tiles][BN][BM] partial accumulators (splits > 1)
+    int* tile_count;      // per tile: splits finished (zeroed by the narrowing kernel)
+    unsigned int* err;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+    using C = TileCfg<BN>;
+    constexpr int STAGES = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smA = smem;
+    uint8_t* smB = smem + STAGES * C::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = bars + 2 * STAGES + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tfull[b]), 1);
+            mbar_init(smem_u32(&tempty[b]), kEpiWarps * 32);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                     "r"(C::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    const int kper = (g.kblocks + g.splits - 1) / g.splits;   // k-blocks per split
+    auto work_coords = [&](int w, int& m0, int& n0, int& kb0, int& kb1) {
+        const int tile = w % (g.num_m * g.num_n);
+        const int split = w / (g.num_m * g.num_n);
+        m0 = (tile % g.num_m) * BM;
+        n0 = (tile / g.num_m) * BN;
+        kb0 = split * kper;
+        kb1 = min(kb0 + kper, g.kblocks);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            uint32_t it = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; w < g.num_work && ok; w += gridDim.x) {
+                int m0, n0, kb0, kb1;
+                work_coords(w, m0, n0, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, g.err)) { ok = false; break; }
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_expect_tx(fb, C::kStageBytes);
+                    tma_load_2d(smem_u32(smA + s * C::kABytes), &tmA, fb, kb * BK, m0);
+                    tma_load_2d(smem_u32(smB + s * C::kBBytes), &tmB, fb, kb * BK, n0);
+                }
+            }
+            if (!ok) {
+                // let the copies already issued land before the CTA's smem goes away
+                const uint32_t issued = it;
+                for (uint32_t j = issued > (uint32_t)STAGES ? issued - STAGES : 0; j < issued; ++j) {
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try_wait(smem_u32(&full[j % STAGES]), (j / STAGES) & 1) && global_ns() - t0 < kWaitNs) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer
+            constexpr uint32_t idesc = umma_idesc_f16(BM, BN);
+            uint32_t it = 0, t = 0;
+            bool ok = true;
+            uint32_t last_commit_bar = 0, last_commit_parity = 0;
+            for (int w = blockIdx.x; w < g.num_work && ok; w += gridDim.x, ++t) {
+                int m0, n0, kb0, kb1;
+                work_coords(w, m0, n0, kb0, kb1);
+                const uint32_t b = t & 1;
+                const uint32_t aph = (t >> 1) & 1;
+                if (!mbar_wait(smem_u32(&tempty[b]), aph ^ 1, abort_flag, g.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + b * BN;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, g.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc_sw128(smem_u32(smA + s * C::kABytes));
+                    const uint64_t bd = umma_desc_sw128(smem_u32(smB + s * C::kBBytes));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        // +32 bytes along K inside the swizzle atom = +2 in the encoded address
+                        umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&empty[s]));
+                    last_commit_bar = smem_u32(&empty[s]);
+                    last_commit_parity = ph;
+                }
+                if (!ok) break;
+                umma_commit(smem_u32(&tfull[b]));
+            }
+            if (!ok && last_commit_bar) {
+                // wait (bounded) for the MMAs already issued before the TMEM is released
+                const uint64_t t0 = global_ns();
+                while (!mbar_try_wait(last_commit_bar, last_commit_parity) && global_ns() - t0 < kWaitNs) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: TMEM -> registers -> Y
+        const int quarter = warp & 3;            // TMEM lanes [32*quarter, 32*quarter + 32)
+        uint32_t t = 0;
+        for (int w = blockIdx.x; w < g.num_work; w += gridDim.x, ++t) {
+            int m0, n0, kb0, kb1;
+            work_coords(w, m0, n0, kb0, kb1);
+            const uint32_t b = t & 1;
+            const uint32_t aph = (t >> 1) & 1;
+            if (!mbar_wait(smem_u32(&tfull[b]), aph, abort_flag, g.err)) break;
+            tc_fence_after();
+            const int row = quarter * 32 + lane;      // row of the tile this thread owns
+            const int m = m0 + row;
+            char* ybase = reinterpret_cast<char*>(g.y) + (size_t)m * 4;
+            const int tiles = g.num_m * g.num_n;
+            const int tile = w % tiles;
+            const int split = w / tiles;
+            float* mypart = g.part + ((size_t)split * tiles + tile) * (size_t)(BM * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * BN + c, r);
+                tmem_ld_wait();
+                if (g.splits == 1) {
+                    if (m < g.M) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = n0 + c + j;
+                            if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[j]);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) mypart[(size_t)(c + j) * BM + row] = __uint_as_float(r[j]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tempty[b]));
+            if (g.splits > 1) {
+                // Deterministic split-K: the split that finishes a tile last sums all of the
+                // tile's partials in split order 0..S-1 (no CTA ever waits for another).
+                __threadfence();
+                asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+                if (threadIdx.x == 64) {
+                    const int done = atomicAdd(&g.tile_count[tile], 1);
+                    *abort_flag_or_last(abort_flag) = (done == g.splits - 1) ? 1 : 0;
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+                if (*abort_flag_or_last(abort_flag)) {
+                    __threadfence();
+                    if (m < g.M) {
+                        const float* p0 = g.part + (size_t)tile * (BM * BN) + row;
+                        for (int c = 0; c < BN; ++c) {
+                            const int n = n0 + c;
+                            if (n >= g.N) break;
+                            float acc = 0.0f;
+                            for (int sp = 0; sp < g.splits; ++sp)
+                                acc += __ldcg(p0 + (size_t)sp * tiles * (BM * BN) + (size_t)c * BM);
+                            *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = acc;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::kTmemCols)
+                     : "memory");
+    }
+}
+
+// X (N x K f32, column stride x_cs bytes) -> X16 (N x kp f16, zero padded), RNE.
+__global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N, int K, __half* __restrict__ x16,
+                                  int kp, int vec, int* __restrict__ tile_count, int ntiles) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ntiles; i += gridDim.x * blockDim.x) tile_count[i] = 0;
+    const int cpr = kp / 8;
+    const int64_t total = (int64_t)N * cpr;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i / cpr);
+        const int k0 = (int)(i % cpr) * 8;
+        const float* xr = reinterpret_cast<const float*>(x + (size_t)row * x_cs);
+        float v[8];
+        if (vec && k0 + 8 <= K) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k0));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k0 + 4));
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? xr[k0 + e] : 0.0f;
+        }
+        uint4 o;
+        __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+        __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
+        o.x = *reinterpret_cast<uint32_t*>(&h0);
+        o.y = *reinterpret_cast<uint32_t*>(&h1);
+        o.z = *reinterpret_cast<uint32_t*>(&h2);
+        o.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(x16 + (size_t)row * kp + k0) = o;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode;
+}
+
+// 2-D f16 tensor map: rows of `inner` elements, `rows` rows `row_bytes` apart; box
+// `box_rows` x 64 elements with 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+    auto enc = encoder();
+    if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MLZC_OK;
+}
+
+size_t x16_bytes(int64_t N, int64_t K) {
+    const int64_t kp = (K + 7) / 8 * 8;
+    return ((size_t)N * kp * 2 + 255) / 256 * 256;
+}
+
+struct GemmPlan {
+    int BN, num_m, num_n, kblocks, splits;
+    size_t x16, counters, partials;   // workspace segments (bytes)
+    size_t total() const { return x16 + counters + partials; }
+};
+
+// Tile width and K split for a problem: the widest tile unless a narrower one fills the
+// SMs' waves clearly better; K split when the tiles cannot occupy half of the SMs.
+GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
+    GemmPlan p{};
+    p.num_m = (int)((M + BM - 1) / BM);
+    p.kblocks = (int)((K + BK - 1) / BK);
+    if (N <= 16) p.BN = 16;
+    else if (N <= 32) p.BN = 32;
+    else if (N <= 64) p.BN = 64;
+    else if (N <= 128) p.BN = 128;
+    else {
+        auto score = [&](int bn, double eff) {
+            const long tiles = (long)p.num_m * ((N + bn - 1) / bn);
+            const long waves = (tiles + sm_count - 1) / sm_count;
+            return eff * (double)tiles / (double)(waves * sm_count);
+        };
+        p.BN = score(128, 0.85) > score(256, 1.0) ? 128 : 256;
+    }
+    p.num_n = (int)((N + p.BN - 1) / p.BN);
+    const int tiles = p.num_m * p.num_n;
+    int splits = 1;
+    if (tiles * 2 <= sm_count) splits = std::max(1, std::min(sm_count / tiles, p.kblocks / 4));
+    if (splits > 1) {
+        // every split must own >= 1 k-block: an empty split would add a stale accumulator
+        const int kper = (p.kblocks + splits - 1) / splits;
+        splits = (p.kblocks + kper - 1) / kper;
+    }
+    p.splits = splits;
+    p.x16 = x16_bytes(N, K);
+    p.counters = splits > 1 ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
+    p.partials = splits > 1 ? (size_t)splits * tiles * BM * p.BN * 4 : 0;
+    return p;
+}
+
+int current_sm_count() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 148;   // B200
+    }
+    return sms;
+}
+
+template <int BN>
+int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs g, cudaStream_t s) {
+    using Cfg = TileCfg<BN>;
+    static bool attr_set[64] = {};
+    const int dev = c->device < 64 ? c->device : 63;
+    if (!attr_set[dev]) {
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(gemm_f16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)Cfg::kSmemBytes));
+        attr_set[dev] = true;
+    }
+    const int grid = std::min(g.num_work, c->sm_count);
+    gemm_f16_tc_kernel<BN><<<grid, kGemmThreads, Cfg::kSmemBytes, s>>>(ta, tb, g);
+    MLZC_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    return MLZC_OK;
+}
+
+}  // namespace
+
+size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N) { return plan_gemm(M, K, N, current_sm_count()).total(); }
+
+bool gemm_f16_applicable(int64_t M, int64_t K, int64_t N, const void* w, size_t w_row_bytes, const float*, size_t,
+                         const float*, size_t) {
+    if (M < 1 || K < 1 || N < 1) return false;
+    if ((uintptr_t)w % 16 != 0 || w_row_bytes % 16 != 0) return false;   // TMA base / stride rules
+    if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || K > (1ll << 31) - 1) return false;
+    return true;
+}
+
+int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                    cudaStream_t s) {
+    const GemmPlan pl = plan_gemm(M, K, N, c->sm_count);
+    const size_t need = pl.total();
+    if (!ws || ws_bytes < need)
+        return fail(MLZC_ERR_NOMEM, "mul_mat (tensor-core path): workspace of %zu bytes needed, %zu given", need, ws_bytes);
+    const int64_t kp = (K + 7) / 8 * 8;
+    char* wsc = static_cast<char*>(ws);
+    __half* x16 = reinterpret_cast<__half*>(wsc);
+    int* counters = reinterpret_cast<int*>(wsc + pl.x16);
+    float* partials = reinterpret_cast<float*>(wsc + pl.x16 + pl.counters);
+    const int tiles = pl.num_m * pl.num_n;
+    {
+        const int vec = ((uintptr_t)x % 16 == 0 && x_col_bytes % 16 == 0) ? 1 : 0;
+        const int64_t total = N * (kp / 8);
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)c->sm_count * 8));
+        narrow_f16_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const char*>(x), x_col_bytes, (int)N, (int)K, x16,
+                                               (int)kp, vec, counters, pl.splits > 1 ? tiles : 0);
+        MLZC_CUDA_TRY(cudaGetLastError());
+        count_launch();
+    }
+    const int BN = pl.BN;
+    CUtensorMap ta, tb;
+    int st = make_map(&ta, w, (uint64_t)K, (uint64_t)M, w_row_bytes, BM);
+    if (st != MLZC_OK) return st;
+    st = make_map(&tb, x16, (uint64_t)K, (uint64_t)N, (uint64_t)kp * 2, (uint32_t)BN);
+    if (st != MLZC_OK) return st;
+
+    GemmArgs g{};
+    g.y = y;
+    g.y_cs = y_col_bytes;
+    g.M = (int)M;
+    g.N = (int)N;
+    g.K = (int)K;
+    g.num_m = pl.num_m;
+    g.num_n = pl.num_n;
+    g.kblocks = pl.kblocks;
+    g.err = c->err;
+    g.splits = pl.splits;
+    g.num_work = tiles * pl.splits;
+    g.part = partials;
+    g.tile_count = counters;
+    switch (BN) {
+        case 16: return launch_tile<16>(c, ta, tb, g, s);
+        case 32: return launch_tile<32>(c, ta, tb, g, s);
+        case 64: return launch_tile<64>(c, ta, tb, g, s);
+        case 128: return launch_tile<128>(c, ta, tb, g, s);
+        default: return launch_tile<256>(c, ta, tb, g, s);
+    }
 }
 
 }  // namespace mlzc

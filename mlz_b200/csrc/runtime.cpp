@@ -473,18 +473,44 @@ int run_node(const void* key, int ith, int nth, F&& work) {
 }
 
 using WeightKey = std::tuple<const void*, int, int64_t, int64_t, size_t, int>;
+struct CachedWeight {
+    mlzc_weight w = nullptr;
+    uint64_t fingerprint = 0;
+};
 std::mutex g_wcache_mu;
-std::map<WeightKey, mlzc_weight> g_wcache;
+std::map<WeightKey, CachedWeight> g_wcache;
+
+// FNV-1a over 64-byte samples at the start, middle and end of the host buffer.  ggml
+// weights are immutable for a model's lifetime, so (pointer, type, shape) identifies
+// them; the fingerprint catches a buffer reused for other data at the same address
+// (e.g. after a model reload) without hashing the whole tensor on every call.
+uint64_t fingerprint(const void* data, size_t bytes) {
+    const unsigned char* p = static_cast<const unsigned char*>(data);
+    uint64_t h = 1469598103934665603ull;
+    const size_t win = bytes < 64 ? bytes : 64;
+    const size_t offs[3] = {0, bytes / 2 - (bytes / 2 >= win / 2 ? win / 2 : 0), bytes - win};
+    for (size_t o : offs)
+        for (size_t i = 0; i < win; ++i) h = (h ^ p[o + i]) * 1099511628211ull;
+    return h;
+}
 
 mlzc_weight cached_weight(const mlzc_tensor* src0, int device, int* status) {
     const WeightKey key{src0->data, src0->type, src0->ne[0], src0->ne[1], src0->nb[1], device};
+    const size_t row = src0->type == MLZC_TYPE_Q4_K ? (size_t)(src0->ne[0] / 256) * 144
+                                                     : (size_t)src0->ne[0] * (src0->type == MLZC_TYPE_F16 ? 2 : 4);
+    const size_t bytes = src0->ne[1] > 0 ? (size_t)(src0->ne[1] - 1) * src0->nb[1] + row : 0;
+    const uint64_t fp = bytes ? fingerprint(src0->data, bytes) : 0;
     std::lock_guard<std::mutex> lk(g_wcache_mu);
     auto it = g_wcache.find(key);
-    if (it != g_wcache.end()) return it->second;
+    if (it != g_wcache.end()) {
+        if (it->second.fingerprint == fp) return it->second.w;
+        mlzc_weight_free(it->second.w);
+        g_wcache.erase(it);
+    }
     mlzc_weight w = nullptr;
     *status = mlzc_weight_upload(device, src0->type, src0->data, src0->nb[1], src0->ne[1], src0->ne[0], &w);
     if (*status != MLZC_OK) return nullptr;
-    g_wcache[key] = w;
+    g_wcache[key] = CachedWeight{w, fp};
     return w;
 }
 
@@ -509,7 +535,7 @@ bool mul_mat_gate(const mlzc_tensor* s0, const mlzc_tensor* s1, const mlzc_tenso
 
 extern "C" int mlzc_weight_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_wcache_mu);
-    for (auto& kv : g_wcache) mlzc_weight_free(kv.second);
+    for (auto& kv : g_wcache) mlzc_weight_free(kv.second.w);
     g_wcache.clear();
     return MLZC_OK;
 }

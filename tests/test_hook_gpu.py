@@ -19,6 +19,7 @@ def _views(w, x, y, wtype, K=None):
 
 @pytest.mark.parametrize("nth", [1, 4, 16])
 def test_f16_all_threads_handled(dev, nth):
+    mlz_b200.lib().mlzc_weight_cache_clear()
     g = synth.rng(600 + nth)
     w = synth.f16_weights(g, 1000, 768)
     x = synth.f32_acts(g, 3, 768)
@@ -50,6 +51,20 @@ def test_q4k_and_f32_through_hook(dev):
     y2 = np.zeros((2, 50), dtype=np.float32)
     assert mlz_b200.ggml_simd_try_mul_mat(*_views(wf, x, y2, mlz_b200.TYPE_F32)) == 1
     assert oracle.rel_err(y2, oracle.mul_mat_f32(wf, x)) <= 1e-3
+
+
+def test_reused_host_buffer_is_reuploaded(dev):
+    """A host buffer refilled with other weights at the same address is detected by the
+    cache's content fingerprint and uploaded again."""
+    g = synth.rng(615)
+    w = synth.f16_weights(g, 128, 256)
+    x = synth.f32_acts(g, 2, 256)
+    y = np.zeros((2, 128), dtype=np.float32)
+    views = _views(w, x, y, mlz_b200.TYPE_F16)
+    assert mlz_b200.ggml_simd_try_mul_mat(*views) == 1
+    w[:] = synth.f16_weights(g, 128, 256)      # same address, new contents
+    assert mlz_b200.ggml_simd_try_mul_mat(*views) == 1
+    assert oracle.rel_err(y, oracle.mul_mat_f16(w.view(np.uint16), x)) <= 1e-3
 
 
 def test_weight_cache_reuse_and_strided_dst(dev):

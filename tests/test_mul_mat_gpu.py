@@ -81,6 +81,7 @@ def test_power_of_two_scaling_is_exact_full_size(dev, N):
     gen = torch.Generator(device=dev).manual_seed(5)
     w = synth.f16_weights_dev(gen, 8192, 3072, dev)
     x = torch.randn((N, 3072), generator=gen, device=dev)
+    x = torch.where(x.abs() < 1e-3, torch.zeros_like(x), x)  # keep 4x out of f16 subnormals
     y = mlz_b200.mul_mat(w, x)
     y4 = mlz_b200.mul_mat(w, 4.0 * x)
     torch.cuda.synchronize()
