@@ -331,6 +331,9 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             const int tile = w % tiles;
             const int split = w / tiles;
             float* mypart = g.part + ((size_t)split * tiles + tile) * (size_t)(BM * BN);
+            // columns per TMEM load: 32, or BN for the 16-wide tile (whose 32-column load
+            // also returns the other accumulator's 16 columns, which are not this tile's)
+            constexpr int kCols = BN < 32 ? BN : 32;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
@@ -339,14 +342,14 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 if (g.splits == 1) {
                     if (m < g.M) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
+                        for (int j = 0; j < kCols; ++j) {
                             const int n = n0 + c + j;
                             if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[j]);
                         }
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) mypart[(size_t)(c + j) * BM + row] = __uint_as_float(r[j]);
+                    for (int j = 0; j < kCols; ++j) mypart[(size_t)(c + j) * BM + row] = __uint_as_float(r[j]);
                 }
             }
             tc_fence_before();
