@@ -137,6 +137,17 @@ int mlzc_flash_attn_workspace_bytes(const mlzc_fa_desc* desc, size_t* out_bytes)
 int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Same computation as mlzc_flash_attn_dev, for callers that cannot allocate device memory
+ * per call (a host callback, a thread that must not block on a device-wide allocation, an
+ * engine with a fixed memory budget, a binding without an allocator).  No counterpart in
+ * the reference.  It allocates nothing: the split partials go to a fixed 16 MiB scratch
+ * array inside the library's device image, held by every GPU that loads the library until
+ * the process exits.  Calls needing more than that (mlzc_flash_attn_workspace_bytes)
+ * fail with MLZC_ERR_NOMEM.  The first call on a device looks up the array's device
+ * address (once, with that device current): make it before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race; serialise them. */
+int mlzc_flash_attn_dev_noalloc(const mlzc_fa_desc* desc, void* stream);
+
 /* ------------------------------------------------ host-pointer (hook) level */
 
 /* The subset of struct ggml_tensor the hook reads. */

@@ -24,7 +24,7 @@ UNIQUE_ID_BYTES = 128
 EXPORTS = (
     "mlzc_launch_count", "mlzc_last_error", "mlzc_version", "mlzc_init", "mlzc_shutdown", "mlzc_device_errors",
     "mlzc_mul_mat_workspace_bytes", "mlzc_mul_mat_dev",
-    "mlzc_flash_attn_workspace_bytes", "mlzc_flash_attn_dev",
+    "mlzc_flash_attn_workspace_bytes", "mlzc_flash_attn_dev", "mlzc_flash_attn_dev_noalloc",
     "mlzc_try_mul_mat", "mlzc_try_flash_attn",
     "mlzc_weight_upload", "mlzc_weight_free", "mlzc_mul_mat", "mlzc_weight_cache_clear",
     "mlzc_comm_unique_id", "mlzc_comm_init", "mlzc_comm_destroy",
@@ -90,6 +90,7 @@ def _declare(L: C.CDLL) -> None:
     L.mlzc_mul_mat_dev.argtypes = [i32, vp, sz, i64, i64, vp, sz, i64, vp, sz, vp, sz, vp]
     L.mlzc_flash_attn_workspace_bytes.argtypes = [C.POINTER(FaDesc), psz]
     L.mlzc_flash_attn_dev.argtypes = [C.POINTER(FaDesc), vp, sz, vp]
+    L.mlzc_flash_attn_dev_noalloc.argtypes = [C.POINTER(FaDesc), vp]
     L.mlzc_try_mul_mat.argtypes = [C.POINTER(TensorView)] * 3 + [i32, i32]
     L.mlzc_try_flash_attn.argtypes = [C.POINTER(FaDesc), i32, i32]
     L.mlzc_weight_upload.argtypes = [i32, i32, vp, sz, i64, i64, C.POINTER(vp)]

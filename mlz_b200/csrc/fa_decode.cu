@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "internal.h"
 
@@ -410,3 +411,67 @@ int launch_flash_attn(const DeviceCtx*, const mlzc_fa_desc* d, void* ws, size_t 
 }
 
 }  // namespace mlzc
+
+// ======================================================================
+// Allocation-free flash-attention decode (mlzc_flash_attn_dev_noalloc).
+//
+// Some callers cannot allocate device memory for each call: code that runs where a
+// cudaMalloc would synchronise the device or be refused (a host callback, a thread that
+// must never block behind other streams, an engine whose memory is fully budgeted up
+// front), or a binding that simply has no allocator to hand us a workspace.  For them
+// this variant keeps the split-K partials of the decode kernel in one fixed scratch
+// array that lives in the library's device image instead of a caller workspace.
+//
+// The array is a file-scope __device__ variable, so every GPU that loads this library
+// holds kNoAllocScratchBytes of it until the process exits, whether or not the entry
+// point is used.  Host code cannot use the array's name as a device address (on the host
+// it names a stand-in object), so the device address is looked up with
+// cudaGetSymbolAddress -- once per device, on the first call made while that device is
+// current, and cached.  That first call therefore does the set-up; make it before any
+// stream capture.
+//
+// Every call shares the one array and it keeps whatever the previous call left in it.
+// Nothing in it has to start at zero: each call writes every partial record it later
+// reads.  Calls whose kernels overlap on the GPU (on different streams, or from several
+// host threads) race on the array and corrupt each other's results; serialise them.
+// ======================================================================
+namespace mlzc {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB per device
+static __device__ __align__(256) float g_fa_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+}  // namespace
+}  // namespace mlzc
+
+extern "C" int mlzc_flash_attn_dev_noalloc(const mlzc_fa_desc* desc, void* stream) {
+    using namespace mlzc;
+    int st = check_fa_args(desc);
+    if (st != MLZC_OK) return st;
+    const size_t need = fa_workspace_bytes(desc);
+    if (need > kNoAllocScratchBytes)
+        return fail(MLZC_ERR_NOMEM,
+                    "flash_attn (allocation-free): this call needs %zu bytes of split scratch but the fixed "
+                    "scratch holds %zu; use mlzc_flash_attn_dev with a workspace",
+                    need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    if (need > 0) {
+        int dev = 0;
+        MLZC_CUDA_TRY(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= kNoAllocMaxDevices)
+            return fail(MLZC_ERR_INVALID, "flash_attn (allocation-free): device %d beyond %d", dev, kNoAllocMaxDevices);
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_fa_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(flash-attention scratch)");
+            g_noalloc_addr[dev] = p;
+        }
+        scratch = g_noalloc_addr[dev];
+    }
+    return launch_flash_attn(nullptr, desc, scratch, kNoAllocScratchBytes, static_cast<cudaStream_t>(stream));
+}
