@@ -10,16 +10,20 @@
 // Y: N x M f32 (ggml dst layout).  Two launches per call:
 //   1. narrow X to f16 into the workspace (the same round-to-nearest-even the reference's
 //      F16 path applies to src1);
-//   2. a persistent warp-specialised GEMM, one CTA per SM:
-//        warp 0   TMA producer: 128x64 W tile + BNx64 X tile per stage (128-byte swizzle,
-//                 K-major), STAGES-deep mbarrier ring;
-//        warp 1   MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16, M = 128,
-//                 N = BN, K = 16 per instruction, fp32 accumulator in TMEM; commits free
-//                 smem stages and publish finished accumulators;
+//   2. a persistent warp-specialised GEMM, one CTA per SM, output tile (128*MT) x BN:
+//        warp 0   TMA producer: (128*MT)x64 W box + BNx64 X box per stage (128-byte
+//                 swizzle, K-major), STAGES-deep mbarrier ring;
+//        warp 1   MMA issuer (one thread): MT x tcgen05.mma.cta_group::1.kind::f16
+//                 (M = 128, N = BN, K = 16) per K step, the MT M-tiles sharing the X tile,
+//                 fp32 accumulators in TMEM; commits free smem stages and publish
+//                 finished accumulators;
 //        warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns, coalesced stores of
 //                 Y[n][m] (32 consecutive m per warp store).
-//      TMEM holds two accumulators (2*BN columns), so the epilogue of tile t overlaps the
-//      MMAs of tile t+1.  Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
+//      When two accumulator sets fit in TMEM (2*MT*BN <= 512 columns) the epilogue of
+//      tile t overlaps the MMAs of tile t+1.  MT = 2 (256 x 256 per SM) needs 64 KB of
+//      operands per 1024 MMA cycles instead of 48 KB per 512 for 128 x 256, which is what
+//      bounds this kernel (no TMA multicast is used anywhere).  Every mbarrier wait is
+//      bounded (MLZC_DEVERR_WAIT_TIMEOUT).
 // Small tile counts split K across CTAs: each split stores its partial tile to the
 // workspace and the split that finishes a tile last sums the partials in split order, so
 // results are bitwise reproducible.
@@ -98,14 +102,18 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile i
     }
 }
 
-// Shared-memory word next to the abort flag: "this CTA reduces the current tile".
-__device__ __forceinline__ volatile int* abort_flag_or_last(volatile int* abort_flag) { return abort_flag + 1; }
-
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+// Contiguous bulk copy global -> shared, completing `bytes` on the mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -166,13 +174,23 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // --------------------------------------------------------------------- kernels
 
-template <int BN>
+// MT M-tiles of 128 rows share one BN-column X tile per stage: an SM computes a
+// (128*MT) x BN output tile with MT UMMAs per K step.  The per-SM operand feed per MMA
+// cycle falls with MT (48 KB per 512 MMA cycles for 128x256, 64 KB per 1024 for 256x256),
+// which is what bounds this kernel without cross-SM multicast.
+template <int BN, int MT>
 struct TileCfg {
-    static constexpr uint32_t kABytes = BM * BK * 2;
-    static constexpr uint32_t kBBytes = BN * BK * 2;
+    static constexpr int kRows = BM * MT;
+    static constexpr uint32_t kABytes = (uint32_t)kRows * BK * 2;
+    static constexpr uint32_t kBBytes = (uint32_t)BN * BK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = (kSmemBudget - 2048) / kStageBytes > 12 ? 12 : (kSmemBudget - 2048) / kStageBytes;
-    static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int kAccCols = MT * BN;                           // one accumulator set
+    static constexpr int kBufs = 2 * kAccCols <= 512 ? 2 : 1;          // double-buffered when TMEM allows
+    static constexpr uint32_t kTmemCols = kBufs * kAccCols < 32 ? 32u
+                                          : (kBufs * kAccCols <= 64 ? 64u
+                                          : (kBufs * kAccCols <= 128 ? 128u
+                                          : (kBufs * kAccCols <= 256 ? 256u : 512u)));
     static constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -180,20 +198,23 @@ struct GemmArgs {
     float* y;
     size_t y_cs;          // bytes between output columns (tokens)
     int M, N, K;
-    int num_m, num_n;     // tiles
+    int num_m, num_n;     // tiles ((128*MT) x BN)
     int kblocks;          // BK blocks of the whole K
     int splits;           // K splits; > 1: partial tiles in `part`, the last split to finish sums them
     int num_work;         // num_m * num_n * splits
-    float* part;          // [splits][tiles][BN][BM] partial accumulators (splits > 1)
+    const uint8_t* x16t;  // narrowed activations, one pre-swizzled BN x 64 block per (n-block, k-block)
+    float* part;          // [splits][tiles][BN][128*MT] partial accumulators (splits > 1)
     int* tile_count;      // per tile: splits finished (zeroed by the narrowing kernel)
     unsigned int* err;
 };
 
-template <int BN>
+template <int BN, int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    using C = TileCfg<BN>;
+gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
+    using C = TileCfg<BN, MT>;
     constexpr int STAGES = C::kStages;
+    constexpr int NBUF = C::kBufs;
+    constexpr int ROWS = C::kRows;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smA = smem;
@@ -205,6 +226,7 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     uint64_t* tempty = bars + 2 * STAGES + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* last_flag = abort_flag + 1;   // "this CTA sums the current split tile"
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -216,12 +238,11 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(smem_u32(&tfull[b]), 1);
-            mbar_init(smem_u32(&tempty[b]), kEpiWarps * 32);
+            mbar_init(smem_u32(&tempty[b]), kEpiWarps);   // one arrival per epilogue warp
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -234,11 +255,12 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
+    const int tiles = g.num_m * g.num_n;
     const int kper = (g.kblocks + g.splits - 1) / g.splits;   // k-blocks per split
     auto work_coords = [&](int w, int& m0, int& n0, int& kb0, int& kb1) {
-        const int tile = w % (g.num_m * g.num_n);
-        const int split = w / (g.num_m * g.num_n);
-        m0 = (tile % g.num_m) * BM;
+        const int tile = w % tiles;
+        const int split = w / tiles;
+        m0 = (tile % g.num_m) * ROWS;
         n0 = (tile / g.num_m) * BN;
         kb0 = split * kper;
         kb1 = min(kb0 + kper, g.kblocks);
@@ -259,7 +281,8 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const uint32_t fb = smem_u32(&full[s]);
                     mbar_expect_tx(fb, C::kStageBytes);
                     tma_load_2d(smem_u32(smA + s * C::kABytes), &tmA, fb, kb * BK, m0);
-                    tma_load_2d(smem_u32(smB + s * C::kBBytes), &tmB, fb, kb * BK, n0);
+                    bulk_load(smem_u32(smB + s * C::kBBytes),
+                              g.x16t + ((size_t)(n0 / BN) * g.kblocks + kb) * C::kBBytes, C::kBBytes, fb);
                 }
             }
             if (!ok) {
@@ -282,11 +305,11 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             for (int w = blockIdx.x; w < g.num_work && ok; w += gridDim.x, ++t) {
                 int m0, n0, kb0, kb1;
                 work_coords(w, m0, n0, kb0, kb1);
-                const uint32_t b = t & 1;
-                const uint32_t aph = (t >> 1) & 1;
+                const uint32_t b = NBUF == 2 ? (t & 1) : 0;
+                const uint32_t aph = NBUF == 2 ? ((t >> 1) & 1) : (t & 1);
                 if (!mbar_wait(smem_u32(&tempty[b]), aph ^ 1, abort_flag, g.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + b * BN;
+                const uint32_t d_tmem = tmem_base + b * C::kAccCols;
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
@@ -296,8 +319,13 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const uint64_t bd = umma_desc_sw128(smem_u32(smB + s * C::kBBytes));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
-                        // +32 bytes along K inside the swizzle atom = +2 in the encoded address
-                        umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+#pragma unroll
+                        for (int i = 0; i < MT; ++i) {
+                            // M-tile i starts 128 rows (16 KB, = 1024 in the encoded address) later;
+                            // +32 bytes along K inside the swizzle atom = +2 in the encoded address
+                            umma_f16(d_tmem + i * BN, ad + (uint64_t)i * (BM * BK * 2 >> 4) + 2 * k, bd + 2 * k, idesc,
+                                     (kb > kb0 || k > 0) ? 1u : 0u);
+                        }
                     }
                     umma_commit(smem_u32(&empty[s]));
                     last_commit_bar = smem_u32(&empty[s]);
@@ -314,46 +342,48 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             }
         }
     } else {
-        // ---------------- epilogue: TMEM -> registers -> Y
+        // ---------------- epilogue: TMEM -> registers -> Y (or the split partials)
         const int quarter = warp & 3;            // TMEM lanes [32*quarter, 32*quarter + 32)
+        // columns per TMEM load: 32, or BN for the 16-wide tile
+        constexpr int kCols = BN < 32 ? BN : 32;
         uint32_t t = 0;
         for (int w = blockIdx.x; w < g.num_work; w += gridDim.x, ++t) {
             int m0, n0, kb0, kb1;
             work_coords(w, m0, n0, kb0, kb1);
-            const uint32_t b = t & 1;
-            const uint32_t aph = (t >> 1) & 1;
+            const uint32_t b = NBUF == 2 ? (t & 1) : 0;
+            const uint32_t aph = NBUF == 2 ? ((t >> 1) & 1) : (t & 1);
             if (!mbar_wait(smem_u32(&tfull[b]), aph, abort_flag, g.err)) break;
             tc_fence_after();
-            const int row = quarter * 32 + lane;      // row of the tile this thread owns
-            const int m = m0 + row;
-            char* ybase = reinterpret_cast<char*>(g.y) + (size_t)m * 4;
-            const int tiles = g.num_m * g.num_n;
             const int tile = w % tiles;
             const int split = w / tiles;
-            float* mypart = g.part + ((size_t)split * tiles + tile) * (size_t)(BM * BN);
-            // columns per TMEM load: 32, or BN for the 16-wide tile (whose 32-column load
-            // also returns the other accumulator's 16 columns, which are not this tile's)
-            constexpr int kCols = BN < 32 ? BN : 32;
+            float* mypart = g.part + ((size_t)split * tiles + tile) * (size_t)(ROWS * BN);
+#pragma unroll
+            for (int i = 0; i < MT; ++i) {
+                const int row = i * BM + quarter * 32 + lane;   // row of the tile this thread owns
+                const int m = m0 + row;
+                char* ybase = reinterpret_cast<char*>(g.y) + (size_t)m * 4;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * BN + c, r);
-                tmem_ld_wait();
-                if (g.splits == 1) {
-                    if (m < g.M) {
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * C::kAccCols + i * BN + c, r);
+                    tmem_ld_wait();
+                    if (g.splits == 1) {
+                        if (m < g.M) {
 #pragma unroll
-                        for (int j = 0; j < kCols; ++j) {
-                            const int n = n0 + c + j;
-                            if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[j]);
+                            for (int j = 0; j < kCols; ++j) {
+                                const int n = n0 + c + j;
+                                if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[j]);
+                            }
                         }
-                    }
-                } else {
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < kCols; ++j) mypart[(size_t)(c + j) * BM + row] = __uint_as_float(r[j]);
+                        for (int j = 0; j < kCols; ++j) mypart[(size_t)(c + j) * ROWS + row] = __uint_as_float(r[j]);
+                    }
                 }
             }
             tc_fence_before();
-            mbar_arrive(smem_u32(&tempty[b]));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty[b]));
             if (g.splits > 1) {
                 // Deterministic split-K: the split that finishes a tile last sums all of the
                 // tile's partials in split order 0..S-1 (no CTA ever waits for another).
@@ -361,20 +391,54 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
                 if (threadIdx.x == 64) {
                     const int done = atomicAdd(&g.tile_count[tile], 1);
-                    *abort_flag_or_last(abort_flag) = (done == g.splits - 1) ? 1 : 0;
+                    *last_flag = (done == g.splits - 1) ? 1 : 0;
                 }
                 asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-                if (*abort_flag_or_last(abort_flag)) {
+                if (*last_flag) {
                     __threadfence();
-                    if (m < g.M) {
-                        const float* p0 = g.part + (size_t)tile * (BM * BN) + row;
-                        for (int c = 0; c < BN; ++c) {
-                            const int n = n0 + c;
-                            if (n >= g.N) break;
-                            float acc = 0.0f;
-                            for (int sp = 0; sp < g.splits; ++sp)
-                                acc += __ldcg(p0 + (size_t)sp * tiles * (BM * BN) + (size_t)c * BM);
-                            *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = acc;
+                    // 4 consecutive rows per thread (one float4 per split and column), the
+                    // epilogue's 128 threads spread over ROWS/4 row groups x the columns.
+                    constexpr int RG = ROWS / 4;                 // row groups (32 or 64)
+                    constexpr int CG = (kEpiWarps * 32) / RG;    // column phases (4 or 2)
+                    const int et = threadIdx.x - 64;
+                    const int r4 = (et % RG) * 4;
+                    const int cg = et / RG;
+                    const float* p0 = g.part + (size_t)tile * (ROWS * BN) + r4;
+                    const size_t sstride = (size_t)tiles * (ROWS * BN);
+                    const int ncols = min(BN, g.N - n0);
+                    const int mrow = m0 + r4;
+                    const bool vec_store = mrow + 3 < g.M && ((reinterpret_cast<uintptr_t>(g.y) | g.y_cs) % 16 == 0);
+                    if (mrow < g.M) {
+#pragma unroll 1
+                        for (int c = cg; c < ncols; c += 4 * CG) {
+                            float4 acc[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            for (int sp = 0; sp < g.splits; ++sp) {
+                                float4 v[4];
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    const int cc = c + u * CG;
+                                    v[u] = cc < ncols ? __ldcg(reinterpret_cast<const float4*>(p0 + sp * sstride + (size_t)cc * ROWS))
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                                }
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int cc = c + u * CG;
+                                if (cc >= ncols) continue;
+                                float* dst = reinterpret_cast<float*>(reinterpret_cast<char*>(g.y) + (size_t)(n0 + cc) * g.y_cs) + mrow;
+                                if (vec_store) {
+                                    *reinterpret_cast<float4*>(dst) = acc[u];
+                                } else {
+                                    const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+                                    for (int q = 0; q < 4 && mrow + q < g.M; ++q) dst[q] = a4[q];
+                                }
+                            }
                         }
                     }
                 }
@@ -391,24 +455,34 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     }
 }
 
-// X (N x K f32, column stride x_cs bytes) -> X16 (N x kp f16, zero padded), RNE.
-__global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N, int K, __half* __restrict__ x16,
-                                  int kp, int vec, int* __restrict__ tile_count, int ntiles) {
+// X (N x K f32, column stride x_cs bytes) -> f16 (round-to-nearest-even) in the layout the
+// GEMM's X stages use: one contiguous BN x 64 block per (n-block, k-block), rows of 128
+// bytes with the 16-byte chunks XOR-swizzled by (row % 8) -- the image a 128-byte-swizzle
+// TMA box would leave in shared memory, so each stage is a single bulk copy.  Rows past N
+// and columns past K are zero.  Also zeroes the split-K tile counters.
+__global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N, int K, uint8_t* __restrict__ x16t,
+                                  int BN, int num_n, int kblocks, int vec, int* __restrict__ tile_count, int ntiles) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ntiles; i += gridDim.x * blockDim.x) tile_count[i] = 0;
-    const int cpr = kp / 8;
-    const int64_t total = (int64_t)N * cpr;
+    const int cpr = kblocks * 8;                          // 16-byte chunks per padded row
+    const int64_t total = (int64_t)num_n * BN * cpr;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int row = (int)(i / cpr);
-        const int k0 = (int)(i % cpr) * 8;
-        const float* xr = reinterpret_cast<const float*>(x + (size_t)row * x_cs);
+        const int n = (int)(i / cpr);
+        const int ch = (int)(i % cpr);
+        const int k0 = ch * 8;
         float v[8];
-        if (vec && k0 + 8 <= K) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k0));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k0 + 4));
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        if (n < N) {
+            const float* xr = reinterpret_cast<const float*>(x + (size_t)n * x_cs);
+            if (vec && k0 + 8 <= K) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k0));
+                const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k0 + 4));
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? xr[k0 + e] : 0.0f;
+            }
         } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? xr[k0 + e] : 0.0f;
+            for (int e = 0; e < 8; ++e) v[e] = 0.0f;
         }
         uint4 o;
         __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
@@ -417,7 +491,9 @@ __global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N
         o.y = *reinterpret_cast<uint32_t*>(&h1);
         o.z = *reinterpret_cast<uint32_t*>(&h2);
         o.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(x16 + (size_t)row * kp + k0) = o;
+        const int nb = n / BN, r = n % BN, kb = ch / 8, c16 = ch % 8;
+        const size_t off = (((size_t)nb * kblocks + kb) * BN + r) * 128 + (size_t)((c16 ^ (r & 7)) * 16);
+        *reinterpret_cast<uint4*>(x16t + off) = o;
     }
 }
 
@@ -453,48 +529,69 @@ int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, 
     return MLZC_OK;
 }
 
-size_t x16_bytes(int64_t N, int64_t K) {
-    const int64_t kp = (K + 7) / 8 * 8;
-    return ((size_t)N * kp * 2 + 255) / 256 * 256;
-}
-
 struct GemmPlan {
-    int BN, num_m, num_n, kblocks, splits;
+    int MT, BN, num_m, num_n, kblocks, splits;
     size_t x16, counters, partials;   // workspace segments (bytes)
     size_t total() const { return x16 + counters + partials; }
 };
 
-// Tile width and K split for a problem: the widest tile unless a narrower one fills the
-// SMs' waves clearly better; K split when the tiles cannot occupy half of the SMs.
+// Estimated SM-cycles of one work unit: MMA cycles at full tensor rate divided by the
+// fraction of that rate the per-SM operand feed sustains (about 62 B/cycle measured: the
+// 128x256 tile, which needs 96 B per MMA cycle, runs at ~64%), plus the epilogue when it
+// cannot overlap (one accumulator set) and the partial-tile traffic of a K split.
+double unit_cycles(int MT, int BN, int kb, int splits) {
+    const double feed = (double)MT * BM * BK * 2 + (double)BN * BK * 2;   // bytes per k-block
+    const double mma = (double)MT * BN * 2;                               // cycles per k-block at peak
+    const double eff = std::min(0.92, 62.0 / (feed / mma));
+    double cyc = kb * mma / eff;
+    const bool one_set = 2 * MT * BN > 512;
+    if (one_set) cyc += (double)MT * BN * 4;                              // drain 128*MT x BN floats
+    if (splits > 1) cyc += 2.0 * MT * BM * BN * 4 / 40.0;                 // write + read back a partial tile
+    return cyc;
+}
+
+// Tile shape (MT M-tiles of 128 rows x BN columns per CTA) and K split for a problem.
+// Wide problems (N >= 128) minimise rounds x unit cost over the candidates; narrow ones
+// (decode) use the narrowest BN that holds N and split K to occupy the SMs.
 GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
     GemmPlan p{};
-    p.num_m = (int)((M + BM - 1) / BM);
     p.kblocks = (int)((K + BK - 1) / BK);
-    if (N <= 16) p.BN = 16;
-    else if (N <= 32) p.BN = 32;
-    else if (N <= 64) p.BN = 64;
-    else if (N <= 128) p.BN = 128;
-    else {
-        auto score = [&](int bn, double eff) {
-            const long tiles = (long)p.num_m * ((N + bn - 1) / bn);
-            const long waves = (tiles + sm_count - 1) / sm_count;
-            return eff * (double)tiles / (double)(waves * sm_count);
-        };
-        p.BN = score(128, 0.85) > score(256, 1.0) ? 128 : 256;
+    p.MT = 1;
+    p.splits = 1;
+    if (N >= 128) {
+        double best = 1e300;
+        for (int mt = 2; mt >= 1; --mt)
+            for (int bn = 256; bn >= 128; bn /= 2)
+                for (int sp = 1; sp <= 4; ++sp) {
+                    if (sp > 1 && p.kblocks / sp < 4) break;
+                    const long tiles = (long)((M + BM * mt - 1) / (BM * mt)) * ((N + bn - 1) / bn);
+                    const long units = tiles * sp;
+                    const long rounds = (units + sm_count - 1) / sm_count;
+                    const int kper = (p.kblocks + sp - 1) / sp;
+                    const double cost = (double)rounds * unit_cycles(mt, bn, kper, sp) * (1.0 + 1e-3 * (sp - 1));
+                    if (cost < best * 0.999) {
+                        best = cost;
+                        p.MT = mt;
+                        p.BN = bn;
+                        p.splits = sp;
+                    }
+                }
+    } else {
+        p.BN = N <= 16 ? 16 : (N <= 32 ? 32 : (N <= 64 ? 64 : 128));
+        const int tiles = (int)((M + BM - 1) / BM) * (int)((N + p.BN - 1) / p.BN);
+        if (tiles * 2 <= sm_count) p.splits = std::max(1, std::min(sm_count / tiles, p.kblocks / 4));
     }
+    p.num_m = (int)((M + BM * p.MT - 1) / (BM * p.MT));
     p.num_n = (int)((N + p.BN - 1) / p.BN);
     const int tiles = p.num_m * p.num_n;
-    int splits = 1;
-    if (tiles * 2 <= sm_count) splits = std::max(1, std::min(sm_count / tiles, p.kblocks / 4));
-    if (splits > 1) {
+    if (p.splits > 1) {
         // every split must own >= 1 k-block: an empty split would add a stale accumulator
-        const int kper = (p.kblocks + splits - 1) / splits;
-        splits = (p.kblocks + kper - 1) / kper;
+        const int kper = (p.kblocks + p.splits - 1) / p.splits;
+        p.splits = (p.kblocks + kper - 1) / kper;
     }
-    p.splits = splits;
-    p.x16 = x16_bytes(N, K);
-    p.counters = splits > 1 ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
-    p.partials = splits > 1 ? (size_t)splits * tiles * BM * p.BN * 4 : 0;
+    p.x16 = ((size_t)p.num_n * p.BN * p.kblocks * BK * 2 + 255) / 256 * 256;
+    p.counters = p.splits > 1 ? ((size_t)tiles * 4 + 255) / 256 * 256 : 0;
+    p.partials = p.splits > 1 ? (size_t)p.splits * tiles * BM * p.MT * p.BN * 4 : 0;
     return p;
 }
 
@@ -507,18 +604,18 @@ int current_sm_count() {
     return sms;
 }
 
-template <int BN>
-int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs g, cudaStream_t s) {
-    using Cfg = TileCfg<BN>;
+template <int BN, int MT>
+int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, GemmArgs g, cudaStream_t s) {
+    using Cfg = TileCfg<BN, MT>;
     static bool attr_set[64] = {};
     const int dev = c->device < 64 ? c->device : 63;
     if (!attr_set[dev]) {
-        MLZC_CUDA_TRY(cudaFuncSetAttribute(gemm_f16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(gemm_f16_tc_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)Cfg::kSmemBytes));
         attr_set[dev] = true;
     }
     const int grid = std::min(g.num_work, c->sm_count);
-    gemm_f16_tc_kernel<BN><<<grid, kGemmThreads, Cfg::kSmemBytes, s>>>(ta, tb, g);
+    gemm_f16_tc_kernel<BN, MT><<<grid, kGemmThreads, Cfg::kSmemBytes, s>>>(ta, g);
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;
@@ -543,26 +640,23 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     const size_t need = pl.total();
     if (!ws || ws_bytes < need)
         return fail(MLZC_ERR_NOMEM, "mul_mat (tensor-core path): workspace of %zu bytes needed, %zu given", need, ws_bytes);
-    const int64_t kp = (K + 7) / 8 * 8;
     char* wsc = static_cast<char*>(ws);
-    __half* x16 = reinterpret_cast<__half*>(wsc);
+    uint8_t* x16t = reinterpret_cast<uint8_t*>(wsc);
     int* counters = reinterpret_cast<int*>(wsc + pl.x16);
     float* partials = reinterpret_cast<float*>(wsc + pl.x16 + pl.counters);
     const int tiles = pl.num_m * pl.num_n;
     {
         const int vec = ((uintptr_t)x % 16 == 0 && x_col_bytes % 16 == 0) ? 1 : 0;
-        const int64_t total = N * (kp / 8);
+        const int64_t total = (int64_t)pl.num_n * pl.BN * pl.kblocks * 8;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)c->sm_count * 8));
-        narrow_f16_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const char*>(x), x_col_bytes, (int)N, (int)K, x16,
-                                               (int)kp, vec, counters, pl.splits > 1 ? tiles : 0);
+        narrow_f16_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const char*>(x), x_col_bytes, (int)N, (int)K, x16t,
+                                               pl.BN, pl.num_n, pl.kblocks, vec, counters, pl.splits > 1 ? tiles : 0);
         MLZC_CUDA_TRY(cudaGetLastError());
         count_launch();
     }
     const int BN = pl.BN;
-    CUtensorMap ta, tb;
-    int st = make_map(&ta, w, (uint64_t)K, (uint64_t)M, w_row_bytes, BM);
-    if (st != MLZC_OK) return st;
-    st = make_map(&tb, x16, (uint64_t)K, (uint64_t)N, (uint64_t)kp * 2, (uint32_t)BN);
+    CUtensorMap ta;
+    int st = make_map(&ta, w, (uint64_t)K, (uint64_t)M, w_row_bytes, (uint32_t)(BM * pl.MT));
     if (st != MLZC_OK) return st;
 
     GemmArgs g{};
@@ -577,14 +671,16 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     g.err = c->err;
     g.splits = pl.splits;
     g.num_work = tiles * pl.splits;
+    g.x16t = x16t;
     g.part = partials;
     g.tile_count = counters;
+    if (pl.MT == 2) return BN == 128 ? launch_tile<128, 2>(c, ta, g, s) : launch_tile<256, 2>(c, ta, g, s);
     switch (BN) {
-        case 16: return launch_tile<16>(c, ta, tb, g, s);
-        case 32: return launch_tile<32>(c, ta, tb, g, s);
-        case 64: return launch_tile<64>(c, ta, tb, g, s);
-        case 128: return launch_tile<128>(c, ta, tb, g, s);
-        default: return launch_tile<256>(c, ta, tb, g, s);
+        case 16: return launch_tile<16, 1>(c, ta, g, s);
+        case 32: return launch_tile<32, 1>(c, ta, g, s);
+        case 64: return launch_tile<64, 1>(c, ta, g, s);
+        case 128: return launch_tile<128, 1>(c, ta, g, s);
+        default: return launch_tile<256, 1>(c, ta, g, s);
     }
 }
 

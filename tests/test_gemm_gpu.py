@@ -47,7 +47,9 @@ def test_llama32_3b_layer_projections(dev, tokens, proj):
 
 @pytest.mark.parametrize("M,K,N", [(128, 64, 8), (129, 72, 9), (1, 8, 16), (300, 520, 17), (127, 3072, 31),
                                    (256, 256, 33), (64, 1024, 100), (200, 136, 255), (130, 512, 256),
-                                   (384, 320, 257), (8192, 3072, 32), (1000, 2000, 300)])
+                                   (384, 320, 257), (8192, 3072, 32), (1000, 2000, 300),
+                                   (256, 64, 128), (257, 136, 129), (600, 8, 500), (512, 4096, 160),
+                                   (1024, 200, 2048)])
 def test_edge_shapes(dev, M, K, N):
     g = synth.rng(700 + M + K + N)
     w = synth.f16_weights(g, M, K)
