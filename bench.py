@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU sample length")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the eager launches instead of a CUDA-graph replay of the K steps")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu launch lists: no clock-sampling load loop, no e2e, no CPU leg "
                          "(launch order = warm-up steps, then the timed steps)")
@@ -518,6 +520,15 @@ def mlz_arm(a):
         import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
+    # Hold the GPU with a short spin (torch.cuda._sleep) while the host queues the K steps
+    # and their events, so the per-launch events time the kernels rather than the host's
+    # launch cadence.  The spin is enqueued before t0 and is not part of the timed region.
+    t_host = time.perf_counter()
+    for f, _ in w.launches(0):
+        f()
+    torch.cuda.synchronize()
+    host_per_step = time.perf_counter() - t_host
+    torch.cuda._sleep(int(min(2e9, max(2e6, 3.0 * host_per_step * K * 2.0e9))))
     n0 = mlz_b200.launch_count()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -530,12 +541,48 @@ def mlz_arm(a):
     t1.record(stream)
     torch.cuda.synchronize()
     n_launch = mlz_b200.launch_count() - n0
+    ms_eager = t0.elapsed_time(t1)
+    per_launch_ms = [sum(ev[s][j][0].elapsed_time(ev[s][j][1]) for s in range(K)) / K for j in range(len(units_l))]
+
+    # The same K steps captured once as a CUDA graph and replayed: the decode kernels are
+    # shorter than the host's per-call launch cost, so the eager loop would time Python.
+    use_graph = not a.no_graph and not a.profile_run and not isinstance(w, C5)
+    timing = "eager launches"
+    if use_graph:
+        gs = torch.cuda.Stream()
+        gs.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        n0 = mlz_b200.launch_count()
+        with torch.cuda.graph(graph, stream=gs):
+            for s_ in range(K):
+                for f, _ in w.launches(s_):
+                    f()
+        n_launch = mlz_b200.launch_count() - n0       # kernels the replay runs
+        with torch.cuda.stream(gs):
+            graph.replay()                              # untimed first replay
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(gs):
+            g0.record(gs)
+            graph.replay()
+            g1.record(gs)
+        torch.cuda.synchronize()
+        ms_local = g0.elapsed_time(g1)
+        timing = "CUDA graph replay of the K steps"
+        del graph
+    else:
+        ms_local = ms_eager
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
     clocks = sampler.stop()
-    ms = max_over_ranks(t0.elapsed_time(t1), world)
-    per_launch_ms = [sum(ev[s][j][0].elapsed_time(ev[s][j][1]) for s in range(K)) / K for j in range(len(units_l))]
+    ms = max_over_ranks(ms_local, world)
+    max_ms_eager = max_over_ranks(ms_eager, world)
 
     units = w.work_units()
     job_units = units if isinstance(w, C5) else units * world
@@ -576,6 +623,8 @@ def mlz_arm(a):
     if rank == 0:
         cfg = dict(w.config)
         cfg["parallelism"] = cfg.get("parallelism", f"replicas x{world}" if world > 1 else "single GPU")
+        cfg["timing"] = timing
+        cfg["eager_ms_per_step"] = max_ms_eager / K
         line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world, "steps": K,
                 "warmup": a.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": w.scaling,
                 "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded), random-init weights",

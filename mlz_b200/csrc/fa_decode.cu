@@ -8,19 +8,30 @@
 //
 // GPU design (HBM-bound: every K/V byte is read once):
 //   - Grouped-query packing: the G = n_head_q / n_head_kv query heads (times n_queries)
-//     that share a KV head are one "row group"; a CTA serves RG of those rows, so each
-//     K/V row is read once for all of them.
-//   - Split-K ("flash decoding"): the keys of a sequence are cut into chunks of
-//     kChunk positions, one CTA per (chunk, row group, kv head, sequence); chunks past a
+//     that share a KV head are the columns of one MMA tile (up to 8 query rows per CTA),
+//     so each K/V row is read once for all of them.
+//   - Split-K ("flash decoding"): the keys of a sequence are cut into chunks of kChunk
+//     positions, one CTA per (chunk, row group, kv head, sequence); chunks past a
 //     sequence's kv_len exit at once, so a ragged batch costs only its real keys.
-//   - Inside a CTA each warp runs its own online softmax over every 4th group of 4 keys:
-//     8 lanes per key, each lane holding D/8 query dims (pre-scaled) and D/8 output dims
-//     in registers; scores are reduced over the 8 lanes with shuffles, K/V rows are
-//     loaded as 16-byte vectors one step ahead of their use.
-//   - The 4 warps' (max, sum, O) states merge in shared memory; a CTA then writes its
+//   - A producer warp streams 64-key K and V tiles into a shared-memory ring with TMA
+//     (4-d tensor maps over the ggml strides, 64-dim boxes with 128-byte swizzle).
+//   - Four consumer warps own 16 keys of every tile.  Scores S^T = K . Q^T and the update
+//     O^T += V^T . P^T run on the tensor cores (mma.sync m16n8k16, f16 operands, f32
+//     accumulators in registers): keys fill the MMA's M side (16) and the query rows its
+//     N side (8), and the S^T accumulators become the P^T operand through an in-register
+//     8x8 transpose (movmatrix).  With 3-8 query rows per KV head the tcgen05 MMA's
+//     minimum M of 64 would be mostly padding and every online-softmax rescale would go
+//     through TMEM; here the accumulators stay in registers and the tensor pipe stays far
+//     below its bound (D/4 MMAs per 16 keys).
+//     fp32-level accuracy: Q and P are split into f16 hi + lo parts (two MMAs each), K
+//     and V are f16 already.  Online softmax (max / rescale / exp) in fp32 per warp.
+//   - The warps' (max, sum, O) states merge in shared memory; a CTA then writes its
 //     partial (max, sum, unnormalised O) to the workspace, and the combine kernel merges
 //     the chunks of each row.  With a single chunk the CTA writes the final row itself.
+//     Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
 // Score order (flash_attention.cpp:339-363): s = <q*scale, k>, + mask, softcap, + ALiBi.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -28,18 +39,33 @@
 #include <mutex>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace mlzc {
 namespace {
 
-constexpr int kFaWarps = 4;
-constexpr int kFaThreads = kFaWarps * 32;
-constexpr int kLanesPerKey = 8;
-constexpr int kKeysPerWarpStep = 32 / kLanesPerKey;             // 4
-constexpr int kKeysPerCtaStep = kKeysPerWarpStep * kFaWarps;    // 16
-constexpr int kChunk = 256;                                     // keys per CTA
+constexpr int kFaWarps = 4;                          // consumer warps
+constexpr int kFaThreads = (kFaWarps + 1) * 32;      // + one producer warp
+constexpr int kTile = 64;                            // keys per shared-memory stage
+constexpr int kWarpKeys = kTile / kFaWarps;          // 16 keys per consumer warp and tile
+constexpr int kChunk = 512;                          // keys per CTA
+constexpr int kRows = 8;                             // query rows per CTA (the MMA's N)
+constexpr int kBox = 64;                             // dims per TMA box (128 bytes, swizzled)
 
-struct FaParams {
+template <int D>
+struct FaCfg {
+    static constexpr int kBoxes = D / kBox;
+    static constexpr uint32_t kOperandBytes = kBoxes * kTile * 128;   // K or V of one tile
+    static constexpr uint32_t kStageBytes = 2 * kOperandBytes;
+    static constexpr int kStages = D == 256 ? 2 : (D == 128 ? 3 : 4);
+    static constexpr int kQStride = D + 8;                            // f16 elements per Q row
+    static constexpr uint32_t kQBytes = 2 * kRows * kQStride * 2;     // hi and lo
+    static constexpr uint32_t kMergeBytes = kFaWarps * kRows * (D + 2) * 4;
+    static_assert(kMergeBytes <= kStages * kStageBytes, "merge area must fit in the ring");
+    static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kQBytes + 256;
+};
+
+struct __align__(64) FaParams {
     const char* q;
     const char* k;
     const char* v;
@@ -48,37 +74,19 @@ struct FaParams {
     float* part;                 // workspace partials, or nullptr when nsplit == 1
     const int32_t* kv_len;
     int64_t q_nb1, q_nb2, q_nb3;
-    int64_t k_nb1, k_nb2, k_nb3;
-    int64_t v_nb1, v_nb2, v_nb3;
     int64_t m_nb0, m_nb1, m_nb2, m_nb3;
     int64_t d_nb1, d_nb2, d_nb3;
     int n_kv, n_q, n_head_q, n_head_kv;
     int G;                       // query heads per row group
     int rows_total;              // G * n_q
-    int n_rgroups;               // ceil(rows_total / RG)
+    int n_rgroups;               // ceil(rows_total / kRows)
     int nsplit;
     int packed;                  // 1: grid.y walks kv heads; 0: grid.y walks query heads
     float scale, softcap, alibi_p2inv;  // alibi_p2inv = -8 / P (0 = no ALiBi)
     int use_softcap;
+    unsigned int* err;           // device error word (bounded waits)
+    CUtensorMap tm_k, tm_v;      // [B][Hkv][n_kv][D] with 64 x 64 swizzled boxes
 };
-
-__device__ __forceinline__ void f16x8_to_f32(const uint4& u, float* f) {
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float2 t = __half22float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
-}
-
-__device__ __forceinline__ uint4 ld_kv16(const char* p) {
-    uint4 v;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-        : "l"(p));
-    return v;
-}
 
 // Row r of a row group -> (query position, query head).
 __device__ __forceinline__ void row_coords(const FaParams& p, int head_base, int r, int& iq, int& ihq) {
@@ -86,12 +94,82 @@ __device__ __forceinline__ void row_coords(const FaParams& p, int head_base, int
     ihq = head_base + r % p.G;
 }
 
-template <int D, int RG>
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y, int z,
+                                            int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// c += a . b, m16n8k16, f16 x f16 -> f32.
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// f16 hi + lo split of two floats: x ~= hi + lo with |x - hi - lo| ~ 2^-22 |x|.
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_h2(x0 - hf.x, x1 - hf.y);
+}
+
+// Address of the 16-byte chunk `chunk` (of 8 dims) of key row `key` in a tile operand
+// stored as kBoxes boxes of [64 keys][128 bytes] with the TMA 128-byte swizzle.
+__device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk) {
+    return base + (uint32_t)((chunk >> 3) * (kTile * 128) + key * 128 + (((chunk & 7) ^ (key & 7)) << 4));
+}
+
+// Transposes an 8x8 f16 matrix held as the standard mma fragment (lane: row lane/4,
+// columns 2*(lane%4) and +1).
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// Score and value steps per tile and warp, in the transposed form that puts keys on the
+// MMA's M side (16) and the query rows on N (8):
+//   S^T [16 keys x 8 rows]  = K [16 keys x D] . Q^T [D x 8 rows]      (D/16 k-steps)
+//   O^T [D x 8 rows]       += V^T [D x 16 keys] . P^T [16 keys x 8 rows]
+// Fragment ownership (g = lane/4, q = lane%4): S^T element (key g or g+8, row 2q or 2q+1),
+// O^T element (dim 16t + g or +8, row 2q or 2q+1): every lane keeps two query rows.
+template <int D>
 __global__ void __launch_bounds__(kFaThreads)
-fa_decode_kernel(FaParams p) {
-    constexpr int DL = D / kLanesPerKey;      // dims per lane
-    constexpr int NV = DL / 8;                // 16-byte vectors per lane per row
-    static_assert(DL % 8 == 0, "D must be a multiple of 64");
+fa_decode_kernel(const __grid_constant__ FaParams p) {
+    using C = FaCfg<D>;
+    constexpr int STAGES = C::kStages;
+    constexpr int KS = D / 16;                   // 16-dim steps (QK) and 16-dim output tiles (PV)
+    extern __shared__ uint8_t fa_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem;
+    __half* qs = reinterpret_cast<__half*>(smem + STAGES * C::kStageBytes);    // [hi, lo][kRows][kQStride]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kQBytes);
+    uint64_t* empty = full + STAGES;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
 
     const int split = blockIdx.x;
     const int rg = blockIdx.y % p.n_rgroups;
@@ -99,181 +177,234 @@ fa_decode_kernel(FaParams p) {
     const int ib = blockIdx.z;
     const int kvh = p.packed ? hidx : (int)((int64_t)hidx * p.n_head_kv / p.n_head_q);
     const int head_base = p.packed ? hidx * p.G : hidx;
+    const int nrows = min(kRows, p.rows_total - rg * kRows);
 
     const int L = p.kv_len ? min(p.kv_len[ib], p.n_kv) : p.n_kv;
     const int k0 = split * kChunk;
     const int k1 = min(k0 + kChunk, L);
-
     if (k0 >= L && p.nsplit > 1) return;   // chunk past this sequence's keys: no record
+    const int ntiles = k1 > k0 ? (k1 - k0 + kTile - 1) / kTile : 0;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int sub = lane & (kLanesPerKey - 1);    // dims [sub*DL, sub*DL + DL)
-    const int kslot = lane / kLanesPerKey;        // which of the warp's 4 keys
+    const int g = lane >> 2;
+    const int q4 = lane & 3;
 
-    // rows of this CTA
-    int iq_r[RG], ihq_r[RG];
-    bool valid[RG];
-#pragma unroll
-    for (int r = 0; r < RG; r++) {
-        const int row = rg * RG + r;
-        valid[r] = row < p.rows_total;
-        row_coords(p, head_base, valid[r] ? row : 0, iq_r[r], ihq_r[r]);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+            ptx::mbar_init(ptx::smem_u32(&empty[s]), kFaWarps);
+        }
+        *abort_flag = 0;
+        ptx::mbar_init_fence();
     }
-
-    // query slice in registers, pre-scaled
-    float qv[RG][DL];
-#pragma unroll
-    for (int r = 0; r < RG; r++) {
-        const float* qr = reinterpret_cast<const float*>(p.q + iq_r[r] * p.q_nb1 + ihq_r[r] * p.q_nb2 + ib * p.q_nb3);
-#pragma unroll
-        for (int i = 0; i < DL; i += 4) {
-            const float4 t = *reinterpret_cast<const float4*>(qr + sub * DL + i);
-            qv[r][i] = t.x * p.scale; qv[r][i + 1] = t.y * p.scale;
-            qv[r][i + 2] = t.z * p.scale; qv[r][i + 3] = t.w * p.scale;
+    // query rows (pre-scaled), split into f16 hi and lo, zero past nrows
+    for (int idx = threadIdx.x; idx < kRows * D; idx += kFaThreads) {
+        const int r = idx / D, d = idx % D;
+        float qv = 0.0f;
+        if (r < nrows) {
+            int iq, ihq;
+            row_coords(p, head_base, rg * kRows + r, iq, ihq);
+            qv = reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3)[d] * p.scale;
         }
-    }
-    float slope[RG];
-#pragma unroll
-    for (int r = 0; r < RG; r++) slope[r] = p.alibi_p2inv != 0.0f ? exp2f(p.alibi_p2inv * (float)(ihq_r[r] + 1)) : 0.0f;
-
-    float m[RG], l[RG], o[RG][DL];
-#pragma unroll
-    for (int r = 0; r < RG; r++) {
-        m[r] = -INFINITY;
-        l[r] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < DL; i++) o[r][i] = 0.0f;
-    }
-
-    const char* kbase = p.k + kvh * p.k_nb2 + ib * p.k_nb3 + sub * DL * 2;
-    const char* vbase = p.v + kvh * p.v_nb2 + ib * p.v_nb3 + sub * DL * 2;
-
-    // key handled by this lane at step t: k0 + t*16 + warp*4 + kslot
-    int j = k0 + warp * kKeysPerWarpStep + kslot;
-    uint4 kn[NV], vn[NV];
-#pragma unroll
-    for (int u = 0; u < NV; u++) { kn[u] = make_uint4(0, 0, 0, 0); vn[u] = kn[u]; }
-    if (j < k1) {
-#pragma unroll
-        for (int u = 0; u < NV; u++) {
-            kn[u] = ld_kv16(kbase + (int64_t)j * p.k_nb1 + u * 16);
-            vn[u] = ld_kv16(vbase + (int64_t)j * p.v_nb1 + u * 16);
-        }
-    }
-    for (int jb = k0 + warp * kKeysPerWarpStep; jb < k1; jb += kKeysPerCtaStep) {
-        const bool live = j < k1;
-        uint4 kc[NV], vc[NV];
-#pragma unroll
-        for (int u = 0; u < NV; u++) { kc[u] = kn[u]; vc[u] = vn[u]; }
-        const int jn = j + kKeysPerCtaStep;
-        if (jn < k1) {
-#pragma unroll
-            for (int u = 0; u < NV; u++) {
-                kn[u] = ld_kv16(kbase + (int64_t)jn * p.k_nb1 + u * 16);
-                vn[u] = ld_kv16(vbase + (int64_t)jn * p.v_nb1 + u * 16);
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < NV; u++) { kn[u] = make_uint4(0, 0, 0, 0); vn[u] = kn[u]; }
-        }
-        // scores of this lane's key for the RG rows
-        float kf[DL];
-#pragma unroll
-        for (int u = 0; u < NV; u++) f16x8_to_f32(kc[u], kf + 8 * u);
-        float s[RG];
-#pragma unroll
-        for (int r = 0; r < RG; r++) {
-            float a = 0.0f;
-#pragma unroll
-            for (int i = 0; i < DL; i++) a = fmaf(qv[r][i], kf[i], a);
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            a += __shfl_xor_sync(0xffffffffu, a, 2);
-            a += __shfl_xor_sync(0xffffffffu, a, 4);
-            s[r] = a;
-        }
-#pragma unroll
-        for (int r = 0; r < RG; r++) {
-            float sr = s[r];
-            if (p.mask) {
-                const int jj = live ? j : k0;
-                sr += *reinterpret_cast<const float*>(p.mask + iq_r[r] * p.m_nb1 + (int64_t)jj * p.m_nb0 +
-                                                     ihq_r[r] * p.m_nb2 + ib * p.m_nb3);
-            }
-            if (p.use_softcap) sr = p.softcap * tanhf(sr / p.softcap);
-            if (p.alibi_p2inv != 0.0f) sr += slope[r] * (float)(j - iq_r[r]);
-            s[r] = live ? sr : -INFINITY;
-        }
-        // warp-wide max over the 4 keys of the step, online rescale, accumulate PV
-        float vf[DL];
-#pragma unroll
-        for (int u = 0; u < NV; u++) f16x8_to_f32(vc[u], vf + 8 * u);
-#pragma unroll
-        for (int r = 0; r < RG; r++) {
-            float mx = fmaxf(s[r], __shfl_xor_sync(0xffffffffu, s[r], 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float mnew = fmaxf(m[r], mx);
-            if (mnew == -INFINITY) continue;          // nothing visible yet (warp-uniform)
-            if (mnew > m[r]) {                        // warp-uniform branch
-                const float corr = __expf(m[r] - mnew);
-                l[r] *= corr;
-#pragma unroll
-                for (int i = 0; i < DL; i++) o[r][i] *= corr;
-                m[r] = mnew;
-            }
-            const float pr = __expf(s[r] - mnew);
-            l[r] += pr;
-#pragma unroll
-            for (int i = 0; i < DL; i++) o[r][i] = fmaf(pr, vf[i], o[r][i]);
-        }
-        j = jn;
-    }
-
-    // merge the 4 key slots of the warp (same m within a warp; sum l and o)
-#pragma unroll
-    for (int r = 0; r < RG; r++) {
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 8);
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 16);
-#pragma unroll
-        for (int i = 0; i < DL; i++) {
-            o[r][i] += __shfl_xor_sync(0xffffffffu, o[r][i], 8);
-            o[r][i] += __shfl_xor_sync(0xffffffffu, o[r][i], 16);
-        }
-    }
-
-    // merge the warps through shared memory
-    __shared__ float sm_m[kFaWarps][RG], sm_l[kFaWarps][RG];
-    __shared__ float sm_o[kFaWarps][RG][D];
-    if (lane < kLanesPerKey) {
-#pragma unroll
-        for (int r = 0; r < RG; r++) {
-#pragma unroll
-            for (int i = 0; i < DL; i++) sm_o[warp][r][sub * DL + i] = o[r][i];
-        }
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < RG; r++) { sm_m[warp][r] = m[r]; sm_l[warp][r] = l[r]; }
+        const __half h = __float2half_rn(qv);
+        qs[r * C::kQStride + d] = h;
+        qs[(kRows + r) * C::kQStride + d] = __float2half_rn(qv - __half2float(h));
     }
     __syncthreads();
 
-    const int rows_here = RG;
-    for (int idx = threadIdx.x; idx < rows_here * D; idx += kFaThreads) {
+    float m_row[2] = {-INFINITY, -INFINITY};
+    float l_row[2] = {0.0f, 0.0f};
+    float o[KS][4];
+#pragma unroll
+    for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+
+    if (warp == kFaWarps) {
+        // ---------------- producer: K and V tiles into the ring with TMA
+        if (lane == 0) {
+            for (int t = 0; t < ntiles; ++t) {
+                const int s = t % STAGES;
+                const uint32_t ph = (t / STAGES) & 1;
+                if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+                const uint32_t fb = ptx::smem_u32(&full[s]);
+                const uint32_t st = ptx::smem_u32(ring + s * C::kStageBytes);
+                const int j0 = k0 + t * kTile;
+                ptx::mbar_expect_tx(fb, C::kStageBytes);
+#pragma unroll
+                for (int b = 0; b < C::kBoxes; ++b) {
+                    tma_load_4d(st + b * (kTile * 128), &p.tm_k, fb, b * kBox, j0, kvh, ib);
+                    tma_load_4d(st + C::kOperandBytes + b * (kTile * 128), &p.tm_v, fb, b * kBox, j0, kvh, ib);
+                }
+            }
+        }
+    } else {
+        // ---------------- consumers: 16 keys of every tile per warp
+        int iq_r[2], ihq_r[2];
+        bool row_ok[2];
+        float slope[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = 2 * q4 + h;
+            row_ok[h] = r < nrows;
+            row_coords(p, head_base, rg * kRows + (row_ok[h] ? r : 0), iq_r[h], ihq_r[h]);
+            slope[h] = p.alibi_p2inv != 0.0f ? exp2f(p.alibi_p2inv * (float)(ihq_r[h] + 1)) : 0.0f;
+        }
+        const int mat = lane >> 3;               // ldmatrix: matrix whose row this lane addresses
+        // B fragments of Q^T for every 16-dim step: {hi b0, hi b1, lo b0, lo b1}
+        uint32_t qf[KS][4];
+        {
+            const uint32_t qrow =
+                ptx::smem_u32(qs) + (uint32_t)((((mat >> 1) * kRows + (lane & 7)) * C::kQStride + 8 * (mat & 1)) * 2);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) ldsm_x4(qrow + ks * 32, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+        }
+        const int kw = warp * kWarpKeys;
+        const int k_key = kw + (lane & 7) + 8 * (mat & 1);     // K: matrices (keys, dims) = (0,0) (8,0) (0,8) (8,8)
+        const int k_half = mat >> 1;
+        const int v_key = kw + (lane & 7) + 8 * (mat >> 1);    // V^T: matrices (dims, keys) = (0,0) (8,0) (0,8) (8,8)
+        const int v_half = mat & 1;
+
+        for (int t = 0; t < ntiles; ++t) {
+            const int s = t % STAGES;
+            const uint32_t ph = (t / STAGES) & 1;
+            if (!ptx::mbar_wait(ptx::smem_u32(&full[s]), ph, abort_flag, p.err)) break;
+            const uint32_t kbuf = ptx::smem_u32(ring + s * C::kStageBytes);
+            const uint32_t vbuf = kbuf + C::kOperandBytes;
+            const int j0 = k0 + t * kTile;
+            if (j0 + kw + kWarpKeys > k1) {
+                // V rows past the sequence's last key may hold any bits (NaN included) and
+                // 0 * NaN in P . V would poison O: zero this warp's rows of them
+                const int first = max(0, k1 - j0 - kw);
+                uint8_t* vgen = ring + s * C::kStageBytes + C::kOperandBytes;
+                for (int idx = lane; idx < (kWarpKeys - first) * (D / 8); idx += 32) {
+                    const int key = kw + first + idx / (D / 8);
+                    const int c = idx % (D / 8);
+                    *reinterpret_cast<uint4*>(vgen + (tile_addr(vbuf, key, c) - vbuf)) = make_uint4(0, 0, 0, 0);
+                }
+                // these generic writes precede the next TMA write into the stage
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+            }
+
+            // S^T = K . Q^T (Q as hi + lo)
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(tile_addr(kbuf, k_key, 2 * ks + k_half), a0, a1, a2, a3);
+                mma16816(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                mma16816(sc, a0, a1, a2, a3, qf[ks][2], qf[ks][3]);
+            }
+            // mask / softcap / ALiBi / validity; element e: key g + 8 (e >> 1), row 2 q4 + (e & 1)
+            float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e & 1;
+                const int j = j0 + kw + g + 8 * (e >> 1);
+                float a = sc[e];
+                if (j < k1 && row_ok[h]) {
+                    if (p.mask)
+                        a += *reinterpret_cast<const float*>(p.mask + iq_r[h] * p.m_nb1 + (int64_t)j * p.m_nb0 +
+                                                            ihq_r[h] * p.m_nb2 + ib * p.m_nb3);
+                    if (p.use_softcap) a = p.softcap * tanhf(a / p.softcap);
+                    if (p.alibi_p2inv != 0.0f) a += slope[h] * (float)(j - iq_r[h]);
+                } else {
+                    a = -INFINITY;
+                }
+                sc[e] = a;
+                tmax[h] = fmaxf(tmax[h], a);
+            }
+            float corr[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 4));
+                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 8));
+                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 16));
+                const float mnew = fmaxf(m_row[h], tmax[h]);
+                corr[h] = (mnew == -INFINITY) ? 1.0f : __expf(m_row[h] - mnew);
+                m_row[h] = mnew;
+                l_row[h] *= corr[h];
+            }
+            if (corr[0] != 1.0f || corr[1] != 1.0f) {
+#pragma unroll
+                for (int t2 = 0; t2 < KS; ++t2) {
+                    o[t2][0] *= corr[0]; o[t2][1] *= corr[1];
+                    o[t2][2] *= corr[0]; o[t2][3] *= corr[1];
+                }
+            }
+            float pe[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e & 1;
+                pe[e] = (sc[e] == -INFINITY) ? 0.0f : __expf(sc[e] - m_row[h]);
+                l_row[h] += pe[e];
+            }
+            // P^T (keys x rows) as f16 hi + lo, transposed in registers into B fragments
+            uint32_t h0, l0, h1, l1;
+            split_h2(pe[0], pe[1], h0, l0);      // key g
+            split_h2(pe[2], pe[3], h1, l1);      // key g + 8
+            const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1);
+            const uint32_t bl0 = movtrans(l0), bl1 = movtrans(l1);
+            // O^T += V^T . P^T
+#pragma unroll
+            for (int dt = 0; dt < KS; ++dt) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(tile_addr(vbuf, v_key, 2 * dt + v_half), a0, a1, a2, a3);
+                mma16816(o[dt], a0, a1, a2, a3, bh0, bh1);
+                mma16816(o[dt], a0, a1, a2, a3, bl0, bl1);
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
+        }
+        // row sums over the lanes that share the rows (same q4)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 4);
+            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 8);
+            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 16);
+        }
+    }
+
+    // merge the consumer warps (their rows' max, sum and O) through shared memory; the
+    // ring is free once every tile has been consumed
+    __syncthreads();
+    float* mo = reinterpret_cast<float*>(ring);                 // [warp][row][D]
+    float* mm = mo + kFaWarps * kRows * D;                      // [warp][row]
+    float* ml = mm + kFaWarps * kRows;                          // [warp][row]
+    if (warp < kFaWarps) {
+#pragma unroll
+        for (int dt = 0; dt < KS; ++dt) {
+            const int d = 16 * dt + g;
+            const int r = warp * kRows + 2 * q4;
+            mo[r * D + d] = o[dt][0];
+            mo[(r + 1) * D + d] = o[dt][1];
+            mo[r * D + d + 8] = o[dt][2];
+            mo[(r + 1) * D + d + 8] = o[dt][3];
+        }
+        if (g == 0) {
+            mm[warp * kRows + 2 * q4] = m_row[0];
+            mm[warp * kRows + 2 * q4 + 1] = m_row[1];
+            ml[warp * kRows + 2 * q4] = l_row[0];
+            ml[warp * kRows + 2 * q4 + 1] = l_row[1];
+        }
+    }
+    __syncthreads();
+
+    for (int idx = threadIdx.x; idx < nrows * D; idx += kFaThreads) {
         const int r = idx / D, d = idx % D;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kFaWarps; w++) M = fmaxf(M, sm_m[w][r]);
+        for (int w = 0; w < kFaWarps; w++) M = fmaxf(M, mm[w * kRows + r]);
         float Ls = 0.0f, Os = 0.0f;
         if (M != -INFINITY) {
 #pragma unroll
             for (int w = 0; w < kFaWarps; w++) {
-                const float e = __expf(sm_m[w][r] - M);
-                Ls += sm_l[w][r] * e;
-                Os += sm_o[w][r][d] * e;
+                const float e = __expf(mm[w * kRows + r] - M);
+                Ls += ml[w * kRows + r] * e;
+                Os += mo[(w * kRows + r) * D + d] * e;
             }
         }
-        const int row = rg * RG + r;
-        if (row >= p.rows_total) continue;
+        const int row = rg * kRows + r;
         int iq, ihq;
         row_coords(p, head_base, row, iq, ihq);
         if (p.nsplit == 1) {
@@ -293,7 +424,7 @@ fa_decode_kernel(FaParams p) {
 // Merges the chunk partials of every (sequence, head index, row): one CTA per row.
 template <int D>
 __global__ void __launch_bounds__(D)
-fa_combine_kernel(FaParams p, int n_hidx) {
+fa_combine_kernel(const __grid_constant__ FaParams p, int n_hidx) {
     const int row = blockIdx.x;
     const int hidx = blockIdx.y;
     const int ib = blockIdx.z;
@@ -322,7 +453,6 @@ fa_combine_kernel(FaParams p, int n_hidx) {
 
 struct FaPlan {
     FaParams p;
-    int RG;
     int n_hidx;
     dim3 grid;
     size_t ws_bytes;
@@ -336,8 +466,7 @@ FaPlan make_plan(const mlzc_fa_desc* d) {
     p.G = p.packed ? Hq / Hkv : 1;
     p.n_q = (int)d->n_queries;
     p.rows_total = p.G * p.n_q;
-    pl.RG = p.rows_total >= 4 ? 4 : (p.rows_total >= 2 ? 2 : 1);
-    p.n_rgroups = (p.rows_total + pl.RG - 1) / pl.RG;
+    p.n_rgroups = (p.rows_total + kRows - 1) / kRows;
     p.n_kv = (int)d->n_kv;
     p.n_head_q = Hq;
     p.n_head_kv = Hkv;
@@ -351,12 +480,94 @@ FaPlan make_plan(const mlzc_fa_desc* d) {
     return pl;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 kv_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// 4-d f16 map of a K or V tensor (ggml dims [D, n_kv, Hkv, B], byte strides nb[1..3]) with
+// 64 x 64 boxes in the 128-byte swizzle (the layout tile_addr() reads).
+int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, int64_t hkv, int64_t B, const size_t* nb) {
+    auto enc = kv_encoder();
+    if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_kv, (cuuint64_t)hkv, (cuuint64_t)B};
+    // a broadcast (stride 0) or size-1 dimension gets a harmless stride
+    cuuint64_t st1 = nb[1];
+    cuuint64_t st2 = (hkv == 1 || nb[2] == 0) ? st1 * (cuuint64_t)n_kv : nb[2];
+    cuuint64_t st3 = (B == 1 || nb[3] == 0) ? st2 * (cuuint64_t)hkv : nb[3];
+    const cuuint64_t strides[3] = {st1, st2, st3};
+    const cuuint32_t box[4] = {(cuuint32_t)kBox, (cuuint32_t)kTile, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V strides not expressible as a TMA map (%d)", (int)r);
+    return MLZC_OK;
+}
+
 }  // namespace
 
 size_t fa_workspace_bytes(const mlzc_fa_desc* d) { return make_plan(d).ws_bytes; }
 
-int launch_flash_attn(const DeviceCtx*, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
-                      cudaStream_t s) {
+namespace {
+
+template <int D>
+int fa_launch(const FaPlan& pl, cudaStream_t s) {
+    constexpr size_t smem = FaCfg<D>::kSmemBytes;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    MLZC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MLZC_ERR_INVALID, "flash_attn: device %d beyond 64", dev);
+    if (!attr_set[dev]) {
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_decode_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                           (int)cudaSharedmemCarveoutMaxShared));
+        attr_set[dev] = true;
+    }
+    fa_decode_kernel<D><<<pl.grid, kFaThreads, smem, s>>>(pl.p);
+    MLZC_CUDA_TRY(cudaGetLastError());
+    return MLZC_OK;
+}
+
+// Error word of calls made without a library context (the allocation-free entry point):
+// a device variable of this module, so it needs no allocation either.
+__device__ unsigned int g_fa_static_err;
+std::mutex g_fa_err_mu;
+unsigned int* g_fa_err_addr[64] = {};
+
+unsigned int* static_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_fa_err_mu);
+    if (!g_fa_err_addr[dev]) {
+        void* a = nullptr;
+        if (cudaGetSymbolAddress(&a, g_fa_static_err) != cudaSuccess) return nullptr;
+        g_fa_err_addr[dev] = static_cast<unsigned int*>(a);
+    }
+    return g_fa_err_addr[dev];
+}
+
+}  // namespace
+
+int fa_take_static_errors(unsigned int* out) {
+    *out = 0;
+    unsigned int* a = static_error_word();
+    if (!a) return MLZC_OK;
+    unsigned int v = 0;
+    MLZC_CUDA_TRY(cudaMemcpy(&v, a, sizeof v, cudaMemcpyDeviceToHost));
+    if (v) MLZC_CUDA_TRY(cudaMemset(a, 0, sizeof v));
+    *out = v;
+    return MLZC_OK;
+}
+
+int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes, cudaStream_t s) {
     FaPlan pl = make_plan(d);
     if (pl.ws_bytes > ws_bytes || (pl.ws_bytes && !ws))
         return fail(MLZC_ERR_NOMEM, "flash_attn: workspace of %zu bytes needed, %zu given", pl.ws_bytes, ws_bytes);
@@ -369,8 +580,6 @@ int launch_flash_attn(const DeviceCtx*, const mlzc_fa_desc* d, void* ws, size_t 
     p.part = static_cast<float*>(ws);
     p.kv_len = d->kv_len;
     p.q_nb1 = d->q_nb[1]; p.q_nb2 = d->q_nb[2]; p.q_nb3 = d->q_nb[3];
-    p.k_nb1 = d->k_nb[1]; p.k_nb2 = d->k_nb[2]; p.k_nb3 = d->k_nb[3];
-    p.v_nb1 = d->v_nb[1]; p.v_nb2 = d->v_nb[2]; p.v_nb3 = d->v_nb[3];
     p.m_nb0 = d->mask_nb[0]; p.m_nb1 = d->mask_nb[1]; p.m_nb2 = d->mask_nb[2]; p.m_nb3 = d->mask_nb[3];
     p.d_nb1 = d->dst_nb[1]; p.d_nb2 = d->dst_nb[2]; p.d_nb3 = d->dst_nb[3];
     p.scale = d->scale;
@@ -383,21 +592,21 @@ int launch_flash_attn(const DeviceCtx*, const mlzc_fa_desc* d, void* ws, size_t 
     } else {
         p.alibi_p2inv = 0.0f;
     }
+    p.err = c ? c->err : static_error_word();
+    if (!p.err) return fail(MLZC_ERR_CUDA, "flash_attn: no device error word");
+    if (d->n_kv > 0) {
+        int st = encode_kv_map(&p.tm_k, d->k, d->head_dim_k, d->n_kv, d->n_head_kv, d->batch_size, d->k_nb);
+        if (st != MLZC_OK) return st;
+        st = encode_kv_map(&p.tm_v, d->v, d->head_dim_v, d->n_kv, d->n_head_kv, d->batch_size, d->v_nb);
+        if (st != MLZC_OK) return st;
+    }
     const int D = (int)d->head_dim_k;
-#define MLZC_FA_LAUNCH(DD, RGV) fa_decode_kernel<DD, RGV><<<pl.grid, kFaThreads, 0, s>>>(p)
-#define MLZC_FA_RG(DD)                                  \
-    do {                                                \
-        if (pl.RG == 4) MLZC_FA_LAUNCH(DD, 4);          \
-        else if (pl.RG == 2) MLZC_FA_LAUNCH(DD, 2);     \
-        else MLZC_FA_LAUNCH(DD, 1);                     \
-    } while (0)
-    if (D == 64) MLZC_FA_RG(64);
-    else if (D == 128) MLZC_FA_RG(128);
-    else if (D == 256) MLZC_FA_RG(256);
+    int st;
+    if (D == 64) st = fa_launch<64>(pl, s);
+    else if (D == 128) st = fa_launch<128>(pl, s);
+    else if (D == 256) st = fa_launch<256>(pl, s);
     else return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: head_dim %d (64, 128, 256 supported)", D);
-#undef MLZC_FA_RG
-#undef MLZC_FA_LAUNCH
-    MLZC_CUDA_TRY(cudaGetLastError());
+    if (st != MLZC_OK) return st;
     count_launch();
     if (p.nsplit > 1) {
         const dim3 g((unsigned)p.rows_total, (unsigned)pl.n_hidx, (unsigned)d->batch_size);

@@ -34,9 +34,10 @@ constexpr int kThreads = kWarps * 32;
 
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     uint4 v;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-        : "l"(p));
+    // volatile: keeps the unrolled prefetch loads ahead of the math that consumes them
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
     return v;
 }
 
@@ -81,7 +82,9 @@ struct WF32 {
 };
 
 // Vectorised kernel: requires 16-byte aligned rows/columns and K % kPerChunk == 0.
-template <class WT, int NB, int ROWS>
+// Each lane keeps ROWS x U 16-byte weight loads in flight (U chunks 32 apart), which is
+// what hides the HBM latency: ~128 KB in flight per SM at ROWS = 2, U = 4.
+template <class WT, int NB, int ROWS, int U>
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
                 const char* __restrict__ X, size_t x_cs, int ncols,
@@ -102,31 +105,41 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
         for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
 
     const int64_t nchunk = K / CH;
-    for (int64_t c = lane; c < nchunk; c += 32) {
-        uint4 wv[ROWS];
+    for (int64_t base = 0; base < nchunk; base += 32 * U) {
+        uint4 wv[ROWS][U];
 #pragma unroll
-        for (int r = 0; r < ROWS; r++) wv[r] = ld_stream16(wrow[r] + (size_t)c * 16);
-        float wf[ROWS][CH];
+        for (int u = 0; u < U; u++) {
+            const int64_t c = base + lane + 32 * u;
 #pragma unroll
-        for (int r = 0; r < ROWS; r++) WT::unpack(wv[r], wf[r]);
+            for (int r = 0; r < ROWS; r++)
+                wv[r][u] = c < nchunk ? ld_stream16(wrow[r] + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+        }
 #pragma unroll
-        for (int n = 0; n < NB; n++) {
-            if (n < ncols) {
-                const float4* xp = reinterpret_cast<const float4*>(X + (size_t)n * x_cs) + c * (CH / 4);
-                float xf[CH];
+        for (int u = 0; u < U; u++) {
+            const int64_t c = base + lane + 32 * u;
+            if (c >= nchunk) break;
+            float wf[ROWS][CH];
 #pragma unroll
-                for (int q = 0; q < CH / 4; q++) {
-                    const float4 t = __ldg(xp + q);
-                    xf[4 * q + 0] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+            for (int r = 0; r < ROWS; r++) WT::unpack(wv[r][u], wf[r]);
+#pragma unroll
+            for (int n = 0; n < NB; n++) {
+                if (n < ncols) {
+                    const float4* xp = reinterpret_cast<const float4*>(X + (size_t)n * x_cs) + c * (CH / 4);
+                    float xf[CH];
+#pragma unroll
+                    for (int q = 0; q < CH / 4; q++) {
+                        const float4 t = __ldg(xp + q);
+                        xf[4 * q + 0] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
+                    }
+                    if (WT::kRoundX) {
+#pragma unroll
+                        for (int i = 0; i < CH; i++) xf[i] = round_to_f16(xf[i]);
+                    }
+#pragma unroll
+                    for (int r = 0; r < ROWS; r++)
+#pragma unroll
+                        for (int i = 0; i < CH; i++) acc[r][n] = fmaf(wf[r][i], xf[i], acc[r][n]);
                 }
-                if (WT::kRoundX) {
-#pragma unroll
-                    for (int i = 0; i < CH; i++) xf[i] = round_to_f16(xf[i]);
-                }
-#pragma unroll
-                for (int r = 0; r < ROWS; r++)
-#pragma unroll
-                    for (int i = 0; i < CH; i++) acc[r][n] = fmaf(wf[r][i], xf[i], acc[r][n]);
             }
         }
     }
@@ -166,10 +179,11 @@ gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K
 template <class WT, int NB>
 void launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
                 int ncols, char* y, size_t y_cs, cudaStream_t s) {
-    constexpr int ROWS = 4;
+    constexpr int ROWS = 2;
+    constexpr int U = NB <= 2 ? 4 : 2;
     const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
     const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    gemv_vec_kernel<WT, NB, ROWS><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
+    gemv_vec_kernel<WT, NB, ROWS, U><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
     count_launch();
 }
 
@@ -221,12 +235,20 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, float& sc
     mn = (float)b;
 }
 
-// Exact nibble -> float: 0x4B000000 | q is the float 2^23 + q.
-__device__ __forceinline__ float nib_f(uint32_t word, int shift) {
-    return __uint_as_float(0x4B000000u | ((word >> shift) & 0xFu)) - 8388608.0f;
+
+// Two exact nibble floats (bytes b and b+1 of `word` after `shift`) as a float2.
+__device__ __forceinline__ float2 nib2(uint32_t word, int byte, int shift) {
+    const uint32_t a = (word >> (8 * byte + shift)) & 0xFu;
+    const uint32_t b = (word >> (8 * byte + 8 + shift)) & 0xFu;
+    const float2 f = make_float2(__uint_as_float(0x4B000000u | a), __uint_as_float(0x4B000000u | b));
+    return __fadd2_rn(f, make_float2(-8388608.0f, -8388608.0f));   // exact: 2^23 + q - 2^23
 }
 
-template <int NB, int ROWS>
+// Q4_K x f32 for NB activation columns.  Lane = one 64-value chunk (the 32-byte qs run of
+// sub-blocks 2c and 2c+1) of each of the warp's ROWS rows; U chunk iterations are loaded
+// ahead.  Per sub-block the weight sum is d*sc*sum(q*x) - dmin*m*sum(x): sum(q*x) in
+// packed f32x2 FMAs on exact nibble floats, sum(x) once per chunk and column for all rows.
+template <int NB, int ROWS, int U>
 __global__ void __launch_bounds__(kThreads)
 q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
                 const char* __restrict__ X, size_t x_cs, int ncols,
@@ -245,63 +267,80 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
         for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
 
     const int64_t nchunk = K / 64;   // 64-value chunks, 4 per super-block
-    for (int64_t ch = lane; ch < nchunk; ch += 32) {
-        const int64_t b = ch >> 2;
-        const int c = (int)(ch & 3);
-        uint4 hdr[ROWS], qa[ROWS], qb[ROWS];
+    for (int64_t base = 0; base < nchunk; base += 32 * U) {
+        uint4 hdr[U][ROWS], qa[U][ROWS], qb[U][ROWS];
 #pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            const char* blk = wrow[r] + (size_t)b * kQ4KBytes;
-            hdr[r] = ld_stream16(blk);
-            qa[r] = ld_stream16(blk + 16 + 32 * c);
-            qb[r] = ld_stream16(blk + 32 + 32 * c);
-        }
-        float ds0[ROWS], dm0[ROWS], ds1[ROWS], dm1[ROWS];
-#pragma unroll
-        for (int r = 0; r < ROWS; r++) {
-            const float d = __half2float(__ushort_as_half((unsigned short)(hdr[r].x & 0xFFFFu)));
-            const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[r].x >> 16)));
-            uint8_t sb[12];
-            *reinterpret_cast<uint32_t*>(sb + 0) = hdr[r].y;
-            *reinterpret_cast<uint32_t*>(sb + 4) = hdr[r].z;
-            *reinterpret_cast<uint32_t*>(sb + 8) = hdr[r].w;
-            float sc, mn;
-            q4k_scale_min(sb, 2 * c, sc, mn);
-            ds0[r] = d * sc;
-            dm0[r] = dmin * mn;
-            q4k_scale_min(sb, 2 * c + 1, sc, mn);
-            ds1[r] = d * sc;
-            dm1[r] = dmin * mn;
-        }
-        const int64_t kbase = ch * 64;
-        // 8 words of 4 qs bytes: word i covers values kbase+4i..+4 (low nibbles) and
-        // kbase+32+4i..+4 (high nibbles).
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float wl[ROWS][4], wh[ROWS][4];
+        for (int u = 0; u < U; u++) {
+            const int64_t ch = base + lane + 32 * u;
+            const int64_t chc = ch < nchunk ? ch : nchunk - 1;
+            const int64_t b = chc >> 2;
+            const int c = (int)(chc & 3);
 #pragma unroll
             for (int r = 0; r < ROWS; r++) {
-                const uint32_t word = (i < 4) ? (&qa[r].x)[i] : (&qb[r].x)[i - 4];
+                const char* blk = wrow[r] + (size_t)b * kQ4KBytes;
+                hdr[u][r] = ld_stream16(blk);
+                qa[u][r] = ld_stream16(blk + 16 + 32 * c);
+                qb[u][r] = ld_stream16(blk + 32 + 32 * c);
+            }
+        }
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    wl[r][e] = fmaf(ds0[r], nib_f(word, 8 * e), -dm0[r]);
-                    wh[r][e] = fmaf(ds1[r], nib_f(word, 8 * e + 4), -dm1[r]);
-                }
+        for (int u = 0; u < U; u++) {
+            const int64_t ch = base + lane + 32 * u;
+            if (ch >= nchunk) break;
+            const int c = (int)(ch & 3);
+            const int64_t kbase = ch * 64;
+            // per-row scales of the chunk's two sub-blocks
+            float ds0[ROWS], dm0[ROWS], ds1[ROWS], dm1[ROWS];
+#pragma unroll
+            for (int r = 0; r < ROWS; r++) {
+                const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u][r].x & 0xFFFFu)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u][r].x >> 16)));
+                uint8_t sb[12];
+                *reinterpret_cast<uint32_t*>(sb + 0) = hdr[u][r].y;
+                *reinterpret_cast<uint32_t*>(sb + 4) = hdr[u][r].z;
+                *reinterpret_cast<uint32_t*>(sb + 8) = hdr[u][r].w;
+                float sc, mn;
+                q4k_scale_min(sb, 2 * c, sc, mn);
+                ds0[r] = d * sc;
+                dm0[r] = dmin * mn;
+                q4k_scale_min(sb, 2 * c + 1, sc, mn);
+                ds1[r] = d * sc;
+                dm1[r] = dmin * mn;
             }
 #pragma unroll
             for (int n = 0; n < NB; n++) {
                 if (n < ncols) {
-                    const float* xc = reinterpret_cast<const float*>(X + (size_t)n * x_cs);
-                    const float4 xl = __ldg(reinterpret_cast<const float4*>(xc + kbase + 4 * i));
-                    const float4 xh = __ldg(reinterpret_cast<const float4*>(xc + kbase + 32 + 4 * i));
+                    const float* xc = reinterpret_cast<const float*>(X + (size_t)n * x_cs) + kbase;
+                    float2 ql[ROWS], qh[ROWS];      // sum(q*x) of sub-blocks 2c / 2c+1, pairwise
+#pragma unroll
+                    for (int r = 0; r < ROWS; r++) { ql[r] = make_float2(0.f, 0.f); qh[r] = ql[r]; }
+                    float2 xl = make_float2(0.f, 0.f), xh = xl;   // sum(x) of the two sub-blocks
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const float4 a = __ldg(reinterpret_cast<const float4*>(xc + 4 * i));
+                        const float4 bq = __ldg(reinterpret_cast<const float4*>(xc + 32 + 4 * i));
+                        const float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
+                        const float2 b01 = make_float2(bq.x, bq.y), b23 = make_float2(bq.z, bq.w);
+                        xl = __fadd2_rn(xl, __fadd2_rn(a01, a23));
+                        xh = __fadd2_rn(xh, __fadd2_rn(b01, b23));
+#pragma unroll
+                        for (int r = 0; r < ROWS; r++) {
+                            const uint32_t word = (i < 4) ? (&qa[u][r].x)[i] : (&qb[u][r].x)[i - 4];
+                            ql[r] = __ffma2_rn(nib2(word, 0, 0), a01, ql[r]);
+                            ql[r] = __ffma2_rn(nib2(word, 2, 0), a23, ql[r]);
+                            qh[r] = __ffma2_rn(nib2(word, 0, 4), b01, qh[r]);
+                            qh[r] = __ffma2_rn(nib2(word, 2, 4), b23, qh[r]);
+                        }
+                    }
+                    const float sxl = xl.x + xl.y, sxh = xh.x + xh.y;
 #pragma unroll
                     for (int r = 0; r < ROWS; r++) {
-                        float a = acc[r][n];
-                        a = fmaf(wl[r][0], xl.x, a); a = fmaf(wl[r][1], xl.y, a);
-                        a = fmaf(wl[r][2], xl.z, a); a = fmaf(wl[r][3], xl.w, a);
-                        a = fmaf(wh[r][0], xh.x, a); a = fmaf(wh[r][1], xh.y, a);
-                        a = fmaf(wh[r][2], xh.z, a); a = fmaf(wh[r][3], xh.w, a);
-                        acc[r][n] = a;
+                        float a2 = acc[r][n];
+                        a2 = fmaf(ds0[r], ql[r].x + ql[r].y, a2);
+                        a2 = fmaf(-dm0[r], sxl, a2);
+                        a2 = fmaf(ds1[r], qh[r].x + qh[r].y, a2);
+                        a2 = fmaf(-dm1[r], sxh, a2);
+                        acc[r][n] = a2;
                     }
                 }
             }
@@ -320,10 +359,11 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
 template <int NB>
 void launch_q4k(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
                 int ncols, char* y, size_t y_cs, cudaStream_t s) {
-    constexpr int ROWS = 2;
+    constexpr int ROWS = NB <= 4 ? 2 : 1;
+    constexpr int U = 2;
     const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
     const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    q4k_gemv_kernel<NB, ROWS><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
+    q4k_gemv_kernel<NB, ROWS, U><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
     count_launch();
 }
 
@@ -370,15 +410,14 @@ int launch_q4k_gemv(const DeviceCtx*, const void* w, size_t w_row_bytes, int64_t
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
-    for (int64_t n0 = 0; n0 < N; n0 += 16) {
-        const int nc = (int)std::min<int64_t>(16, N - n0);
+    for (int64_t n0 = 0; n0 < N; n0 += 8) {
+        const int nc = (int)std::min<int64_t>(8, N - n0);
         const char* xn = xc + (size_t)n0 * x_col_bytes;
         char* yn = yc + (size_t)n0 * y_col_bytes;
         if (nc == 1) launch_q4k<1>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
         else if (nc <= 2) launch_q4k<2>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
         else if (nc <= 4) launch_q4k<4>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        else if (nc <= 8) launch_q4k<8>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        else launch_q4k<16>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
+        else launch_q4k<8>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
         MLZC_CUDA_TRY(cudaGetLastError());
     }
     return MLZC_OK;

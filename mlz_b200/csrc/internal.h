@@ -66,6 +66,10 @@ size_t fa_workspace_bytes(const mlzc_fa_desc* d);
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
                       cudaStream_t s);
 
+// Reads and clears the error word used by flash-attention calls made without a library
+// context (the allocation-free entry point) on the current device.
+int fa_take_static_errors(unsigned int* out);
+
 // Dispatch of one validated mul_mat to the kernel that fits its shape (GEMV, Q4_K,
 // tensor-core GEMM); asynchronous on `s`.
 int mul_mat_run(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64_t M, int64_t K,

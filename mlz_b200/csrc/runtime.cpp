@@ -224,13 +224,15 @@ extern "C" int mlzc_device_errors(int device, uint32_t* out_bits) {
     int prev = 0;
     cudaGetDevice(&prev);
     MLZC_CUDA_TRY(cudaSetDevice(device));
-    unsigned int v = 0;
+    unsigned int v = 0, vs = 0;
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpy(&v, c->err, sizeof v, cudaMemcpyDeviceToHost);
     if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof v);
+    int st = e == cudaSuccess ? fa_take_static_errors(&vs) : MLZC_OK;
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "mlzc_device_errors");
-    *out_bits = v;
+    if (st != MLZC_OK) return st;
+    *out_bits = v | vs;
     return MLZC_OK;
 }
 
