@@ -8,13 +8,18 @@
 //
 // GPU design (HBM-bound: every K/V byte is read once):
 //   - Grouped-query packing: the G = n_head_q / n_head_kv query heads (times n_queries)
-//     that share a KV head are the columns of one MMA tile (up to 8 query rows per CTA),
-//     so each K/V row is read once for all of them.
-//   - Split-K ("flash decoding"): the keys of a sequence are cut into chunks of kChunk
-//     positions, one CTA per (chunk, row group, kv head, sequence); chunks past a
-//     sequence's kv_len exit at once, so a ragged batch costs only its real keys.
-//   - A producer warp streams 64-key K and V tiles into a shared-memory ring with TMA
-//     (4-d tensor maps over the ggml strides, 64-dim boxes with 128-byte swizzle).
+//     that share a KV head are the columns of one MMA tile (up to 8 query rows), so each
+//     K/V row is read once for all of them.  A "segment" is one (sequence, kv head, row
+//     group) and its keys are cut into 64-key tiles.
+//   - Persistent, stream-K balanced: a grid of (SMs x resident CTAs) walks the tiles of
+//     all segments in one global order, each CTA taking an equal contiguous range, so a
+//     ragged batch costs only its real keys and no CTA idles while another finishes.  A
+//     CTA's range covers whole segments or parts of them ("pieces"); a piece that is a
+//     whole segment writes the final row, the others write a partial (max, sum,
+//     unnormalised O) record that the combine kernel merges in CTA order.
+//   - A producer warp streams K and V tiles into a shared-memory ring with TMA (4-d tensor
+//     maps over the ggml strides, 64-dim boxes with 128-byte swizzle), across piece
+//     boundaries without a pause.
 //   - Four consumer warps own 16 keys of every tile.  Scores S^T = K . Q^T and the update
 //     O^T += V^T . P^T run on the tensor cores (mma.sync m16n8k16, f16 operands, f32
 //     accumulators in registers): keys fill the MMA's M side (16) and the query rows its
@@ -24,11 +29,10 @@
 //     through TMEM; here the accumulators stay in registers and the tensor pipe stays far
 //     below its bound (D/4 MMAs per 16 keys).
 //     fp32-level accuracy: Q and P are split into f16 hi + lo parts (two MMAs each), K
-//     and V are f16 already.  Online softmax (max / rescale / exp) in fp32 per warp.
-//   - The warps' (max, sum, O) states merge in shared memory; a CTA then writes its
-//     partial (max, sum, unnormalised O) to the workspace, and the combine kernel merges
-//     the chunks of each row.  With a single chunk the CTA writes the final row itself.
-//     Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
+//     and V are f16 already.  Online softmax (max / rescale / exp) in fp32 per warp; the
+//     warps' states merge in shared memory at the end of each piece, in a fixed order, so
+//     results repeat bit for bit.
+//   - Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
 // Score order (flash_attention.cpp:339-363): s = <q*scale, k>, + mask, softcap, + ALiBi.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -48,31 +52,31 @@ constexpr int kFaWarps = 4;                          // consumer warps
 constexpr int kFaThreads = (kFaWarps + 1) * 32;      // + one producer warp
 constexpr int kTile = 64;                            // keys per shared-memory stage
 constexpr int kWarpKeys = kTile / kFaWarps;          // 16 keys per consumer warp and tile
-constexpr int kChunk = 512;                          // keys per CTA
-constexpr int kRows = 8;                             // query rows per CTA (the MMA's N)
+constexpr int kRows = 8;                             // query rows per segment (the MMA's N)
 constexpr int kBox = 64;                             // dims per TMA box (128 bytes, swizzled)
+constexpr int kMaxBatch = 1024;                      // sequences per launch (prefix table in smem)
 
 template <int D>
 struct FaCfg {
     static constexpr int kBoxes = D / kBox;
     static constexpr uint32_t kOperandBytes = kBoxes * kTile * 128;   // K or V of one tile
     static constexpr uint32_t kStageBytes = 2 * kOperandBytes;
-    static constexpr int kStages = D == 256 ? 2 : (D == 128 ? 3 : 4);
-    static constexpr int kQStride = D + 8;                            // f16 elements per Q row
-    static constexpr uint32_t kQBytes = 2 * kRows * kQStride * 2;     // hi and lo
-    static constexpr uint32_t kMergeBytes = kFaWarps * kRows * (D + 2) * 4;
-    static_assert(kMergeBytes <= kStages * kStageBytes, "merge area must fit in the ring");
-    static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kQBytes + 256;
+    static constexpr int kStages = D == 64 ? 4 : 3;
+    static constexpr int kAreaStride = D + 4;                         // floats per merge row
+    static constexpr uint32_t kAreaBytes = kRows * kAreaStride * 4;
+    static constexpr uint32_t kStatBytes = 2 * kFaWarps * kRows * 4;  // m and l per warp and row
+    static constexpr uint32_t kPrefBytes = ((kMaxBatch + 1) * 4 + 15) / 16 * 16;
+    static constexpr size_t kSmemBytes =
+        1024 + (size_t)kStages * kStageBytes + kAreaBytes + kStatBytes + kPrefBytes + 128;
 };
 
 struct __align__(64) FaParams {
     const char* q;
-    const char* k;
-    const char* v;
     const char* mask;
     char* dst;
-    float* part;                 // workspace partials, or nullptr when nsplit == 1
-    const int32_t* kv_len;
+    float* part;                 // partial records: (CTAs + segments) x kRows x (D + 2)
+    int* pref_out;               // the prefix table, for the combine kernel
+    const int32_t* kv_len;       // per sequence, or nullptr (every sequence has n_kv keys)
     int64_t q_nb1, q_nb2, q_nb3;
     int64_t m_nb0, m_nb1, m_nb2, m_nb3;
     int64_t d_nb1, d_nb2, d_nb3;
@@ -80,10 +84,13 @@ struct __align__(64) FaParams {
     int G;                       // query heads per row group
     int rows_total;              // G * n_q
     int n_rgroups;               // ceil(rows_total / kRows)
-    int nsplit;
-    int packed;                  // 1: grid.y walks kv heads; 0: grid.y walks query heads
+    int n_hidx;                  // kv heads (packed) or query heads
+    int HR;                      // segments per sequence: n_hidx * n_rgroups
+    int b_base, nB;              // sequences [b_base, b_base + nB) in this launch
+    int packed;                  // 1: a segment's heads share one kv head; 0: one query head
     float scale, softcap, alibi_p2inv;  // alibi_p2inv = -8 / P (0 = no ALiBi)
     int use_softcap;
+    int k_hmul, k_bmul, v_hmul, v_bmul;   // 0 where K / V is shared across heads / sequences
     unsigned int* err;           // device error word (bounded waits)
     CUtensorMap tm_k, tm_v;      // [B][Hkv][n_kv][D] with 64 x 64 swizzled boxes
 };
@@ -151,13 +158,55 @@ __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
     return y;
 }
 
+__device__ __forceinline__ int seq_len(const FaParams& p, int b) {
+    return p.kv_len ? min(max(p.kv_len[p.b_base + b], 0), p.n_kv) : p.n_kv;
+}
+
+// CTA of global tile t when W tiles are cut into P equal contiguous ranges
+// [c W / P, (c + 1) W / P).
+__device__ __forceinline__ int cta_of_tile(int64_t t, int64_t W, int P) {
+    return (int)(((t + 1) * P - 1) / W);
+}
+
+// Position in the global tile order: sequence b, segment sl of the sequence, tile j of
+// the segment (nb tiles).  Segments of a sequence come in (head index, row group) order.
+struct Walk {
+    int b, sl, j, nb;
+    __device__ __forceinline__ void init(const int* pref, int nB, int HR, int64_t t) {
+        int lo = 0, hi = nB - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((int64_t)HR * pref[mid] <= t) lo = mid; else hi = mid - 1;
+        }
+        b = lo;
+        nb = pref[b + 1] - pref[b];
+        const int64_t u = t - (int64_t)HR * pref[b];
+        sl = (int)(u / nb);
+        j = (int)(u % nb);
+    }
+    __device__ __forceinline__ void next(const int* pref, int nB, int HR) {
+        if (++j < nb) return;
+        j = 0;
+        if (++sl < HR) return;
+        sl = 0;
+        do { ++b; } while (b < nB && pref[b + 1] == pref[b]);
+        if (b < nB) nb = pref[b + 1] - pref[b];
+    }
+};
+
+__device__ __forceinline__ void consumer_bar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kFaWarps * 32) : "memory");
+}
+
 // Score and value steps per tile and warp, in the transposed form that puts keys on the
 // MMA's M side (16) and the query rows on N (8):
 //   S^T [16 keys x 8 rows]  = K [16 keys x D] . Q^T [D x 8 rows]      (D/16 k-steps)
 //   O^T [D x 8 rows]       += V^T [D x 16 keys] . P^T [16 keys x 8 rows]
 // Fragment ownership (g = lane/4, q = lane%4): S^T element (key g or g+8, row 2q or 2q+1),
 // O^T element (dim 16t + g or +8, row 2q or 2q+1): every lane keeps two query rows.
-template <int D>
+// GEN = false is plain decode (no mask, softcap or ALiBi): the score path carries no
+// branches for them.
+template <int D, bool GEN>
 __global__ void __launch_bounds__(kFaThreads)
 fa_decode_kernel(const __grid_constant__ FaParams p) {
     using C = FaCfg<D>;
@@ -166,24 +215,14 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
     extern __shared__ uint8_t fa_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
-    __half* qs = reinterpret_cast<__half*>(smem + STAGES * C::kStageBytes);    // [hi, lo][kRows][kQStride]
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kQBytes);
+    float* area = reinterpret_cast<float*>(smem + STAGES * C::kStageBytes);            // [kRows][kAreaStride]
+    float* stat_m = reinterpret_cast<float*>(smem + STAGES * C::kStageBytes + C::kAreaBytes);   // [warp][row]
+    float* stat_l = stat_m + kFaWarps * kRows;
+    int* pref = reinterpret_cast<int*>(smem + STAGES * C::kStageBytes + C::kAreaBytes + C::kStatBytes);
+    uint64_t* full =
+        reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kAreaBytes + C::kStatBytes + C::kPrefBytes);
     uint64_t* empty = full + STAGES;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
-
-    const int split = blockIdx.x;
-    const int rg = blockIdx.y % p.n_rgroups;
-    const int hidx = blockIdx.y / p.n_rgroups;
-    const int ib = blockIdx.z;
-    const int kvh = p.packed ? hidx : (int)((int64_t)hidx * p.n_head_kv / p.n_head_q);
-    const int head_base = p.packed ? hidx * p.G : hidx;
-    const int nrows = min(kRows, p.rows_total - rg * kRows);
-
-    const int L = p.kv_len ? min(p.kv_len[ib], p.n_kv) : p.n_kv;
-    const int k0 = split * kChunk;
-    const int k1 = min(k0 + kChunk, L);
-    if (k0 >= L && p.nsplit > 1) return;   // chunk past this sequence's keys: no record
-    const int ntiles = k1 > k0 ? (k1 - k0 + kTile - 1) / kTile : 0;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -198,270 +237,383 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
         *abort_flag = 0;
         ptx::mbar_init_fence();
     }
-    // query rows (pre-scaled), split into f16 hi and lo, zero past nrows
-    for (int idx = threadIdx.x; idx < kRows * D; idx += kFaThreads) {
-        const int r = idx / D, d = idx % D;
-        float qv = 0.0f;
-        if (r < nrows) {
-            int iq, ihq;
-            row_coords(p, head_base, rg * kRows + r, iq, ihq);
-            qv = reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3)[d] * p.scale;
+    // prefix table: pref[b] = tiles of one segment summed over sequences < b
+    if (warp == 0) {
+        int run = 0;
+        for (int base = 0; base < p.nB; base += 32) {
+            const int b = base + lane;
+            const int nb = b < p.nB ? (seq_len(p, b) + kTile - 1) / kTile : 0;
+            int x = nb;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            if (b < p.nB) pref[b + 1] = run + x;
+            run += __shfl_sync(0xffffffffu, x, 31);
         }
-        const __half h = __float2half_rn(qv);
-        qs[r * C::kQStride + d] = h;
-        qs[(kRows + r) * C::kQStride + d] = __float2half_rn(qv - __half2float(h));
+        if (lane == 0) pref[0] = 0;
     }
     __syncthreads();
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i <= p.nB; i += kFaThreads) p.pref_out[i] = pref[i];
 
-    float m_row[2] = {-INFINITY, -INFINITY};
-    float l_row[2] = {0.0f, 0.0f};
-    float o[KS][4];
-#pragma unroll
-    for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    const int64_t W = (int64_t)p.HR * pref[p.nB];
+    const int P = gridDim.x;
+    const int64_t t_begin = W * blockIdx.x / P;
+    const int64_t t_end = W * (blockIdx.x + 1) / P;
+    const int count = (int)(t_end - t_begin);
+    if (count <= 0) return;
 
     if (warp == kFaWarps) {
         // ---------------- producer: K and V tiles into the ring with TMA
         if (lane == 0) {
-            for (int t = 0; t < ntiles; ++t) {
-                const int s = t % STAGES;
-                const uint32_t ph = (t / STAGES) & 1;
+            Walk w;
+            w.init(pref, p.nB, p.HR, t_begin);
+            for (int i = 0; i < count; ++i) {
+                const int s = i % STAGES;
+                const uint32_t ph = (i / STAGES) & 1;
                 if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+                const int hidx = w.sl / p.n_rgroups;
+                const int kvh = p.packed ? hidx : (int)((int64_t)hidx * p.n_head_kv / p.n_head_q);
                 const uint32_t fb = ptx::smem_u32(&full[s]);
                 const uint32_t st = ptx::smem_u32(ring + s * C::kStageBytes);
-                const int j0 = k0 + t * kTile;
+                const int j0 = w.j * kTile;
                 ptx::mbar_expect_tx(fb, C::kStageBytes);
 #pragma unroll
-                for (int b = 0; b < C::kBoxes; ++b) {
-                    tma_load_4d(st + b * (kTile * 128), &p.tm_k, fb, b * kBox, j0, kvh, ib);
-                    tma_load_4d(st + C::kOperandBytes + b * (kTile * 128), &p.tm_v, fb, b * kBox, j0, kvh, ib);
+                for (int bx = 0; bx < C::kBoxes; ++bx) {
+                    tma_load_4d(st + bx * (kTile * 128), &p.tm_k, fb, bx * kBox, j0, kvh * p.k_hmul,
+                                (p.b_base + w.b) * p.k_bmul);
+                    tma_load_4d(st + C::kOperandBytes + bx * (kTile * 128), &p.tm_v, fb, bx * kBox, j0,
+                                kvh * p.v_hmul, (p.b_base + w.b) * p.v_bmul);
                 }
+                w.next(pref, p.nB, p.HR);
             }
         }
-    } else {
-        // ---------------- consumers: 16 keys of every tile per warp
-        int iq_r[2], ihq_r[2];
-        bool row_ok[2];
-        float slope[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int r = 2 * q4 + h;
-            row_ok[h] = r < nrows;
-            row_coords(p, head_base, rg * kRows + (row_ok[h] ? r : 0), iq_r[h], ihq_r[h]);
-            slope[h] = p.alibi_p2inv != 0.0f ? exp2f(p.alibi_p2inv * (float)(ihq_r[h] + 1)) : 0.0f;
-        }
-        const int mat = lane >> 3;               // ldmatrix: matrix whose row this lane addresses
-        // B fragments of Q^T for every 16-dim step: {hi b0, hi b1, lo b0, lo b1}
-        uint32_t qf[KS][4];
-        {
-            const uint32_t qrow =
-                ptx::smem_u32(qs) + (uint32_t)((((mat >> 1) * kRows + (lane & 7)) * C::kQStride + 8 * (mat & 1)) * 2);
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) ldsm_x4(qrow + ks * 32, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-        }
-        const int kw = warp * kWarpKeys;
-        const int k_key = kw + (lane & 7) + 8 * (mat & 1);     // K: matrices (keys, dims) = (0,0) (8,0) (0,8) (8,8)
-        const int k_half = mat >> 1;
-        const int v_key = kw + (lane & 7) + 8 * (mat >> 1);    // V^T: matrices (dims, keys) = (0,0) (8,0) (0,8) (8,8)
-        const int v_half = mat & 1;
+        return;
+    }
 
-        for (int t = 0; t < ntiles; ++t) {
-            const int s = t % STAGES;
-            const uint32_t ph = (t / STAGES) & 1;
-            if (!ptx::mbar_wait(ptx::smem_u32(&full[s]), ph, abort_flag, p.err)) break;
-            const uint32_t kbuf = ptx::smem_u32(ring + s * C::kStageBytes);
-            const uint32_t vbuf = kbuf + C::kOperandBytes;
-            const int j0 = k0 + t * kTile;
-            if (j0 + kw + kWarpKeys > k1) {
-                // V rows past the sequence's last key may hold any bits (NaN included) and
-                // 0 * NaN in P . V would poison O: zero this warp's rows of them
-                const int first = max(0, k1 - j0 - kw);
-                uint8_t* vgen = ring + s * C::kStageBytes + C::kOperandBytes;
-                for (int idx = lane; idx < (kWarpKeys - first) * (D / 8); idx += 32) {
-                    const int key = kw + first + idx / (D / 8);
-                    const int c = idx % (D / 8);
-                    *reinterpret_cast<uint4*>(vgen + (tile_addr(vbuf, key, c) - vbuf)) = make_uint4(0, 0, 0, 0);
-                }
-                // these generic writes precede the next TMA write into the stage
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
+    // ---------------- consumers: 16 keys of every tile per warp
+    const int mat = lane >> 3;                   // ldmatrix: matrix whose row this lane addresses
+    const int kw = warp * kWarpKeys;
+    const int k_key = kw + (lane & 7) + 8 * (mat & 1);     // K: matrices (keys, dims) = (0,0) (8,0) (0,8) (8,8)
+    const int k_half = mat >> 1;
+    const int v_key = kw + (lane & 7) + 8 * (mat >> 1);    // V^T: matrices (dims, keys) = (0,0) (8,0) (0,8) (8,8)
+    const int v_half = mat & 1;
+
+    Walk w;
+    w.init(pref, p.nB, p.HR, t_begin);
+    // per-piece state
+    int L = 0, ib = 0, head_base = 0, rg = 0, nrows = 0;
+    bool whole = false;
+    int iq_r[2] = {0, 0}, ihq_r[2] = {0, 0};
+    bool row_ok[2] = {false, false};
+    float slope[2] = {0.0f, 0.0f};
+    uint32_t qf[KS][4];
+    float m_row[2], l_row[2];
+    float o[KS][4];
+
+    for (int i = 0; i < count; ++i) {
+        if (i == 0 || w.j == 0) {
+            // ---- a new piece: segment (w.b, w.sl)
+            whole = (w.j == 0);
+            ib = p.b_base + w.b;
+            L = seq_len(p, w.b);
+            const int hidx = w.sl / p.n_rgroups;
+            rg = w.sl % p.n_rgroups;
+            head_base = p.packed ? hidx * p.G : hidx;
+            nrows = min(kRows, p.rows_total - rg * kRows);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = 2 * q4 + h;
+                row_ok[h] = r < nrows;
+                row_coords(p, head_base, rg * kRows + (row_ok[h] ? r : 0), iq_r[h], ihq_r[h]);
+                slope[h] = p.alibi_p2inv != 0.0f ? exp2f(p.alibi_p2inv * (float)(ihq_r[h] + 1)) : 0.0f;
+                m_row[h] = -INFINITY;
+                l_row[h] = 0.0f;
             }
-
-            // S^T = K . Q^T (Q as hi + lo)
-            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            // B fragments of Q^T (pre-scaled, f16 hi + lo): row g, dims 16 ks + {2 q4, +1, +8, +9}
+            const float* qr = nullptr;
+            if (g < nrows) {
+                int iq, ihq;
+                row_coords(p, head_base, rg * kRows + g, iq, ihq);
+                qr = reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3);
+            }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4(tile_addr(kbuf, k_key, 2 * ks + k_half), a0, a1, a2, a3);
-                mma16816(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-                mma16816(sc, a0, a1, a2, a3, qf[ks][2], qf[ks][3]);
+                const int d0 = 16 * ks + 2 * q4;
+                float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+                if (qr) {
+                    x0 = qr[d0] * p.scale;
+                    x1 = qr[d0 + 1] * p.scale;
+                    x2 = qr[d0 + 8] * p.scale;
+                    x3 = qr[d0 + 9] * p.scale;
+                }
+                split_h2(x0, x1, qf[ks][0], qf[ks][2]);
+                split_h2(x2, x3, qf[ks][1], qf[ks][3]);
             }
-            // mask / softcap / ALiBi / validity; element e: key g + 8 (e >> 1), row 2 q4 + (e & 1)
-            float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int h = e & 1;
-                const int j = j0 + kw + g + 8 * (e >> 1);
-                float a = sc[e];
-                if (j < k1 && row_ok[h]) {
+            for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+        }
+
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!ptx::mbar_wait(ptx::smem_u32(&full[s]), ph, abort_flag, p.err)) return;   // all consumers stop here
+        const uint32_t kbuf = ptx::smem_u32(ring + s * C::kStageBytes);
+        const uint32_t vbuf = kbuf + C::kOperandBytes;
+        const int j0 = w.j * kTile;
+        if (j0 + kw + kWarpKeys > L) {
+            // V rows past the sequence's last key may hold any bits (NaN included) and
+            // 0 * NaN in P . V would poison O: zero this warp's rows of them
+            const int first = max(0, L - j0 - kw);
+            uint8_t* vgen = ring + s * C::kStageBytes + C::kOperandBytes;
+            for (int idx = lane; idx < (kWarpKeys - first) * (D / 8); idx += 32) {
+                const int key = kw + first + idx / (D / 8);
+                const int c = idx % (D / 8);
+                *reinterpret_cast<uint4*>(vgen + (tile_addr(vbuf, key, c) - vbuf)) = make_uint4(0, 0, 0, 0);
+            }
+            // these generic writes precede the next TMA write into the stage
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+        }
+
+        // S^T = K . Q^T in four independent accumulator chains (Q hi / lo x even / odd
+        // 16-dim steps), summed at the end
+        float acc[4][4] = {};
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(tile_addr(kbuf, k_key, 2 * ks + k_half), a0, a1, a2, a3);
+            mma16816(acc[2 * (ks & 1)], a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            mma16816(acc[2 * (ks & 1) + 1], a0, a1, a2, a3, qf[ks][2], qf[ks][3]);
+        }
+        // mask / softcap / ALiBi / validity; element e: key g + 8 (e >> 1), row 2 q4 + (e & 1)
+        float sc[4];
+        float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int h = e & 1;
+            const int j = j0 + kw + g + 8 * (e >> 1);
+            float a = (acc[0][e] + acc[2][e]) + (acc[1][e] + acc[3][e]);
+            if (j < L && row_ok[h]) {
+                if constexpr (GEN) {
                     if (p.mask)
                         a += *reinterpret_cast<const float*>(p.mask + iq_r[h] * p.m_nb1 + (int64_t)j * p.m_nb0 +
                                                             ihq_r[h] * p.m_nb2 + ib * p.m_nb3);
                     if (p.use_softcap) a = p.softcap * tanhf(a / p.softcap);
                     if (p.alibi_p2inv != 0.0f) a += slope[h] * (float)(j - iq_r[h]);
-                } else {
-                    a = -INFINITY;
                 }
-                sc[e] = a;
-                tmax[h] = fmaxf(tmax[h], a);
+            } else {
+                a = -INFINITY;
             }
-            float corr[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 4));
-                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 8));
-                tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 16));
-                const float mnew = fmaxf(m_row[h], tmax[h]);
-                corr[h] = (mnew == -INFINITY) ? 1.0f : __expf(m_row[h] - mnew);
-                m_row[h] = mnew;
-                l_row[h] *= corr[h];
-            }
-            if (corr[0] != 1.0f || corr[1] != 1.0f) {
-#pragma unroll
-                for (int t2 = 0; t2 < KS; ++t2) {
-                    o[t2][0] *= corr[0]; o[t2][1] *= corr[1];
-                    o[t2][2] *= corr[0]; o[t2][3] *= corr[1];
-                }
-            }
-            float pe[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int h = e & 1;
-                pe[e] = (sc[e] == -INFINITY) ? 0.0f : __expf(sc[e] - m_row[h]);
-                l_row[h] += pe[e];
-            }
-            // P^T (keys x rows) as f16 hi + lo, transposed in registers into B fragments
-            uint32_t h0, l0, h1, l1;
-            split_h2(pe[0], pe[1], h0, l0);      // key g
-            split_h2(pe[2], pe[3], h1, l1);      // key g + 8
-            const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1);
-            const uint32_t bl0 = movtrans(l0), bl1 = movtrans(l1);
-            // O^T += V^T . P^T
-#pragma unroll
-            for (int dt = 0; dt < KS; ++dt) {
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4_t(tile_addr(vbuf, v_key, 2 * dt + v_half), a0, a1, a2, a3);
-                mma16816(o[dt], a0, a1, a2, a3, bh0, bh1);
-                mma16816(o[dt], a0, a1, a2, a3, bl0, bl1);
-            }
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
+            sc[e] = a;
+            tmax[h] = fmaxf(tmax[h], a);
         }
-        // row sums over the lanes that share the rows (same q4)
+        float corr[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 4);
-            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 8);
-            l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 16);
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 4));
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 8));
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 16));
+            const float mnew = fmaxf(m_row[h], tmax[h]);
+            corr[h] = (mnew == -INFINITY) ? 1.0f : __expf(m_row[h] - mnew);
+            m_row[h] = mnew;
+            l_row[h] *= corr[h];
         }
-    }
-
-    // merge the consumer warps (their rows' max, sum and O) through shared memory; the
-    // ring is free once every tile has been consumed
-    __syncthreads();
-    float* mo = reinterpret_cast<float*>(ring);                 // [warp][row][D]
-    float* mm = mo + kFaWarps * kRows * D;                      // [warp][row]
-    float* ml = mm + kFaWarps * kRows;                          // [warp][row]
-    if (warp < kFaWarps) {
+        if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
-        for (int dt = 0; dt < KS; ++dt) {
-            const int d = 16 * dt + g;
-            const int r = warp * kRows + 2 * q4;
-            mo[r * D + d] = o[dt][0];
-            mo[(r + 1) * D + d] = o[dt][1];
-            mo[r * D + d + 8] = o[dt][2];
-            mo[(r + 1) * D + d + 8] = o[dt][3];
-        }
-        if (g == 0) {
-            mm[warp * kRows + 2 * q4] = m_row[0];
-            mm[warp * kRows + 2 * q4 + 1] = m_row[1];
-            ml[warp * kRows + 2 * q4] = l_row[0];
-            ml[warp * kRows + 2 * q4 + 1] = l_row[1];
-        }
-    }
-    __syncthreads();
-
-    for (int idx = threadIdx.x; idx < nrows * D; idx += kFaThreads) {
-        const int r = idx / D, d = idx % D;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kFaWarps; w++) M = fmaxf(M, mm[w * kRows + r]);
-        float Ls = 0.0f, Os = 0.0f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < kFaWarps; w++) {
-                const float e = __expf(mm[w * kRows + r] - M);
-                Ls += ml[w * kRows + r] * e;
-                Os += mo[(w * kRows + r) * D + d] * e;
+            for (int t2 = 0; t2 < KS; ++t2) {
+                o[t2][0] *= corr[0]; o[t2][1] *= corr[1];
+                o[t2][2] *= corr[0]; o[t2][3] *= corr[1];
             }
         }
-        const int row = rg * kRows + r;
-        int iq, ihq;
-        row_coords(p, head_base, row, iq, ihq);
-        if (p.nsplit == 1) {
-            float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
-            dr[d] = Ls > 0.0f ? Os / Ls : 0.0f;
-        } else {
-            // partial record: [m, l, o[0..D)] per (ib, hidx, row, split)
-            const int64_t n_hidx = gridDim.y / p.n_rgroups;
-            const int64_t rec = (((int64_t)ib * n_hidx + hidx) * p.rows_total + row) * p.nsplit + split;
-            float* pr = p.part + rec * (D + 2);
-            if (d == 0) { pr[0] = M; pr[1] = Ls; }
-            pr[2 + d] = Os;
+        float pe[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int h = e & 1;
+            pe[e] = (sc[e] == -INFINITY) ? 0.0f : __expf(sc[e] - m_row[h]);
+            l_row[h] += pe[e];
         }
+        // P^T (keys x rows) as f16 hi + lo, transposed in registers into B fragments
+        uint32_t h0, l0, h1, l1;
+        split_h2(pe[0], pe[1], h0, l0);      // key g
+        split_h2(pe[2], pe[3], h1, l1);      // key g + 8
+        const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1);
+        const uint32_t bl0 = movtrans(l0), bl1 = movtrans(l1);
+        // O^T += V^T . P^T
+#pragma unroll
+        for (int dt = 0; dt < KS; ++dt) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(tile_addr(vbuf, v_key, 2 * dt + v_half), a0, a1, a2, a3);
+            mma16816(o[dt], a0, a1, a2, a3, bh0, bh1);
+            mma16816(o[dt], a0, a1, a2, a3, bl0, bl1);
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
+
+        const bool seg_end = (w.j == w.nb - 1);
+        if (seg_end || i == count - 1) {
+            // ---- end of the piece: merge the four warps in a fixed order, write it out
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 4);
+                l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 8);
+                l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 16);
+            }
+            if (g == 0) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    stat_m[warp * kRows + 2 * q4 + h] = m_row[h];
+                    stat_l[warp * kRows + 2 * q4 + h] = l_row[h];
+                }
+            }
+            consumer_bar();
+            float e_w[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = 2 * q4 + h;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w2 = 0; w2 < kFaWarps; ++w2) M = fmaxf(M, stat_m[w2 * kRows + r]);
+                e_w[h] = (m_row[h] == -INFINITY) ? 0.0f : __expf(m_row[h] - M);
+            }
+            for (int turn = kFaWarps - 1; turn >= 0; --turn) {
+                if (warp == turn) {
+#pragma unroll
+                    for (int dt = 0; dt < KS; ++dt) {
+                        const int d = 16 * dt + g;
+                        float* a0p = area + (2 * q4) * C::kAreaStride + d;
+                        float* a1p = a0p + C::kAreaStride;
+                        const bool first = (turn == kFaWarps - 1);
+                        a0p[0] = (first ? 0.0f : a0p[0]) + e_w[0] * o[dt][0];
+                        a1p[0] = (first ? 0.0f : a1p[0]) + e_w[1] * o[dt][1];
+                        a0p[8] = (first ? 0.0f : a0p[8]) + e_w[0] * o[dt][2];
+                        a1p[8] = (first ? 0.0f : a1p[8]) + e_w[1] * o[dt][3];
+                    }
+                }
+                consumer_bar();
+            }
+            const bool final_row = whole && seg_end;
+            const int64_t slot = (int64_t)blockIdx.x + (int64_t)w.b * p.HR + w.sl;
+            for (int idx = threadIdx.x; idx < nrows * D; idx += kFaWarps * 32) {
+                const int r = idx / D, d = idx % D;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w2 = 0; w2 < kFaWarps; ++w2) M = fmaxf(M, stat_m[w2 * kRows + r]);
+                float Ls = 0.0f;
+                if (M != -INFINITY) {
+#pragma unroll
+                    for (int w2 = 0; w2 < kFaWarps; ++w2) {
+                        const float mw = stat_m[w2 * kRows + r];
+                        if (mw != -INFINITY) Ls += stat_l[w2 * kRows + r] * __expf(mw - M);
+                    }
+                }
+                const float Os = area[r * C::kAreaStride + d];
+                if (final_row) {
+                    int iq, ihq;
+                    row_coords(p, head_base, rg * kRows + r, iq, ihq);
+                    float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
+                    dr[d] = Ls > 0.0f ? Os / Ls : 0.0f;
+                } else {
+                    float* pr = p.part + (slot * kRows + r) * (D + 2);
+                    if (d == 0) { pr[0] = M; pr[1] = Ls; }
+                    pr[2 + d] = Os;
+                }
+            }
+            consumer_bar();   // the stats and the area are free for the next piece
+        }
+        w.next(pref, p.nB, p.HR);
     }
 }
 
-// Merges the chunk partials of every (sequence, head index, row): one CTA per row.
+// Writes every row whose segment the decode kernel split across CTAs (merging the
+// pieces' records in CTA order), and zeros for empty sequences: one CTA per row.
 template <int D>
 __global__ void __launch_bounds__(D)
-fa_combine_kernel(const __grid_constant__ FaParams p, int n_hidx) {
+fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
     const int row = blockIdx.x;
     const int hidx = blockIdx.y;
-    const int ib = blockIdx.z;
+    const int b = blockIdx.z;
     const int d = threadIdx.x;
-    const int64_t rec0 = (((int64_t)ib * n_hidx + hidx) * p.rows_total + row) * p.nsplit;
-    const float* base = p.part + rec0 * (D + 2);
-    const int L = p.kv_len ? min(p.kv_len[ib], p.n_kv) : p.n_kv;
-    const int used = min(p.nsplit, (L + kChunk - 1) / kChunk);
+    const int* pref = p.pref_out;
+    const int nb = pref[b + 1] - pref[b];
+    const int rg = row / kRows, r = row % kRows;
+    const int sl = hidx * p.n_rgroups + rg;
+    const int ib = p.b_base + b;
+    const int head_base = p.packed ? hidx * p.G : hidx;
+    int iq, ihq;
+    row_coords(p, head_base, row, iq, ihq);
+    float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
+    if (nb == 0) {
+        dr[d] = 0.0f;
+        return;
+    }
+    const int64_t W = (int64_t)p.HR * pref[p.nB];
+    const int64_t T = (int64_t)p.HR * pref[b] + (int64_t)sl * nb;
+    const int cf = cta_of_tile(T, W, P);
+    const int cl = cta_of_tile(T + nb - 1, W, P);
+    if (cf == cl) return;   // one CTA held the whole segment and wrote the row
+    const int64_t seg = (int64_t)b * p.HR + sl;
+    // CTAs with an empty range (more CTAs than tiles) wrote no record
+    auto empty_range = [&](int c) { return W * c / P == W * (c + 1) / P; };
     float M = -INFINITY;
-    for (int s = 0; s < used; s++) M = fmaxf(M, base[(int64_t)s * (D + 2)]);
+    for (int c = cf; c <= cl; ++c)
+        if (!empty_range(c)) M = fmaxf(M, p.part[((c + seg) * kRows + r) * (D + 2)]);
     float Ls = 0.0f, Os = 0.0f;
     if (M != -INFINITY) {
-        for (int s = 0; s < used; s++) {
-            const float* pr = base + (int64_t)s * (D + 2);
+        for (int c = cf; c <= cl; ++c) {
+            if (empty_range(c)) continue;
+            const float* pr = p.part + ((c + seg) * kRows + r) * (D + 2);
+            if (pr[0] == -INFINITY) continue;
             const float e = __expf(pr[0] - M);
             Ls += pr[1] * e;
             Os += pr[2 + d] * e;
         }
     }
-    const int head_base = p.packed ? hidx * p.G : hidx;
-    int iq, ihq;
-    row_coords(p, head_base, row, iq, ihq);
-    float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
     dr[d] = Ls > 0.0f ? Os / Ls : 0.0f;
+}
+
+// Resident CTAs of the decode kernel per SM on the current device (sets the kernel's
+// shared-memory attributes on first use).
+template <int D>
+int fa_ctas_per_sm(int* out) {
+    static int cached[64] = {};
+    int dev = 0;
+    MLZC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MLZC_ERR_INVALID, "flash_attn: device %d beyond 64", dev);
+    if (!cached[dev]) {
+        constexpr size_t smem = FaCfg<D>::kSmemBytes;
+        for (auto* k : {fa_decode_kernel<D, false>, fa_decode_kernel<D, true>}) {
+            MLZC_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            MLZC_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                               (int)cudaSharedmemCarveoutMaxShared));
+        }
+        int occ = 0, occ_gen = 0;
+        MLZC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fa_decode_kernel<D, false>, kFaThreads, smem));
+        MLZC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_gen, fa_decode_kernel<D, true>, kFaThreads, smem));
+        occ = std::min(occ, occ_gen);
+        int sms = 0;
+        MLZC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        if (occ < 1) return fail(MLZC_ERR_CUDA, "flash_attn: decode kernel does not fit on an SM");
+        cached[dev] = occ * sms;
+    }
+    *out = cached[dev];
+    return MLZC_OK;
 }
 
 struct FaPlan {
     FaParams p;
-    int n_hidx;
-    dim3 grid;
+    int ctas;          // decode grid (persistent)
+    int slice;         // sequences per launch
+    size_t pref_bytes;
     size_t ws_bytes;
 };
 
-FaPlan make_plan(const mlzc_fa_desc* d) {
+int make_plan(const mlzc_fa_desc* d, FaPlan* out) {
     FaPlan pl{};
     FaParams& p = pl.p;
     const int Hq = (int)d->n_head_q, Hkv = (int)d->n_head_kv;
+    const int D = (int)d->head_dim_k;
     p.packed = (Hq % Hkv == 0) ? 1 : 0;
     p.G = p.packed ? Hq / Hkv : 1;
     p.n_q = (int)d->n_queries;
@@ -470,14 +622,23 @@ FaPlan make_plan(const mlzc_fa_desc* d) {
     p.n_kv = (int)d->n_kv;
     p.n_head_q = Hq;
     p.n_head_kv = Hkv;
-    p.nsplit = std::max(1, (p.n_kv + kChunk - 1) / kChunk);
-    pl.n_hidx = p.packed ? Hkv : Hq;
-    pl.grid = dim3((unsigned)p.nsplit, (unsigned)(p.n_rgroups * pl.n_hidx), (unsigned)d->batch_size);
-    const int64_t D = d->head_dim_v;
-    pl.ws_bytes = p.nsplit > 1
-        ? (size_t)d->batch_size * pl.n_hidx * p.rows_total * p.nsplit * (D + 2) * sizeof(float)
-        : 0;
-    return pl;
+    p.n_hidx = p.packed ? Hkv : Hq;
+    p.HR = p.n_hidx * p.n_rgroups;
+    pl.slice = (int)std::min<int64_t>(d->batch_size, kMaxBatch);
+    int resident = 0;
+    int st = MLZC_OK;
+    if (D == 64) st = fa_ctas_per_sm<64>(&resident);
+    else if (D == 128) st = fa_ctas_per_sm<128>(&resident);
+    else if (D == 256) st = fa_ctas_per_sm<256>(&resident);
+    else return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: head_dim %d (64, 128, 256 supported)", D);
+    if (st != MLZC_OK) return st;
+    const int64_t tiles_max = (int64_t)pl.slice * p.HR * ((p.n_kv + kTile - 1) / kTile);
+    pl.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(resident, tiles_max));
+    pl.pref_bytes = ((size_t)(pl.slice + 1) * sizeof(int) + 255) / 256 * 256;
+    pl.ws_bytes = pl.pref_bytes +
+                  ((size_t)pl.ctas + (size_t)pl.slice * p.HR) * kRows * (size_t)(d->head_dim_v + 2) * sizeof(float);
+    *out = pl;
+    return MLZC_OK;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 kv_encoder() {
@@ -493,15 +654,22 @@ PFN_cuTensorMapEncodeTiled_v12000 kv_encoder() {
 }
 
 // 4-d f16 map of a K or V tensor (ggml dims [D, n_kv, Hkv, B], byte strides nb[1..3]) with
-// 64 x 64 boxes in the 128-byte swizzle (the layout tile_addr() reads).
-int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, int64_t hkv, int64_t B, const size_t* nb) {
+// 64 x 64 boxes in the 128-byte swizzle (the layout tile_addr() reads).  A dimension with
+// stride 0 (one K/V shared by every head or sequence) gets extent 1 in the map and its
+// coordinate multiplier (*hmul, *bmul) is 0; a tensor map cannot hold a 0 stride.
+int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, int64_t hkv, int64_t B, const size_t* nb,
+                  int* hmul, int* bmul) {
     auto enc = kv_encoder();
     if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_kv, (cuuint64_t)hkv, (cuuint64_t)B};
-    // a broadcast (stride 0) or size-1 dimension gets a harmless stride
-    cuuint64_t st1 = nb[1];
-    cuuint64_t st2 = (hkv == 1 || nb[2] == 0) ? st1 * (cuuint64_t)n_kv : nb[2];
-    cuuint64_t st3 = (B == 1 || nb[3] == 0) ? st2 * (cuuint64_t)hkv : nb[3];
+    if (nb[1] == 0) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V with a 0 key stride");
+    const bool hb = (hkv == 1 || nb[2] == 0), bb = (B == 1 || nb[3] == 0);
+    *hmul = hb ? 0 : 1;
+    *bmul = bb ? 0 : 1;
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_kv, hb ? 1u : (cuuint64_t)hkv, bb ? 1u : (cuuint64_t)B};
+    // strides of extent-1 dimensions are never stepped; keep them legal
+    const cuuint64_t st1 = nb[1];
+    const cuuint64_t st2 = hb ? st1 * (cuuint64_t)n_kv : nb[2];
+    const cuuint64_t st3 = bb ? st2 * dims[2] : nb[3];
     const cuuint64_t strides[3] = {st1, st2, st3};
     const cuuint32_t box[4] = {(cuuint32_t)kBox, (cuuint32_t)kTile, 1, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -514,27 +682,14 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, i
 
 }  // namespace
 
-size_t fa_workspace_bytes(const mlzc_fa_desc* d) { return make_plan(d).ws_bytes; }
+int fa_workspace_bytes(const mlzc_fa_desc* d, size_t* out) {
+    FaPlan pl;
+    const int st = make_plan(d, &pl);
+    *out = st == MLZC_OK ? pl.ws_bytes : 0;
+    return st;
+}
 
 namespace {
-
-template <int D>
-int fa_launch(const FaPlan& pl, cudaStream_t s) {
-    constexpr size_t smem = FaCfg<D>::kSmemBytes;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    MLZC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(MLZC_ERR_INVALID, "flash_attn: device %d beyond 64", dev);
-    if (!attr_set[dev]) {
-        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_decode_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                           (int)cudaSharedmemCarveoutMaxShared));
-        attr_set[dev] = true;
-    }
-    fa_decode_kernel<D><<<pl.grid, kFaThreads, smem, s>>>(pl.p);
-    MLZC_CUDA_TRY(cudaGetLastError());
-    return MLZC_OK;
-}
 
 // Error word of calls made without a library context (the allocation-free entry point):
 // a device variable of this module, so it needs no allocation either.
@@ -554,6 +709,20 @@ unsigned int* static_error_word() {
     return g_fa_err_addr[dev];
 }
 
+template <int D>
+int fa_launch(const FaPlan& pl, cudaStream_t s) {
+    const bool gen = pl.p.mask || pl.p.use_softcap || pl.p.alibi_p2inv != 0.0f;
+    if (gen) fa_decode_kernel<D, true><<<pl.ctas, kFaThreads, FaCfg<D>::kSmemBytes, s>>>(pl.p);
+    else fa_decode_kernel<D, false><<<pl.ctas, kFaThreads, FaCfg<D>::kSmemBytes, s>>>(pl.p);
+    MLZC_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    const dim3 g((unsigned)pl.p.rows_total, (unsigned)pl.p.n_hidx, (unsigned)pl.p.nB);
+    fa_combine_kernel<D><<<g, D, 0, s>>>(pl.p, pl.ctas);
+    MLZC_CUDA_TRY(cudaGetLastError());
+    count_launch();
+    return MLZC_OK;
+}
+
 }  // namespace
 
 int fa_take_static_errors(unsigned int* out) {
@@ -568,16 +737,18 @@ int fa_take_static_errors(unsigned int* out) {
 }
 
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes, cudaStream_t s) {
-    FaPlan pl = make_plan(d);
-    if (pl.ws_bytes > ws_bytes || (pl.ws_bytes && !ws))
+    FaPlan pl;
+    int st = make_plan(d, &pl);
+    if (st != MLZC_OK) return st;
+    if (pl.ws_bytes > ws_bytes || !ws)
         return fail(MLZC_ERR_NOMEM, "flash_attn: workspace of %zu bytes needed, %zu given", pl.ws_bytes, ws_bytes);
+    if ((reinterpret_cast<uintptr_t>(ws) & 15) != 0) return fail(MLZC_ERR_INVALID, "flash_attn: workspace not 16-byte aligned");
     FaParams& p = pl.p;
     p.q = reinterpret_cast<const char*>(d->q);
-    p.k = static_cast<const char*>(d->k);
-    p.v = static_cast<const char*>(d->v);
     p.mask = reinterpret_cast<const char*>(d->mask);
     p.dst = reinterpret_cast<char*>(d->dst);
-    p.part = static_cast<float*>(ws);
+    p.pref_out = static_cast<int*>(ws);
+    p.part = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.pref_bytes);
     p.kv_len = d->kv_len;
     p.q_nb1 = d->q_nb[1]; p.q_nb2 = d->q_nb[2]; p.q_nb3 = d->q_nb[3];
     p.m_nb0 = d->mask_nb[0]; p.m_nb1 = d->mask_nb[1]; p.m_nb2 = d->mask_nb[2]; p.m_nb3 = d->mask_nb[3];
@@ -595,26 +766,21 @@ int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_
     p.err = c ? c->err : static_error_word();
     if (!p.err) return fail(MLZC_ERR_CUDA, "flash_attn: no device error word");
     if (d->n_kv > 0) {
-        int st = encode_kv_map(&p.tm_k, d->k, d->head_dim_k, d->n_kv, d->n_head_kv, d->batch_size, d->k_nb);
+        st = encode_kv_map(&p.tm_k, d->k, d->head_dim_k, d->n_kv, d->n_head_kv, d->batch_size, d->k_nb, &p.k_hmul,
+                           &p.k_bmul);
         if (st != MLZC_OK) return st;
-        st = encode_kv_map(&p.tm_v, d->v, d->head_dim_v, d->n_kv, d->n_head_kv, d->batch_size, d->v_nb);
+        st = encode_kv_map(&p.tm_v, d->v, d->head_dim_v, d->n_kv, d->n_head_kv, d->batch_size, d->v_nb, &p.v_hmul,
+                           &p.v_bmul);
         if (st != MLZC_OK) return st;
     }
     const int D = (int)d->head_dim_k;
-    int st;
-    if (D == 64) st = fa_launch<64>(pl, s);
-    else if (D == 128) st = fa_launch<128>(pl, s);
-    else if (D == 256) st = fa_launch<256>(pl, s);
-    else return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: head_dim %d (64, 128, 256 supported)", D);
-    if (st != MLZC_OK) return st;
-    count_launch();
-    if (p.nsplit > 1) {
-        const dim3 g((unsigned)p.rows_total, (unsigned)pl.n_hidx, (unsigned)d->batch_size);
-        if (D == 64) fa_combine_kernel<64><<<g, 64, 0, s>>>(p, pl.n_hidx);
-        else if (D == 128) fa_combine_kernel<128><<<g, 128, 0, s>>>(p, pl.n_hidx);
-        else fa_combine_kernel<256><<<g, 256, 0, s>>>(p, pl.n_hidx);
-        MLZC_CUDA_TRY(cudaGetLastError());
-        count_launch();
+    for (int64_t b0 = 0; b0 < d->batch_size; b0 += pl.slice) {
+        p.b_base = (int)b0;
+        p.nB = (int)std::min<int64_t>(pl.slice, d->batch_size - b0);
+        if (D == 64) st = fa_launch<64>(pl, s);
+        else if (D == 128) st = fa_launch<128>(pl, s);
+        else st = fa_launch<256>(pl, s);
+        if (st != MLZC_OK) return st;
     }
     return MLZC_OK;
 }
@@ -628,8 +794,8 @@ int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_
 // cudaMalloc would synchronise the device or be refused (a host callback, a thread that
 // must never block behind other streams, an engine whose memory is fully budgeted up
 // front), or a binding that simply has no allocator to hand us a workspace.  For them
-// this variant keeps the split-K partials of the decode kernel in one fixed scratch
-// array that lives in the library's device image instead of a caller workspace.
+// this variant keeps the decode kernel's prefix table and partial records in one fixed
+// scratch array that lives in the library's device image instead of a caller workspace.
 //
 // The array is a file-scope __device__ variable, so every GPU that loads this library
 // holds kNoAllocScratchBytes of it until the process exits, whether or not the entry
@@ -661,14 +827,16 @@ extern "C" int mlzc_flash_attn_dev_noalloc(const mlzc_fa_desc* desc, void* strea
     using namespace mlzc;
     int st = check_fa_args(desc);
     if (st != MLZC_OK) return st;
-    const size_t need = fa_workspace_bytes(desc);
+    size_t need = 0;
+    st = fa_workspace_bytes(desc, &need);
+    if (st != MLZC_OK) return st;
     if (need > kNoAllocScratchBytes)
         return fail(MLZC_ERR_NOMEM,
                     "flash_attn (allocation-free): this call needs %zu bytes of split scratch but the fixed "
                     "scratch holds %zu; use mlzc_flash_attn_dev with a workspace",
                     need, kNoAllocScratchBytes);
     void* scratch = nullptr;
-    if (need > 0) {
+    {
         int dev = 0;
         MLZC_CUDA_TRY(cudaGetDevice(&dev));
         if (dev < 0 || dev >= kNoAllocMaxDevices)

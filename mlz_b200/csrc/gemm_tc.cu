@@ -35,6 +35,7 @@
 #include <mutex>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace mlzc {
 namespace {
@@ -43,77 +44,25 @@ constexpr int BM = 128;
 constexpr int BK = 64;                       // one 128-byte swizzle atom of f16
 constexpr int kEpiWarps = 4;
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s bound on any single mbarrier wait
 constexpr int kSmemBudget = 200 * 1024;
 
 // ------------------------------------------------------------------ PTX wrappers
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n"
-        " .reg .pred p;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n"
-        "}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Waits for the phase of parity `parity` of `bar`; gives up after kWaitNs (setting the
-// error word and the CTA's abort flag) or when another role of the CTA already aborted.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 31) == 0) {
-            if (*abort_flag) return false;
-            if (global_ns() - t0 > kWaitNs) {
-                atomicOr(err, MLZC_DEVERR_WAIT_TIMEOUT);
-                *abort_flag = 1;
-                return false;
-            }
-        }
-    }
-}
+using ptx::bulk_load;
+using ptx::global_ns;
+using ptx::kWaitNs;
+using ptx::mbar_arrive;
+using ptx::mbar_expect_tx;
+using ptx::mbar_init;
+using ptx::mbar_try_wait;
+using ptx::mbar_wait;
+using ptx::smem_u32;
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
-}
-
-// Contiguous bulk copy global -> shared, completing `bytes` on the mbarrier.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -61,8 +61,9 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
                     int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
                     size_t y_col_bytes, void* ws, size_t ws_bytes, cudaStream_t s);
 
-// Flash-attention decode (split-K over keys + combine).
-size_t fa_workspace_bytes(const mlzc_fa_desc* d);
+// Flash-attention decode (persistent stream-K over key tiles + combine).  The workspace
+// size depends on the current device (its resident CTA count).
+int fa_workspace_bytes(const mlzc_fa_desc* d, size_t* out);
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
                       cudaStream_t s);
 

@@ -51,11 +51,10 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Waits for the phase of parity `parity` of `bar`; gives up after kWaitNs (setting the
-// error word and `abort_flag`) or as soon as another thread of the CTA set `abort_flag`.
-__device__ __noinline__ inline bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                              unsigned int* err) {
-    if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait: polls until the phase completes, gives up after kWaitNs (setting
+// the error word and `abort_flag`) or as soon as another thread of the CTA set `abort_flag`.
+__device__ __noinline__ inline bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                   unsigned int* err) {
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -68,6 +67,13 @@ __device__ __noinline__ inline bool mbar_wait(uint32_t bar, uint32_t parity, vol
             }
         }
     }
+}
+
+// Waits for the phase of parity `parity` of `bar` (bounded, see mbar_wait_slow).  The
+// common case -- the phase has already completed -- stays inline, with no call.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, unsigned int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, abort_flag, err);
 }
 
 // Contiguous bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing

@@ -258,8 +258,7 @@ extern "C" int mlzc_flash_attn_workspace_bytes(const mlzc_fa_desc* desc, size_t*
     if (!out_bytes) return fail(MLZC_ERR_INVALID, "null out_bytes");
     int st = check_fa_args(desc);
     if (st != MLZC_OK) return st;
-    *out_bytes = fa_workspace_bytes(desc);
-    return MLZC_OK;
+    return fa_workspace_bytes(desc, out_bytes);
 }
 
 extern "C" int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t workspace_bytes,
@@ -583,7 +582,8 @@ extern "C" int mlzc_try_flash_attn(const mlzc_fa_desc* desc, int ith, int nth) {
         const size_t mb = d.mask ? extent(d.n_kv, 4, d.n_queries, d.mask_nb[1], d.n_head_q, d.mask_nb[2], d.batch_size, d.mask_nb[3]) : 0;
         if (d.mask && d.mask_nb[0] != 4) return 0;
         mlzc_fa_desc dd = d;
-        const size_t wsb = fa_workspace_bytes(&d);
+        size_t wsb = 0;
+        if (fa_workspace_bytes(&d, &wsb) != MLZC_OK) return 0;
         cudaStream_t s = c->stream;
         if (a->q.ensure(qb) || a->k.ensure(kb) || a->v.ensure(vb) || a->dst.ensure(db) || a->ws.ensure(wsb)) return 0;
         if (mb && a->mask.ensure(mb)) return 0;

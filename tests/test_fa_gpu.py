@@ -103,3 +103,51 @@ def test_hook_flash_attn_host_buffers(dev):
     assert mlz_b200.ggml_simd_try_flash_attn(desc, 0, 1) == 1
     want = oracle.flash_attn(q, kb, vb, 0.125)
     assert oracle.rel_err(out, want) <= TOL
+
+
+def test_kv_shared_across_sequences(dev):
+    """One K/V (batch stride 0) serves every sequence, each with its own length."""
+    import torch
+    from mlz_b200.ops import _nb
+    g = synth.rng(91)
+    B, Hq, Hkv, L, D = 6, 16, 4, 900, 128
+    q, k1, v1 = synth.fa_inputs(g, B, Hq, Hkv, L, D)
+    k1, v1 = k1[:1], v1[:1]
+    kv_len = synth.kv_lengths(g, B, 1, L)
+    qd = torch.from_numpy(q).to(dev)
+    kd = torch.from_numpy(k1).to(dev)
+    vd = torch.from_numpy(v1).to(dev)
+    kl = torch.from_numpy(kv_len).to(dev)
+    out = torch.full((B, Hq, 1, D), float("nan"), device=dev)
+    knb = (2, 2 * D, 2 * D * L, 0)
+    desc = mlz_b200.make_fa_desc(qd.data_ptr(), _nb(qd, 4), kd.data_ptr(), knb, vd.data_ptr(), knb,
+                                 out.data_ptr(), _nb(out, 4), (B, Hq, 1, Hkv, L, D), 0.088,
+                                 kv_len_ptr=kl.data_ptr())
+    import ctypes as C
+    wsb = mlz_b200.ops.flash_attn_workspace_bytes(desc)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    mlz_b200.check(mlz_b200.lib().mlzc_flash_attn_dev(C.byref(desc), ws.data_ptr(), wsb,
+                                                      torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    kb = np.broadcast_to(k1, (B, Hkv, L, D))
+    vb = np.broadcast_to(v1, (B, Hkv, L, D))
+    want = oracle.flash_attn(q, np.ascontiguousarray(kb).view(np.uint16), np.ascontiguousarray(vb).view(np.uint16),
+                             0.088, kv_len=kv_len)
+    assert oracle.rel_err(out.cpu().numpy(), want) <= TOL
+
+
+def test_cache_rows_past_kv_len_may_hold_nan(dev):
+    """Unused cache rows (past each sequence's length) hold NaN bit patterns; they must not
+    reach the output (P = 0 there, and 0 * NaN would)."""
+    g = synth.rng(92)
+    B, Hq, Hkv, L, D = 3, 8, 2, 700, 64
+    q, k, v = synth.fa_inputs(g, B, Hq, Hkv, L, D)
+    kv_len = np.array([1, 333, 650], dtype=np.int32)
+    kn, vn = k.copy(), v.copy()
+    for b, n in enumerate(kv_len):
+        kn[b, :, n:, :] = np.float16(np.nan)
+        vn[b, :, n:, :] = np.float16(np.nan)
+    got = _run(dev, q, kn, vn, 0.125, kv_len=kv_len)
+    want = oracle.flash_attn(q, k.view(np.uint16), v.view(np.uint16), 0.125, kv_len=kv_len)
+    assert np.isfinite(got).all()
+    assert oracle.rel_err(got, want) <= TOL

@@ -58,13 +58,16 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(dev):
 
 def test_noalloc_rejects_calls_beyond_its_scratch(dev):
     import torch
-    # 64 sequences x 8 kv heads x 4 rows x 256 chunks x 130 floats needs ~68 MB > 16 MiB
-    B, Hq, Hkv, Lmax, D = 64, 32, 8, 65536, 128
+    # 2048 sequences (launched 1024 at a time) x 8 kv heads: 1024 x 8 segment records of
+    # 8 rows x 130 floats plus one record per CTA is ~35 MB > 16 MiB.  Every declared
+    # extent lies inside real memory (K/V broadcast over the batch), so nothing would read
+    # out of bounds even if the call were not refused.
+    B, Hq, Hkv, L, D = 2048, 32, 8, 16, 128
     q = torch.zeros((B, Hq, 1, D), device=dev)
-    k = torch.zeros((1, Hkv, 16, D), dtype=torch.float16, device=dev)
+    k = torch.zeros((1, Hkv, L, D), dtype=torch.float16, device=dev)
     out = torch.zeros((B, Hq, 1, D), device=dev)
-    d = mlz_b200.make_fa_desc(q.data_ptr(), _nb(q, 4), k.data_ptr(), (2, 256, 256 * 16, 0), k.data_ptr(),
-                              (2, 256, 256 * 16, 0), out.data_ptr(), _nb(out, 4), (B, Hq, 1, Hkv, Lmax, D),
+    d = mlz_b200.make_fa_desc(q.data_ptr(), _nb(q, 4), k.data_ptr(), (2, 2 * D, 2 * D * L, 0), k.data_ptr(),
+                              (2, 2 * D, 2 * D * L, 0), out.data_ptr(), _nb(out, 4), (B, Hq, 1, Hkv, L, D),
                               0.088)
     st = mlz_b200.lib().mlzc_flash_attn_dev_noalloc(C.byref(d), None)
     assert st == -4  # MLZC_ERR_NOMEM, before anything is launched
