@@ -14,9 +14,10 @@
 //   - Persistent, stream-K balanced: a grid of (SMs x resident CTAs) walks the tiles of
 //     all segments in one global order, each CTA taking an equal contiguous range, so a
 //     ragged batch costs only its real keys and no CTA idles while another finishes.  A
-//     CTA's range covers whole segments or parts of them ("pieces"); a piece that is a
-//     whole segment writes the final row, the others write a partial (max, sum,
-//     unnormalised O) record that the combine kernel merges in CTA order.
+//     CTA's range covers whole segments or parts of them ("pieces"); at the end of a piece
+//     every consumer warp writes a partial (max, sum, unnormalised O) record of its rows,
+//     and the combine kernel merges a row's records in CTA then warp order, so results
+//     repeat bit for bit.
 //   - A producer warp streams K and V tiles into a shared-memory ring with TMA (4-d tensor
 //     maps over the ggml strides, 64-dim boxes with 128-byte swizzle), across piece
 //     boundaries without a pause.
@@ -29,9 +30,7 @@
 //     through TMEM; here the accumulators stay in registers and the tensor pipe stays far
 //     below its bound (D/4 MMAs per 16 keys).
 //     fp32-level accuracy: Q and P are split into f16 hi + lo parts (two MMAs each), K
-//     and V are f16 already.  Online softmax (max / rescale / exp) in fp32 per warp; the
-//     warps' states merge in shared memory at the end of each piece, in a fixed order, so
-//     results repeat bit for bit.
+//     and V are f16 already.  Online softmax (max / rescale / exp) in fp32 per warp.
 //   - Every mbarrier wait is bounded (MLZC_DEVERR_WAIT_TIMEOUT).
 // Score order (flash_attention.cpp:339-363): s = <q*scale, k>, + mask, softcap, + ALiBi.
 #include <cuda.h>
@@ -62,19 +61,15 @@ struct FaCfg {
     static constexpr uint32_t kOperandBytes = kBoxes * kTile * 128;   // K or V of one tile
     static constexpr uint32_t kStageBytes = 2 * kOperandBytes;
     static constexpr int kStages = D == 64 ? 4 : 3;
-    static constexpr int kAreaStride = D + 4;                         // floats per merge row
-    static constexpr uint32_t kAreaBytes = kRows * kAreaStride * 4;
-    static constexpr uint32_t kStatBytes = 2 * kFaWarps * kRows * 4;  // m and l per warp and row
     static constexpr uint32_t kPrefBytes = ((kMaxBatch + 1) * 4 + 15) / 16 * 16;
-    static constexpr size_t kSmemBytes =
-        1024 + (size_t)kStages * kStageBytes + kAreaBytes + kStatBytes + kPrefBytes + 128;
+    static constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kPrefBytes + 128;
 };
 
 struct __align__(64) FaParams {
     const char* q;
     const char* mask;
     char* dst;
-    float* part;                 // partial records: (CTAs + segments) x kRows x (D + 2)
+    float* part;                 // partial records: (CTAs + segments) x warps x kRows x (D + 2)
     int* pref_out;               // the prefix table, for the combine kernel
     const int32_t* kv_len;       // per sequence, or nullptr (every sequence has n_kv keys)
     int64_t q_nb1, q_nb2, q_nb3;
@@ -194,10 +189,6 @@ struct Walk {
     }
 };
 
-__device__ __forceinline__ void consumer_bar() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kFaWarps * 32) : "memory");
-}
-
 // Score and value steps per tile and warp, in the transposed form that puts keys on the
 // MMA's M side (16) and the query rows on N (8):
 //   S^T [16 keys x 8 rows]  = K [16 keys x D] . Q^T [D x 8 rows]      (D/16 k-steps)
@@ -215,12 +206,8 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
     extern __shared__ uint8_t fa_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
-    float* area = reinterpret_cast<float*>(smem + STAGES * C::kStageBytes);            // [kRows][kAreaStride]
-    float* stat_m = reinterpret_cast<float*>(smem + STAGES * C::kStageBytes + C::kAreaBytes);   // [warp][row]
-    float* stat_l = stat_m + kFaWarps * kRows;
-    int* pref = reinterpret_cast<int*>(smem + STAGES * C::kStageBytes + C::kAreaBytes + C::kStatBytes);
-    uint64_t* full =
-        reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kAreaBytes + C::kStatBytes + C::kPrefBytes);
+    int* pref = reinterpret_cast<int*>(smem + STAGES * C::kStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kPrefBytes);
     uint64_t* empty = full + STAGES;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + STAGES);
 
@@ -305,7 +292,6 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
     w.init(pref, p.nB, p.HR, t_begin);
     // per-piece state
     int L = 0, ib = 0, head_base = 0, rg = 0, nrows = 0;
-    bool whole = false;
     int iq_r[2] = {0, 0}, ihq_r[2] = {0, 0};
     bool row_ok[2] = {false, false};
     float slope[2] = {0.0f, 0.0f};
@@ -316,7 +302,6 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
     for (int i = 0; i < count; ++i) {
         if (i == 0 || w.j == 0) {
             // ---- a new piece: segment (w.b, w.sl)
-            whole = (w.j == 0);
             ib = p.b_base + w.b;
             L = seq_len(p, w.b);
             const int hidx = w.sl / p.n_rgroups;
@@ -453,88 +438,47 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
 
         const bool seg_end = (w.j == w.nb - 1);
         if (seg_end || i == count - 1) {
-            // ---- end of the piece: merge the four warps in a fixed order, write it out
+            // ---- end of the piece: this warp's (max, sum, unnormalised O) of its rows
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 4);
                 l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 8);
                 l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 16);
             }
-            if (g == 0) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    stat_m[warp * kRows + 2 * q4 + h] = m_row[h];
-                    stat_l[warp * kRows + 2 * q4 + h] = l_row[h];
-                }
-            }
-            consumer_bar();
-            float e_w[2];
+            float* rec = p.part + (((int64_t)blockIdx.x + (int64_t)w.b * p.HR + w.sl) * kFaWarps + warp) * kRows * (D + 2);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const int r = 2 * q4 + h;
-                float M = -INFINITY;
+                if (!row_ok[h]) continue;
+                float* rr = rec + (2 * q4 + h) * (D + 2);
+                if (g == 0) { rr[0] = m_row[h]; rr[1] = l_row[h]; }
 #pragma unroll
-                for (int w2 = 0; w2 < kFaWarps; ++w2) M = fmaxf(M, stat_m[w2 * kRows + r]);
-                e_w[h] = (m_row[h] == -INFINITY) ? 0.0f : __expf(m_row[h] - M);
-            }
-            for (int turn = kFaWarps - 1; turn >= 0; --turn) {
-                if (warp == turn) {
-#pragma unroll
-                    for (int dt = 0; dt < KS; ++dt) {
-                        const int d = 16 * dt + g;
-                        float* a0p = area + (2 * q4) * C::kAreaStride + d;
-                        float* a1p = a0p + C::kAreaStride;
-                        const bool first = (turn == kFaWarps - 1);
-                        a0p[0] = (first ? 0.0f : a0p[0]) + e_w[0] * o[dt][0];
-                        a1p[0] = (first ? 0.0f : a1p[0]) + e_w[1] * o[dt][1];
-                        a0p[8] = (first ? 0.0f : a0p[8]) + e_w[0] * o[dt][2];
-                        a1p[8] = (first ? 0.0f : a1p[8]) + e_w[1] * o[dt][3];
-                    }
-                }
-                consumer_bar();
-            }
-            const bool final_row = whole && seg_end;
-            const int64_t slot = (int64_t)blockIdx.x + (int64_t)w.b * p.HR + w.sl;
-            for (int idx = threadIdx.x; idx < nrows * D; idx += kFaWarps * 32) {
-                const int r = idx / D, d = idx % D;
-                float M = -INFINITY;
-#pragma unroll
-                for (int w2 = 0; w2 < kFaWarps; ++w2) M = fmaxf(M, stat_m[w2 * kRows + r]);
-                float Ls = 0.0f;
-                if (M != -INFINITY) {
-#pragma unroll
-                    for (int w2 = 0; w2 < kFaWarps; ++w2) {
-                        const float mw = stat_m[w2 * kRows + r];
-                        if (mw != -INFINITY) Ls += stat_l[w2 * kRows + r] * __expf(mw - M);
-                    }
-                }
-                const float Os = area[r * C::kAreaStride + d];
-                if (final_row) {
-                    int iq, ihq;
-                    row_coords(p, head_base, rg * kRows + r, iq, ihq);
-                    float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
-                    dr[d] = Ls > 0.0f ? Os / Ls : 0.0f;
-                } else {
-                    float* pr = p.part + (slot * kRows + r) * (D + 2);
-                    if (d == 0) { pr[0] = M; pr[1] = Ls; }
-                    pr[2 + d] = Os;
+                for (int dt = 0; dt < KS; ++dt) {
+                    rr[2 + 16 * dt + g] = o[dt][h];
+                    rr[2 + 16 * dt + g + 8] = o[dt][2 + h];
                 }
             }
-            consumer_bar();   // the stats and the area are free for the next piece
         }
         w.next(pref, p.nB, p.HR);
     }
 }
 
-// Writes every row whose segment the decode kernel split across CTAs (merging the
-// pieces' records in CTA order), and zeros for empty sequences: one CTA per row.
+// Writes every output row: merges the per-warp records of the CTAs that held pieces of its
+// segment, in CTA then warp order (zeros for an empty sequence).  One CTA of D threads per
+// row, latency-lean: record headers are read in parallel (one per thread), the maximum and
+// the weighted sum come from block reductions, then each thread sums its dimension over
+// the records with independent loads.
 template <int D>
 __global__ void __launch_bounds__(D)
 fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
+    constexpr int NW = D / 32;
+    __shared__ float s_e[D];          // record weights of the current chunk
+    __shared__ float s_red[NW];
+    __shared__ float s_bcast;
     const int row = blockIdx.x;
     const int hidx = blockIdx.y;
     const int b = blockIdx.z;
-    const int d = threadIdx.x;
+    const int t = threadIdx.x;
+    const int lane = t & 31, wid = t >> 5;
     const int* pref = p.pref_out;
     const int nb = pref[b + 1] - pref[b];
     const int rg = row / kRows, r = row % kRows;
@@ -545,32 +489,78 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
     row_coords(p, head_base, row, iq, ihq);
     float* dr = reinterpret_cast<float*>(p.dst + iq * p.d_nb1 + ihq * p.d_nb2 + ib * p.d_nb3);
     if (nb == 0) {
-        dr[d] = 0.0f;
+        dr[t] = 0.0f;
         return;
     }
     const int64_t W = (int64_t)p.HR * pref[p.nB];
     const int64_t T = (int64_t)p.HR * pref[b] + (int64_t)sl * nb;
     const int cf = cta_of_tile(T, W, P);
-    const int cl = cta_of_tile(T + nb - 1, W, P);
-    if (cf == cl) return;   // one CTA held the whole segment and wrote the row
-    const int64_t seg = (int64_t)b * p.HR + sl;
-    // CTAs with an empty range (more CTAs than tiles) wrote no record
-    auto empty_range = [&](int c) { return W * c / P == W * (c + 1) / P; };
-    float M = -INFINITY;
-    for (int c = cf; c <= cl; ++c)
-        if (!empty_range(c)) M = fmaxf(M, p.part[((c + seg) * kRows + r) * (D + 2)]);
-    float Ls = 0.0f, Os = 0.0f;
-    if (M != -INFINITY) {
-        for (int c = cf; c <= cl; ++c) {
-            if (empty_range(c)) continue;
-            const float* pr = p.part + ((c + seg) * kRows + r) * (D + 2);
-            if (pr[0] == -INFINITY) continue;
-            const float e = __expf(pr[0] - M);
-            Ls += pr[1] * e;
-            Os += pr[2 + d] * e;
+    const int nrec = (cta_of_tile(T + nb - 1, W, P) - cf + 1) * kFaWarps;
+    const float* base = p.part + (((int64_t)cf + (int64_t)b * p.HR + sl) * kFaWarps * kRows + r) * (D + 2);
+    // record q = (CTA cf + q / kFaWarps, warp q % kFaWarps) sits at base + q * kRows * (D + 2);
+    // CTAs with an empty range (more CTAs than tiles) wrote none
+    auto rec_m = [&](int q) {
+        const int64_t c = cf + q / kFaWarps;
+        return (W * c / P == W * (c + 1) / P) ? -INFINITY : base[(int64_t)q * kRows * (D + 2)];
+    };
+    auto block_reduce = [&](float v, bool is_max) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float u = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, u) : v + u;
         }
+        if (lane == 0) s_red[wid] = v;
+        __syncthreads();
+        if (t == 0) {
+            float a = s_red[0];
+            for (int w = 1; w < NW; ++w) a = is_max ? fmaxf(a, s_red[w]) : a + s_red[w];
+            s_bcast = a;
+        }
+        __syncthreads();
+        const float res = s_bcast;
+        __syncthreads();
+        return res;
+    };
+    float mloc = -INFINITY;
+    for (int q = t; q < nrec; q += D) mloc = fmaxf(mloc, rec_m(q));
+    const float M = block_reduce(mloc, true);
+    if (M == -INFINITY) {
+        dr[t] = 0.0f;
+        return;
     }
-    dr[d] = Ls > 0.0f ? Os / Ls : 0.0f;
+    float Ls = 0.0f, Os = 0.0f;
+    for (int q0 = 0; q0 < nrec; q0 += D) {
+        const int q = q0 + t;
+        float e = 0.0f, lw = 0.0f;
+        if (q < nrec) {
+            const float m = rec_m(q);
+            if (m != -INFINITY) {
+                e = __expf(m - M);
+                lw = e * base[(int64_t)q * kRows * (D + 2) + 1];
+            }
+        }
+        s_e[t] = e;
+        Ls += block_reduce(lw, false);   // also orders the s_e writes before the reads below
+        const int n = min(D, nrec - q0);
+        int k = 0;
+        // a record of weight 0 is not read: an empty-range CTA's slot holds stale bits
+        for (; k + 4 <= n; k += 4) {
+            const float* o0 = base + (int64_t)(q0 + k) * kRows * (D + 2) + 2 + t;
+            const float e0 = s_e[k], e1 = s_e[k + 1], e2 = s_e[k + 2], e3 = s_e[k + 3];
+            const float v0 = e0 != 0.0f ? o0[0] : 0.0f;
+            const float v1 = e1 != 0.0f ? o0[kRows * (D + 2)] : 0.0f;
+            const float v2 = e2 != 0.0f ? o0[2 * kRows * (D + 2)] : 0.0f;
+            const float v3 = e3 != 0.0f ? o0[3 * kRows * (D + 2)] : 0.0f;
+            Os += e0 * v0;
+            Os += e1 * v1;
+            Os += e2 * v2;
+            Os += e3 * v3;
+        }
+        for (; k < n; ++k)
+            if (s_e[k] != 0.0f) Os += s_e[k] * base[(int64_t)(q0 + k) * kRows * (D + 2) + 2 + t];
+        __syncthreads();   // s_e is rewritten by the next chunk
+    }
+    dr[t] = Ls > 0.0f ? Os / Ls : 0.0f;
 }
 
 // Resident CTAs of the decode kernel per SM on the current device (sets the kernel's
@@ -635,8 +625,8 @@ int make_plan(const mlzc_fa_desc* d, FaPlan* out) {
     const int64_t tiles_max = (int64_t)pl.slice * p.HR * ((p.n_kv + kTile - 1) / kTile);
     pl.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(resident, tiles_max));
     pl.pref_bytes = ((size_t)(pl.slice + 1) * sizeof(int) + 255) / 256 * 256;
-    pl.ws_bytes = pl.pref_bytes +
-                  ((size_t)pl.ctas + (size_t)pl.slice * p.HR) * kRows * (size_t)(d->head_dim_v + 2) * sizeof(float);
+    pl.ws_bytes = pl.pref_bytes + ((size_t)pl.ctas + (size_t)pl.slice * p.HR) * kFaWarps * kRows *
+                                      (size_t)(d->head_dim_v + 2) * sizeof(float);
     *out = pl;
     return MLZC_OK;
 }
