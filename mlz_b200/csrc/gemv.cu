@@ -3,8 +3,7 @@
 // Replaces the per-row dot products of the reference: matrix_mult_avx512's k-loop
 // (kernels/x86/matrix_mult_avx512.asm:165-181) reached through simd_matmul_f32
 // (src/simd/simd_matmul.cpp:214-251), the upstream F16 vec_dot path the hook falls back
-// to (src/simd/ggml-cpu-simd.c:1145-1244), and the per-(m, n) Q4_K x Q8_K vec_dot loop of
-// ggml_simd_try_mul_mat (src/simd/ggml_simd_hook.cpp:254-299).
+// to (src/simd/ggml-cpu-simd.c:1145-1244).
 //
 // Design (HBM-bound: every weight byte is read exactly once):
 //   - one warp owns ROWS consecutive weight rows; its 32 lanes stride over K in 16-byte
@@ -15,11 +14,6 @@
 //   - fp32 accumulation per lane, butterfly shuffle reduction at the end;
 //   - the ROWS rows of a warp share each activation load, which keeps the L1 traffic
 //     per FMA at or below one byte.
-// Q4_K: each lane decodes a 64-value chunk (one 32-byte qs run, sub-blocks 2c and 2c+1
-// of its super-block) with the 6-bit scale/min unpack of GGUF, folds the minimum into
-// the weight (w = d*sc*q - dmin*m, exact nibble-to-float via a float bit trick) and
-// accumulates w*x in fp32 -- no activation quantisation (the reference's Q8_K step,
-// ggml_simd_hook.cpp:109-148, is what the parity gate excludes).
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -215,158 +209,6 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
     return MLZC_OK;
 }
 
-// ---------------------------------------------------------------- Q4_K
-
-constexpr int kQK = 256;
-constexpr int kQ4KBytes = 144;
-
-// 6-bit scale / min of sub-block j from the 12 packed scale bytes (GGUF order; the
-// unpack of vec_dot_q4_k_q8_k_avx2.asm:101-150).
-__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, float& sc, float& mn) {
-    int a, b;
-    if (j < 4) {
-        a = s[j] & 63;
-        b = s[j + 4] & 63;
-    } else {
-        a = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
-        b = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-    }
-    sc = (float)a;
-    mn = (float)b;
-}
-
-
-// Two exact nibble floats (bytes b and b+1 of `word` after `shift`) as a float2.
-__device__ __forceinline__ float2 nib2(uint32_t word, int byte, int shift) {
-    const uint32_t a = (word >> (8 * byte + shift)) & 0xFu;
-    const uint32_t b = (word >> (8 * byte + 8 + shift)) & 0xFu;
-    const float2 f = make_float2(__uint_as_float(0x4B000000u | a), __uint_as_float(0x4B000000u | b));
-    return __fadd2_rn(f, make_float2(-8388608.0f, -8388608.0f));   // exact: 2^23 + q - 2^23
-}
-
-// Q4_K x f32 for NB activation columns.  Lane = one 64-value chunk (the 32-byte qs run of
-// sub-blocks 2c and 2c+1) of each of the warp's ROWS rows; U chunk iterations are loaded
-// ahead.  Per sub-block the weight sum is d*sc*sum(q*x) - dmin*m*sum(x): sum(q*x) in
-// packed f32x2 FMAs on exact nibble floats, sum(x) once per chunk and column for all rows.
-template <int NB, int ROWS, int U>
-__global__ void __launch_bounds__(kThreads)
-q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
-                const char* __restrict__ X, size_t x_cs, int ncols,
-                char* __restrict__ Y, size_t y_cs) {
-    const int lane = threadIdx.x & 31;
-    const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
-    if (row0 >= M) return;
-    const char* wrow[ROWS];
-#pragma unroll
-    for (int r = 0; r < ROWS; r++) wrow[r] = W + (size_t)min(row0 + r, M - 1) * w_rs;
-
-    float acc[ROWS][NB];
-#pragma unroll
-    for (int r = 0; r < ROWS; r++)
-#pragma unroll
-        for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
-
-    const int64_t nchunk = K / 64;   // 64-value chunks, 4 per super-block
-    for (int64_t base = 0; base < nchunk; base += 32 * U) {
-        uint4 hdr[U][ROWS], qa[U][ROWS], qb[U][ROWS];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int64_t ch = base + lane + 32 * u;
-            const int64_t chc = ch < nchunk ? ch : nchunk - 1;
-            const int64_t b = chc >> 2;
-            const int c = (int)(chc & 3);
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) {
-                const char* blk = wrow[r] + (size_t)b * kQ4KBytes;
-                hdr[u][r] = ld_stream16(blk);
-                qa[u][r] = ld_stream16(blk + 16 + 32 * c);
-                qb[u][r] = ld_stream16(blk + 32 + 32 * c);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int64_t ch = base + lane + 32 * u;
-            if (ch >= nchunk) break;
-            const int c = (int)(ch & 3);
-            const int64_t kbase = ch * 64;
-            // per-row scales of the chunk's two sub-blocks
-            float ds0[ROWS], dm0[ROWS], ds1[ROWS], dm1[ROWS];
-#pragma unroll
-            for (int r = 0; r < ROWS; r++) {
-                const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u][r].x & 0xFFFFu)));
-                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u][r].x >> 16)));
-                uint8_t sb[12];
-                *reinterpret_cast<uint32_t*>(sb + 0) = hdr[u][r].y;
-                *reinterpret_cast<uint32_t*>(sb + 4) = hdr[u][r].z;
-                *reinterpret_cast<uint32_t*>(sb + 8) = hdr[u][r].w;
-                float sc, mn;
-                q4k_scale_min(sb, 2 * c, sc, mn);
-                ds0[r] = d * sc;
-                dm0[r] = dmin * mn;
-                q4k_scale_min(sb, 2 * c + 1, sc, mn);
-                ds1[r] = d * sc;
-                dm1[r] = dmin * mn;
-            }
-#pragma unroll
-            for (int n = 0; n < NB; n++) {
-                if (n < ncols) {
-                    const float* xc = reinterpret_cast<const float*>(X + (size_t)n * x_cs) + kbase;
-                    float2 ql[ROWS], qh[ROWS];      // sum(q*x) of sub-blocks 2c / 2c+1, pairwise
-#pragma unroll
-                    for (int r = 0; r < ROWS; r++) { ql[r] = make_float2(0.f, 0.f); qh[r] = ql[r]; }
-                    float2 xl = make_float2(0.f, 0.f), xh = xl;   // sum(x) of the two sub-blocks
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const float4 a = __ldg(reinterpret_cast<const float4*>(xc + 4 * i));
-                        const float4 bq = __ldg(reinterpret_cast<const float4*>(xc + 32 + 4 * i));
-                        const float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
-                        const float2 b01 = make_float2(bq.x, bq.y), b23 = make_float2(bq.z, bq.w);
-                        xl = __fadd2_rn(xl, __fadd2_rn(a01, a23));
-                        xh = __fadd2_rn(xh, __fadd2_rn(b01, b23));
-#pragma unroll
-                        for (int r = 0; r < ROWS; r++) {
-                            const uint32_t word = (i < 4) ? (&qa[u][r].x)[i] : (&qb[u][r].x)[i - 4];
-                            ql[r] = __ffma2_rn(nib2(word, 0, 0), a01, ql[r]);
-                            ql[r] = __ffma2_rn(nib2(word, 2, 0), a23, ql[r]);
-                            qh[r] = __ffma2_rn(nib2(word, 0, 4), b01, qh[r]);
-                            qh[r] = __ffma2_rn(nib2(word, 2, 4), b23, qh[r]);
-                        }
-                    }
-                    const float sxl = xl.x + xl.y, sxh = xh.x + xh.y;
-#pragma unroll
-                    for (int r = 0; r < ROWS; r++) {
-                        float a2 = acc[r][n];
-                        a2 = fmaf(ds0[r], ql[r].x + ql[r].y, a2);
-                        a2 = fmaf(-dm0[r], sxl, a2);
-                        a2 = fmaf(ds1[r], qh[r].x + qh[r].y, a2);
-                        a2 = fmaf(-dm1[r], sxh, a2);
-                        acc[r][n] = a2;
-                    }
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < ROWS; r++)
-#pragma unroll
-        for (int n = 0; n < NB; n++) {
-            const float v = warp_sum(acc[r][n]);
-            if (lane == 0 && n < ncols && row0 + r < M)
-                reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row0 + r] = v;
-        }
-}
-
-template <int NB>
-void launch_q4k(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
-                int ncols, char* y, size_t y_cs, cudaStream_t s) {
-    constexpr int ROWS = NB <= 4 ? 2 : 1;
-    constexpr int U = 2;
-    const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
-    const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    q4k_gemv_kernel<NB, ROWS, U><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
-    count_launch();
-}
-
 __global__ void gather_permute_kernel(const float* __restrict__ src, char* __restrict__ dst,
                                       size_t dst_cs, int G, int64_t N, int64_t m_loc) {
     const int64_t total = (int64_t)G * N * m_loc;
@@ -399,28 +241,6 @@ int launch_gemv(const DeviceCtx*, int w_type, const void* w, size_t w_row_bytes,
     if (w_type == MLZC_TYPE_F32)
         return run_gemv<WF32>(w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
     return fail(MLZC_ERR_UNSUPPORTED, "gemv: weight type %d", w_type);
-}
-
-int launch_q4k_gemv(const DeviceCtx*, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
-                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
-                    cudaStream_t s) {
-    if (K % kQK != 0) return fail(MLZC_ERR_INVALID, "Q4_K: K=%lld is not a multiple of 256", (long long)K);
-    if ((uintptr_t)w % 16 || w_row_bytes % 16 || (uintptr_t)x % 16 || x_col_bytes % 16)
-        return fail(MLZC_ERR_INVALID, "Q4_K: weights and activations must be 16-byte aligned");
-    const char* wc = static_cast<const char*>(w);
-    const char* xc = reinterpret_cast<const char*>(x);
-    char* yc = reinterpret_cast<char*>(y);
-    for (int64_t n0 = 0; n0 < N; n0 += 8) {
-        const int nc = (int)std::min<int64_t>(8, N - n0);
-        const char* xn = xc + (size_t)n0 * x_col_bytes;
-        char* yn = yc + (size_t)n0 * y_col_bytes;
-        if (nc == 1) launch_q4k<1>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        else if (nc <= 2) launch_q4k<2>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        else if (nc <= 4) launch_q4k<4>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        else launch_q4k<8>(wc, w_row_bytes, M, K, xn, x_col_bytes, nc, yn, y_col_bytes, s);
-        MLZC_CUDA_TRY(cudaGetLastError());
-    }
-    return MLZC_OK;
 }
 
 }  // namespace mlzc

@@ -48,10 +48,9 @@ int launch_gemv(const DeviceCtx* c, int w_type, const void* w, size_t w_row_byte
                 int64_t M, int64_t K, const float* x, size_t x_col_bytes, int64_t N,
                 float* y, size_t y_col_bytes, cudaStream_t s);
 
-// Q4_K dequant-dot on CUDA cores, any N.
-int launch_q4k_gemv(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M,
-                    int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
-                    size_t y_col_bytes, cudaStream_t s);
+// Q4_K dequant-dot on the tensor cores (mma.sync), any N.
+int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
 
 // tcgen05/TMEM GEMM for F16 weights (activations narrowed to f16 in the workspace).
 size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N);

@@ -84,5 +84,18 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
+// c += a . b for one m16n8k16 tile: A 16x16 and B 16x8 f16 fragments, f32 accumulators
+// (fragment ownership per the PTX ISA: lane l holds rows l/4 and l/4 + 8, k pairs 2(l%4)
+// and 2(l%4) + 8 of A; k pairs of column l/4 of B; rows l/4, l/4 + 8 x columns 2(l%4), +1
+// of C).
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 }  // namespace ptx
 }  // namespace mlzc

@@ -155,7 +155,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
         }
         return MLZC_OK;
     }
-    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_gemv(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
+    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
     if (use_gemm(w_type, M, K, N, w, w_rs, x, x_cs, y, y_cs))
         return launch_gemm_f16(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
     return launch_gemv(c, w_type, w, w_rs, M, K, x, x_cs, N, y, y_cs, s);

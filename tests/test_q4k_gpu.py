@@ -60,7 +60,10 @@ def test_known_answer_block(dev):
     blk = blk.reshape(1, -1)
     x = synth.f32_acts(synth.rng(8), 5, K)
     y = _run(dev, blk, x)
-    np.testing.assert_allclose(y[:, 0], 0.5 * x.astype(np.float64).sum(axis=1), rtol=1e-5, atol=1e-5)
+    # every weight is d * sc * q - dmin * m = 0.5 * 1 * 1 - 0.25 * 0; the kernel rounds the
+    # activations to f16 once, so the exact answer is 0.5 * sum(f16(x))
+    want = 0.5 * x.astype(np.float16).astype(np.float64).sum(axis=1)
+    np.testing.assert_allclose(y[:, 0], want, rtol=1e-5, atol=1e-5)
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 256, 1), (3, 512, 2), (37, 768, 5), (300, 256, 17), (8, 1024, 33)])
@@ -70,3 +73,24 @@ def test_edge_shapes(dev, M, K, N):
     x = synth.f32_acts(g, N, K)
     y = _run(dev, blocks, x, y_pad=1)
     assert oracle.rel_err(y, oracle.mul_mat_q4k(blocks, x)) <= TOL
+
+
+@pytest.mark.parametrize("MK", [(14336, 4096), (4096, 14336)])
+@pytest.mark.parametrize("B", [1, 16])
+def test_power_of_two_scaling_is_exact_full_size(dev, MK, B):
+    """Size-independent properties at the benchmark size: linearity (scaling the activations
+    by 4 scales y by 4, to 1e-6 of max |y|: the f16 low part of a sub-block sum may be
+    subnormal, where rounding does not commute with scaling) and bitwise repeatability."""
+    import torch
+    M, K = MK
+    gen = torch.Generator(device=dev).manual_seed(11 + B)
+    w = synth.q4k_blocks_dev(gen, M, K, dev)
+    x = torch.randn((B, K), generator=gen, device=dev)
+    x = torch.where(x.abs() < 1e-3, torch.zeros_like(x), x)  # keep 4x out of f16 subnormals
+    y = mlz_b200.mul_mat(w, x)
+    y4 = mlz_b200.mul_mat(w, 4.0 * x)
+    y2 = mlz_b200.mul_mat(w, x)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()
+    assert ((y4 - 4.0 * y).abs().max() / (4.0 * y).abs().max()).item() <= 1e-6
+    assert torch.equal(y2, y), "repeat is bitwise identical"
