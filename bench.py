@@ -282,8 +282,10 @@ class C5(Workload):
         self.W = [synth.f16_weights_dev(gen, m // world, k, dev) for (_, m, k) in self.mats]
         self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, _, k) in self.mats]
         self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (_, m, _) in self.mats]
-        self.ws = torch.empty(max(comm.workspace_bytes(1, m, k, n) for (_, m, k) in self.mats) if comm else 1,
-                              dtype=torch.uint8, device=dev)
+        import mlz_b200
+        wsb = (max(comm.workspace_bytes(1, m, k, n) for (_, m, k) in self.mats) if comm else
+               max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, m, k, n) for (_, m, k) in self.mats))
+        self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
         self.config = {"workload": f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}", "N": n,
                        "parallelism": f"row-shard x{world} + all-gather", "l2": "inputs larger than L2"}
 

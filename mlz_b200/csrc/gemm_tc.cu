@@ -484,23 +484,23 @@ struct GemmPlan {
     size_t total() const { return x16 + counters + partials; }
 };
 
-// Estimated SM-cycles of one work unit: MMA cycles at full tensor rate divided by the
-// fraction of that rate the per-SM operand feed sustains (about 62 B/cycle measured: the
-// 128x256 tile, which needs 96 B per MMA cycle, runs at ~64%), plus the epilogue when it
-// cannot overlap (one accumulator set) and the partial-tile traffic of a K split.
-double unit_cycles(int MT, int BN, int kb, int splits) {
-    const double feed = (double)MT * BM * BK * 2 + (double)BN * BK * 2;   // bytes per k-block
-    const double mma = (double)MT * BN * 2;                               // cycles per k-block at peak
-    const double eff = std::min(0.92, 62.0 / (feed / mma));
-    double cyc = kb * mma / eff;
-    const bool one_set = 2 * MT * BN > 512;
-    if (one_set) cyc += (double)MT * BN * 4;                              // drain 128*MT x BN floats
-    if (splits > 1) cyc += 2.0 * MT * BM * BN * 4 / 40.0;                 // write + read back a partial tile
-    return cyc;
-}
+// Measured cost of one work unit on B200 (SM clocks, 148 SMs), per tile shape (MT, BN):
+// cycles per 64-deep k-block, and fixed cycles per unit (pipeline fill, and the epilogue
+// drain where only one accumulator set fits in TMEM).  Least-squares fit over the
+// Llama-3 projection shapes (3072x3072, 1024x3072, 8192x3072, 3072x8192) at 512 and 2048
+// tokens, narrowing excluded.  Only shapes that won somewhere are candidates.
+struct ShapeCost {
+    int mt, bn;
+    double kb_cycles, unit_cycles;
+};
+constexpr ShapeCost kShapeCosts[] = {
+    {2, 256, 1139.0, 37410.0}, {2, 192, 1078.0, 23966.0}, {1, 256, 633.0, 17195.0},
+    {1, 192, 665.0, 6990.0},   {1, 128, 491.0, 8523.0},   {1, 96, 548.0, 11869.0},
+};
 
 // Tile shape (MT M-tiles of 128 rows x BN columns per CTA) and K split for a problem.
-// Wide problems (N >= 128) minimise rounds x unit cost over the candidates; narrow ones
+// Wide problems (N >= 128) minimise rounds x measured unit cost over the candidates, with
+// at most two K splits (a split's partial tile goes through the workspace); narrow ones
 // (decode) use the narrowest BN that holds N and split K to occupy the SMs.
 GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
     GemmPlan p{};
@@ -509,22 +509,20 @@ GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
     p.splits = 1;
     if (N >= 128) {
         double best = 1e300;
-        for (int mt = 2; mt >= 1; --mt)
-            for (int bn = 256; bn >= 128; bn /= 2)
-                for (int sp = 1; sp <= 4; ++sp) {
-                    if (sp > 1 && p.kblocks / sp < 4) break;
-                    const long tiles = (long)((M + BM * mt - 1) / (BM * mt)) * ((N + bn - 1) / bn);
-                    const long units = tiles * sp;
-                    const long rounds = (units + sm_count - 1) / sm_count;
-                    const int kper = (p.kblocks + sp - 1) / sp;
-                    const double cost = (double)rounds * unit_cycles(mt, bn, kper, sp) * (1.0 + 1e-3 * (sp - 1));
-                    if (cost < best * 0.999) {
-                        best = cost;
-                        p.MT = mt;
-                        p.BN = bn;
-                        p.splits = sp;
-                    }
+        for (const ShapeCost& sc : kShapeCosts)
+            for (int sp = 1; sp <= 2; ++sp) {
+                if (sp > 1 && p.kblocks / sp < 4) break;
+                const long tiles = (long)((M + BM * sc.mt - 1) / (BM * sc.mt)) * ((N + sc.bn - 1) / sc.bn);
+                const long rounds = (tiles * sp + sm_count - 1) / sm_count;
+                const int kper = (p.kblocks + sp - 1) / sp;
+                const double cost = (double)rounds * (kper * sc.kb_cycles + sc.unit_cycles * (sp > 1 ? 1.5 : 1.0));
+                if (cost < best * 0.999) {
+                    best = cost;
+                    p.MT = sc.mt;
+                    p.BN = sc.bn;
+                    p.splits = sp;
                 }
+            }
     } else {
         p.BN = N <= 16 ? 16 : (N <= 32 ? 32 : (N <= 64 ? 64 : 128));
         const int tiles = (int)((M + BM - 1) / BM) * (int)((N + p.BN - 1) / p.BN);
@@ -623,12 +621,14 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     g.x16t = x16t;
     g.part = partials;
     g.tile_count = counters;
-    if (pl.MT == 2) return BN == 128 ? launch_tile<128, 2>(c, ta, g, s) : launch_tile<256, 2>(c, ta, g, s);
+    if (pl.MT == 2) return BN == 192 ? launch_tile<192, 2>(c, ta, g, s) : launch_tile<256, 2>(c, ta, g, s);
     switch (BN) {
         case 16: return launch_tile<16, 1>(c, ta, g, s);
         case 32: return launch_tile<32, 1>(c, ta, g, s);
         case 64: return launch_tile<64, 1>(c, ta, g, s);
+        case 96: return launch_tile<96, 1>(c, ta, g, s);
         case 128: return launch_tile<128, 1>(c, ta, g, s);
+        case 192: return launch_tile<192, 1>(c, ta, g, s);
         default: return launch_tile<256, 1>(c, ta, g, s);
     }
 }
