@@ -36,6 +36,11 @@ sys.path.insert(0, HERE)
 
 L2_BYTES = 126 * 1024 * 1024
 
+# DRAM bytes per call of the roofline's call (dram__bytes_read.sum + dram__bytes_write.sum),
+# from one ncu capture of the same kernels on the same workload; the captures are
+# summarised, with their commands, in the profiles/ folder.
+NCU_TRAFFIC = {}
+
 
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -87,6 +92,9 @@ class Workload:
     def unit_scale(self) -> float:        # units/s -> metric unit
         return 1e-9 if self.unit == "GB/s" else 1e-12
 
+    def roofline_kernel(self, j: int) -> str:  # what the roofline's call runs
+        return f"call {j} of the step"
+
 
 def _rot_copies(nbytes: int) -> int:
     return max(1, math.ceil(4 * L2_BYTES / max(nbytes, 1)))
@@ -95,6 +103,10 @@ def _rot_copies(nbytes: int) -> int:
 class C1(Workload):
     unit = "GB/s"
     bound = "hbm"
+
+    def roofline_kernel(self, j):
+        return ("gemv_vec_kernel (one call, one launch)" if self.N < 8 else
+                "one mul_mat call: narrow_f16_kernel + gemm_f16_tc_kernel")
 
     def __init__(self, n, dev, gen):
         import torch
@@ -138,6 +150,9 @@ class C2(Workload):
     bound = "tensor"
     PROJ = [("q", 3072, 3072, 0), ("k", 1024, 3072, 0), ("v", 1024, 3072, 0), ("o", 3072, 3072, 1),
             ("gate", 8192, 3072, 2), ("up", 8192, 3072, 2), ("down", 3072, 8192, 3)]
+
+    def roofline_kernel(self, j):
+        return "the 7 mul_mat calls pooled (narrow_f16_kernel + gemm_f16_tc_kernel each)"
 
     def __init__(self, n, dev, gen):
         import torch
@@ -187,6 +202,9 @@ class C3(Workload):
     dtype = "q4_k/f32"
     SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
 
+    def roofline_kernel(self, j):
+        return f"q4k_mma_kernel, {self.SHAPES[j][0]}x{self.SHAPES[j][1]} (one call, one launch)"
+
     def __init__(self, n, dev, gen):
         import torch
         from mlz_b200 import synth
@@ -230,6 +248,9 @@ class C4(Workload):
     unit = "GB/s"
     bound = "hbm"
     dtype = "f16 kv / f32"
+
+    def roofline_kernel(self, j):
+        return "one flash-attention call: fa_decode_kernel + fa_combine_kernel"
 
     def __init__(self, n, dev, gen):
         import numpy as np
@@ -550,6 +571,7 @@ def mlz_arm(a):
     # shorter than the host's per-call launch cost, so the eager loop would time Python.
     use_graph = not a.no_graph and not a.profile_run and not isinstance(w, C5)
     timing = "eager launches"
+    call_timing = "eager events around each call"
     if use_graph:
         gs = torch.cuda.Stream()
         gs.wait_stream(torch.cuda.current_stream())
@@ -577,6 +599,27 @@ def mlz_arm(a):
         ms_local = g0.elapsed_time(g1)
         timing = "CUDA graph replay of the K steps"
         del graph
+        # Per-call device times for the roofline: a second capture of the K steps with
+        # event-record nodes around every call (the clean graph above gives `value`).
+        try:
+            gev = [[(torch.cuda.Event(enable_timing=True, external=True),
+                     torch.cuda.Event(enable_timing=True, external=True)) for _ in units_l] for _ in range(K)]
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=gs):
+                for s_ in range(K):
+                    for j, (f, _) in enumerate(w.launches(s_)):
+                        gev[s_][j][0].record(gs)
+                        f()
+                        gev[s_][j][1].record(gs)
+            with torch.cuda.stream(gs):
+                graph.replay()
+            torch.cuda.synchronize()
+            per_launch_ms = [sum(gev[s_][j][0].elapsed_time(gev[s_][j][1]) for s_ in range(K)) / K
+                             for j in range(len(units_l))]
+            call_timing = "events around each call inside a CUDA graph replay"
+            del graph
+        except Exception as exc:  # keep the eager per-call events
+            call_timing = f"eager events around each call ({type(exc).__name__} with graph events)"
     else:
         ms_local = ms_eager
     if world > 1:
@@ -605,7 +648,11 @@ def mlz_arm(a):
     roofline = {"bound": w.bound, "achieved": ach, "peak": peak,
                 "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s", "frac": ach / peak, "traffic": None,
                 "peak_source": f"{peaks['source']} {peak_name}",
-                "kernel": "mul_mat (all projections)" if isinstance(w, C2) else f"launch {jdom} of the step"}
+                "kernel": w.roofline_kernel(jdom), "call_timing": call_timing}
+    tr = NCU_TRAFFIC.get((a.config, n))
+    if tr is not None and not isinstance(w, C2):
+        roofline["traffic"] = tr[0]
+        roofline["traffic_source"] = tr[1]
 
     # end to end through the plugin entry point with pinned host buffers
     e2e = None
