@@ -39,7 +39,11 @@ L2_BYTES = 126 * 1024 * 1024
 # DRAM bytes per call of the roofline's call (dram__bytes_read.sum + dram__bytes_write.sum),
 # from one ncu capture of the same kernels on the same workload; the captures are
 # summarised, with their commands, in the profiles/ folder.
-NCU_TRAFFIC = {}
+NCU_TRAFFIC = {
+    ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
+    ("c3", 1): (33.07e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
+    ("c3", 16): (33.31e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
+}
 
 
 def parse_args():
