@@ -603,27 +603,33 @@ def mlz_arm(a):
         ms_local = g0.elapsed_time(g1)
         timing = "CUDA graph replay of the K steps"
         del graph
-        # Per-call device times for the roofline: a second capture of the K steps with
-        # event-record nodes around every call (the clean graph above gives `value`).
+        # Per-call device times for the roofline: each call's K repetitions (the same
+        # inputs and weight rotation as in the steps) captured as their own graph and timed
+        # by events around its replay -- event nodes inside a graph would add microseconds
+        # to every call.
         try:
-            gev = [[(torch.cuda.Event(enable_timing=True, external=True),
-                     torch.cuda.Event(enable_timing=True, external=True)) for _ in units_l] for _ in range(K)]
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=gs):
-                for s_ in range(K):
-                    for j, (f, _) in enumerate(w.launches(s_)):
-                        gev[s_][j][0].record(gs)
-                        f()
-                        gev[s_][j][1].record(gs)
-            with torch.cuda.stream(gs):
-                graph.replay()
-            torch.cuda.synchronize()
-            per_launch_ms = [sum(gev[s_][j][0].elapsed_time(gev[s_][j][1]) for s_ in range(K)) / K
-                             for j in range(len(units_l))]
-            call_timing = "events around each call inside a CUDA graph replay"
-            del graph
+            per = []
+            for j in range(len(units_l)):
+                gj = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gj, stream=gs):
+                    for s_ in range(K):
+                        w.launches(s_)[j][0]()
+                with torch.cuda.stream(gs):
+                    gj.replay()                         # untimed first replay
+                torch.cuda.synchronize()
+                c0 = torch.cuda.Event(enable_timing=True)
+                c1 = torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(gs):
+                    c0.record(gs)
+                    gj.replay()
+                    c1.record(gs)
+                torch.cuda.synchronize()
+                per.append(c0.elapsed_time(c1) / K)
+                del gj
+            per_launch_ms = per
+            call_timing = "each call's K repetitions replayed as a CUDA graph, timed by events"
         except Exception as exc:  # keep the eager per-call events
-            call_timing = f"eager events around each call ({type(exc).__name__} with graph events)"
+            call_timing = f"eager events around each call ({type(exc).__name__} with per-call graphs)"
     else:
         ms_local = ms_eager
     if world > 1:

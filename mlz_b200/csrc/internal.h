@@ -48,6 +48,12 @@ int launch_gemv(const DeviceCtx* c, int w_type, const void* w, size_t w_row_byte
                 int64_t M, int64_t K, const float* x, size_t x_col_bytes, int64_t N,
                 float* y, size_t y_col_bytes, cudaStream_t s);
 
+// Skinny F16 mul_mat (2 <= N <= 16) on the tensor cores (mma.sync).
+bool gemv_f16_mma_applicable(int64_t M, int64_t K, int64_t N, const void* w, size_t w_row_bytes,
+                             const float* x, size_t x_col_bytes);
+int launch_gemv_f16_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                        size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
+
 // Q4_K dequant-dot on the tensor cores (mma.sync), any N.
 int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
