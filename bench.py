@@ -207,7 +207,7 @@ class C3(Workload):
     SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
 
     def roofline_kernel(self, j):
-        return f"q4k_mma_kernel, {self.SHAPES[j][0]}x{self.SHAPES[j][1]} (one call, one launch)"
+        return f"q4k_prep_kernel + q4k_mma_kernel, {self.SHAPES[j][0]}x{self.SHAPES[j][1]} (one call)"
 
     def __init__(self, n, dev, gen):
         import torch
@@ -219,6 +219,9 @@ class C3(Workload):
         self.W = [[synth.q4k_blocks_dev(gen, m, k, dev) for (m, k) in self.SHAPES] for _ in range(self.R)]
         self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, k) in self.SHAPES]
         self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (m, _) in self.SHAPES]
+        import mlz_b200
+        wsb = max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q4_K, m, k, n) for (m, k) in self.SHAPES)
+        self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
         self.config = {"workload": f"c3 Q4_K mul_mat Llama-3.1-8B shapes, batch {n}", "batch": n,
                        "shapes": "4096x4096, 14336x4096, 4096x14336",
                        "l2": f"rotates {self.R} weight sets ({self.R * per_step / 1e6:.0f} MB >= 4x L2)"}
@@ -232,7 +235,7 @@ class C3(Workload):
     def launches(self, i):
         import mlz_b200
         Ws = self.W[i % self.R]
-        return [(lambda j=j: mlz_b200.mul_mat(Ws[j], self.X[j], out=self.Y[j]), self._bytes(m, k))
+        return [(lambda j=j: mlz_b200.mul_mat(Ws[j], self.X[j], out=self.Y[j], workspace=self.ws), self._bytes(m, k))
                 for j, (m, k) in enumerate(self.SHAPES)]
 
     def host_weights(self):

@@ -54,9 +54,12 @@ bool gemv_f16_mma_applicable(int64_t M, int64_t K, int64_t N, const void* w, siz
 int launch_gemv_f16_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                         size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
 
-// Q4_K dequant-dot on the tensor cores (mma.sync), any N.
+// Q4_K dequant-dot on the tensor cores (mma.sync), any N: an activation prep launch (f16
+// fragments + sub-block sums into the workspace) and the main kernel.
+size_t q4k_workspace_bytes(int64_t K, int64_t N);
 int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
+                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws,
+                   size_t ws_bytes, cudaStream_t s);
 
 // tcgen05/TMEM GEMM for F16 weights (activations narrowed to f16 in the workspace).
 size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N);

@@ -155,7 +155,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
         }
         return MLZC_OK;
     }
-    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
+    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
     if (w_type == MLZC_TYPE_F16 && gemv_f16_mma_applicable(M, K, N, w, w_rs, x, x_cs))
         return launch_gemv_f16_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
     if (use_gemm(w_type, M, K, N, w, w_rs, x, x_cs, y, y_cs))
@@ -164,6 +164,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
 }
 
 size_t mul_mat_ws(int w_type, int64_t M, int64_t K, int64_t N) {
+    if (w_type == MLZC_TYPE_Q4_K) return K % 256 == 0 ? q4k_workspace_bytes(K, N) : 0;
     // N in [8, 16] normally takes the skinny tensor-core path (no workspace), but the
     // tcgen05 GEMM it falls back to for unaligned operands needs one
     if (w_type == MLZC_TYPE_F16 && N >= kGemmMinN) return gemm_f16_workspace_bytes(M, K, N);
