@@ -52,7 +52,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--n", type=int, default=None, help="activation columns / tokens / batch")
+    ap.add_argument("--n", "--size", dest="n", type=int, default=None,
+                    help="activation columns / tokens / batch (--size under torchrun, whose parser takes --n)")
     ap.add_argument("--impl", default="mlz", choices=["mlz", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

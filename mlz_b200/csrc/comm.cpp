@@ -81,7 +81,9 @@ struct mlzc_comm_s {
 
 namespace {
 
-// Polls a non-blocking communicator until its pending operation leaves ncclInProgress.
+// Polls a non-blocking communicator until its pending operation leaves ncclInProgress:
+// spinning for the first 100 us (an enqueue normally completes within microseconds), then
+// sleeping 50 us between polls, bounded by the communicator's timeout.
 int wait_comm(const NcclApi* api, mlzc_comm c, const char* what) {
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -97,7 +99,8 @@ int wait_comm(const NcclApi* api, mlzc_comm c, const char* what) {
             c->comm = nullptr;
             return fail(MLZC_ERR_COMM, "%s: no progress within %d ms; communicator aborted", what, c->timeout_ms);
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        const auto us = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (us > 100) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
@@ -206,7 +209,8 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
         c->broken = true;
         return nccl_fail(api, r, "ncclAllGather");
     }
-    if ((st = wait_comm(api, c, "ncclAllGather")) != MLZC_OK) return st;
+    // the enqueue must finish before the next NCCL call only when it reported in progress
+    if (r == ncclInProgress && (st = wait_comm(api, c, "ncclAllGather")) != MLZC_OK) return st;
     if (!direct) return launch_gather_permute(gathered, y, y_col_bytes, c->nranks, N, m_loc, s);
     return MLZC_OK;
 }
