@@ -17,8 +17,10 @@
 //                 (M = 128, N = BN, K = 16) per K step, the MT M-tiles sharing the X tile,
 //                 fp32 accumulators in TMEM; commits free smem stages and publish
 //                 finished accumulators;
-//        warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns, coalesced stores of
-//                 Y[n][m] (32 consecutive m per warp store).
+//        warps 2-9 epilogue: tcgen05.ld 32 lanes x 32 columns, coalesced stores of
+//                 Y[n][m] (32 consecutive m per warp store); two warps per TMEM lane
+//                 quarter split the columns, which doubles the stores in flight (the
+//                 drain of an accumulator is store-bound).
 //      When two accumulator sets fit in TMEM (2*MT*BN <= 512 columns) the epilogue of
 //      tile t overlaps the MMAs of tile t+1.  MT = 2 (256 x 256 per SM) needs 64 KB of
 //      operands per 1024 MMA cycles instead of 48 KB per 512 for 128 x 256, which is what
@@ -42,7 +44,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                       // one 128-byte swizzle atom of f16
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;       // two warps per TMEM lane quarter, each draining half the columns
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;
 constexpr int kSmemBudget = 200 * 1024;
 
@@ -293,8 +295,14 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
     } else {
         // ---------------- epilogue: TMEM -> registers -> Y (or the split partials)
         const int quarter = warp & 3;            // TMEM lanes [32*quarter, 32*quarter + 32)
-        // columns per TMEM load: 32, or BN for the 16-wide tile
+        constexpr int NSUB = kEpiWarps / 4;      // warps per TMEM lane quarter
+        const int sub = (warp - 2) >> 2;         // which of them this warp is
+        // columns per TMEM load: 32, or BN for the 16-wide tile; G loads are issued before
+        // one wait, so the drain pays the TMEM load latency once per G x 32 columns
         constexpr int kCols = BN < 32 ? BN : 32;
+        constexpr int kChunks = BN < 32 ? 1 : BN / 32;
+        // chunk groups of G go round-robin to the NSUB warps of a quarter
+        constexpr int G = kChunks >= 2 * NSUB ? 2 : 1;
         uint32_t t = 0;
         for (int w = blockIdx.x; w < g.num_work; w += gridDim.x, ++t) {
             int m0, n0, kb0, kb1;
@@ -312,21 +320,28 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
                 const int m = m0 + row;
                 char* ybase = reinterpret_cast<char*>(g.y) + (size_t)m * 4;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * C::kAccCols + i * BN + c, r);
+                for (int c0 = sub * G; c0 < kChunks; c0 += NSUB * G) {
+                    uint32_t r[G][32];
+#pragma unroll
+                    for (int gg = 0; gg < G; ++gg)
+                        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * C::kAccCols + i * BN + (c0 + gg) * 32,
+                                  r[gg]);
                     tmem_ld_wait();
-                    if (g.splits == 1) {
-                        if (m < g.M) {
 #pragma unroll
-                            for (int j = 0; j < kCols; ++j) {
-                                const int n = n0 + c + j;
-                                if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[j]);
+                    for (int gg = 0; gg < G; ++gg) {
+                        const int c = (c0 + gg) * 32;
+                        if (g.splits == 1) {
+                            if (m < g.M) {
+#pragma unroll
+                                for (int j = 0; j < kCols; ++j) {
+                                    const int n = n0 + c + j;
+                                    if (n < g.N) *reinterpret_cast<float*>(ybase + (size_t)n * g.y_cs) = __uint_as_float(r[gg][j]);
+                                }
                             }
-                        }
-                    } else {
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < kCols; ++j) mypart[(size_t)(c + j) * ROWS + row] = __uint_as_float(r[j]);
+                            for (int j = 0; j < kCols; ++j) mypart[(size_t)(c + j) * ROWS + row] = __uint_as_float(r[gg][j]);
+                        }
                     }
                 }
             }
