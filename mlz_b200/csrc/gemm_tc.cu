@@ -322,13 +322,19 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
 #pragma unroll 1
                 for (int c0 = sub * G; c0 < kChunks; c0 += NSUB * G) {
                     uint32_t r[G][32];
+                    // a group may run past the last chunk when kChunks is not a multiple of G:
+                    // those chunks are neither loaded nor stored (they would be columns of
+                    // the next accumulator and of the neighbouring tile)
 #pragma unroll
                     for (int gg = 0; gg < G; ++gg)
-                        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * C::kAccCols + i * BN + (c0 + gg) * 32,
-                                  r[gg]);
+                        if (c0 + gg < kChunks)
+                            tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + b * C::kAccCols + i * BN +
+                                          (c0 + gg) * 32,
+                                      r[gg]);
                     tmem_ld_wait();
 #pragma unroll
                     for (int gg = 0; gg < G; ++gg) {
+                        if (c0 + gg >= kChunks) continue;
                         const int c = (c0 + gg) * 32;
                         if (g.splits == 1) {
                             if (m < g.M) {
@@ -503,15 +509,18 @@ struct GemmPlan {
 // cycles per 64-deep k-block, and fixed cycles per unit (pipeline fill, and the epilogue
 // drain where only one accumulator set fits in TMEM).  Least-squares fit over the
 // Llama-3 projection shapes (3072x3072, 1024x3072, 8192x3072, 3072x8192) at 512 and 2048
-// tokens, narrowing excluded.  Only shapes that won somewhere are candidates.
+// tokens, narrowing excluded.  Only shapes that won somewhere are candidates.  A K split
+// also writes its partial tile and the last split reads them all back: priced at the
+// store-bound drain rate (~10 bytes per cycle per SM).
 struct ShapeCost {
     int mt, bn;
     double kb_cycles, unit_cycles;
 };
 constexpr ShapeCost kShapeCosts[] = {
-    {2, 256, 1139.0, 37410.0}, {2, 192, 1078.0, 23966.0}, {1, 256, 633.0, 17195.0},
-    {1, 192, 665.0, 6990.0},   {1, 128, 491.0, 8523.0},   {1, 96, 548.0, 11869.0},
+    {2, 256, 1076.0, 31962.0}, {2, 192, 1119.0, 16248.0}, {1, 256, 561.0, 17288.0},
+    {1, 128, 581.0, 5909.0},   {1, 96, 596.0, 8882.0},
 };
+constexpr double kSplitBytesPerCycle = 10.0;
 
 // Tile shape (MT M-tiles of 128 rows x BN columns per CTA) and K split for a problem.
 // Wide problems (N >= 128) minimise rounds x measured unit cost over the candidates, with
@@ -530,7 +539,8 @@ GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
                 const long tiles = (long)((M + BM * sc.mt - 1) / (BM * sc.mt)) * ((N + sc.bn - 1) / sc.bn);
                 const long rounds = (tiles * sp + sm_count - 1) / sm_count;
                 const int kper = (p.kblocks + sp - 1) / sp;
-                const double cost = (double)rounds * (kper * sc.kb_cycles + sc.unit_cycles * (sp > 1 ? 1.5 : 1.0));
+                const double split_io = sp > 1 ? 2.0 * sc.mt * BM * sc.bn * 4 / kSplitBytesPerCycle : 0.0;
+                const double cost = (double)rounds * (kper * sc.kb_cycles + sc.unit_cycles + split_io);
                 if (cost < best * 0.999) {
                     best = cost;
                     p.MT = sc.mt;
@@ -643,7 +653,6 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
         case 64: return launch_tile<64, 1>(c, ta, g, s);
         case 96: return launch_tile<96, 1>(c, ta, g, s);
         case 128: return launch_tile<128, 1>(c, ta, g, s);
-        case 192: return launch_tile<192, 1>(c, ta, g, s);
         default: return launch_tile<256, 1>(c, ta, g, s);
     }
 }
