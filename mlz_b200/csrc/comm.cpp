@@ -209,7 +209,8 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
         c->broken = true;
         return nccl_fail(api, r, "ncclAllGather");
     }
-    // the enqueue must finish before the next NCCL call only when it reported in progress
+    // ncclInProgress: the collective may not be in the stream yet, so it must finish
+    // enqueueing before anything that reads its output is launched
     if (r == ncclInProgress && (st = wait_comm(api, c, "ncclAllGather")) != MLZC_OK) return st;
     if (!direct) return launch_gather_permute(gathered, y, y_col_bytes, c->nranks, N, m_loc, s);
     return MLZC_OK;

@@ -209,14 +209,22 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
     return MLZC_OK;
 }
 
-__global__ void gather_permute_kernel(const float* __restrict__ src, char* __restrict__ dst,
-                                      size_t dst_cs, int G, int64_t N, int64_t m_loc) {
-    const int64_t total = (int64_t)G * N * m_loc;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t m = i % m_loc;
-        const int64_t n = (i / m_loc) % N;
-        const int64_t r = i / (m_loc * N);
-        reinterpret_cast<float*>(dst + (size_t)n * dst_cs)[r * m_loc + m] = src[i];
+// gathered [G][N][m_loc] -> dst [N][G * m_loc] (column stride dst_cs bytes): one CTA row per
+// (rank slice r, column n) -- blockIdx.y = r * N + n -- threads over m, float4 when the
+// slices and the destination are 16-byte aligned.
+__global__ void gather_permute_kernel(const float* __restrict__ src, char* __restrict__ dst, size_t dst_cs, int N,
+                                      int64_t m_loc, int vec) {
+    const int64_t rn = blockIdx.y;
+    const int64_t n = rn % N, r = rn / N;
+    const float* srow = src + rn * m_loc;
+    float* drow = reinterpret_cast<float*>(dst + (size_t)n * dst_cs) + r * m_loc;
+    if (vec) {
+        const int64_t m4 = m_loc / 4;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m4; i += (int64_t)gridDim.x * blockDim.x)
+            reinterpret_cast<float4*>(drow)[i] = reinterpret_cast<const float4*>(srow)[i];
+    } else {
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m_loc; i += (int64_t)gridDim.x * blockDim.x)
+            drow[i] = srow[i];
     }
 }
 
@@ -224,10 +232,13 @@ __global__ void gather_permute_kernel(const float* __restrict__ src, char* __res
 
 int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,
                           int64_t m_loc, cudaStream_t s) {
-    const int64_t total = (int64_t)G * N * m_loc;
-    if (total == 0) return MLZC_OK;
-    const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    gather_permute_kernel<<<grid, 256, 0, s>>>(src, reinterpret_cast<char*>(dst), dst_col_bytes, G, N, m_loc);
+    if ((int64_t)G * N == 0 || m_loc == 0) return MLZC_OK;
+    if ((int64_t)G * N > 65535) return fail(MLZC_ERR_INVALID, "gather: %lld slices x columns", (long long)(G * N));
+    const int vec = (m_loc % 4 == 0 && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0 && dst_col_bytes % 16 == 0) ? 1 : 0;
+    const int64_t per_row = vec ? m_loc / 4 : m_loc;
+    const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((per_row + 255) / 256, 64));
+    gather_permute_kernel<<<dim3(gx, (unsigned)(G * N)), 256, 0, s>>>(src, reinterpret_cast<char*>(dst), dst_col_bytes,
+                                                                     (int)N, m_loc, vec);
     count_launch();
     MLZC_CUDA_TRY(cudaGetLastError());
     return MLZC_OK;

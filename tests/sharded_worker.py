@@ -30,7 +30,8 @@ def main(out_path: str) -> None:
     res = {"rank": rank, "cases": []}
     try:
         for (kind, M, K, N) in [("f16", 1024, 512, 1), ("f16", 2048, 1024, 4), ("f16", 512, 768, 33),
-                                ("f16", 1024, 256, 256), ("q4k", 1024, 1024, 1), ("q4k", 512, 512, 16)]:
+                                ("f16", 1024, 256, 256), ("f16", 516, 256, 5), ("q4k", 1024, 1024, 1),
+                                ("q4k", 512, 512, 16)]:
             g = synth.rng(5000 + M + K + N)
             if kind == "f16":
                 w = synth.f16_weights(g, M, K)
