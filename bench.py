@@ -40,6 +40,8 @@ L2_BYTES = 126 * 1024 * 1024
 # from one ncu capture of the same kernels on the same workload; the captures are
 # summarised, with their commands, in the profiles/ folder.
 NCU_TRAFFIC = {
+    ("c1", 1): (50.35e6 + 0.02e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_vec_kernel)"),
+    ("c1", 4): (50.39e6 + 0.07e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel)"),
     ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
     ("c3", 1): (33.07e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
     ("c3", 16): (33.31e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
