@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace mlzc {
 namespace {
@@ -52,6 +53,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 struct WF16 {
     static constexpr int kPerChunk = 8;
     static constexpr bool kRoundX = true;
+    static constexpr bool kEarlyLoads = true;   // f16 weights are never an output of these kernels
     __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
         float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
         w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
@@ -66,6 +68,7 @@ struct WF16 {
 struct WF32 {
     static constexpr int kPerChunk = 4;
     static constexpr bool kRoundX = false;
+    static constexpr bool kEarlyLoads = false;  // f32 weights may be an earlier call's output
     __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
         w[0] = __uint_as_float(v.x); w[1] = __uint_as_float(v.y);
         w[2] = __uint_as_float(v.z); w[3] = __uint_as_float(v.w);
@@ -86,7 +89,9 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
     constexpr int CH = WT::kPerChunk;
     const int lane = threadIdx.x & 31;
     const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
+    ptx::pdl_launch_dependents();
     if (row0 >= M) return;
+    if (!WT::kEarlyLoads) ptx::pdl_wait();
 
     const char* wrow[ROWS];
 #pragma unroll
@@ -108,6 +113,9 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
             for (int r = 0; r < ROWS; r++)
                 wv[r][u] = c < nchunk ? ld_stream16(wrow[r] + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
         }
+        // the first weight loads are in flight while the previous kernel finishes; the
+        // activations (and every write) come after it
+        if (base == 0) ptx::pdl_wait();
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int64_t c = base + lane + 32 * u;
@@ -171,14 +179,16 @@ gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K
 }
 
 template <class WT, int NB>
-void launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
-                int ncols, char* y, size_t y_cs, cudaStream_t s) {
+int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
+               int ncols, char* y, size_t y_cs, cudaStream_t s) {
     constexpr int ROWS = 2;
     constexpr int U = NB <= 2 ? 4 : 2;
     const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
     const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    gemv_vec_kernel<WT, NB, ROWS, U><<<grid, kThreads, 0, s>>>(w, w_rs, M, K, x, x_cs, ncols, y, y_cs);
+    MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U>, dim3(grid), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs,
+                             ncols, y, y_cs));
     count_launch();
+    return MLZC_OK;
 }
 
 template <class WT>
@@ -200,11 +210,12 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
         const int nc = (int)std::min<int64_t>(8, N - n0);
         const char* xn = xc + (size_t)n0 * x_cs;
         char* yn = yc + (size_t)n0 * y_cs;
-        if (nc == 1) launch_vec<WT, 1>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
-        else if (nc == 2) launch_vec<WT, 2>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
-        else if (nc <= 4) launch_vec<WT, 4>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
-        else launch_vec<WT, 8>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
-        MLZC_CUDA_TRY(cudaGetLastError());
+        int st;
+        if (nc == 1) st = launch_vec<WT, 1>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else if (nc == 2) st = launch_vec<WT, 2>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else if (nc <= 4) st = launch_vec<WT, 4>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        else st = launch_vec<WT, 8>(wc, w_rs, M, K, xn, x_cs, nc, yn, y_cs, s);
+        if (st != MLZC_OK) return st;
     }
     return MLZC_OK;
 }

@@ -67,6 +67,7 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) xcol[nt] = X + (size_t)min(n0 + 8 * nt + g, N - 1) * x_cs + 32 * q4;
 
+    ptx::pdl_launch_dependents();
     const int nch = (K + kChunkK - 1) / kChunkK;
     const int c_begin = (int)((int64_t)nch * warp / kSkWarps);
     const int c_end = (int)((int64_t)nch * (warp + 1) / kSkWarps);
@@ -85,6 +86,14 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
                     wv[u][t][h] = ok ? ld_w16(wrow[t][h] + (size_t)c * (kChunkK * 2)) : make_uint4(0, 0, 0, 0);
+        }
+        // (f16 weights are never an output of these kernels: their first loads may overlap the
+        // previous kernel's tail; the activations may not)
+        if (c0 == c_begin) ptx::pdl_wait();
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = c0 + u;
+            const bool ok = c < c_end && c * kChunkK + 8 * q4 < K;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float4* xp = reinterpret_cast<const float4*>(xcol[nt] + (size_t)c * (kChunkK * 4));
@@ -116,6 +125,7 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
         }
     }
 
+    ptx::pdl_wait();   // (again, for warps whose K range was empty)
     // fixed-order sum of the warps' tiles through one shared buffer (warp 7 first)
     for (int w = kSkWarps - 1; w >= 0; --w) {
         if (warp == w) {
@@ -143,8 +153,8 @@ template <int MT, int NT, int U>
 int launch_sk(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs, int64_t N, char* y,
               size_t y_cs, cudaStream_t s) {
     const dim3 grid((unsigned)((M + 16 * MT - 1) / (16 * MT)), (unsigned)((N + 8 * NT - 1) / (8 * NT)));
-    gemv_f16_mma_kernel<MT, NT, U><<<grid, kSkThreads, 0, s>>>(w, w_rs, (int)M, (int)K, x, x_cs, (int)N, y, y_cs);
-    MLZC_CUDA_TRY(cudaGetLastError());
+    MLZC_CUDA_TRY(launch_pdl(gemv_f16_mma_kernel<MT, NT, U>, grid, dim3(kSkThreads), 0, s, w, w_rs, (int)M, (int)K, x,
+                             x_cs, (int)N, y, y_cs));
     count_launch();
     return MLZC_OK;
 }

@@ -152,10 +152,14 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
     float y[2][4] = {};
     RowBlock cur[4], nxt[4];
     int kb = warp;
+    ptx::pdl_launch_dependents();
     if (kb < nblk) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) cur[i] = load_row_block(rowp[i] + (size_t)kb * kQ4KBytes, q4);
     }
+    // Q4_K blocks are never an output of these kernels: the first block's loads may overlap
+    // the previous kernel's tail; the activations and every write come after it
+    ptx::pdl_wait();
     for (; kb < nblk; kb += kQWarps) {
         const int kn = kb + kQWarps;
         if (kn < nblk) {
@@ -430,9 +434,8 @@ int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, cons
     if (N <= 8) {
         const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
         if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
-        q4k_gemv_kernel<<<grid, kQThreads, 0, s>>>(wc, w_row_bytes, (int)M, (int)(K / kQK), xc, x_col_bytes, (int)N, yc,
-                                                   y_col_bytes);
-        MLZC_CUDA_TRY(cudaGetLastError());
+        MLZC_CUDA_TRY(launch_pdl(q4k_gemv_kernel, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, (int)(K / kQK), xc,
+                                 x_col_bytes, (int)N, yc, y_col_bytes));
         count_launch();
         return MLZC_OK;
     }
