@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU sample length")
     ap.add_argument("--no-graph", action="store_true",
                     help="time the eager launches instead of a CUDA-graph replay of the K steps")
+    ap.add_argument("--overlap", default="weights", choices=["off", "safe", "weights"],
+                    help="launch overlap of consecutive kernels (mlzc_set_launch_overlap); 'weights' "
+                         "is valid here because no kernel of any workload writes the weights")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu launch lists: no clock-sampling load loop, no e2e, no CPU leg "
                          "(launch order = warm-up steps, then the timed steps)")
@@ -508,6 +511,8 @@ def mlz_arm(a):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     mlz_b200.init(local)
+    mlz_b200.set_launch_overlap({"off": mlz_b200.OVERLAP_OFF, "safe": mlz_b200.OVERLAP_SAFE,
+                                 "weights": mlz_b200.OVERLAP_WEIGHTS}[a.overlap])
     n = a.n or DEFAULT_N[a.config]
     if world > 1:
         import datetime
@@ -696,6 +701,7 @@ def mlz_arm(a):
         cfg = dict(w.config)
         cfg["parallelism"] = cfg.get("parallelism", f"replicas x{world}" if world > 1 else "single GPU")
         cfg["timing"] = timing
+        cfg["launch_overlap"] = a.overlap
         cfg["eager_ms_per_step"] = max_ms_eager / K
         line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world, "steps": K,
                 "warmup": a.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": w.scaling,

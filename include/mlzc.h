@@ -68,6 +68,21 @@ enum mlzc_type { MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_K = 12 };
  * timed region. */
 int mlzc_launch_count(uint64_t* out_count);
 
+/* Launch overlap (programmatic dependent launch).  With MLZC_OVERLAP_SAFE (the default)
+ * each kernel of a call may start while the previous kernel of its stream finishes and
+ * does its set-up then, but reads and writes global memory only after that kernel has
+ * completed: any producer of W, X or the workspace is safe.  MLZC_OVERLAP_WEIGHTS also
+ * issues the first weight (W) loads of the decode-shaped kernels before that point; use it
+ * only when no kernel still running on the stream writes W (model weights), the case of
+ * a decode loop.  MLZC_OVERLAP_OFF launches every kernel in plain stream order.  The mode
+ * is process-wide and read at each launch (so at capture time for CUDA graphs).
+ * No counterpart in the reference (its CPU kernels have no launches to overlap). */
+#define MLZC_OVERLAP_OFF 0
+#define MLZC_OVERLAP_SAFE 1
+#define MLZC_OVERLAP_WEIGHTS 2
+int mlzc_set_launch_overlap(int mode);
+int mlzc_get_launch_overlap(int* out_mode);
+
 /* Message of the calling thread's last failed call ("" if none). */
 const char* mlzc_last_error(void);
 int mlzc_version(void);

@@ -6,8 +6,9 @@ Importing it loads the library and fails if it has not been built -- there is no
 fallback.
 """
 from ._lib import (EXPORTS, FA_MODE_ALIBI, FA_MODE_GQA_BATCH, FA_MODE_SOFTCAP, LIB_PATH,
-                   TYPE_F16, TYPE_F32, TYPE_Q4_K, UNIQUE_ID_BYTES, FaDesc, MlzcError,
-                   TensorView, check, last_error, launch_count, lib)
+                   OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS, TYPE_F16, TYPE_F32, TYPE_Q4_K,
+                   UNIQUE_ID_BYTES, FaDesc, MlzcError, TensorView, check, get_launch_overlap,
+                   last_error, launch_count, lib, set_launch_overlap)
 from .ops import (Comm, Weight, device_errors, flash_attn_dispatch, flash_attn_workspace_bytes,
                   ggml_simd_try_flash_attn, ggml_simd_try_mul_mat, init, make_fa_desc, mul_mat,
                   mul_mat_workspace_bytes, shutdown, tensor_view, weight_type_of)
@@ -15,7 +16,8 @@ from .ops import (Comm, Weight, device_errors, flash_attn_dispatch, flash_attn_w
 lib()  # load now: a missing or broken build is an import error, not a silent fallback
 
 __all__ = [
-    "EXPORTS", "FA_MODE_ALIBI", "FA_MODE_GQA_BATCH", "FA_MODE_SOFTCAP", "LIB_PATH", "TYPE_F16",
+    "EXPORTS", "FA_MODE_ALIBI", "FA_MODE_GQA_BATCH", "FA_MODE_SOFTCAP", "LIB_PATH", "OVERLAP_OFF",
+    "OVERLAP_SAFE", "OVERLAP_WEIGHTS", "get_launch_overlap", "set_launch_overlap", "TYPE_F16",
     "TYPE_F32", "TYPE_Q4_K", "UNIQUE_ID_BYTES", "FaDesc", "MlzcError", "TensorView", "check",
     "last_error", "launch_count", "lib", "Comm", "Weight", "device_errors", "flash_attn_dispatch",
     "flash_attn_workspace_bytes", "ggml_simd_try_flash_attn", "ggml_simd_try_mul_mat", "init",

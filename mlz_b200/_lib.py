@@ -18,11 +18,13 @@ STATUS_NAMES = {
 }
 TYPE_F32, TYPE_F16, TYPE_Q4_K = 0, 1, 12
 FA_MODE_GQA_BATCH, FA_MODE_ALIBI, FA_MODE_SOFTCAP = 0x04, 0x08, 0x10
+OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS = 0, 1, 2
 UNIQUE_ID_BYTES = 128
 
 # every symbol include/mlzc.h declares (checked by the CPU test suite)
 EXPORTS = (
     "mlzc_launch_count", "mlzc_last_error", "mlzc_version", "mlzc_init", "mlzc_shutdown", "mlzc_device_errors",
+    "mlzc_set_launch_overlap", "mlzc_get_launch_overlap",
     "mlzc_mul_mat_workspace_bytes", "mlzc_mul_mat_dev",
     "mlzc_flash_attn_workspace_bytes", "mlzc_flash_attn_dev", "mlzc_flash_attn_dev_noalloc",
     "mlzc_try_mul_mat", "mlzc_try_flash_attn",
@@ -80,6 +82,8 @@ def _declare(L: C.CDLL) -> None:
     for name in EXPORTS:
         getattr(L, name).restype = C.c_int
     L.mlzc_launch_count.argtypes = [C.POINTER(C.c_uint64)]
+    L.mlzc_set_launch_overlap.argtypes = [i32]
+    L.mlzc_get_launch_overlap.argtypes = [C.POINTER(i32)]
     L.mlzc_last_error.restype = C.c_char_p
     L.mlzc_last_error.argtypes = []
     L.mlzc_version.argtypes = []
@@ -107,6 +111,17 @@ def _declare(L: C.CDLL) -> None:
 def launch_count() -> int:
     v = C.c_uint64(0)
     check(lib().mlzc_launch_count(C.byref(v)))
+    return v.value
+
+
+def set_launch_overlap(mode: int) -> None:
+    """OVERLAP_OFF / OVERLAP_SAFE (default) / OVERLAP_WEIGHTS, process-wide (see mlzc.h)."""
+    check(lib().mlzc_set_launch_overlap(mode))
+
+
+def get_launch_overlap() -> int:
+    v = C.c_int32(0)
+    check(lib().mlzc_get_launch_overlap(C.byref(v)))
     return v.value
 
 

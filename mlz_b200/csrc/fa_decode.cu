@@ -146,7 +146,7 @@ __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
 }
 
 __device__ __forceinline__ int seq_len(const FaParams& p, int b) {
-    return p.kv_len ? min(max(p.kv_len[p.b_base + b], 0), p.n_kv) : p.n_kv;
+    return p.kv_len ? min(max(ptx::ld_act(p.kv_len + p.b_base + b), 0), p.n_kv) : p.n_kv;
 }
 
 // CTA of global tile t when W tiles are cut into P equal contiguous ranges
@@ -216,6 +216,10 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
         *abort_flag = 0;
         ptx::mbar_init_fence();
     }
+    // the set-up above overlaps the previous kernel's tail; kv_len, Q, K, V and the outputs
+    // wait for it
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();
     // prefix table: pref[b] = tiles of one segment summed over sequences < b
     if (warp == 0) {
         int run = 0;
@@ -253,6 +257,10 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
                 const int s = i % STAGES;
                 const uint32_t ph = (i / STAGES) & 1;
                 if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+                // the consumers read this stage with ldmatrix (generic proxy); order those
+                // reads, which the empty barrier has made visible here, before the TMA
+                // (async proxy) overwrites the stage
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 const int hidx = w.sl / p.n_rgroups;
                 const int kvh = p.packed ? hidx : (int)((int64_t)hidx * p.n_head_kv / p.n_head_q);
                 const uint32_t fb = ptx::smem_u32(&full[s]);
@@ -321,10 +329,10 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
                 const int d0 = 16 * ks + 2 * q4;
                 float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
                 if (qr) {
-                    x0 = qr[d0] * p.scale;
-                    x1 = qr[d0 + 1] * p.scale;
-                    x2 = qr[d0 + 8] * p.scale;
-                    x3 = qr[d0 + 9] * p.scale;
+                    x0 = ptx::ld_act(qr + d0) * p.scale;
+                    x1 = ptx::ld_act(qr + d0 + 1) * p.scale;
+                    x2 = ptx::ld_act(qr + d0 + 8) * p.scale;
+                    x3 = ptx::ld_act(qr + d0 + 9) * p.scale;
                 }
                 split_h2(x0, x1, qf[ks][0], qf[ks][2]);
                 split_h2(x2, x3, qf[ks][1], qf[ks][3]);
@@ -375,8 +383,8 @@ fa_decode_kernel(const __grid_constant__ FaParams p) {
             if (j < L && row_ok[h]) {
                 if constexpr (GEN) {
                     if (p.mask)
-                        a += *reinterpret_cast<const float*>(p.mask + iq_r[h] * p.m_nb1 + (int64_t)j * p.m_nb0 +
-                                                            ihq_r[h] * p.m_nb2 + ib * p.m_nb3);
+                        a += ptx::ld_act(reinterpret_cast<const float*>(p.mask + iq_r[h] * p.m_nb1 + (int64_t)j * p.m_nb0 +
+                                                            ihq_r[h] * p.m_nb2 + ib * p.m_nb3));
                     if (p.use_softcap) a = p.softcap * tanhf(a / p.softcap);
                     if (p.alibi_p2inv != 0.0f) a += slope[h] * (float)(j - iq_r[h]);
                 }
@@ -471,8 +479,10 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
     const int b = blockIdx.z;
     const int t = threadIdx.x;
     const int lane = t & 31, wid = t >> 5;
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();   // the partial records come from the decode kernel
     const int* pref = p.pref_out;
-    const int nb = pref[b + 1] - pref[b];
+    const int nb = ptx::ld_act(pref + b + 1) - ptx::ld_act(pref + b);
     const int rg = row / kRows, r = row % kRows;
     const int sl = hidx * p.n_rgroups + rg;
     const int ib = p.b_base + b;
@@ -484,8 +494,8 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
         dr[t] = 0.0f;
         return;
     }
-    const int64_t W = (int64_t)p.HR * pref[p.nB];
-    const int64_t T = (int64_t)p.HR * pref[b] + (int64_t)sl * nb;
+    const int64_t W = (int64_t)p.HR * ptx::ld_act(pref + p.nB);
+    const int64_t T = (int64_t)p.HR * ptx::ld_act(pref + b) + (int64_t)sl * nb;
     const int cf = cta_of_tile(T, W, P);
     const int nrec = (cta_of_tile(T + nb - 1, W, P) - cf + 1) * kFaWarps;
     const float* base = p.part + (((int64_t)cf + (int64_t)b * p.HR + sl) * kFaWarps * kRows + r) * (D + 2);
@@ -493,7 +503,7 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
     // CTAs with an empty range (more CTAs than tiles) wrote none
     auto rec_m = [&](int q) {
         const int64_t c = cf + q / kFaWarps;
-        return (W * c / P == W * (c + 1) / P) ? -INFINITY : base[(int64_t)q * kRows * (D + 2)];
+        return (W * c / P == W * (c + 1) / P) ? -INFINITY : ptx::ld_act(base + (int64_t)q * kRows * (D + 2));
     };
     auto block_reduce = [&](float v, bool is_max) {
 #pragma unroll
@@ -528,7 +538,7 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
             const float m = rec_m(q);
             if (m != -INFINITY) {
                 e = __expf(m - M);
-                lw = e * base[(int64_t)q * kRows * (D + 2) + 1];
+                lw = e * ptx::ld_act(base + (int64_t)q * kRows * (D + 2) + 1);
             }
         }
         s_e[t] = e;
@@ -539,17 +549,17 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
         for (; k + 4 <= n; k += 4) {
             const float* o0 = base + (int64_t)(q0 + k) * kRows * (D + 2) + 2 + t;
             const float e0 = s_e[k], e1 = s_e[k + 1], e2 = s_e[k + 2], e3 = s_e[k + 3];
-            const float v0 = e0 != 0.0f ? o0[0] : 0.0f;
-            const float v1 = e1 != 0.0f ? o0[kRows * (D + 2)] : 0.0f;
-            const float v2 = e2 != 0.0f ? o0[2 * kRows * (D + 2)] : 0.0f;
-            const float v3 = e3 != 0.0f ? o0[3 * kRows * (D + 2)] : 0.0f;
+            const float v0 = e0 != 0.0f ? ptx::ld_act(o0) : 0.0f;
+            const float v1 = e1 != 0.0f ? ptx::ld_act(o0 + kRows * (D + 2)) : 0.0f;
+            const float v2 = e2 != 0.0f ? ptx::ld_act(o0 + 2 * kRows * (D + 2)) : 0.0f;
+            const float v3 = e3 != 0.0f ? ptx::ld_act(o0 + 3 * kRows * (D + 2)) : 0.0f;
             Os += e0 * v0;
             Os += e1 * v1;
             Os += e2 * v2;
             Os += e3 * v3;
         }
         for (; k < n; ++k)
-            if (s_e[k] != 0.0f) Os += s_e[k] * base[(int64_t)(q0 + k) * kRows * (D + 2) + 2 + t];
+            if (s_e[k] != 0.0f) Os += s_e[k] * ptx::ld_act(base + (int64_t)(q0 + k) * kRows * (D + 2) + 2 + t);
         __syncthreads();   // s_e is rewritten by the next chunk
     }
     dr[t] = Ls > 0.0f ? Os / Ls : 0.0f;
@@ -694,12 +704,14 @@ unsigned int* static_error_word() {
 template <int D>
 int fa_launch(const FaPlan& pl, cudaStream_t s) {
     const bool gen = pl.p.mask || pl.p.use_softcap || pl.p.alibi_p2inv != 0.0f;
-    if (gen) fa_decode_kernel<D, true><<<pl.ctas, kFaThreads, FaCfg<D>::kSmemBytes, s>>>(pl.p);
-    else fa_decode_kernel<D, false><<<pl.ctas, kFaThreads, FaCfg<D>::kSmemBytes, s>>>(pl.p);
+    if (gen)
+        MLZC_CUDA_TRY(launch_pdl(fa_decode_kernel<D, true>, dim3(pl.ctas), dim3(kFaThreads), FaCfg<D>::kSmemBytes, s, pl.p));
+    else
+        MLZC_CUDA_TRY(launch_pdl(fa_decode_kernel<D, false>, dim3(pl.ctas), dim3(kFaThreads), FaCfg<D>::kSmemBytes, s, pl.p));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     const dim3 g((unsigned)pl.p.rows_total, (unsigned)pl.p.n_hidx, (unsigned)pl.p.nB);
-    fa_combine_kernel<D><<<g, D, 0, s>>>(pl.p, pl.ctas);
+    MLZC_CUDA_TRY(launch_pdl(fa_combine_kernel<D>, g, dim3(D), 0, s, pl.p, pl.ctas));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;

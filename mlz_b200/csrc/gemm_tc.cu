@@ -205,6 +205,9 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    // set-up above overlaps the previous kernel's tail; operands and outputs wait for it
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();
 
     const int tiles = g.num_m * g.num_n;
     const int kper = (g.kblocks + g.splits - 1) / g.splits;   // k-blocks per split
@@ -430,8 +433,10 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
 // bytes with the 16-byte chunks XOR-swizzled by (row % 8) -- the image a 128-byte-swizzle
 // TMA box would leave in shared memory, so each stage is a single bulk copy.  Rows past N
 // and columns past K are zero.  Also zeroes the split-K tile counters.
-__global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N, int K, uint8_t* __restrict__ x16t,
+__global__ void narrow_f16_kernel(const char* x, size_t x_cs, int N, int K, uint8_t* __restrict__ x16t,
                                   int BN, int num_n, int kblocks, int vec, int* __restrict__ tile_count, int ntiles) {
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();   // X may come from, and X16 / the counters be in use by, the previous kernel
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ntiles; i += gridDim.x * blockDim.x) tile_count[i] = 0;
     const int cpr = kblocks * 8;                          // 16-byte chunks per padded row
     const int64_t total = (int64_t)num_n * BN * cpr;
@@ -443,12 +448,12 @@ __global__ void narrow_f16_kernel(const char* __restrict__ x, size_t x_cs, int N
         if (n < N) {
             const float* xr = reinterpret_cast<const float*>(x + (size_t)n * x_cs);
             if (vec && k0 + 8 <= K) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k0));
-                const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k0 + 4));
+                const float4 a = ptx::ld_act(reinterpret_cast<const float4*>(xr + k0));
+                const float4 b = ptx::ld_act(reinterpret_cast<const float4*>(xr + k0 + 4));
                 v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? xr[k0 + e] : 0.0f;
+                for (int e = 0; e < 8; ++e) v[e] = (k0 + e < K) ? ptx::ld_act(xr + k0 + e) : 0.0f;
             }
         } else {
 #pragma unroll
@@ -587,7 +592,7 @@ int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, GemmArgs g, cudaStrea
         attr_set[dev] = true;
     }
     const int grid = std::min(g.num_work, c->sm_count);
-    gemm_f16_tc_kernel<BN, MT><<<grid, kGemmThreads, Cfg::kSmemBytes, s>>>(ta, g);
+    MLZC_CUDA_TRY(launch_pdl(gemm_f16_tc_kernel<BN, MT>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, s, ta, g));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;
@@ -621,8 +626,8 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
         const int vec = ((uintptr_t)x % 16 == 0 && x_col_bytes % 16 == 0) ? 1 : 0;
         const int64_t total = (int64_t)pl.num_n * pl.BN * pl.kblocks * 8;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)c->sm_count * 8));
-        narrow_f16_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const char*>(x), x_col_bytes, (int)N, (int)K, x16t,
-                                               pl.BN, pl.num_n, pl.kblocks, vec, counters, pl.splits > 1 ? tiles : 0);
+        MLZC_CUDA_TRY(launch_pdl(narrow_f16_kernel, dim3(grid), dim3(256), 0, s, reinterpret_cast<const char*>(x), x_col_bytes, (int)N, (int)K, x16t,
+                                               pl.BN, pl.num_n, pl.kblocks, vec, counters, pl.splits > 1 ? tiles : 0));
         MLZC_CUDA_TRY(cudaGetLastError());
         count_launch();
     }

@@ -8,9 +8,8 @@
 // Design (HBM-bound: every weight byte is read exactly once):
 //   - one warp owns ROWS consecutive weight rows; its 32 lanes stride over K in 16-byte
 //     chunks, so every load instruction of the warp reads 512 contiguous bytes per row;
-//   - weights are read with ld.global.nc.L1::no_allocate (streamed, never re-read),
-//     activations through the read-only path (they are re-read by every warp and stay
-//     in L1/L2);
+//   - weights are streamed with L1::no_allocate loads (never re-read), activations with
+//     weak L1-cached loads (they are re-read by every warp of a CTA and stay in L1/L2);
 //   - fp32 accumulation per lane, butterfly shuffle reduction at the end;
 //   - the ROWS rows of a warp share each activation load, which keeps the L1 traffic
 //     per FMA at or below one byte.
@@ -26,15 +25,6 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-
-__device__ __forceinline__ uint4 ld_stream16(const void* p) {
-    uint4 v;
-    // volatile: keeps the unrolled prefetch loads ahead of the math that consumes them
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 
 __device__ __forceinline__ float2 h2_to_f2(uint32_t u) {
     __half2 h = *reinterpret_cast<__half2*>(&u);
@@ -53,7 +43,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 struct WF16 {
     static constexpr int kPerChunk = 8;
     static constexpr bool kRoundX = true;
-    static constexpr bool kEarlyLoads = true;   // f16 weights are never an output of these kernels
+    static constexpr bool kNcWeights = true;   // f16 weights are never an output of these kernels
     __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
         float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
         w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
@@ -68,7 +58,7 @@ struct WF16 {
 struct WF32 {
     static constexpr int kPerChunk = 4;
     static constexpr bool kRoundX = false;
-    static constexpr bool kEarlyLoads = false;  // f32 weights may be an earlier call's output
+    static constexpr bool kNcWeights = false;  // f32 weights may be an earlier call's output
     __device__ __forceinline__ static void unpack(const uint4& v, float* w) {
         w[0] = __uint_as_float(v.x); w[1] = __uint_as_float(v.y);
         w[2] = __uint_as_float(v.z); w[3] = __uint_as_float(v.w);
@@ -81,17 +71,18 @@ struct WF32 {
 // Vectorised kernel: requires 16-byte aligned rows/columns and K % kPerChunk == 0.
 // Each lane keeps ROWS x U 16-byte weight loads in flight (U chunks 32 apart), which is
 // what hides the HBM latency: ~128 KB in flight per SM at ROWS = 2, U = 4.
+// early != 0 (f16 weights only): the first weight loads are issued before pdl_wait().
 template <class WT, int NB, int ROWS, int U>
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
-                const char* __restrict__ X, size_t x_cs, int ncols,
-                char* __restrict__ Y, size_t y_cs) {
+                const char* X, size_t x_cs, int ncols,
+                char* __restrict__ Y, size_t y_cs, int early) {
     constexpr int CH = WT::kPerChunk;
     const int lane = threadIdx.x & 31;
     const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
     ptx::pdl_launch_dependents();
     if (row0 >= M) return;
-    if (!WT::kEarlyLoads) ptx::pdl_wait();
+    if (!(WT::kNcWeights && early)) ptx::pdl_wait();
 
     const char* wrow[ROWS];
 #pragma unroll
@@ -111,7 +102,7 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
             const int64_t c = base + lane + 32 * u;
 #pragma unroll
             for (int r = 0; r < ROWS; r++)
-                wv[r][u] = c < nchunk ? ld_stream16(wrow[r] + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+                wv[r][u] = c >= nchunk ? make_uint4(0, 0, 0, 0) : ptx::ld_weight16<WT::kNcWeights>(wrow[r] + (size_t)c * 16);
         }
         // the first weight loads are in flight while the previous kernel finishes; the
         // activations (and every write) come after it
@@ -130,7 +121,7 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
                     float xf[CH];
 #pragma unroll
                     for (int q = 0; q < CH / 4; q++) {
-                        const float4 t = __ldg(xp + q);
+                        const float4 t = ptx::ld_act(xp + q);
                         xf[4 * q + 0] = t.x; xf[4 * q + 1] = t.y; xf[4 * q + 2] = t.z; xf[4 * q + 3] = t.w;
                     }
                     if (WT::kRoundX) {
@@ -186,7 +177,7 @@ int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, 
     const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
     const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
     MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U>, dim3(grid), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs,
-                             ncols, y, y_cs));
+                             ncols, y, y_cs, weights_before_wait() ? 1 : 0));
     count_launch();
     return MLZC_OK;
 }
@@ -223,8 +214,10 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
 // gathered [G][N][m_loc] -> dst [N][G * m_loc] (column stride dst_cs bytes): one CTA row per
 // (rank slice r, column n) -- blockIdx.y = r * N + n -- threads over m, float4 when the
 // slices and the destination are 16-byte aligned.
-__global__ void gather_permute_kernel(const float* __restrict__ src, char* __restrict__ dst, size_t dst_cs, int N,
+__global__ void gather_permute_kernel(const float* src, char* __restrict__ dst, size_t dst_cs, int N,
                                       int64_t m_loc, int vec) {
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();   // the gathered slices come from the all-gather
     const int64_t rn = blockIdx.y;
     const int64_t n = rn % N, r = rn / N;
     const float* srow = src + rn * m_loc;
@@ -232,10 +225,10 @@ __global__ void gather_permute_kernel(const float* __restrict__ src, char* __res
     if (vec) {
         const int64_t m4 = m_loc / 4;
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m4; i += (int64_t)gridDim.x * blockDim.x)
-            reinterpret_cast<float4*>(drow)[i] = reinterpret_cast<const float4*>(srow)[i];
+            reinterpret_cast<float4*>(drow)[i] = ptx::ld_act(reinterpret_cast<const float4*>(srow) + i);
     } else {
         for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m_loc; i += (int64_t)gridDim.x * blockDim.x)
-            drow[i] = srow[i];
+            drow[i] = ptx::ld_act(srow + i);
     }
 }
 
@@ -248,8 +241,8 @@ int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, in
     const int vec = (m_loc % 4 == 0 && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0 && dst_col_bytes % 16 == 0) ? 1 : 0;
     const int64_t per_row = vec ? m_loc / 4 : m_loc;
     const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((per_row + 255) / 256, 64));
-    gather_permute_kernel<<<dim3(gx, (unsigned)(G * N)), 256, 0, s>>>(src, reinterpret_cast<char*>(dst), dst_col_bytes,
-                                                                     (int)N, m_loc, vec);
+    MLZC_CUDA_TRY(launch_pdl(gather_permute_kernel, dim3(gx, (unsigned)(G * N)), dim3(256), 0, s, src,
+                             reinterpret_cast<char*>(dst), dst_col_bytes, (int)N, m_loc, vec));
     count_launch();
     MLZC_CUDA_TRY(cudaGetLastError());
     return MLZC_OK;

@@ -45,8 +45,8 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 template <int MT, int NT, int U>
 __global__ void __launch_bounds__(kSkThreads)
-gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const char* __restrict__ X, size_t x_cs,
-                    int N, char* __restrict__ Y, size_t y_cs) {
+gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const char* X, size_t x_cs,
+                    int N, char* __restrict__ Y, size_t y_cs, int early) {
     constexpr int ROWS = 16 * MT, COLS = 8 * NT;
     __shared__ float red[ROWS * COLS];
     const int warp = threadIdx.x >> 5;
@@ -68,6 +68,7 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
     for (int nt = 0; nt < NT; ++nt) xcol[nt] = X + (size_t)min(n0 + 8 * nt + g, N - 1) * x_cs + 32 * q4;
 
     ptx::pdl_launch_dependents();
+    if (!early) ptx::pdl_wait();
     const int nch = (K + kChunkK - 1) / kChunkK;
     const int c_begin = (int)((int64_t)nch * warp / kSkWarps);
     const int c_end = (int)((int64_t)nch * (warp + 1) / kSkWarps);
@@ -87,8 +88,8 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
                 for (int h = 0; h < 2; ++h)
                     wv[u][t][h] = ok ? ld_w16(wrow[t][h] + (size_t)c * (kChunkK * 2)) : make_uint4(0, 0, 0, 0);
         }
-        // (f16 weights are never an output of these kernels: their first loads may overlap the
-        // previous kernel's tail; the activations may not)
+        // (f16 weights are never an output of these kernels: with early != 0 their first loads
+        // overlap the previous kernel's tail; the activations never do)
         if (c0 == c_begin) ptx::pdl_wait();
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -97,8 +98,8 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float4* xp = reinterpret_cast<const float4*>(xcol[nt] + (size_t)c * (kChunkK * 4));
-                xv[u][nt][0] = ok ? xp[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-                xv[u][nt][1] = ok ? xp[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[u][nt][0] = ok ? ptx::ld_act(xp) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[u][nt][1] = ok ? ptx::ld_act(xp + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
 #pragma unroll
@@ -154,7 +155,7 @@ int launch_sk(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, s
               size_t y_cs, cudaStream_t s) {
     const dim3 grid((unsigned)((M + 16 * MT - 1) / (16 * MT)), (unsigned)((N + 8 * NT - 1) / (8 * NT)));
     MLZC_CUDA_TRY(launch_pdl(gemv_f16_mma_kernel<MT, NT, U>, grid, dim3(kSkThreads), 0, s, w, w_rs, (int)M, (int)K, x,
-                             x_cs, (int)N, y, y_cs));
+                             x_cs, (int)N, y, y_cs, weights_before_wait() ? 1 : 0));
     count_launch();
     return MLZC_OK;
 }

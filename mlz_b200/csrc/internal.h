@@ -38,6 +38,11 @@ DeviceCtx* current_ctx();
 // Counts one kernel launch (read by mlzc_launch_count).
 void count_launch(int n = 1);
 
+// Process-wide launch-overlap mode (MLZC_OVERLAP_*), set by mlzc_set_launch_overlap.
+int overlap_mode();
+// True when weight loads may be issued before pdl_wait() (MLZC_OVERLAP_WEIGHTS).
+inline bool weights_before_wait() { return overlap_mode() == MLZC_OVERLAP_WEIGHTS; }
+
 // Bounded-wait budget for every spin loop in the kernels (mbarrier polls).
 constexpr long long kSpinLimit = 1ll << 26;
 

@@ -101,13 +101,64 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 // attribute may start while the previous kernel of the stream finishes; it must call
 // pdl_wait() before it reads anything the previous kernel may have written or writes
 // anything the previous kernel may still read.  pdl_launch_dependents() lets the next such
-// kernel start early (its own pdl_wait() still waits for this whole grid).
+// kernel start early (its own pdl_wait() still waits for this whole grid).  After the
+// wait the previous grid's writes are visible to ordinary (weak) loads -- ld_act() below,
+// TMA and bulk copies -- but not to the non-coherent read-only path (__ldg,
+// ld.global.nc), which assumes data unchanged for the kernel's whole life and which a
+// compiler may also hoist above the wait.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Loads of data that an earlier kernel of the stream may have written (activations,
+// prepared operands, partial records): weak ld.global, cached in L1 for reuse within the
+// kernel.  volatile keeps them in program order after pdl_wait().
+__device__ __forceinline__ float ld_act(const float* p) {
+    float v;
+    asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_act(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int ld_act(const int* p) {
+    int v;
+    asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_act(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_act(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// 16-byte weight load, streamed (never re-read, not allocated in L1).  `nc` = the weights
+// cannot be an output of a kernel still running on the stream (read-only path); otherwise
+// a weak coherent load.
+template <bool nc>
+__device__ __forceinline__ uint4 ld_weight16(const void* p) {
+    uint4 v;
+    if constexpr (nc)
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+    else
+        asm volatile("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(p));
+    return v;
+}
+
 }  // namespace ptx
 
-// Launches `kernel` with programmatic stream serialization allowed (see pdl_wait).
+// Launches `kernel` with programmatic stream serialization allowed (see pdl_wait), unless
+// the launch-overlap mode is MLZC_OVERLAP_OFF.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                               Args... args) {
@@ -120,7 +171,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = overlap_mode() == MLZC_OVERLAP_OFF ? 0 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 }  // namespace mlzc

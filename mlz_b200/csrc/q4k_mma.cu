@@ -129,8 +129,8 @@ __device__ __forceinline__ uint32_t word_of(const RowBlock& r, int wi) {
 // and the next block's weights prefetched into registers (one CTA per SM at ~250
 // registers; the prefetch, not occupancy, hides the load latency).
 __global__ void __launch_bounds__(kQThreads)
-q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const char* __restrict__ X, size_t x_cs,
-               int N, char* __restrict__ Y, size_t y_cs) {
+q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const char* X, size_t x_cs,
+               int N, char* __restrict__ Y, size_t y_cs, int early) {
     __shared__ float red[kQWarps][kQRows * 8];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -153,12 +153,13 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
     RowBlock cur[4], nxt[4];
     int kb = warp;
     ptx::pdl_launch_dependents();
+    if (!early) ptx::pdl_wait();
     if (kb < nblk) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) cur[i] = load_row_block(rowp[i] + (size_t)kb * kQ4KBytes, q4);
     }
-    // Q4_K blocks are never an output of these kernels: the first block's loads may overlap
-    // the previous kernel's tail; the activations and every write come after it
+    // Q4_K blocks are never an output of these kernels: with early != 0 the first block's
+    // loads overlap the previous kernel's tail; the activations and every write come after it
     ptx::pdl_wait();
     for (; kb < nblk; kb += kQWarps) {
         const int kn = kb + kQWarps;
@@ -177,7 +178,7 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
         for (int hi = 0; hi < 2; ++hi) {
             float4 xv[8];
 #pragma unroll
-            for (int wi = 0; wi < 8; ++wi) xv[wi] = col_ok ? xb[8 * hi + wi] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int wi = 0; wi < 8; ++wi) xv[wi] = col_ok ? ptx::ld_act(xb + 8 * hi + wi) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int wi = 0; wi < 8; ++wi) {
                 S[hi] += (xv[wi].x + xv[wi].y) + (xv[wi].z + xv[wi].w);
@@ -250,8 +251,10 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
 // N are zero.
 //   xf: [n-tile][block][q][g][16 k-steps] uint2 (b0, b1)   (g = column within the 8-column tile)
 //   xs: [n-tile][block][q][g] uint2 (hi pair, lo pair)
-__global__ void q4k_prep_kernel(const char* __restrict__ X, size_t x_cs, int N, int n_pad, int nblk,
+__global__ void q4k_prep_kernel(const char* X, size_t x_cs, int N, int n_pad, int nblk,
                                 uint2* __restrict__ xf, uint2* __restrict__ xs) {
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();   // X may come from, and the workspace be in use by, the previous kernel
     const int64_t total = (int64_t)n_pad * nblk * 64;     // a multiple of 32: whole warps
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int st = (int)(i & 15);
@@ -263,7 +266,7 @@ __global__ void q4k_prep_kernel(const char* __restrict__ X, size_t x_cs, int N, 
         const int hi = st >> 3, wi = st & 7;
         const int64_t slot = (((int64_t)nt * nblk + kb) * 4 + q) * 8 + g;
         const float4* src = reinterpret_cast<const float4*>(X + (size_t)(n < N ? n : 0) * x_cs) + (size_t)kb * (kQK / 4) + 16 * q;
-        const float4 v = n < N ? src[8 * hi + wi] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 v = n < N ? ptx::ld_act(src + 8 * hi + wi) : make_float4(0.f, 0.f, 0.f, 0.f);
         const __half2 b0 = __floats2half2_rn(v.x, v.z), b1 = __floats2half2_rn(v.y, v.w);
         xf[slot * 16 + st] = make_uint2(h2u(b0), h2u(b1));
         const float2 f0 = __half22float2(b0), f1 = __half22float2(b1);
@@ -288,8 +291,8 @@ __global__ void q4k_prep_kernel(const char* __restrict__ X, size_t x_cs, int N, 
 // registers stay at <= 128, so two CTAs (16 warps) share an SM and hide the load latency.
 template <int NT>
 __global__ void __launch_bounds__(kQThreads, NT == 1 ? 2 : 1)
-q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const uint2* __restrict__ xf,
-               const uint2* __restrict__ xs, int N, char* __restrict__ Y, size_t y_cs) {
+q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const uint2* xf,
+               const uint2* xs, int N, char* __restrict__ Y, size_t y_cs, int early) {
     constexpr int COLS = 8 * NT;
     __shared__ float red[kQRows * COLS];
     const int warp = threadIdx.x >> 5;
@@ -308,21 +311,25 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
     }
 
     float y[NT][2][4] = {};
+    ptx::pdl_launch_dependents();
+    if (!early) ptx::pdl_wait();
     for (int kb = warp; kb < nblk; kb += kQWarps) {
         RowBlock cur[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) cur[i] = load_row_block(rowp[i] + (size_t)kb * kQ4KBytes, q4);
+        // Q4_K blocks are never an output of these kernels; the prepared activations are
+        if (kb == warp) ptx::pdl_wait();
         const uint4* xfrag[NT];
         uint2 sv[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int64_t slot = (((int64_t)(ntile0 + nt) * nblk + kb) * 4 + q4) * 8 + g;
             xfrag[nt] = reinterpret_cast<const uint4*>(xf + slot * 16);
-            sv[nt] = __ldg(xs + slot);
+            sv[nt] = ptx::ld_act(xs + slot);
         }
         uint4 xp[2][NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) xp[0][nt] = __ldg(xfrag[nt]);
+        for (int nt = 0; nt < NT; ++nt) xp[0][nt] = ptx::ld_act(xfrag[nt]);
         RowScales sc[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) sc[i] = row_scales(cur[i].hdr, q4);
@@ -332,7 +339,7 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
         for (int p = 0; p < 8; ++p) {          // k-step pairs 2p, 2p+1
             if (p < 7) {
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) xp[(p + 1) & 1][nt] = __ldg(xfrag[nt] + p + 1);
+                for (int nt = 0; nt < NT; ++nt) xp[(p + 1) & 1][nt] = ptx::ld_act(xfrag[nt] + p + 1);
             }
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -375,6 +382,7 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
             }
     }
 
+    ptx::pdl_wait();   // (again, for warps without a block)
     // fixed-order sum of the warps' partial rows through one shared buffer (warp 7 first)
     for (int w = kQWarps - 1; w >= 0; --w) {
         if (warp == w) {
@@ -435,7 +443,7 @@ int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, cons
         const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
         if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
         MLZC_CUDA_TRY(launch_pdl(q4k_gemv_kernel, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, (int)(K / kQK), xc,
-                                 x_col_bytes, (int)N, yc, y_col_bytes));
+                                 x_col_bytes, (int)N, yc, y_col_bytes, weights_before_wait() ? 1 : 0));
         count_launch();
         return MLZC_OK;
     }
@@ -447,14 +455,14 @@ int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, cons
     {
         const int64_t total = (int64_t)q.n_pad * q.nblk * 64;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 16));
-        q4k_prep_kernel<<<grid, 256, 0, s>>>(xc, x_col_bytes, (int)N, q.n_pad, q.nblk, xf, xs);
-        MLZC_CUDA_TRY(cudaGetLastError());
+        MLZC_CUDA_TRY(launch_pdl(q4k_prep_kernel, dim3(grid), dim3(256), 0, s, xc, x_col_bytes, (int)N, q.n_pad, q.nblk,
+                                 xf, xs));
         count_launch();
     }
     const dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + kQRows - 1) / kQRows));
     if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
-    q4k_mma_kernel<2><<<grid, kQThreads, 0, s>>>(wc, w_row_bytes, (int)M, q.nblk, xf, xs, (int)N, yc, y_col_bytes);
-    MLZC_CUDA_TRY(cudaGetLastError());
+    MLZC_CUDA_TRY(launch_pdl(q4k_mma_kernel<2>, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, q.nblk, xf, xs,
+                             (int)N, yc, y_col_bytes, weights_before_wait() ? 1 : 0));
     count_launch();
     return MLZC_OK;
 }

@@ -37,9 +37,12 @@ int g_hook_device = 0;                           // device of the hook-level ent
 
 namespace {
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_overlap{MLZC_OVERLAP_SAFE};
 }  // namespace
 
 void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int overlap_mode() { return g_overlap.load(std::memory_order_relaxed); }
 
 int fail(int status, const char* fmt, ...) {
     char buf[512];
@@ -194,6 +197,19 @@ extern "C" int mlzc_version(void) { return MLZC_VERSION; }
 extern "C" int mlzc_launch_count(uint64_t* out_count) {
     if (!out_count) return fail(MLZC_ERR_INVALID, "null out_count");
     *out_count = g_launches.load(std::memory_order_relaxed);
+    return MLZC_OK;
+}
+
+extern "C" int mlzc_set_launch_overlap(int mode) {
+    if (mode != MLZC_OVERLAP_OFF && mode != MLZC_OVERLAP_SAFE && mode != MLZC_OVERLAP_WEIGHTS)
+        return fail(MLZC_ERR_INVALID, "launch overlap mode %d (0, 1 or 2)", mode);
+    g_overlap.store(mode, std::memory_order_relaxed);
+    return MLZC_OK;
+}
+
+extern "C" int mlzc_get_launch_overlap(int* out_mode) {
+    if (!out_mode) return fail(MLZC_ERR_INVALID, "null out_mode");
+    *out_mode = overlap_mode();
     return MLZC_OK;
 }
 

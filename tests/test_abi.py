@@ -36,6 +36,23 @@ def test_version_and_error_string():
     assert "weight type 7" in mlz_b200.last_error()
 
 
+def test_launch_overlap_mode():
+    assert mlz_b200.get_launch_overlap() == mlz_b200.OVERLAP_SAFE   # the default
+    try:
+        for m in (mlz_b200.OVERLAP_OFF, mlz_b200.OVERLAP_WEIGHTS, mlz_b200.OVERLAP_SAFE):
+            mlz_b200.set_launch_overlap(m)
+            assert mlz_b200.get_launch_overlap() == m
+        for bad in (-1, 3):
+            try:
+                mlz_b200.set_launch_overlap(bad)
+                raise AssertionError("mode %d accepted" % bad)
+            except mlz_b200.MlzcError as e:
+                assert e.status == -1
+        assert mlz_b200.get_launch_overlap() == mlz_b200.OVERLAP_SAFE
+    finally:
+        mlz_b200.set_launch_overlap(mlz_b200.OVERLAP_SAFE)
+
+
 def test_argument_gates():
     L = mlz_b200.lib()
     # Q4_K with K not a multiple of 256
