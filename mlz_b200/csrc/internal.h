@@ -62,9 +62,15 @@ int launch_gemv_f16_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K,
 // Q4_K dequant-dot on the tensor cores (mma.sync), any N: an activation prep launch (f16
 // fragments + sub-block sums into the workspace) and the main kernel.
 size_t q4k_workspace_bytes(int64_t K, int64_t N);
-int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws,
-                   size_t ws_bytes, cudaStream_t s);
+int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                   const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
+                   void* ws, size_t ws_bytes, cudaStream_t s);
+// Decode-shaped Q4_K (N <= 2): persistent kernel fed by a TMA ring, activations converted
+// once per CTA into shared memory.
+bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
+int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
+                    cudaStream_t s);
 
 // tcgen05/TMEM GEMM for F16 weights (activations narrowed to f16 in the workspace).
 size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N);

@@ -31,14 +31,20 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "q4k.cuh"
 
 namespace mlzc {
 namespace {
 
 using ptx::mma16816;
+using q4k::RowScales;
+using q4k::deq_hi;
+using q4k::deq_lo;
+using q4k::h2u;
+using q4k::row_scales;
 
-constexpr int kQK = 256;
-constexpr int kQ4KBytes = 144;
+constexpr int kQK = q4k::kQK;
+constexpr int kQ4KBytes = q4k::kBlockBytes;
 constexpr int kQWarps = 8;
 constexpr int kQThreads = kQWarps * 32;
 constexpr int kQRows = 32;     // rows per CTA: two 16-row MMA tiles
@@ -51,9 +57,6 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
     return v;
 }
 
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-
 // One row's share of a block for this thread: header (d, dmin, scales) and its 32-byte chunk.
 struct RowBlock {
     uint4 hdr, qa, qb;
@@ -65,50 +68,6 @@ __device__ __forceinline__ RowBlock load_row_block(const char* blk, int q4) {
     r.qa = ld_stream(blk + 16 + 32 * q4);
     r.qb = ld_stream(blk + 16 + 32 * q4 + 16);
     return r;
-}
-
-// Per row and block: the HFMA2 constants that turn nibble bits into sc * q for sub-blocks
-// 2c (low nibbles) and 2c+1 (high nibbles), the (m_2c, m_2c+1) pair, and d, dmin.
-struct RowScales {
-    __half2 mul_lo, add_lo, mul_hi, add_hi;
-    uint32_t mpair;
-    float d, dmin;
-};
-
-__device__ __forceinline__ RowScales row_scales(const uint4& hdr, int c) {
-    // scale bytes s[0..11] = hdr.y (s0-s3), hdr.z (s4-s7), hdr.w (s8-s11); this thread needs
-    // sub-blocks j = 2c, 2c+1, i.e. byte pair j' = 2 (c & 1), +1 of each word
-    const int sh = 16 * (c & 1);
-    const uint32_t A = (hdr.y >> sh) & 0xFFFFu, B = (hdr.z >> sh) & 0xFFFFu, Cw = (hdr.w >> sh) & 0xFFFFu;
-    uint32_t sc2, m2;
-    if (c < 2) {   // j < 4: sc = s[j] & 63, m = s[j+4] & 63
-        sc2 = A & 0x3F3Fu;
-        m2 = B & 0x3F3Fu;
-    } else {       // j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4
-        sc2 = (Cw & 0x0F0Fu) | ((A >> 2) & 0x3030u);
-        m2 = ((Cw >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
-    }
-    const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-    const __half2 sch = __hsub2(u2h(__byte_perm(sc2, 0x6464u, 0x5140)), k1024);   // (sc_2c, sc_2c+1)
-    RowScales r;
-    r.mpair = h2u(__hsub2(u2h(__byte_perm(m2, 0x6464u, 0x5140)), k1024));          // (m_2c, m_2c+1)
-    const __half2 lo = __low2half2(sch), hi = __high2half2(sch);
-    r.mul_lo = lo;
-    r.add_lo = __hmul2(lo, __float2half2_rn(-1024.0f));
-    r.mul_hi = __hmul2(hi, __float2half2_rn(0.0625f));
-    r.add_hi = __hmul2(hi, __float2half2_rn(-64.0f));
-    const __half2 dd = u2h(hdr.x);
-    r.d = __low2float(dd);
-    r.dmin = __high2float(dd);
-    return r;
-}
-
-// sc * q for the nibble pair (bytes 0 and 2 of w) of the low or high half.
-__device__ __forceinline__ uint32_t deq_lo(uint32_t w, const RowScales& s) {
-    return h2u(__hfma2(u2h((w & 0x000F000Fu) | 0x64006400u), s.mul_lo, s.add_lo));
-}
-__device__ __forceinline__ uint32_t deq_hi(uint32_t w, const RowScales& s) {
-    return h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), s.mul_hi, s.add_hi));
 }
 
 __device__ __forceinline__ uint32_t word_of(const RowBlock& r, int wi) {
@@ -429,8 +388,9 @@ size_t q4k_workspace_bytes(int64_t K, int64_t N) {
     return w.xf_bytes + w.xs_bytes;
 }
 
-int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x, size_t x_col_bytes,
-                   int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes, cudaStream_t s) {
+int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                   cudaStream_t s) {
     if (K % kQK != 0) return fail(MLZC_ERR_INVALID, "Q4_K: K=%lld is not a multiple of 256", (long long)K);
     if ((uintptr_t)w % 16 || w_row_bytes % 16 || (uintptr_t)x % 16 || x_col_bytes % 16)
         return fail(MLZC_ERR_INVALID, "Q4_K: weights and activations must be 16-byte aligned");
@@ -439,6 +399,8 @@ int launch_q4k_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K, cons
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
+    if (N <= 8 && q4k_ring_applicable(M, K, N))
+        return launch_q4k_ring(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
     if (N <= 8) {
         const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
         if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);

@@ -158,7 +158,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
         }
         return MLZC_OK;
     }
-    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
+    if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
     if (w_type == MLZC_TYPE_F16 && gemv_f16_mma_applicable(M, K, N, w, w_rs, x, x_cs))
         return launch_gemv_f16_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
     if (use_gemm(w_type, M, K, N, w, w_rs, x, x_cs, y, y_cs))
