@@ -65,8 +65,8 @@ size_t q4k_workspace_bytes(int64_t K, int64_t N);
 int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
                    void* ws, size_t ws_bytes, cudaStream_t s);
-// Decode-shaped Q4_K (N <= 2): persistent kernel fed by a TMA ring, activations converted
-// once per CTA into shared memory.
+// Decode-shaped Q4_K (N <= 2, or N <= 8 with many short rows): persistent kernel fed by a
+// TMA ring, activations converted once per CTA into shared memory.
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                     const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,

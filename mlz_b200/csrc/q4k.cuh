@@ -57,12 +57,19 @@ __device__ __forceinline__ RowScales row_scales(const uint4& hdr, int c) {
     return r;
 }
 
-// sc * q for the nibble pair (bytes 0 and 2 of w) of the low or high half.
+// (w & mask) | 0x64006400 as one LOP3 with the magic constant in a register (written as two
+// C operations, each with an immediate, it measured as two integer instructions per call).
+template <uint32_t kMask>
+__device__ __forceinline__ uint32_t nib_f16x2(uint32_t w) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "n"(kMask), "r"(0x64006400u));
+    return d;
+}
 __device__ __forceinline__ uint32_t deq_lo(uint32_t w, const RowScales& s) {
-    return h2u(__hfma2(u2h((w & 0x000F000Fu) | 0x64006400u), s.mul_lo, s.add_lo));
+    return h2u(__hfma2(u2h(nib_f16x2<0x000F000Fu>(w)), s.mul_lo, s.add_lo));
 }
 __device__ __forceinline__ uint32_t deq_hi(uint32_t w, const RowScales& s) {
-    return h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), s.mul_hi, s.add_hi));
+    return h2u(__hfma2(u2h(nib_f16x2<0x00F000F0u>(w)), s.mul_hi, s.add_hi));
 }
 
 }  // namespace q4k

@@ -367,9 +367,12 @@ int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
 }  // namespace
 
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N) {
-    // N <= 2: measured on B200 over the Llama-3.1-8B shapes, the per-CTA activation prep
-    // makes N >= 3 slower here than the register-prefetch decode kernel (N = 4: 51 vs 49 us)
-    if (N < 1 || N > 2 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
+    // Measured on B200 over the Llama-3.1-8B shapes: N <= 2 everywhere; 3 <= N <= 8 only
+    // for many rows and short rows (14336 x 4096, N = 4: 18.3 vs 22.1 us), because each CTA
+    // converts all of X for itself and with more columns or longer rows that prep costs more
+    // than the register-prefetch decode kernel loses.
+    if (N < 1 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
+    if (N > 2 && (M < 8192 || K > 4096)) return false;
     const int ncol = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8;
     return ring_smem_bytes(ncol, (int)(K / q4k::kQK)) <= 227 * 1024;
 }
