@@ -43,7 +43,8 @@ NCU_TRAFFIC = {
     ("c1", 1): (50.35e6 + 0.02e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_vec_kernel)"),
     ("c1", 4): (50.39e6 + 0.07e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel)"),
     ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
-    ("c3", 1): (33.07e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
+    ("c3", 1): (33.07e6, "profiles/q4k_ring_kernel_c3_14336x4096.md (14336x4096 launch; the 4096x14336 "
+                         "launch reads the same block bytes)"),
     ("c3", 16): (33.31e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
 }
 
@@ -213,7 +214,16 @@ class C3(Workload):
     SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
 
     def roofline_kernel(self, j):
-        return f"q4k_prep_kernel + q4k_mma_kernel, {self.SHAPES[j][0]}x{self.SHAPES[j][1]} (one call)"
+        m, k = self.SHAPES[j]
+        n = self.N
+        # the library's dispatch (q4k_ring_applicable / launch_q4k_mma)
+        if n <= 2 or (n <= 8 and m >= 8192 and k <= 4096):
+            kern = "q4k_ring_kernel"
+        elif n <= 8:
+            kern = "q4k_gemv_kernel"
+        else:
+            kern = "q4k_prep_kernel + q4k_mma_kernel"
+        return f"{kern}, {m}x{k} (one call)"
 
     def __init__(self, n, dev, gen):
         import torch
