@@ -29,32 +29,42 @@ struct RowScales {
     float d, dmin;
 };
 
-__device__ __forceinline__ RowScales row_scales(const uint4& hdr, int c) {
-    // scale bytes s[0..11] = hdr.y (s0-s3), hdr.z (s4-s7), hdr.w (s8-s11); this thread needs
-    // sub-blocks j = 2c, 2c+1, i.e. byte pair j' = 2 (c & 1), +1 of each word
-    const int sh = 16 * (c & 1);
-    const uint32_t A = (hdr.y >> sh) & 0xFFFFu, B = (hdr.z >> sh) & 0xFFFFu, Cw = (hdr.w >> sh) & 0xFFFFu;
-    uint32_t sc2, m2;
-    if (c < 2) {   // j < 4: sc = s[j] & 63, m = s[j+4] & 63
-        sc2 = A & 0x3F3Fu;
-        m2 = B & 0x3F3Fu;
-    } else {       // j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4
-        sc2 = (Cw & 0x0F0Fu) | ((A >> 2) & 0x3030u);
-        m2 = ((Cw >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
+// The scale constants of rows g (header h0) and g + 8 (header h1) for sub-blocks j = 2c,
+// 2c + 1.  Scale bytes s[0..11] = hdr.y (s0-s3), hdr.z (s4-s7), hdr.w (s8-s11); this
+// thread needs byte pair j' = 2 (c & 1), +1 of each word, and one byte permute per word
+// packs both rows' pairs into one register (row g in bytes 0-1, row g + 8 in bytes 2-3),
+// so the 6-bit unpack runs once for the two rows:
+//   j < 4:  sc = s[j] & 63, m = s[j+4] & 63
+//   j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4
+__device__ __forceinline__ void row_scales2(const uint4& h0, const uint4& h1, int c, RowScales& s0, RowScales& s1) {
+    const uint32_t sel = (c & 1) ? 0x7632u : 0x5410u;
+    const uint32_t A = __byte_perm(h0.y, h1.y, sel), B = __byte_perm(h0.z, h1.z, sel), Cw = __byte_perm(h0.w, h1.w, sel);
+    uint32_t sc, m;
+    if (c < 2) {
+        sc = A & 0x3F3F3F3Fu;
+        m = B & 0x3F3F3F3Fu;
+    } else {
+        sc = (Cw & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u);
+        m = ((Cw >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u);
     }
     const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-    const __half2 sch = __hsub2(u2h(__byte_perm(sc2, 0x6464u, 0x5140)), k1024);   // (sc_2c, sc_2c+1)
-    RowScales r;
-    r.mpair = h2u(__hsub2(u2h(__byte_perm(m2, 0x6464u, 0x5140)), k1024));          // (m_2c, m_2c+1)
-    const __half2 lo = __low2half2(sch), hi = __high2half2(sch);
-    r.mul_lo = lo;
-    r.add_lo = __hmul2(lo, __float2half2_rn(-1024.0f));
-    r.mul_hi = __hmul2(hi, __float2half2_rn(0.0625f));
-    r.add_hi = __hmul2(hi, __float2half2_rn(-64.0f));
-    const __half2 dd = u2h(hdr.x);
-    r.d = __low2float(dd);
-    r.dmin = __high2float(dd);
-    return r;
+    const uint32_t selr[2] = {0x5140u, 0x5342u};
+    RowScales* out[2] = {&s0, &s1};
+    const uint4* hd[2] = {&h0, &h1};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const __half2 sch = __hsub2(u2h(__byte_perm(sc, 0x6464u, selr[r])), k1024);
+        RowScales& o = *out[r];
+        o.mpair = h2u(__hsub2(u2h(__byte_perm(m, 0x6464u, selr[r])), k1024));
+        const __half2 lo = __low2half2(sch), hi = __high2half2(sch);
+        o.mul_lo = lo;
+        o.add_lo = __hmul2(lo, __float2half2_rn(-1024.0f));
+        o.mul_hi = __hmul2(hi, __float2half2_rn(0.0625f));
+        o.add_hi = __hmul2(hi, __float2half2_rn(-64.0f));
+        const __half2 dd = u2h(hd[r]->x);
+        o.d = __low2float(dd);
+        o.dmin = __high2float(dd);
+    }
 }
 
 // (w & mask) | 0x64006400 as one LOP3 with the magic constant in a register (written as two

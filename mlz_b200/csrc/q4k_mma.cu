@@ -41,7 +41,6 @@ using q4k::RowScales;
 using q4k::deq_hi;
 using q4k::deq_lo;
 using q4k::h2u;
-using q4k::row_scales;
 
 constexpr int kQK = q4k::kQK;
 constexpr int kQ4KBytes = q4k::kBlockBytes;
@@ -126,9 +125,9 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
 #pragma unroll
             for (int i = 0; i < 4; ++i) nxt[i] = load_row_block(rowp[i] + (size_t)kn * kQ4KBytes, q4);
         }
-        RowScales sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = row_scales(cur[i].hdr, q4);
+        RowScales sc[4];   // rows g, g + 8 of tile 0, then of tile 1
+        q4k::row_scales2(cur[0].hdr, cur[1].hdr, q4, sc[0], sc[1]);
+        q4k::row_scales2(cur[2].hdr, cur[3].hdr, q4, sc[2], sc[3]);
 
         float acc[2][4] = {};
         float S[2] = {0.0f, 0.0f};
@@ -289,9 +288,9 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
         uint4 xp[2][NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) xp[0][nt] = ptx::ld_act(xfrag[nt]);
-        RowScales sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = row_scales(cur[i].hdr, q4);
+        RowScales sc[4];   // rows g, g + 8 of tile 0, then of tile 1
+        q4k::row_scales2(cur[0].hdr, cur[1].hdr, q4, sc[0], sc[1]);
+        q4k::row_scales2(cur[2].hdr, cur[3].hdr, q4, sc[2], sc[3]);
 
         float acc[NT][2][4] = {};
 #pragma unroll

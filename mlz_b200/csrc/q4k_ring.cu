@@ -46,7 +46,6 @@ using ptx::mma16816;
 using q4k::deq_hi;
 using q4k::deq_lo;
 using q4k::h2u;
-using q4k::row_scales;
 using q4k::RowScales;
 
 constexpr int kRWarps = 8;                                 // consumer warps
@@ -248,7 +247,8 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
                 const uint4 h0 = lds128(r0), h1 = lds128(r1);
                 const uint4 a0w = lds128(r0 + 16 + 32 * q4), b0w = lds128(r0 + 32 + 32 * q4);
                 const uint4 a1w = lds128(r1 + 16 + 32 * q4), b1w = lds128(r1 + 32 + 32 * q4);
-                const RowScales s0 = row_scales(h0, q4), s1 = row_scales(h1, q4);
+                RowScales s0, s1;
+                q4k::row_scales2(h0, h1, q4, s0, s1);
                 const uint4* xb = xfr + ((size_t)kb * 8 * 4 + q4) * NCOL + (colv ? g : 0);
                 float acc[4][4] = {};
 #pragma unroll
