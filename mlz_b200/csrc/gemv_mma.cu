@@ -64,8 +64,14 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
 #pragma unroll
         for (int h = 0; h < 2; ++h) wrow[t][h] = W + (size_t)min(m0 + 16 * t + 8 * h + g, M - 1) * w_rs + 16 * q4;
     const char* xcol[NT];
+    bool xok[NT];   // this lane's B column is a real one
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) xcol[nt] = X + (size_t)min(n0 + 8 * nt + g, N - 1) * x_cs + 32 * q4;
+    for (int nt = 0; nt < NT; ++nt) {
+        // with one column tile the lanes past N load nothing (N = 2: 6 of 8 lanes; measured
+        // 11.7 -> 10.6 us on 8192 x 3072); with two tiles (N > 8) the predicate measured slower
+        xok[nt] = NT > 1 || n0 + 8 * nt + g < N;
+        xcol[nt] = X + (size_t)min(n0 + 8 * nt + g, N - 1) * x_cs + 32 * q4;
+    }
 
     ptx::pdl_launch_dependents();
     if (!early) ptx::pdl_wait();
@@ -98,8 +104,8 @@ gemv_f16_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int K, const
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float4* xp = reinterpret_cast<const float4*>(xcol[nt] + (size_t)c * (kChunkK * 4));
-                xv[u][nt][0] = ok ? ptx::ld_act(xp) : make_float4(0.f, 0.f, 0.f, 0.f);
-                xv[u][nt][1] = ok ? ptx::ld_act(xp + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[u][nt][0] = ok && xok[nt] ? ptx::ld_act(xp) : make_float4(0.f, 0.f, 0.f, 0.f);
+                xv[u][nt][1] = ok && xok[nt] ? ptx::ld_act(xp + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
 #pragma unroll
