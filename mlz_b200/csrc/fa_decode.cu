@@ -633,25 +633,13 @@ int make_plan(const mlzc_fa_desc* d, FaPlan* out) {
     return MLZC_OK;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 kv_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
 // 4-d f16 map of a K or V tensor (ggml dims [D, n_kv, Hkv, B], byte strides nb[1..3]) with
 // 64 x 64 boxes in the 128-byte swizzle (the layout tile_addr() reads).  A dimension with
 // stride 0 (one K/V shared by every head or sequence) gets extent 1 in the map and its
 // coordinate multiplier (*hmul, *bmul) is 0; a tensor map cannot hold a 0 stride.
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, int64_t hkv, int64_t B, const size_t* nb,
                   int* hmul, int* bmul) {
-    auto enc = kv_encoder();
+    auto enc = tensor_map_encoder();
     if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     if (nb[1] == 0) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V with a 0 key stride");
     const bool hb = (hkv == 1 || nb[2] == 0), bb = (B == 1 || nb[3] == 0);

@@ -34,7 +34,6 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
-#include <mutex>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -474,24 +473,10 @@ __global__ void narrow_f16_kernel(const char* x, size_t x_cs, int N, int K, uint
 
 // ------------------------------------------------------------------ host side
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::once_flag g_encode_once;
-
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-    std::call_once(g_encode_once, [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    });
-    return g_encode;
-}
-
 // 2-D f16 tensor map: rows of `inner` elements, `rows` rows `row_bytes` apart; box
 // `box_rows` x 64 elements with 128-byte swizzle.
 int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
-    auto enc = encoder();
+    auto enc = tensor_map_encoder();
     if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {row_bytes};

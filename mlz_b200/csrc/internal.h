@@ -1,6 +1,8 @@
 // internal.h -- shared declarations of the mlzc library (host and device side).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -34,6 +36,9 @@ struct DeviceCtx {
 DeviceCtx* device_ctx(int device);
 // Context of the calling thread's current device.
 DeviceCtx* current_ctx();
+
+// The driver's cuTensorMapEncodeTiled (looked up once), or nullptr if the driver lacks it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Counts one kernel launch (read by mlzc_launch_count).
 void count_launch(int n = 1);

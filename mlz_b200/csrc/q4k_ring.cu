@@ -305,18 +305,6 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
 // Resident CTAs of q4k_ring_kernel<NCOL> with `smem` bytes, over all SMs (the kernel's
 // shared-memory limit is raised to the device's opt-in maximum once per device; occupancy
 // is queried once per device and size).
@@ -382,7 +370,7 @@ int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     if (!q4k_ring_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
     if ((uintptr_t)w % 16 || w_row_bytes % 16 || (uintptr_t)x % 16 || x_col_bytes % 16)
         return fail(MLZC_ERR_INVALID, "Q4_K: weights and activations must be 16-byte aligned");
-    auto enc = map_encoder();
+    auto enc = tensor_map_encoder();
     if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     RingParams p{};
     p.x = reinterpret_cast<const char*>(x);
