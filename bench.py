@@ -116,8 +116,12 @@ class C1(Workload):
     bound = "hbm"
 
     def roofline_kernel(self, j):
-        return ("gemv_vec_kernel (one call, one launch)" if self.N < 8 else
-                "one mul_mat call: narrow_f16_kernel + gemm_f16_tc_kernel")
+        # the library's dispatch (gemv_f16_mma_applicable, use_gemm)
+        if self.N == 1:
+            return "gemv_vec_kernel (one call, one launch)"
+        if self.N <= 16:
+            return "gemv_f16_mma_kernel (one call, one launch)"
+        return "one mul_mat call: narrow_f16_kernel + gemm_f16_tc_kernel"
 
     def __init__(self, n, dev, gen):
         import torch
