@@ -201,13 +201,14 @@ q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const 
     }
 }
 
-// Activation prep (N > 8): X (N x K f32) rounded to f16 once, in the order the main
-// kernel's B fragments use, plus the sub-block sums as f16 hi + lo pairs.  One thread per
-// (column, block, quad slot q, k-step s = 8 hi + wi): the values e = 64q + 32 hi + 4 wi +
-// {0, 2} go to b0 and {1, 3} to b1; the 8 k-steps of a half (16 consecutive threads per
-// (column, block, q): lanes 0-7 hi = 0, 8-15 hi = 1) sum S_2q+hi by shuffles.  Columns past
-// N are zero.
-//   xf: [n-tile][block][q][g][16 k-steps] uint2 (b0, b1)   (g = column within the 8-column tile)
+// Activation prep: X (N x K f32) rounded to f16 once, in the order the B fragments use,
+// plus the sub-block sums as f16 hi + lo pairs.  One thread per (column, block, quad slot
+// q, k-step s = 8 hi + wi): the values e = 64q + 32 hi + 4 wi + {0, 2} go to b0 and {1, 3}
+// to b1; the 8 k-steps of a half (16 consecutive threads per (column, block, q): lanes 0-7
+// hi = 0, 8-15 hi = 1) sum S_2q+hi by shuffles.  Columns past N are zero.
+//   xf: [n-tile][block][k-step pair p][q][g] uint4 = (b0, b1) of steps 2p, 2p + 1
+//       (g = column within the 8-column tile): the 32 lanes (g, q) of a warp read one
+//       k-step pair of a block as 512 contiguous bytes, from global or shared memory
 //   xs: [n-tile][block][q][g] uint2 (hi pair, lo pair)
 __global__ void q4k_prep_kernel(const char* X, size_t x_cs, int N, int n_pad, int nblk,
                                 uint2* __restrict__ xf, uint2* __restrict__ xs) {
@@ -223,10 +224,11 @@ __global__ void q4k_prep_kernel(const char* X, size_t x_cs, int N, int n_pad, in
         const int nt = n >> 3, g = n & 7;
         const int hi = st >> 3, wi = st & 7;
         const int64_t slot = (((int64_t)nt * nblk + kb) * 4 + q) * 8 + g;
+        const int64_t fslot = ((((int64_t)nt * nblk + kb) * 8 + (st >> 1)) * 4 + q) * 8 + g;
         const float4* src = reinterpret_cast<const float4*>(X + (size_t)(n < N ? n : 0) * x_cs) + (size_t)kb * (kQK / 4) + 16 * q;
         const float4 v = n < N ? ptx::ld_act(src + 8 * hi + wi) : make_float4(0.f, 0.f, 0.f, 0.f);
         const __half2 b0 = __floats2half2_rn(v.x, v.z), b1 = __floats2half2_rn(v.y, v.w);
-        xf[slot * 16 + st] = make_uint2(h2u(b0), h2u(b1));
+        xf[fslot * 2 + (st & 1)] = make_uint2(h2u(b0), h2u(b1));
         const float2 f0 = __half22float2(b0), f1 = __half22float2(b1);
         float S = (f0.x + f0.y) + (f1.x + f1.y);
         S += __shfl_xor_sync(0xffffffffu, S, 1);
@@ -282,7 +284,7 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int64_t slot = (((int64_t)(ntile0 + nt) * nblk + kb) * 4 + q4) * 8 + g;
-            xfrag[nt] = reinterpret_cast<const uint4*>(xf + slot * 16);
+            xfrag[nt] = reinterpret_cast<const uint4*>(xf) + ((((int64_t)(ntile0 + nt) * nblk + kb) * 8) * 4 + q4) * 8 + g;
             sv[nt] = ptx::ld_act(xs + slot);
         }
         uint4 xp[2][NT];
@@ -297,7 +299,7 @@ q4k_mma_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const u
         for (int p = 0; p < 8; ++p) {          // k-step pairs 2p, 2p+1
             if (p < 7) {
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) xp[(p + 1) & 1][nt] = ptx::ld_act(xfrag[nt] + p + 1);
+                for (int nt = 0; nt < NT; ++nt) xp[(p + 1) & 1][nt] = ptx::ld_act(xfrag[nt] + (p + 1) * 32);
             }
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -372,7 +374,8 @@ struct Q4kWs {
 
 Q4kWs q4k_ws(int64_t K, int64_t N) {
     Q4kWs w;
-    w.n_pad = (int)((N + 15) / 16 * 16);   // whole 8-column tiles, and pairs of them
+    // whole 8-column tiles; pairs of them for the batched kernel (N > 8)
+    w.n_pad = N <= 8 ? 8 : (int)((N + 15) / 16 * 16);
     w.nblk = (int)(K / kQK);
     w.xf_bytes = ((size_t)w.n_pad * w.nblk * 4 * 16 * sizeof(uint2) + 255) / 256 * 256;
     w.xs_bytes = ((size_t)w.n_pad * w.nblk * 4 * sizeof(uint2) + 255) / 256 * 256;
@@ -382,7 +385,8 @@ Q4kWs q4k_ws(int64_t K, int64_t N) {
 }  // namespace
 
 size_t q4k_workspace_bytes(int64_t K, int64_t N) {
-    if (N <= 8) return 0;
+    // prepared activations: the batched kernel (N > 8) and the shared-X ring (5 <= N <= 8)
+    if (N <= 2 || (N <= 8 && !q4k_ring_xg_applicable(1, K, N))) return 0;
     const Q4kWs w = q4k_ws(K, N);
     return w.xf_bytes + w.xs_bytes;
 }
@@ -398,9 +402,10 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
-    if (N <= 8 && q4k_ring_applicable(M, K, N))
+    if (q4k_ring_applicable(M, K, N))
         return launch_q4k_ring(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
-    if (N <= 8) {
+    const bool xg = q4k_ring_xg_applicable(M, K, N);
+    if (N <= 8 && !xg) {
         const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
         if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
         MLZC_CUDA_TRY(launch_pdl(q4k_gemv_kernel, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, (int)(K / kQK), xc,
@@ -420,6 +425,8 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
                                  xf, xs));
         count_launch();
     }
+    if (xg)
+        return launch_q4k_ring_xg(c, w, w_row_bytes, M, K, reinterpret_cast<const uint4*>(xf), xs, N, y, y_col_bytes, s);
     const dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + kQRows - 1) / kQRows));
     if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
     MLZC_CUDA_TRY(launch_pdl(q4k_mma_kernel<2>, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, q.nblk, xf, xs,

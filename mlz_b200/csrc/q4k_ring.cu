@@ -65,6 +65,8 @@ struct RingParams {
     size_t y_cs;
     int M, nblk, N, tiles;       // tiles = ceil(M / 16)
     int early;                   // 1: the producer may load blocks before pdl_wait()
+    const uint4* xf;             // prepared B fragments (q4k_prep_kernel layout), shared-X form only
+    const uint2* xs;             // prepared sub-block sums, shared-X form only
     unsigned int* err;           // device error word (bounded waits)
     CUtensorMap tm_w;            // W as 8-byte elements: [M][nblk * 18], box 18 x 16
 };
@@ -104,6 +106,40 @@ __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int 
     }
 }
 
+// Producer (one thread) of both ring kernels: the stages of this CTA's tiles (t =
+// blockIdx.x, + gridDim.x, ...), 16 rows x 8 blocks each, into the ring with TMA.
+template <int STAGES>
+__device__ __forceinline__ void ring_producer(const RingParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                              volatile int* abort_flag, int my_tiles, int nst) {
+    const int G = gridDim.x;
+    if (!p.early) ptx::pdl_wait();
+    const int total = my_tiles * nst;
+    int issued = 0;
+    for (int it = 0; it < total; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        // the consumers read the stage with generic loads: order them before the TMA
+        // (async proxy) overwrites it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const int ti = it / nst, si = it % nst;
+        const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
+        const int kb0 = si * kStageBlocks;   // blocks past the row end are zero-filled by the map
+        const uint32_t fb = ptx::smem_u32(&full[s]);
+        const uint32_t st = ptx::smem_u32(ring + (size_t)s * kStageBytes);
+        ptx::mbar_expect_tx(fb, kStageBytes);
+        tma_load_2d(st, &p.tm_w, fb, kb0 * kU64PerBlock, m0);
+        issued = it + 1;
+    }
+    // no copy may still be landing when the CTA exits (consumers that gave up do not
+    // wait for theirs): the last fill of every slot has completed (bounded)
+    volatile int no_abort = 0;
+    for (int s = 0; s < STAGES && s < issued; ++s) {
+        const int last = s + (issued - 1 - s) / STAGES * STAGES;
+        ptx::mbar_wait(ptx::smem_u32(&full[s]), (last / STAGES) & 1, &no_abort, p.err);
+    }
+}
+
 // NCOL: activation columns held in shared memory (N rounded up to 1, 2, 4 or 8).
 template <int NCOL>
 __global__ void __launch_bounds__(kRThreads, 2)
@@ -138,37 +174,7 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
     const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
 
     if (warp == kRWarps) {
-        // ---------------- producer: Q4_K blocks of this CTA's tiles into the ring
-        if (lane == 0) {
-            if (!p.early) ptx::pdl_wait();
-            const int total = my_tiles * nst;
-            int issued = 0;
-            for (int it = 0; it < total; ++it) {
-                const int s = it % kStages;
-                const uint32_t ph = (it / kStages) & 1;
-                if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
-                // the consumers read the stage with generic loads: order them before the TMA
-                // (async proxy) overwrites it
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                const int ti = it / nst, si = it % nst;
-                const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
-                const int kb0 = si * kStageBlocks;
-                const int nb = min(kStageBlocks, p.nblk - kb0);
-                const uint32_t fb = ptx::smem_u32(&full[s]);
-                const uint32_t st = ptx::smem_u32(ring + (size_t)s * kStageBytes);
-                (void)nb;
-                ptx::mbar_expect_tx(fb, kStageBytes);
-                tma_load_2d(st, &p.tm_w, fb, kb0 * kU64PerBlock, m0);
-                issued = it + 1;
-            }
-            // no copy may still be landing when the CTA exits (consumers that gave up do not
-            // wait for theirs): the last fill of every slot has completed (bounded)
-            volatile int no_abort = 0;
-            for (int s = 0; s < kStages && s < issued; ++s) {
-                const int last = s + (issued - 1 - s) / kStages * kStages;
-                ptx::mbar_wait(ptx::smem_u32(&full[s]), (last / kStages) & 1, &no_abort, p.err);
-            }
-        }
+        if (lane == 0) ring_producer<kStages>(p, ring, full, empty, abort_flag, my_tiles, nst);
         return;
     }
 
@@ -305,34 +311,197 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
     }
 }
 
-// Resident CTAs of q4k_ring_kernel<NCOL> with `smem` bytes, over all SMs (the kernel's
-// shared-memory limit is raised to the device's opt-in maximum once per device; occupancy
-// is queried once per device and size).
-template <int NCOL>
-int ring_slots(size_t smem, int* out) {
+// Shared-X form (5 <= N <= 8, rows of up to 35 blocks): the activations were prepared once for the
+// call by q4k_prep_kernel; each CTA bulk-copies the NT column tiles' fragments and sums
+// (4 KB + 256 B per tile and block) into shared memory at its start, then runs the ring as
+// above with NT 8-column MMA tiles sharing every dequantised A fragment.
+// One column tile: 2 stages and two CTAs per SM (16 consumer warps, the same bytes in flight
+// per SM as one CTA with 4); two tiles: 4 stages, one CTA.
+constexpr int xg_stages(int nt) { return nt == 1 ? 2 : 4; }
+
+constexpr size_t ring_xg_smem_bytes(int nt, int nblk) {
+    return 1024 + (size_t)xg_stages(nt) * kStageBytes + (size_t)nt * nblk * (4096 + 256) +
+           2 * (size_t)kRWarps * kTileRows * 8 * nt * 4 + (2 * xg_stages(nt) + 1) * 8 + 16;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kRThreads, NT == 1 ? 2 : 1)
+q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
+    constexpr int kStagesX = xg_stages(NT);
+    constexpr int kRedX = kRWarps * kTileRows * 8 * NT;   // one set of the warps' partial tiles
+    extern __shared__ uint8_t q4x_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4x_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem;
+    uint4* xfr = reinterpret_cast<uint4*>(smem + (size_t)kStagesX * kStageBytes);               // [t][kb][pair][q][g]
+    uint2* xsum = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xfr) + (size_t)NT * p.nblk * 4096);   // [t][kb][q][g]
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsum) + (size_t)NT * p.nblk * 256);
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRedX);
+    uint64_t* empty = full + kStagesX;
+    uint64_t* xbar = empty + kStagesX;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(xbar + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesX; ++s) {
+            ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+            ptx::mbar_init(ptx::smem_u32(&empty[s]), kRWarps);
+        }
+        ptx::mbar_init(ptx::smem_u32(xbar), 1);
+        *abort_flag = 0;
+        ptx::mbar_init_fence();
+    }
+    __syncthreads();
+    ptx::pdl_launch_dependents();
+
+    const int G = gridDim.x;
+    const int nst = (p.nblk + kStageBlocks - 1) / kStageBlocks;
+    const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    if (warp == kRWarps) {
+        if (lane == 0) ring_producer<kStagesX>(p, ring, full, empty, abort_flag, my_tiles, nst);
+        return;
+    }
+
+    // ---------------- consumers
+    ptx::pdl_wait();   // the prepared activations come from the previous kernel
+    const uint32_t xb_bar = ptx::smem_u32(xbar);
+    const uint32_t fbytes = (uint32_t)NT * p.nblk * 4096, sbytes = (uint32_t)NT * p.nblk * 256;
+    if (threadIdx.x == 0) {
+        // tiles 0 .. NT-1 of the workspace are contiguous (its layout is [tile][block][...])
+        ptx::mbar_expect_tx(xb_bar, fbytes + sbytes);
+        ptx::bulk_load(ptx::smem_u32(xfr), p.xf, fbytes, xb_bar);
+        ptx::bulk_load(ptx::smem_u32(xsum), p.xs, sbytes, xb_bar);
+    }
+    bool ok = ptx::mbar_wait(xb_bar, 0, abort_flag, p.err);
+
+    const int g = lane >> 2;
+    const int q4 = lane & 3;
+    const uint32_t ring_u32 = ptx::smem_u32(ring);
+    int it = 0;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+        const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
+        float y[NT][4];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) y[t][0] = y[t][1] = y[t][2] = y[t][3] = 0.0f;
+        for (int si = 0; si < nst; ++si, ++it) {
+            const int s = it % kStagesX;
+            const uint32_t ph = (it / kStagesX) & 1;
+            if (ok && !ptx::mbar_wait(ptx::smem_u32(&full[s]), ph, abort_flag, p.err)) ok = false;
+            if (!ok) continue;
+            const int kb = si * kStageBlocks + warp;
+            if (kb < p.nblk) {
+                const uint32_t bb = ring_u32 + (uint32_t)s * kStageBytes + (uint32_t)warp * q4k::kBlockBytes;
+                const uint32_t r0 = bb + (uint32_t)g * (kStageBlocks * q4k::kBlockBytes), r1 = r0 + 8 * (kStageBlocks * q4k::kBlockBytes);
+                const uint4 h0 = lds128(r0), h1 = lds128(r1);
+                const uint4 a0w = lds128(r0 + 16 + 32 * q4), b0w = lds128(r0 + 32 + 32 * q4);
+                const uint4 a1w = lds128(r1 + 16 + 32 * q4), b1w = lds128(r1 + 32 + 32 * q4);
+                RowScales s0, s1;
+                q4k::row_scales2(h0, h1, q4, s0, s1);
+                const uint4* xb[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) xb[t] = xfr + (size_t)(t * p.nblk + kb) * 256 + q4 * 8 + g;
+                float acc[NT][2][4];
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) acc[t][c][0] = acc[t][c][1] = acc[t][c][2] = acc[t][c][3] = 0.0f;
+#pragma unroll
+                for (int pr = 0; pr < 8; ++pr) {
+                    uint4 xv[NT];
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) xv[t] = xb[t][pr * 32];
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const int stp = 2 * pr + h2, wi = stp & 7;
+                        const uint32_t w0 = word_of(a0w, b0w, wi), w1 = word_of(a1w, b1w, wi);
+                        uint32_t a0, a1, a2, a3;
+                        if (stp < 8) {
+                            a0 = deq_lo(w0, s0);
+                            a1 = deq_lo(w1, s1);
+                            a2 = deq_lo(w0 >> 8, s0);
+                            a3 = deq_lo(w1 >> 8, s1);
+                        } else {
+                            a0 = deq_hi(w0, s0);
+                            a1 = deq_hi(w1, s1);
+                            a2 = deq_hi(w0 >> 8, s0);
+                            a3 = deq_hi(w1 >> 8, s1);
+                        }
+#pragma unroll
+                        for (int t = 0; t < NT; ++t)
+                            mma16816(acc[t][h2], a0, a1, a2, a3, h2 ? xv[t].z : xv[t].x, h2 ? xv[t].w : xv[t].y);
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    // min term: sum_j m_j S_j with S as f16 hi + lo
+                    const uint2 sv = xsum[(size_t)(t * p.nblk + kb) * 32 + q4 * 8 + g];
+                    float mn[4] = {0.f, 0.f, 0.f, 0.f}, ml[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(mn, s0.mpair, s1.mpair, 0u, 0u, sv.x, 0u);
+                    mma16816(ml, s0.mpair, s1.mpair, 0u, 0u, sv.y, 0u);
+                    y[t][0] += s0.d * (acc[t][0][0] + acc[t][1][0]) - s0.dmin * (mn[0] + ml[0]);
+                    y[t][1] += s0.d * (acc[t][0][1] + acc[t][1][1]) - s0.dmin * (mn[1] + ml[1]);
+                    y[t][2] += s1.d * (acc[t][0][2] + acc[t][1][2]) - s1.dmin * (mn[2] + ml[2]);
+                    y[t][3] += s1.d * (acc[t][0][3] + acc[t][1][3]) - s1.dmin * (mn[3] + ml[3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
+        }
+        // ---- the eight warps' partial tiles -> rows of Y, summed in warp order
+        float* rb = red + (ti & 1) * kRedX;
+        float* mine = rb + warp * (kTileRows * 8 * NT);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            mine[t * 128 + g * 8 + 2 * q4] = y[t][0];
+            mine[t * 128 + g * 8 + 2 * q4 + 1] = y[t][1];
+            mine[t * 128 + (g + 8) * 8 + 2 * q4] = y[t][2];
+            mine[t * 128 + (g + 8) * 8 + 2 * q4 + 1] = y[t][3];
+        }
+        consumer_sync();
+        const int tid = threadIdx.x;
+        if (ok && tid < kTileRows * p.N && !*abort_flag) {
+            const int r = tid & (kTileRows - 1), c = tid >> 4;
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kRWarps; ++w) v += rb[w * (kTileRows * 8 * NT) + (c >> 3) * 128 + r * 8 + (c & 7)];
+            if (m0 + r < p.M) reinterpret_cast<float*>(p.y + (size_t)c * p.y_cs)[m0 + r] = v;
+        }
+    }
+    if (threadIdx.x == 0) {
+        // the activation copy has landed before the CTA exits, even if a wait gave up
+        volatile int no_abort = 0;
+        ptx::mbar_wait(xb_bar, 0, &no_abort, p.err);
+    }
+}
+
+// Resident CTAs of a ring kernel with `smem` bytes, over all SMs (the kernel's shared-memory
+// limit is raised to the device's opt-in maximum once per device; occupancy is queried once
+// per device and size; one cache per kernel instantiation).
+template <typename Kern>
+int ring_slots(Kern kernel, size_t smem, int* out) {
     static std::mutex mu;
-    static std::map<std::tuple<int, size_t>, int> cache;
-    static bool attr_set[64] = {};
+    static std::map<std::tuple<const void*, int, size_t>, int> cache;
+    static std::map<std::tuple<const void*, int>, bool> attr_set;
     int dev = 0;
     MLZC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(MLZC_ERR_INVALID, "Q4_K ring: device %d beyond 64", dev);
+    const void* key = reinterpret_cast<const void*>(kernel);
     std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find({dev, smem});
+    auto it = cache.find({key, dev, smem});
     if (it != cache.end()) {
         *out = it->second;
         return MLZC_OK;
     }
-    if (!attr_set[dev]) {
+    if (!attr_set[{key, dev}]) {
         int optin = 0;
         MLZC_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-        MLZC_CUDA_TRY(cudaFuncSetAttribute(q4k_ring_kernel<NCOL>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
-        attr_set[dev] = true;
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+        attr_set[{key, dev}] = true;
     }
     int occ = 0, sms = 0;
-    MLZC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, q4k_ring_kernel<NCOL>, kRThreads, smem));
+    MLZC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kRThreads, smem));
     MLZC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     if (occ < 1) return fail(MLZC_ERR_CUDA, "Q4_K ring kernel does not fit on an SM");
-    cache[{dev, smem}] = occ * sms;
+    cache[{key, dev, smem}] = occ * sms;
     *out = occ * sms;
     return MLZC_OK;
 }
@@ -341,7 +510,7 @@ template <int NCOL>
 int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
     const size_t smem = ring_smem_bytes(NCOL, p.nblk);
     int slots = 0;
-    const int st = ring_slots<NCOL>(smem, &slots);
+    const int st = ring_slots(q4k_ring_kernel<NCOL>, smem, &slots);
     if (st != MLZC_OK) return st;
     // one CTA per resident slot (or per tile): with two CTAs per SM this keeps the tiles per
     // SM within one of each other
@@ -352,29 +521,27 @@ int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
     return MLZC_OK;
 }
 
-}  // namespace
-
-bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N) {
-    // Measured on B200 over the Llama-3.1-8B shapes: N <= 2 everywhere; 3 <= N <= 8 only
-    // for many rows and short rows (14336 x 4096, N = 4: 18.3 vs 22.1 us), because each CTA
-    // converts all of X for itself and with more columns or longer rows that prep costs more
-    // than the register-prefetch decode kernel loses.
-    if (N < 1 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
-    if (N > 2 && (M < 8192 || K > 4096)) return false;
-    const int ncol = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8;
-    return ring_smem_bytes(ncol, (int)(K / q4k::kQK)) <= 227 * 1024;
+template <int NT>
+int launch_ring_xg(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
+    const size_t smem = ring_xg_smem_bytes(NT, p.nblk);
+    int slots = 0;
+    const int st = ring_slots(q4k_ring_xg_kernel<NT>, smem, &slots);
+    if (st != MLZC_OK) return st;
+    const int grid = std::min(p.tiles, slots);
+    p.err = c->err;
+    MLZC_CUDA_TRY(launch_pdl(q4k_ring_xg_kernel<NT>, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
+    count_launch();
+    return MLZC_OK;
 }
 
-int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
-    if (!q4k_ring_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
-    if ((uintptr_t)w % 16 || w_row_bytes % 16 || (uintptr_t)x % 16 || x_col_bytes % 16)
-        return fail(MLZC_ERR_INVALID, "Q4_K: weights and activations must be 16-byte aligned");
+// Everything but the activation source (p.x / p.xf, p.xs), which the two forms set.
+int make_ring_params(const void* w, size_t w_row_bytes, int64_t M, int64_t K, int64_t N, float* y, size_t y_col_bytes,
+                     RingParams* out) {
+    if ((uintptr_t)w % 16 || w_row_bytes % 16) return fail(MLZC_ERR_INVALID, "Q4_K: weights must be 16-byte aligned");
     auto enc = tensor_map_encoder();
     if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    RingParams p{};
-    p.x = reinterpret_cast<const char*>(x);
-    p.x_cs = x_col_bytes;
+    RingParams& p = *out;
+    p = RingParams{};
     p.y = reinterpret_cast<char*>(y);
     p.y_cs = y_col_bytes;
     p.M = (int)M;
@@ -390,10 +557,55 @@ int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MLZC_ERR_INVALID, "Q4_K ring: weight rows not expressible as a TMA map (%d)", (int)r);
+    return MLZC_OK;
+}
+
+}  // namespace
+
+bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N) {
+    // Measured on B200 over the Llama-3.1-8B shapes (us, this form / the best other):
+    // N <= 2 everywhere; N = 3..4 only for many short rows (14336 x 4096, N = 4: 18.3 / 21.2;
+    // 4096 x 4096: 8.6 / 6.5), because each CTA converts all of X for itself; N >= 5 goes to
+    // the shared-X form below.
+    if (N < 1 || N > 4 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
+    if (N > 2 && (M < 8192 || K > 4096)) return false;
+    const int ncol = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8;
+    return ring_smem_bytes(ncol, (int)(K / q4k::kQK)) <= 227 * 1024;
+}
+
+int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
+    if (!q4k_ring_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
+    if ((uintptr_t)x % 16 || x_col_bytes % 16) return fail(MLZC_ERR_INVALID, "Q4_K: activations must be 16-byte aligned");
+    RingParams p;
+    const int st = make_ring_params(w, w_row_bytes, M, K, N, y, y_col_bytes, &p);
+    if (st != MLZC_OK) return st;
+    p.x = reinterpret_cast<const char*>(x);
+    p.x_cs = x_col_bytes;
     if (N <= 1) return launch_ring<1>(c, p, s);
     if (N <= 2) return launch_ring<2>(c, p, s);
     if (N <= 4) return launch_ring<4>(c, p, s);
     return launch_ring<8>(c, p, s);
+}
+
+bool q4k_ring_xg_applicable(int64_t M, int64_t K, int64_t N) {
+    // Measured (us, this form / the best other): N = 8: 4096 x 4096 8.0 / 9.5, 14336 x 4096
+    // 19.4 / 31.2; N = 4 loses to the forms above (8.0 / 6.5, 19.2 / 18.3) and a second
+    // column tile (N = 16) to the batched kernel (11.3 / 9.2, 31.5 / 29.1).
+    if (N < 5 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
+    return ring_xg_smem_bytes(1, (int)(K / q4k::kQK)) <= 227 * 1024;
+}
+
+int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                       const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
+    if (!q4k_ring_xg_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
+    if ((uintptr_t)xf % 16 || (uintptr_t)xs % 16) return fail(MLZC_ERR_INVALID, "Q4_K ring: workspace not 16-byte aligned");
+    RingParams p;
+    const int st = make_ring_params(w, w_row_bytes, M, K, N, y, y_col_bytes, &p);
+    if (st != MLZC_OK) return st;
+    p.xf = xf;
+    p.xs = xs;
+    return launch_ring_xg<1>(c, p, s);
 }
 
 }  // namespace mlzc
