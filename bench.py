@@ -683,7 +683,10 @@ def mlz_arm(a):
         ach = sum(units_l) / (sum(per_launch_ms) * 1e-3) * 1e-12
     else:
         ach = units_l[jdom] / (per_launch_ms[jdom] * 1e-3) * w.unit_scale()
-    long_run = ms * 1e-3 > 1.0
+    # tensor peak: the sustained (power-capped) figure when the timed region ran under the
+    # power cap or for over a second -- the regime that figure was measured in -- else burst
+    power_capped = "sw_power_cap" in (clocks.get("reasons") or [])
+    long_run = ms * 1e-3 > 1.0 or power_capped
     if w.bound == "hbm":
         peak, peak_name = peaks["hbm_gbs"], "hbm_gbs"
     else:
@@ -691,8 +694,11 @@ def mlz_arm(a):
         peak_name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
     roofline = {"bound": w.bound, "achieved": ach, "peak": peak,
                 "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s", "frac": ach / peak, "traffic": None,
-                "peak_source": f"{peaks['source']} {peak_name}",
+                "peak_source": f"{peaks['source']} {peak_name}" + (" (sw_power_cap active in the timed region)"
+                                                                      if power_capped and w.bound != "hbm" else ""),
                 "kernel": w.roofline_kernel(jdom), "call_timing": call_timing}
+    if w.bound != "hbm":
+        roofline["frac_of_burst"] = ach / peaks["bf16_tflops"]
     tr = NCU_TRAFFIC.get((a.config, n))
     if tr is not None and not isinstance(w, C2):
         roofline["traffic"] = tr[0]
