@@ -223,7 +223,7 @@ class C3(Workload):
         # the library's dispatch (q4k_ring_applicable, q4k_ring_xg_applicable, launch_q4k_mma)
         if n <= 2 or (n <= 4 and m >= 8192 and k <= 4096):
             kern = "q4k_ring_kernel"
-        elif 5 <= n <= 8 and k // 256 <= 35:
+        elif 5 <= n <= 8 and k // 256 <= 42:
             kern = "q4k_prep_kernel + q4k_ring_xg_kernel"
         elif n <= 8:
             kern = "q4k_gemv_kernel"

@@ -76,7 +76,7 @@ bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                     const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
                     cudaStream_t s);
-// The same ring for 5 <= N <= 8 with rows of up to 35 blocks, fed by activations prepared once per call
+// The same ring for 5 <= N <= 8 with rows of up to 42 blocks, fed by activations prepared once per call
 // (q4k_prep_kernel's xf / xs) and bulk-copied into each CTA's shared memory.
 bool q4k_ring_xg_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,

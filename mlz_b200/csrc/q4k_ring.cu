@@ -311,7 +311,7 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
     }
 }
 
-// Shared-X form (5 <= N <= 8, rows of up to 35 blocks): the activations were prepared once for the
+// Shared-X form (5 <= N <= 8, rows of up to 42 blocks): the activations were prepared once for the
 // call by q4k_prep_kernel; each CTA bulk-copies the NT column tiles' fragments and sums
 // (4 KB + 256 B per tile and block) into shared memory at its start, then runs the ring as
 // above with NT 8-column MMA tiles sharing every dequantised A fragment.
