@@ -179,9 +179,11 @@ int launch_gemv_f16_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K,
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
-    // measured on B200 (8192 x 3072): more, smaller CTAs with two chunks in flight per warp
-    // beat deeper per-warp pipelines; beyond 16 columns the tcgen05 GEMM is faster
-    if (N <= 8) return launch_sk<1, 1, 2>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+    // measured on B200 (8192 x 3072, us for U = 2 / 3 / 4 chunks in flight per warp): N = 2
+    // 10.6 / 9.7 / 10.5, N = 4 10.9 / 10.0 / 10.2, N = 8 11.4 / 10.8 / 10.4; 16-row CTAs beat
+    // 32-row ones; beyond 16 columns the tcgen05 GEMM is faster
+    if (N <= 4) return launch_sk<1, 1, 3>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+    if (N <= 8) return launch_sk<1, 1, 4>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
     return launch_sk<2, 2, 2>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
 }
 

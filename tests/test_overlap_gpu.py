@@ -42,7 +42,7 @@ def _in_mode(mode, fn):
 
 
 @pytest.mark.parametrize("kind", ["f16", "f32", "q4k"])
-@pytest.mark.parametrize("N", [1, 4, 16, 64])
+@pytest.mark.parametrize("N", [1, 4, 8, 16, 64])
 def test_chained_mul_mat(dev, kind, N):
     import torch
     gen = torch.Generator(device=dev).manual_seed(9100 + N)
