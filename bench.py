@@ -224,7 +224,9 @@ class C3(Workload):
         if n <= 2 or (n <= 4 and m >= 8192 and k <= 4096):
             kern = "q4k_ring_kernel"
         elif 5 <= n <= 8 and k // 256 <= 42:
-            kern = "q4k_prep_kernel + q4k_ring_xg_kernel"
+            kern = "q4k_prep_kernel + q4k_ring_xg_kernel (resident X)"
+        elif 3 <= n <= 8 and k // 256 > 42:
+            kern = "q4k_prep_kernel + q4k_ring_xg_kernel (streaming X)"
         elif n <= 8:
             kern = "q4k_gemv_kernel"
         else:

@@ -82,6 +82,12 @@ bool q4k_ring_xg_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                        const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes,
                        cudaStream_t s);
+// The same with rows too long for a resident copy (3 <= N <= 8): each stage carries its
+// blocks' prepared activations.
+bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N);
+int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                       const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes,
+                       cudaStream_t s);
 
 // tcgen05/TMEM GEMM for F16 weights (activations narrowed to f16 in the workspace).
 size_t gemm_f16_workspace_bytes(int64_t M, int64_t K, int64_t N);

@@ -140,6 +140,50 @@ __device__ __forceinline__ void ring_producer(const RingParams& p, uint8_t* ring
     }
 }
 
+// Streaming shared-X stage: the 16 x 8-block weight box, then the 8 blocks' prepared B
+// fragments (4 KB each) and sub-block sums (256 B each) of the single column tile.
+constexpr uint32_t kXsStageBytes = kStageBytes + kStageBlocks * (4096 + 256);   // 53248
+constexpr int kXsStages = 2;
+
+// Producer of the streaming shared-X form: as ring_producer, and each stage also gets its
+// blocks' prepared activations by bulk copy from the workspace -- after pdl_wait(), since the
+// prep kernel wrote them (in the weights-first mode the first weight box goes out before it).
+__device__ __forceinline__ void ring_producer_xs(const RingParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                                 volatile int* abort_flag, int my_tiles, int nst) {
+    const int G = gridDim.x;
+    bool waited = !p.early;
+    if (waited) ptx::pdl_wait();
+    const int total = my_tiles * nst;
+    int issued = 0;
+    for (int it = 0; it < total; ++it) {
+        const int s = it % kXsStages;
+        const uint32_t ph = (it / kXsStages) & 1;
+        if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const int ti = it / nst, si = it % nst;
+        const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
+        const int kb0 = si * kStageBlocks;
+        const int nb = min(kStageBlocks, p.nblk - kb0);   // the fragment copies stop at the row end
+        const uint32_t fb = ptx::smem_u32(&full[s]);
+        const uint32_t st = ptx::smem_u32(ring + (size_t)s * kXsStageBytes);
+        ptx::mbar_expect_tx(fb, kStageBytes + (uint32_t)nb * (4096 + 256));
+        tma_load_2d(st, &p.tm_w, fb, kb0 * kU64PerBlock, m0);
+        if (!waited) {
+            ptx::pdl_wait();
+            waited = true;
+        }
+        ptx::bulk_load(st + kStageBytes, reinterpret_cast<const char*>(p.xf) + (size_t)kb0 * 4096, (uint32_t)nb * 4096, fb);
+        ptx::bulk_load(st + kStageBytes + kStageBlocks * 4096, reinterpret_cast<const char*>(p.xs) + (size_t)kb0 * 256,
+                       (uint32_t)nb * 256, fb);
+        issued = it + 1;
+    }
+    volatile int no_abort = 0;
+    for (int s = 0; s < kXsStages && s < issued; ++s) {
+        const int last = s + (issued - 1 - s) / kXsStages * kXsStages;
+        ptx::mbar_wait(ptx::smem_u32(&full[s]), (last / kXsStages) & 1, &no_abort, p.err);
+    }
+}
+
 // NCOL: activation columns held in shared memory (N rounded up to 1, 2, 4 or 8).
 template <int NCOL>
 __global__ void __launch_bounds__(kRThreads, 2)
@@ -324,17 +368,29 @@ constexpr size_t ring_xg_smem_bytes(int nt, int nblk) {
            2 * (size_t)kRWarps * kTileRows * 8 * nt * 4 + (2 * xg_stages(nt) + 1) * 8 + 16;
 }
 
-template <int NT>
+// Streaming shared-X form (rows too long for the resident copy): the fragments travel with
+// each stage instead.  Shared memory aligned to 128 bytes (enough for the non-swizzled weight
+// box), so that two CTAs fit on an SM.
+constexpr size_t ring_xs_smem_bytes() {
+    return 128 + (size_t)kXsStages * kXsStageBytes + 2 * (size_t)kRWarps * kTileRows * 8 * 4 + (2 * kXsStages + 1) * 8 + 16;
+}
+
+// STREAM = false: the resident shared-X form; true: the streaming one (NT = 1 only).
+template <int NT, bool STREAM>
 __global__ void __launch_bounds__(kRThreads, NT == 1 ? 2 : 1)
 q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
-    constexpr int kStagesX = xg_stages(NT);
+    static_assert(!STREAM || NT == 1, "the streaming form has one column tile");
+    constexpr int kStagesX = STREAM ? kXsStages : xg_stages(NT);
+    constexpr uint32_t kSB = STREAM ? kXsStageBytes : kStageBytes;   // stage stride
+    constexpr uintptr_t kAlign = STREAM ? 127 : 1023;
     constexpr int kRedX = kRWarps * kTileRows * 8 * NT;   // one set of the warps' partial tiles
     extern __shared__ uint8_t q4x_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4x_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4x_smem_raw) + kAlign) & ~kAlign);
     uint8_t* ring = smem;
-    uint4* xfr = reinterpret_cast<uint4*>(smem + (size_t)kStagesX * kStageBytes);               // [t][kb][pair][q][g]
-    uint2* xsum = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xfr) + (size_t)NT * p.nblk * 4096);   // [t][kb][q][g]
-    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsum) + (size_t)NT * p.nblk * 256);
+    // resident form: [t][kb][pair][q][g] fragments and [t][kb][q][g] sums after the ring
+    uint4* xfr = reinterpret_cast<uint4*>(smem + (size_t)kStagesX * kSB);
+    uint2* xsum = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xfr) + (STREAM ? 0 : (size_t)NT * p.nblk * 4096));
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsum) + (STREAM ? 0 : (size_t)NT * p.nblk * 256));
     uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRedX);
     uint64_t* empty = full + kStagesX;
     uint64_t* xbar = empty + kStagesX;
@@ -358,21 +414,27 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
     const int nst = (p.nblk + kStageBlocks - 1) / kStageBlocks;
     const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
     if (warp == kRWarps) {
-        if (lane == 0) ring_producer<kStagesX>(p, ring, full, empty, abort_flag, my_tiles, nst);
+        if (lane == 0) {
+            if constexpr (STREAM) ring_producer_xs(p, ring, full, empty, abort_flag, my_tiles, nst);
+            else ring_producer<kStagesX>(p, ring, full, empty, abort_flag, my_tiles, nst);
+        }
         return;
     }
 
     // ---------------- consumers
     ptx::pdl_wait();   // the prepared activations come from the previous kernel
     const uint32_t xb_bar = ptx::smem_u32(xbar);
-    const uint32_t fbytes = (uint32_t)NT * p.nblk * 4096, sbytes = (uint32_t)NT * p.nblk * 256;
-    if (threadIdx.x == 0) {
-        // tiles 0 .. NT-1 of the workspace are contiguous (its layout is [tile][block][...])
-        ptx::mbar_expect_tx(xb_bar, fbytes + sbytes);
-        ptx::bulk_load(ptx::smem_u32(xfr), p.xf, fbytes, xb_bar);
-        ptx::bulk_load(ptx::smem_u32(xsum), p.xs, sbytes, xb_bar);
+    bool ok = true;
+    if constexpr (!STREAM) {
+        const uint32_t fbytes = (uint32_t)NT * p.nblk * 4096, sbytes = (uint32_t)NT * p.nblk * 256;
+        if (threadIdx.x == 0) {
+            // tiles 0 .. NT-1 of the workspace are contiguous (its layout is [tile][block][...])
+            ptx::mbar_expect_tx(xb_bar, fbytes + sbytes);
+            ptx::bulk_load(ptx::smem_u32(xfr), p.xf, fbytes, xb_bar);
+            ptx::bulk_load(ptx::smem_u32(xsum), p.xs, sbytes, xb_bar);
+        }
+        ok = ptx::mbar_wait(xb_bar, 0, abort_flag, p.err);
     }
-    bool ok = ptx::mbar_wait(xb_bar, 0, abort_flag, p.err);
 
     const int g = lane >> 2;
     const int q4 = lane & 3;
@@ -390,16 +452,20 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
             if (!ok) continue;
             const int kb = si * kStageBlocks + warp;
             if (kb < p.nblk) {
-                const uint32_t bb = ring_u32 + (uint32_t)s * kStageBytes + (uint32_t)warp * q4k::kBlockBytes;
+                const uint32_t bb = ring_u32 + (uint32_t)s * kSB + (uint32_t)warp * q4k::kBlockBytes;
                 const uint32_t r0 = bb + (uint32_t)g * (kStageBlocks * q4k::kBlockBytes), r1 = r0 + 8 * (kStageBlocks * q4k::kBlockBytes);
                 const uint4 h0 = lds128(r0), h1 = lds128(r1);
                 const uint4 a0w = lds128(r0 + 16 + 32 * q4), b0w = lds128(r0 + 32 + 32 * q4);
                 const uint4 a1w = lds128(r1 + 16 + 32 * q4), b1w = lds128(r1 + 32 + 32 * q4);
                 RowScales s0, s1;
                 q4k::row_scales2(h0, h1, q4, s0, s1);
+                // this block's fragments and sums: in the stage (streaming) or resident
+                const uint4* xst = reinterpret_cast<const uint4*>(ring + (size_t)s * kSB + kStageBytes);
+                const uint2* sst = reinterpret_cast<const uint2*>(ring + (size_t)s * kSB + kStageBytes + kStageBlocks * 4096);
                 const uint4* xb[NT];
 #pragma unroll
-                for (int t = 0; t < NT; ++t) xb[t] = xfr + (size_t)(t * p.nblk + kb) * 256 + q4 * 8 + g;
+                for (int t = 0; t < NT; ++t)
+                    xb[t] = (STREAM ? xst + (size_t)warp * 256 : xfr + (size_t)(t * p.nblk + kb) * 256) + q4 * 8 + g;
                 float acc[NT][2][4];
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
@@ -434,7 +500,7 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     // min term: sum_j m_j S_j with S as f16 hi + lo
-                    const uint2 sv = xsum[(size_t)(t * p.nblk + kb) * 32 + q4 * 8 + g];
+                    const uint2 sv = STREAM ? sst[warp * 32 + q4 * 8 + g] : xsum[(size_t)(t * p.nblk + kb) * 32 + q4 * 8 + g];
                     float mn[4] = {0.f, 0.f, 0.f, 0.f}, ml[4] = {0.f, 0.f, 0.f, 0.f};
                     mma16816(mn, s0.mpair, s1.mpair, 0u, 0u, sv.x, 0u);
                     mma16816(ml, s0.mpair, s1.mpair, 0u, 0u, sv.y, 0u);
@@ -467,7 +533,7 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
             if (m0 + r < p.M) reinterpret_cast<float*>(p.y + (size_t)c * p.y_cs)[m0 + r] = v;
         }
     }
-    if (threadIdx.x == 0) {
+    if (!STREAM && threadIdx.x == 0) {
         // the activation copy has landed before the CTA exits, even if a wait gave up
         volatile int no_abort = 0;
         ptx::mbar_wait(xb_bar, 0, &no_abort, p.err);
@@ -521,15 +587,15 @@ int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
     return MLZC_OK;
 }
 
-template <int NT>
+template <int NT, bool STREAM>
 int launch_ring_xg(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
-    const size_t smem = ring_xg_smem_bytes(NT, p.nblk);
+    const size_t smem = STREAM ? ring_xs_smem_bytes() : ring_xg_smem_bytes(NT, p.nblk);
     int slots = 0;
-    const int st = ring_slots(q4k_ring_xg_kernel<NT>, smem, &slots);
+    const int st = ring_slots(q4k_ring_xg_kernel<NT, STREAM>, smem, &slots);
     if (st != MLZC_OK) return st;
     const int grid = std::min(p.tiles, slots);
     p.err = c->err;
-    MLZC_CUDA_TRY(launch_pdl(q4k_ring_xg_kernel<NT>, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
+    MLZC_CUDA_TRY(launch_pdl(q4k_ring_xg_kernel<NT, STREAM>, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
     count_launch();
     return MLZC_OK;
 }
@@ -605,7 +671,25 @@ int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, in
     if (st != MLZC_OK) return st;
     p.xf = xf;
     p.xs = xs;
-    return launch_ring_xg<1>(c, p, s);
+    return launch_ring_xg<1, false>(c, p, s);
+}
+
+bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N) {
+    // rows too long for the resident shared-X copy
+    if (N < 3 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
+    return !q4k_ring_xg_applicable(M, K, N) && ring_xg_smem_bytes(1, (int)(K / q4k::kQK)) > 227 * 1024;
+}
+
+int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                       const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
+    if (!q4k_ring_xs_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
+    if ((uintptr_t)xf % 16 || (uintptr_t)xs % 16) return fail(MLZC_ERR_INVALID, "Q4_K ring: workspace not 16-byte aligned");
+    RingParams p;
+    const int st = make_ring_params(w, w_row_bytes, M, K, N, y, y_col_bytes, &p);
+    if (st != MLZC_OK) return st;
+    p.xf = xf;
+    p.xs = xs;
+    return launch_ring_xg<1, true>(c, p, s);
 }
 
 }  // namespace mlzc

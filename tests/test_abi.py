@@ -54,15 +54,18 @@ def test_launch_overlap_mode():
 
 
 def test_q4k_workspace_follows_the_dispatch():
-    """Host arithmetic only: the Q4_K paths that read prepared activations (shared-X ring,
-    5 <= N <= 8 with rows of <= 42 blocks; batched kernel, N > 8) get a workspace, the others
-    need none."""
+    """Host arithmetic only: the Q4_K paths that read prepared activations (the shared-X
+    ring, resident for 5 <= N <= 8 and rows of <= 42 blocks, streaming for 3 <= N <= 8 and
+    longer rows; the batched kernel, N > 8) get a workspace, the others need none."""
     ws = lambda M, K, N: mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q4_K, M, K, N)
-    for N in (1, 2, 3, 4):
+    for N in (1, 2):
         assert ws(4096, 4096, N) == 0 and ws(4096, 14336, N) == 0
+    for N in (3, 4):
+        assert ws(4096, 4096, N) == 0 and ws(4096, 42 * 256, N) == 0
+        assert ws(4096, 43 * 256, N) > 0 and ws(4096, 14336, N) > 0
     for N in (5, 8):
-        assert ws(4096, 4096, N) > 0 and ws(4096, 42 * 256, N) > 0
-        assert ws(4096, 43 * 256, N) == 0 and ws(4096, 14336, N) == 0
+        for K in (4096, 42 * 256, 43 * 256, 14336):
+            assert ws(4096, K, N) > 0
     for N in (9, 16, 256):
         need = ws(4096, 14336, N)
         # f16 fragments (512 B per column and block) + sums (32 B), columns padded to 16

@@ -68,7 +68,7 @@ def test_known_answer_block(dev):
 
 @pytest.mark.parametrize("M,K,N", [(1, 256, 1), (3, 512, 2), (37, 768, 5), (300, 256, 17), (8, 1024, 33),
                                    (17, 2304, 3), (2053, 4352, 7), (64, 14336, 4), (40, 14336, 8), (16, 256, 8),
-                                   (8200, 512, 3), (8197, 4096, 8)])
+                                   (8200, 512, 3), (8197, 4096, 8), (100, 11520, 3), (33, 11520, 6)])
 def test_edge_shapes(dev, M, K, N):
     g = synth.rng(300 + M + K + N)
     blocks = synth.q4k_blocks(g, M, K)
