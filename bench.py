@@ -220,13 +220,11 @@ class C3(Workload):
     def roofline_kernel(self, j):
         m, k = self.SHAPES[j]
         n = self.N
-        # the library's dispatch (q4k_ring_applicable, q4k_ring_xg_applicable, launch_q4k_mma)
+        # the library's dispatch (q4k_ring_applicable, q4k_ring_xs_applicable, launch_q4k_mma)
         if n <= 2 or (n <= 4 and m >= 8192 and k <= 4096):
             kern = "q4k_ring_kernel"
-        elif 5 <= n <= 8 and k // 256 <= 42:
-            kern = "q4k_prep_kernel + q4k_ring_xg_kernel (resident X)"
-        elif 3 <= n <= 8 and k // 256 > 42:
-            kern = "q4k_prep_kernel + q4k_ring_xg_kernel (streaming X)"
+        elif n <= 8 and (n >= 5 or m >= 8192 or k > 4096):
+            kern = "q4k_prep_kernel + q4k_ring_xs_kernel"
         elif n <= 8:
             kern = "q4k_gemv_kernel"
         else:

@@ -70,20 +70,14 @@ size_t q4k_workspace_bytes(int64_t K, int64_t N);
 int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
                    void* ws, size_t ws_bytes, cudaStream_t s);
-// Decode-shaped Q4_K (N <= 2; N <= 4 for many short rows): persistent kernel fed by a TMA
+// Decode-shaped Q4_K, N <= 2 (N <= 4 with many short rows): persistent kernel fed by a TMA
 // ring, activations converted once per CTA into shared memory.
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                     const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
                     cudaStream_t s);
-// The same ring for 5 <= N <= 8 with rows of up to 42 blocks, fed by activations prepared once per call
-// (q4k_prep_kernel's xf / xs) and bulk-copied into each CTA's shared memory.
-bool q4k_ring_xg_applicable(int64_t M, int64_t K, int64_t N);
-int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
-                       const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes,
-                       cudaStream_t s);
-// The same with rows too long for a resident copy (3 <= N <= 8): each stage carries its
-// blocks' prepared activations.
+// The same ring for 3 <= N <= 8 (where it wins), fed by activations prepared once per call
+// (q4k_prep_kernel's xf / xs) that travel with each stage.
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                        const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes,

@@ -385,9 +385,10 @@ Q4kWs q4k_ws(int64_t K, int64_t N) {
 }  // namespace
 
 size_t q4k_workspace_bytes(int64_t K, int64_t N) {
-    // prepared activations: the batched kernel (N > 8) and the shared-X ring (3 <= N <= 8,
-    // resident or streaming)
-    if (N <= 2 || (N <= 8 && !q4k_ring_xg_applicable(1, K, N) && !q4k_ring_xs_applicable(1, K, N))) return 0;
+    // prepared activations: the batched kernel (N > 8) and the shared-X ring (3 <= N <= 8;
+    // for N = 3..4 on small short-row shapes the register decode kernel runs and the
+    // workspace goes unused -- the size cannot depend on M)
+    if (N <= 2) return 0;
     const Q4kWs w = q4k_ws(K, N);
     return w.xf_bytes + w.xs_bytes;
 }
@@ -405,9 +406,8 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
     char* yc = reinterpret_cast<char*>(y);
     if (q4k_ring_applicable(M, K, N))
         return launch_q4k_ring(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
-    const bool xg = q4k_ring_xg_applicable(M, K, N);
-    const bool xstream = !xg && q4k_ring_xs_applicable(M, K, N);
-    if (N <= 8 && !xg && !xstream) {
+    const bool xstream = q4k_ring_xs_applicable(M, K, N);
+    if (N <= 8 && !xstream) {
         const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
         if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
         MLZC_CUDA_TRY(launch_pdl(q4k_gemv_kernel, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, (int)(K / kQK), xc,
@@ -427,8 +427,6 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
                                  xf, xs));
         count_launch();
     }
-    if (xg)
-        return launch_q4k_ring_xg(c, w, w_row_bytes, M, K, reinterpret_cast<const uint4*>(xf), xs, N, y, y_col_bytes, s);
     if (xstream)
         return launch_q4k_ring_xs(c, w, w_row_bytes, M, K, reinterpret_cast<const uint4*>(xf), xs, N, y, y_col_bytes, s);
     const dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + kQRows - 1) / kQRows));

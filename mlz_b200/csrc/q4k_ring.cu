@@ -1,5 +1,7 @@
-// q4k_ring.cu -- decode-shaped Q4_K mul_mat (N <= 8 activation columns) as a persistent
-// kernel fed by a TMA ring.
+// q4k_ring.cu -- decode-shaped Q4_K mul_mat (N <= 8 activation columns) as persistent
+// kernels fed by a TMA ring: q4k_ring_kernel (N <= 2; N <= 4 with many short rows;
+// activations converted per CTA) and
+// q4k_ring_xs_kernel (3 <= N <= 8, activations prepared once per call, carried by the stages).
 //
 // Replaces, for the decode shapes, the Q4_K branch of ggml_simd_try_mul_mat
 // (src/simd/ggml_simd_hook.cpp:188-231, 238-299): one simd_vec_dot_q4_k_q8_k
@@ -18,9 +20,9 @@
 //   - Eight consumer warps each take one block of every stage: the header and their
 //     32-byte nibble chunk for rows g and g + 8, the (sc, m) unpack, LOP3 + HFMA2 dequant
 //     and 16 MMAs (four accumulator chains).
-//   - The activations are converted once per CTA, before the main loop, into the MMA's f16
-//     B fragments (in the permuted k order the dequant produces) and the sub-block sums
-//     (f16 hi + lo), kept in shared memory for the whole kernel.
+//   - q4k_ring_kernel converts the activations once per CTA, before the main loop, into the
+//     MMA's f16 B fragments (in the permuted k order the dequant produces) and the sub-block
+//     sums (f16 hi + lo), kept in shared memory for the whole kernel.
 //   - At the end of a tile the eight warps' partial rows are summed in warp order through
 //     shared memory (one named barrier per tile; double-buffered), so results repeat bit
 //     for bit.
@@ -355,46 +357,28 @@ q4k_ring_kernel(const __grid_constant__ RingParams p) {
     }
 }
 
-// Shared-X form (5 <= N <= 8, rows of up to 42 blocks): the activations were prepared once for the
-// call by q4k_prep_kernel; each CTA bulk-copies the NT column tiles' fragments and sums
-// (4 KB + 256 B per tile and block) into shared memory at its start, then runs the ring as
-// above with NT 8-column MMA tiles sharing every dequantised A fragment.
-// One column tile: 2 stages and two CTAs per SM (16 consumer warps, the same bytes in flight
-// per SM as one CTA with 4); two tiles: 4 stages, one CTA.
-constexpr int xg_stages(int nt) { return nt == 1 ? 2 : 4; }
-
-constexpr size_t ring_xg_smem_bytes(int nt, int nblk) {
-    return 1024 + (size_t)xg_stages(nt) * kStageBytes + (size_t)nt * nblk * (4096 + 256) +
-           2 * (size_t)kRWarps * kTileRows * 8 * nt * 4 + (2 * xg_stages(nt) + 1) * 8 + 16;
-}
-
-// Streaming shared-X form (rows too long for the resident copy): the fragments travel with
-// each stage instead.  Shared memory aligned to 128 bytes (enough for the non-swizzled weight
-// box), so that two CTAs fit on an SM.
+// Shared-X form (3 <= N <= 8): the activations were prepared once for the call by
+// q4k_prep_kernel (f16 B fragments and sub-block sums, one 8-column tile), and each stage
+// carries its 8 blocks' fragments and sums next to the weight box, so the activations cost a
+// re-read from L2 per tile instead of a conversion per CTA.  Two stages, two CTAs per SM;
+// shared memory aligned to 128 bytes (enough for the non-swizzled weight box) so both fit.
 constexpr size_t ring_xs_smem_bytes() {
     return 128 + (size_t)kXsStages * kXsStageBytes + 2 * (size_t)kRWarps * kTileRows * 8 * 4 + (2 * kXsStages + 1) * 8 + 16;
 }
 
-// STREAM = false: the resident shared-X form; true: the streaming one (NT = 1 only).
-template <int NT, bool STREAM>
-__global__ void __launch_bounds__(kRThreads, NT == 1 ? 2 : 1)
-q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
-    static_assert(!STREAM || NT == 1, "the streaming form has one column tile");
-    constexpr int kStagesX = STREAM ? kXsStages : xg_stages(NT);
-    constexpr uint32_t kSB = STREAM ? kXsStageBytes : kStageBytes;   // stage stride
-    constexpr uintptr_t kAlign = STREAM ? 127 : 1023;
+__global__ void __launch_bounds__(kRThreads, 2)
+q4k_ring_xs_kernel(const __grid_constant__ RingParams p) {
+    constexpr int NT = 1;                                  // one 8-column MMA tile
+    constexpr int kStagesX = kXsStages;
+    constexpr uint32_t kSB = kXsStageBytes;                // stage stride
     constexpr int kRedX = kRWarps * kTileRows * 8 * NT;   // one set of the warps' partial tiles
     extern __shared__ uint8_t q4x_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4x_smem_raw) + kAlign) & ~kAlign);
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4x_smem_raw) + 127) & ~uintptr_t(127));
     uint8_t* ring = smem;
-    // resident form: [t][kb][pair][q][g] fragments and [t][kb][q][g] sums after the ring
-    uint4* xfr = reinterpret_cast<uint4*>(smem + (size_t)kStagesX * kSB);
-    uint2* xsum = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xfr) + (STREAM ? 0 : (size_t)NT * p.nblk * 4096));
-    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsum) + (STREAM ? 0 : (size_t)NT * p.nblk * 256));
+    float* red = reinterpret_cast<float*>(smem + (size_t)kStagesX * kSB);
     uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRedX);
     uint64_t* empty = full + kStagesX;
-    uint64_t* xbar = empty + kStagesX;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(xbar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStagesX);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -403,7 +387,6 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
             ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
             ptx::mbar_init(ptx::smem_u32(&empty[s]), kRWarps);
         }
-        ptx::mbar_init(ptx::smem_u32(xbar), 1);
         *abort_flag = 0;
         ptx::mbar_init_fence();
     }
@@ -414,27 +397,13 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
     const int nst = (p.nblk + kStageBlocks - 1) / kStageBlocks;
     const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
     if (warp == kRWarps) {
-        if (lane == 0) {
-            if constexpr (STREAM) ring_producer_xs(p, ring, full, empty, abort_flag, my_tiles, nst);
-            else ring_producer<kStagesX>(p, ring, full, empty, abort_flag, my_tiles, nst);
-        }
+        if (lane == 0) ring_producer_xs(p, ring, full, empty, abort_flag, my_tiles, nst);
         return;
     }
 
     // ---------------- consumers
-    ptx::pdl_wait();   // the prepared activations come from the previous kernel
-    const uint32_t xb_bar = ptx::smem_u32(xbar);
+    ptx::pdl_wait();   // the writes of Y come after the previous kernel
     bool ok = true;
-    if constexpr (!STREAM) {
-        const uint32_t fbytes = (uint32_t)NT * p.nblk * 4096, sbytes = (uint32_t)NT * p.nblk * 256;
-        if (threadIdx.x == 0) {
-            // tiles 0 .. NT-1 of the workspace are contiguous (its layout is [tile][block][...])
-            ptx::mbar_expect_tx(xb_bar, fbytes + sbytes);
-            ptx::bulk_load(ptx::smem_u32(xfr), p.xf, fbytes, xb_bar);
-            ptx::bulk_load(ptx::smem_u32(xsum), p.xs, sbytes, xb_bar);
-        }
-        ok = ptx::mbar_wait(xb_bar, 0, abort_flag, p.err);
-    }
 
     const int g = lane >> 2;
     const int q4 = lane & 3;
@@ -459,13 +428,13 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
                 const uint4 a1w = lds128(r1 + 16 + 32 * q4), b1w = lds128(r1 + 32 + 32 * q4);
                 RowScales s0, s1;
                 q4k::row_scales2(h0, h1, q4, s0, s1);
-                // this block's fragments and sums: in the stage (streaming) or resident
+                // this block's fragments and sums, in the stage after the weights
                 const uint4* xst = reinterpret_cast<const uint4*>(ring + (size_t)s * kSB + kStageBytes);
                 const uint2* sst = reinterpret_cast<const uint2*>(ring + (size_t)s * kSB + kStageBytes + kStageBlocks * 4096);
                 const uint4* xb[NT];
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    xb[t] = (STREAM ? xst + (size_t)warp * 256 : xfr + (size_t)(t * p.nblk + kb) * 256) + q4 * 8 + g;
+                    xb[t] = xst + (size_t)(t * kStageBlocks + warp) * 256 + q4 * 8 + g;
                 float acc[NT][2][4];
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
@@ -500,7 +469,7 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     // min term: sum_j m_j S_j with S as f16 hi + lo
-                    const uint2 sv = STREAM ? sst[warp * 32 + q4 * 8 + g] : xsum[(size_t)(t * p.nblk + kb) * 32 + q4 * 8 + g];
+                    const uint2 sv = sst[(t * kStageBlocks + warp) * 32 + q4 * 8 + g];
                     float mn[4] = {0.f, 0.f, 0.f, 0.f}, ml[4] = {0.f, 0.f, 0.f, 0.f};
                     mma16816(mn, s0.mpair, s1.mpair, 0u, 0u, sv.x, 0u);
                     mma16816(ml, s0.mpair, s1.mpair, 0u, 0u, sv.y, 0u);
@@ -533,12 +502,8 @@ q4k_ring_xg_kernel(const __grid_constant__ RingParams p) {
             if (m0 + r < p.M) reinterpret_cast<float*>(p.y + (size_t)c * p.y_cs)[m0 + r] = v;
         }
     }
-    if (!STREAM && threadIdx.x == 0) {
-        // the activation copy has landed before the CTA exits, even if a wait gave up
-        volatile int no_abort = 0;
-        ptx::mbar_wait(xb_bar, 0, &no_abort, p.err);
-    }
 }
+
 
 // Resident CTAs of a ring kernel with `smem` bytes, over all SMs (the kernel's shared-memory
 // limit is raised to the device's opt-in maximum once per device; occupancy is queried once
@@ -587,15 +552,14 @@ int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
     return MLZC_OK;
 }
 
-template <int NT, bool STREAM>
-int launch_ring_xg(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
-    const size_t smem = STREAM ? ring_xs_smem_bytes() : ring_xg_smem_bytes(NT, p.nblk);
+int launch_ring_xs(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
+    const size_t smem = ring_xs_smem_bytes();
     int slots = 0;
-    const int st = ring_slots(q4k_ring_xg_kernel<NT, STREAM>, smem, &slots);
+    const int st = ring_slots(q4k_ring_xs_kernel, smem, &slots);
     if (st != MLZC_OK) return st;
     const int grid = std::min(p.tiles, slots);
     p.err = c->err;
-    MLZC_CUDA_TRY(launch_pdl(q4k_ring_xg_kernel<NT, STREAM>, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
+    MLZC_CUDA_TRY(launch_pdl(q4k_ring_xs_kernel, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
     count_launch();
     return MLZC_OK;
 }
@@ -629,14 +593,12 @@ int make_ring_params(const void* w, size_t w_row_bytes, int64_t M, int64_t K, in
 }  // namespace
 
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N) {
-    // Measured on B200 over the Llama-3.1-8B shapes (us, this form / the best other):
-    // N <= 2 everywhere; N = 3..4 only for many short rows (14336 x 4096, N = 4: 18.3 / 21.2;
-    // 4096 x 4096: 8.6 / 6.5), because each CTA converts all of X for itself; N >= 5 goes to
-    // the shared-X form below.
+    // Each CTA converts all of X itself (no prep launch): N <= 2 everywhere, N = 3..4 for many
+    // short rows (the C3 batch-4 step: 42.0 us with 14336 x 4096 here vs 43.8 us with it on
+    // the prepared-activation form below); more columns or longer rows: the form below
     if (N < 1 || N > 4 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
     if (N > 2 && (M < 8192 || K > 4096)) return false;
-    const int ncol = N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8;
-    return ring_smem_bytes(ncol, (int)(K / q4k::kQK)) <= 227 * 1024;
+    return ring_smem_bytes(N <= 1 ? 1 : N <= 2 ? 2 : 4, (int)(K / q4k::kQK)) <= 227 * 1024;
 }
 
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
@@ -650,34 +612,16 @@ int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     p.x_cs = x_col_bytes;
     if (N <= 1) return launch_ring<1>(c, p, s);
     if (N <= 2) return launch_ring<2>(c, p, s);
-    if (N <= 4) return launch_ring<4>(c, p, s);
-    return launch_ring<8>(c, p, s);
-}
-
-bool q4k_ring_xg_applicable(int64_t M, int64_t K, int64_t N) {
-    // Measured (us, this form / the best other): N = 8: 4096 x 4096 8.0 / 9.5, 14336 x 4096
-    // 19.4 / 31.2; N = 4 loses to the forms above (8.0 / 6.5, 19.2 / 18.3) and a second
-    // column tile (N = 16) to the batched kernel (11.3 / 9.2, 31.5 / 29.1).
-    if (N < 5 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
-    return ring_xg_smem_bytes(1, (int)(K / q4k::kQK)) <= 227 * 1024;
-}
-
-int launch_q4k_ring_xg(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
-                       const uint4* xf, const uint2* xs, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
-    if (!q4k_ring_xg_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
-    if ((uintptr_t)xf % 16 || (uintptr_t)xs % 16) return fail(MLZC_ERR_INVALID, "Q4_K ring: workspace not 16-byte aligned");
-    RingParams p;
-    const int st = make_ring_params(w, w_row_bytes, M, K, N, y, y_col_bytes, &p);
-    if (st != MLZC_OK) return st;
-    p.xf = xf;
-    p.xs = xs;
-    return launch_ring_xg<1, false>(c, p, s);
+    return launch_ring<4>(c, p, s);
 }
 
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N) {
-    // rows too long for the resident shared-X copy
+    // Measured on B200 (us, this form / the best other): N = 8: 4096 x 4096 6.9 / 8.0,
+    // 14336 x 4096 16.4 / 19.4, 4096 x 14336 16.5 / 25.0; N = 4: 4096 x 14336 16.2 / 19.5,
+    // but 4096 x 4096 7.0 / 6.5 (the register decode kernel).  The launcher tries the ring
+    // above first, which takes N = 3..4 with many short rows.
     if (N < 3 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
-    return !q4k_ring_xg_applicable(M, K, N) && ring_xg_smem_bytes(1, (int)(K / q4k::kQK)) > 227 * 1024;
+    return N >= 5 || M >= 8192 || K > 4096;
 }
 
 int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
@@ -689,7 +633,7 @@ int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, in
     if (st != MLZC_OK) return st;
     p.xf = xf;
     p.xs = xs;
-    return launch_ring_xg<1, true>(c, p, s);
+    return launch_ring_xs(c, p, s);
 }
 
 }  // namespace mlzc
