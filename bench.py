@@ -45,6 +45,8 @@ NCU_TRAFFIC = {
     ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
     ("c3", 1): (33.07e6, "profiles/q4k_ring_kernel_c3_14336x4096.md (14336x4096 launch; the 4096x14336 "
                          "launch reads the same block bytes)"),
+    ("c3", 8): (33.29e6, "profiles/q4k_ring_xs_kernel_c3_4096x14336_batch8.md (4096x14336 launch; the 14336x4096 "
+                         "launch reads the same block bytes)"),
     ("c3", 16): (33.31e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
 }
 
