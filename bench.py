@@ -42,6 +42,7 @@ L2_BYTES = 126 * 1024 * 1024
 NCU_TRAFFIC = {
     ("c1", 1): (50.35e6 + 0.02e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_vec_kernel)"),
     ("c1", 4): (50.39e6 + 0.07e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel)"),
+    ("c1", 8): (50.44e6 + 0.01e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel<1, 1, 4>)"),
     ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
     ("c3", 1): (33.07e6, "profiles/q4k_ring_kernel_c3_14336x4096.md (14336x4096 launch; the 4096x14336 "
                          "launch reads the same block bytes)"),
