@@ -37,18 +37,18 @@ sys.path.insert(0, HERE)
 L2_BYTES = 126 * 1024 * 1024
 
 # DRAM bytes per call of the roofline's call (dram__bytes_read.sum + dram__bytes_write.sum),
-# from one ncu capture of the same kernels on the same workload; the captures are
-# summarised, with their commands, in the profiles/ folder.
+# from one ncu capture of the same kernels on the same workload (the capture commands and
+# summaries are kept with the profiles).
 NCU_TRAFFIC = {
-    ("c1", 1): (50.35e6 + 0.02e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_vec_kernel)"),
-    ("c1", 4): (50.39e6 + 0.07e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel)"),
-    ("c1", 8): (50.44e6 + 0.01e6, "profiles/gemv_kernels_c1_8192x3072.md (gemv_f16_mma_kernel<1, 1, 4>)"),
-    ("c4", 16): (250.80e6 + 5.98e6, "profiles/fa_decode_kernel_c4_16seq_d128.md (decode kernel of the call)"),
-    ("c3", 1): (33.07e6, "profiles/q4k_ring_kernel_c3_14336x4096.md (14336x4096 launch; the 4096x14336 "
-                         "launch reads the same block bytes)"),
-    ("c3", 8): (33.29e6, "profiles/q4k_ring_xs_kernel_c3_4096x14336_batch8.md (4096x14336 launch; the 14336x4096 "
-                         "launch reads the same block bytes)"),
-    ("c3", 16): (33.31e6, "profiles/q4k_mma_kernel_c3_14336x4096.md (14336x4096 launch)"),
+    ("c1", 1): (50.35e6 + 0.02e6, "ncu capture: gemv_vec_kernel, 8192x3072, N=1"),
+    ("c1", 4): (50.39e6 + 0.07e6, "ncu capture: gemv_f16_mma_kernel, 8192x3072, N=4"),
+    ("c1", 8): (50.44e6 + 0.01e6, "ncu capture: gemv_f16_mma_kernel<1, 1, 4>, 8192x3072, N=8"),
+    ("c4", 16): (250.80e6 + 5.98e6, "ncu capture: fa_decode_kernel of the c4 call (16 sequences)"),
+    ("c3", 1): (33.07e6, "ncu capture: q4k_ring_kernel, 14336x4096 launch (the 4096x14336 launch reads the "
+                         "same block bytes)"),
+    ("c3", 8): (33.29e6, "ncu capture: q4k_ring_xs_kernel, 4096x14336 launch, batch 8 (the 14336x4096 launch "
+                         "reads the same block bytes)"),
+    ("c3", 16): (33.31e6, "ncu capture: q4k_mma_kernel, 14336x4096 launch, batch 16"),
 }
 
 
@@ -76,6 +76,45 @@ def parse_args():
 
 
 DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 256}
+DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16"}
+
+
+def metric_name(cfg: str, n: int, world: int) -> str:
+    """`metric` of a line (the same for both arms)."""
+    if cfg == "c1":
+        return f"decode mul_mat GB/s (F16 W 8192x3072 . X 3072x{n}, fp32 acc)"
+    if cfg == "c2":
+        return f"prefill mul_mat TFLOP/s (Llama-3.2-3B layer, 7 F16 projections, M={n} tokens, fp32 acc)"
+    if cfg == "c3":
+        return f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
+    if cfg == "c4":
+        return f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
+    return (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
+            f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, NCCL all-gather)")
+
+
+C2_PROJ = [("q", 3072, 3072, 0), ("k", 1024, 3072, 0), ("v", 1024, 3072, 0), ("o", 3072, 3072, 1),
+           ("gate", 8192, 3072, 2), ("up", 8192, 3072, 2), ("down", 3072, 8192, 3)]
+C3_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
+C5_MATS = [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]
+
+
+def c4_lengths(n: int):
+    from mlz_b200 import synth
+    return synth.kv_lengths(synth.rng(synth.seed_for(4, n)), n, 512, 8192)
+
+
+def workload_name(cfg: str, n: int, world: int) -> str:
+    """config.workload of a line; both arms print the same string for the same workload."""
+    if cfg == "c1":
+        return f"c1 F16 mul_mat Llama-3.2-3B up-proj 8192x3072, N={n}"
+    if cfg == "c2":
+        return f"c2 Llama-3.2-3B layer prefill, 7 F16 projections, M={n} tokens"
+    if cfg == "c3":
+        return f"c3 Q4_K mul_mat Llama-3.1-8B shapes, batch {n}"
+    if cfg == "c4":
+        return f"c4 FA decode GQA, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
+    return f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}"
 
 
 def load_peaks():
@@ -130,7 +169,7 @@ class C1(Workload):
         import torch
         from mlz_b200 import synth
         self.M, self.K, self.N = 8192, 3072, n
-        self.metric = f"decode mul_mat GB/s (F16 W 8192x3072 . X 3072x{n}, fp32 acc)"
+        self.metric = metric_name("c1", n, 1)
         self.R = _rot_copies(2 * self.M * self.K)
         self.W = [synth.f16_weights_dev(gen, self.M, self.K, dev) for _ in range(self.R)]
         self.X = synth.f32_acts_dev(gen, n, self.K, dev)
@@ -138,7 +177,7 @@ class C1(Workload):
         import mlz_b200
         wsb = mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, self.M, self.K, n)
         self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-        self.config = {"workload": f"c1 F16 mul_mat Llama-3.2-3B up-proj 8192x3072, N={n}",
+        self.config = {"workload": workload_name("c1", n, 1),
                        "M": self.M, "K": self.K, "N": n,
                        "l2": f"rotates {self.R} weight copies ({self.R * 2 * self.M * self.K / 1e6:.0f} MB >= 4x L2)"}
 
@@ -166,8 +205,7 @@ class C1(Workload):
 class C2(Workload):
     unit = "TFLOP/s"
     bound = "tensor"
-    PROJ = [("q", 3072, 3072, 0), ("k", 1024, 3072, 0), ("v", 1024, 3072, 0), ("o", 3072, 3072, 1),
-            ("gate", 8192, 3072, 2), ("up", 8192, 3072, 2), ("down", 3072, 8192, 3)]
+    PROJ = C2_PROJ
 
     def roofline_kernel(self, j):
         return "the 7 mul_mat calls pooled (narrow_f16_kernel + gemm_f16_tc_kernel each)"
@@ -177,14 +215,14 @@ class C2(Workload):
         import mlz_b200
         from mlz_b200 import synth
         self.Mtok = n
-        self.metric = f"prefill mul_mat TFLOP/s (Llama-3.2-3B layer, 7 F16 projections, M={n} tokens, fp32 acc)"
+        self.metric = metric_name("c2", n, 1)
         self.W = [synth.f16_weights_dev(gen, o, i, dev) for (_, o, i, _) in self.PROJ]
         ins = [3072, 3072, 3072, 8192]
         self.X = [synth.f32_acts_dev(gen, n, k, dev) for k in ins]
         self.Y = [torch.empty((n, o), dtype=torch.float32, device=dev) for (_, o, _, _) in self.PROJ]
         wsb = max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, o, i, n) for (_, o, i, _) in self.PROJ)
         self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-        self.config = {"workload": f"c2 Llama-3.2-3B layer prefill, 7 F16 projections, M={n} tokens",
+        self.config = {"workload": workload_name("c2", n, 1),
                        "tokens": n, "projections": "q,k,v,o 3072/1024x3072; gate,up 8192x3072; down 3072x8192",
                        "l2": "inputs larger than L2 (201 MB of weights per step)"}
 
@@ -218,7 +256,7 @@ class C3(Workload):
     unit = "GB/s"
     bound = "hbm"
     dtype = "q4_k/f32"
-    SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
+    SHAPES = C3_SHAPES
 
     def roofline_kernel(self, j):
         m, k = self.SHAPES[j]
@@ -238,7 +276,7 @@ class C3(Workload):
         import torch
         from mlz_b200 import synth
         self.N = n
-        self.metric = f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
+        self.metric = metric_name("c3", n, 1)
         per_step = sum(m * k // 256 * 144 for m, k in self.SHAPES)
         self.R = _rot_copies(per_step)
         self.W = [[synth.q4k_blocks_dev(gen, m, k, dev) for (m, k) in self.SHAPES] for _ in range(self.R)]
@@ -247,7 +285,7 @@ class C3(Workload):
         import mlz_b200
         wsb = max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q4_K, m, k, n) for (m, k) in self.SHAPES)
         self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-        self.config = {"workload": f"c3 Q4_K mul_mat Llama-3.1-8B shapes, batch {n}", "batch": n,
+        self.config = {"workload": workload_name("c3", n, 1), "batch": n,
                        "shapes": "4096x4096, 14336x4096, 4096x14336",
                        "l2": f"rotates {self.R} weight sets ({self.R * per_step / 1e6:.0f} MB >= 4x L2)"}
 
@@ -290,8 +328,7 @@ class C4(Workload):
         import mlz_b200
         from mlz_b200 import synth
         self.B, self.Hq, self.Hkv, self.D = n, 32, 8, 128
-        g = synth.rng(synth.seed_for(4, n))
-        self.kv_len_np = synth.kv_lengths(g, n, 512, 8192)
+        self.kv_len_np = c4_lengths(n)
         self.L = 8192
         s = 1.0 / math.sqrt(self.D)
         self.q = torch.randn((n, self.Hq, 1, self.D), generator=gen, device=dev) * s
@@ -305,9 +342,9 @@ class C4(Workload):
                                      (n, self.Hq, 1, self.Hkv, self.L, self.D), s,
                                      kv_len_ptr=self.kv_len.data_ptr())
         self.ws = torch.empty(max(mlz_b200.flash_attn_workspace_bytes(desc), 1), dtype=torch.uint8, device=dev)
-        self.metric = (f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)")
+        self.metric = metric_name("c4", n, 1)
         tot = int(self.kv_len_np.sum())
-        self.config = {"workload": f"c4 FA decode GQA, {n} sequences, sum L = {tot}", "batch": n,
+        self.config = {"workload": workload_name("c4", n, 1), "batch": n,
                        "sum_kv_len": tot, "l2": "inputs larger than L2 (KV cache 537 MB)"}
 
     def work_units(self):
@@ -329,9 +366,8 @@ class C5(Workload):
         self.N, self.rank, self.world, self.comm = n, rank, world, comm
         self.unit = "GB/s" if n == 1 else "TFLOP/s"
         self.bound = "hbm" if n == 1 else "tensor"
-        self.mats = [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]
-        self.metric = (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
-                       f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, NCCL all-gather)")
+        self.mats = C5_MATS
+        self.metric = metric_name("c5", n, world)
         self.W = [synth.f16_weights_dev(gen, m // world, k, dev) for (_, m, k) in self.mats]
         self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, _, k) in self.mats]
         self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (_, m, _) in self.mats]
@@ -339,7 +375,7 @@ class C5(Workload):
         wsb = (max(comm.workspace_bytes(1, m, k, n) for (_, m, k) in self.mats) if comm else
                max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, m, k, n) for (_, m, k) in self.mats))
         self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-        self.config = {"workload": f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}", "N": n,
+        self.config = {"workload": workload_name("c5", n, world), "N": n,
                        "parallelism": f"row-shard x{world} + all-gather", "l2": "inputs larger than L2"}
 
     def work_units(self):  # whole-job units (all ranks together), reported once
@@ -416,76 +452,106 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+class CpuStep:
+    """One step of a workload on the host cores through the oracle's restatement of the
+    reference kernels (all host threads): every matrix of the step with all its rows
+    (c1/c2/c3/c5), or every sequence of the batch with its own length (c4).  Inputs are
+    generated once; rows past a generated block of weights reuse the block."""
+
+    def __init__(self, cfg: str, n: int):
+        import numpy as np
+        import oracle
+        from mlz_b200 import synth
+        self.cfg, self.n = cfg, n
+        self.nth = oracle.host_threads()
+        g = synth.rng(77)
+        self.parts = []          # (M, K, weight block, x)
+        if cfg in ("c1", "c2", "c5"):
+            shapes = {"c1": [(8192, 3072)], "c2": [(o, i) for (_, o, i, _) in C2_PROJ],
+                      "c5": [(m, k) for (_, m, k) in C5_MATS]}[cfg]
+            blocks = {}
+            for (M, K) in shapes:
+                if K not in blocks:
+                    blocks[K] = synth.f16_weights(g, min(M, 4096), K)
+                self.parts.append((M, K, blocks[K], synth.f32_acts(g, n, K)))
+            self.kernel = lambda w, x: oracle.base_mul_mat_f16(w, x, self.nth)
+            self.flops = cfg == "c2" or (cfg == "c5" and n > 1)
+            self.what = "convert-then-GEMM restatement"
+        elif cfg == "c3":
+            for (M, K) in C3_SHAPES:
+                self.parts.append((M, K, synth.q4k_blocks(g, min(M, 4096), K), synth.f32_acts(g, n, K)))
+            self.kernel = lambda w, x: oracle.base_mul_mat_q4k(w, x, self.nth)
+            self.flops = False
+            self.what = "Q8_K quantise + Q4_K x Q8_K dot restatement"
+        elif cfg == "c4":
+            self.kl = c4_lengths(n)
+            self.slots = 4
+            self.q, self.k, self.v = synth.fa_inputs(g, self.slots, 32, 8, int(self.kl.max()), 128)
+            self.flops = False
+            self.what = "FA2 skeleton restatement"
+        else:
+            raise ValueError(cfg)
+
+    def run(self) -> float:
+        """One step; returns its units (bytes or flops)."""
+        import oracle
+        n = self.n
+        units = 0.0
+        if self.cfg == "c4":
+            for b in range(len(self.kl)):
+                j = b % self.slots
+                oracle.base_flash_attn(self.q[j:j + 1], self.k[j:j + 1], self.v[j:j + 1], 1 / math.sqrt(128),
+                                       kv_len=self.kl[b:b + 1], nth=self.nth)
+                units += 4096.0 * int(self.kl[b]) + 2 * 32 * 128 * 4
+            return units
+        for (M, K, w, x) in self.parts:
+            reps, r = divmod(M, w.shape[0])
+            for _ in range(reps):
+                self.kernel(w, x)
+            if r:
+                self.kernel(w[:r], x)
+            if self.flops:
+                units += 2.0 * M * K * n
+            elif self.cfg == "c3":
+                units += M * (K // 256) * 144 + 4 * K * n + 4 * M * n
+            else:
+                units += 2.0 * M * K + 4 * K * n + 4 * M * n
+        return units
+
+
+_CPU_STEPS = {}
+
+
 def cpu_sample(cfg: str, n: int, target_s: float):
-    """Times the reference's loop structure (oracle port, all host threads) on a bounded
-    sample of the workload; returns (value in the metric's unit, description, threads)."""
-    import numpy as np
+    """Times whole steps of the workload on the host cores (CpuStep), as many as fit in
+    about `target_s` (at least one).  Returns (value in the metric's unit, description,
+    threads)."""
     import oracle
-    from mlz_b200 import synth
-    nth = oracle.host_threads()
-    g = synth.rng(77)
-
-    def grow(run, units_of):
-        rows = 1
-        while True:
-            t0 = time.perf_counter()
-            run(rows)
-            dt = time.perf_counter() - t0
-            if dt >= target_s or rows >= 1 << 20:
-                return units_of(rows) / dt, rows, dt
-            rows = max(rows * 2, int(rows * target_s / max(dt, 1e-3) * 1.1))
-
-    if cfg in ("c1", "c2", "c5"):
-        M, K = {"c1": (8192, 3072), "c2": (3072, 3072), "c5": (28672, 8192)}[cfg]
-        N = n
-        w = synth.f16_weights(g, min(M, 4096), K)
-        x = synth.f32_acts(g, N, K)
-
-        def run(rows):
-            reps, r = divmod(rows, w.shape[0])
-            for _ in range(reps):
-                oracle.base_mul_mat_f16(w, x, nth)
-            if r:
-                oracle.base_mul_mat_f16(w[:r], x, nth)
-
-        if cfg == "c1" or (cfg == "c5" and n == 1):
-            per_row = 2 * K + (4 * K * N) / M + 4 * N
-            v, rows, dt = grow(run, lambda r: per_row * r)
-            return v * 1e-9, f"{rows} weight rows of {M}x{K} x N={N} in {dt:.1f}s", nth
-        v, rows, dt = grow(run, lambda r: 2.0 * r * K * N)
-        return v * 1e-12, f"{rows} weight rows of the {M}x{K} projection x {N} tokens in {dt:.1f}s", nth
-    if cfg == "c3":
-        M, K = 14336, 4096
-        w = synth.q4k_blocks(g, 2048, K)
-        x = synth.f32_acts(g, n, K)
-
-        def run(rows):
-            reps, r = divmod(rows, w.shape[0])
-            for _ in range(reps):
-                oracle.base_mul_mat_q4k(w, x, nth)
-            if r:
-                oracle.base_mul_mat_q4k(w[:r], x, nth)
-        v, rows, dt = grow(run, lambda r: r * (K // 256 * 144 + 4 * n) + 4 * K * n * r / M)
-        return v * 1e-9, f"{rows} Q4_K rows of 14336x4096 x batch {n} in {dt:.1f}s", nth
-    if cfg == "c4":
-        B, Hq, Hkv, D = n, 32, 8, 128
-        kl = synth.kv_lengths(synth.rng(synth.seed_for(4, n)), B, 512, 8192)
-        L = int(kl.max())
-        Lc = min(L, 2048)
-        q, k, v = synth.fa_inputs(g, 1, Hq, Hkv, Lc, D)
-
-        def run(seqs):
-            for _ in range(seqs):
-                oracle.base_flash_attn(q, k, v, 1 / math.sqrt(D), nth=nth)
-        vv, seqs, dt = grow(run, lambda s: s * 4096.0 * Lc)
-        return vv * 1e-9, f"{seqs} sequences of L={Lc} (32q/8kv heads, D=128) in {dt:.1f}s", nth
-    raise ValueError(cfg)
+    key = (cfg, n)
+    if key not in _CPU_STEPS:
+        _CPU_STEPS[key] = CpuStep(cfg, n)
+    st = _CPU_STEPS[key]
+    t0 = time.perf_counter()
+    units = st.run()
+    dt = time.perf_counter() - t0
+    steps = 1
+    more = int(target_s / max(dt, 1e-6)) - 1
+    if more > 0:
+        t1 = time.perf_counter()
+        for _ in range(more):
+            units += st.run()
+        dt += time.perf_counter() - t1
+        steps += more
+    scale = 1e-12 if st.flops else 1e-9
+    return (units / dt * scale, f"{steps} whole step(s) of the workload in {dt:.2f}s ({st.what}, "
+            f"{st.nth} threads); host {oracle.host_cpu_model()}", st.nth)
 
 
 # --------------------------------------------------------------------------- arms
 
 def reference_arm(a):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     n = a.n or DEFAULT_N[a.config]
@@ -502,19 +568,14 @@ def reference_arm(a):
         vals.append(v)
     wall = time.perf_counter() - t0
     value = statistics.median(vals)
-    metric = {"c1": f"decode mul_mat GB/s (F16 W 8192x3072 . X 3072x{n}, fp32 acc)",
-              "c2": f"prefill mul_mat TFLOP/s (Llama-3.2-3B layer, 7 F16 projections, M={n} tokens, fp32 acc)",
-              "c3": f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})",
-              "c4": f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)",
-              "c5": f"sharded FFN mul_mat {unit} (Llama-3-70B, F16, N={n})"}[a.config]
     line = {
-        "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": a.gpus,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * wall / max(a.steps, 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/f32",
-        "data": "synthetic (seeded)",
-        "config": {"workload": f"{a.config} N={n} (CPU restatement of the reference kernels)"},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": nth, "kind": "port",
-                         "sample": desc + f"; host {oracle.host_cpu_model()}"},
+        "impl": "reference", "metric": metric_name(a.config, n, world), "value": value, "unit": unit,
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * wall / max(a.steps, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE[a.config],
+        "data": "synthetic (seeded), random-init weights",
+        "config": {"workload": workload_name(a.config, n, world),
+                   "implementation": "CPU restatement of the reference kernels (oracle/) on the host cores"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": nth, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -716,9 +777,7 @@ def mlz_arm(a):
     if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile_run:
         try:
             v, desc, nth = cpu_sample(a.config, n, a.cpu_seconds)
-            import oracle
-            cpu = {"value": v, "unit": w.unit, "cores": nth, "kind": "port",
-                   "sample": desc + f"; host {oracle.host_cpu_model()}"}
+            cpu = {"value": v, "unit": w.unit, "cores": nth, "kind": "port", "sample": desc}
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "unit": w.unit, "cores": None, "kind": "port", "sample": f"failed: {exc}"}
 

@@ -90,9 +90,18 @@ int mlzc_version(void);
 int mlzc_init(int device);
 /* Release every context, cached weight and workspace this library holds. */
 int mlzc_shutdown(void);
-/* Read and clear the kernel error word of `device` (MLZC_DEVERR_* bits).  Synchronises
- * the device. */
+/* Read and clear the kernel error word of `device` (MLZC_DEVERR_* bits), together with the
+ * word of the allocation-free entry point.  Synchronises the device.  It creates no
+ * context and allocates nothing, so callers of mlzc_flash_attn_dev_noalloc can use it. */
 int mlzc_device_errors(int device, uint32_t* out_bits);
+
+/* Failure-path self-test: launches one small kernel on `device` that waits on an
+ * mbarrier nothing arrives on, through the same bounded wait every kernel uses, with a
+ * limit of `limit_us` microseconds (1 .. 2 000 000).  The wait gives up, the kernel sets
+ * MLZC_DEVERR_WAIT_TIMEOUT in the device error word and returns, and *out_gave_up is 1;
+ * the context stays usable.  Synchronous.  No counterpart in the reference (its kernels
+ * have no waits). */
+int mlzc_selftest_wait_timeout(int device, uint32_t limit_us, int* out_gave_up);
 
 /* --------------------------------------------------- device-pointer kernels */
 
@@ -158,9 +167,12 @@ int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t worksp
  * the reference.  It allocates nothing: the split partials go to a fixed 16 MiB scratch
  * array inside the library's device image, held by every GPU that loads the library until
  * the process exits.  Calls needing more than that (mlzc_flash_attn_workspace_bytes)
- * fail with MLZC_ERR_NOMEM.  The first call on a device looks up the array's device
- * address (once, with that device current): make it before any stream capture.  All
- * calls share the array, so calls that overlap on the GPU race; serialise them. */
+ * fail with MLZC_ERR_NOMEM.  The first call on a device does that device's set-up, with
+ * the device current: it looks up the array's device address and sets the decode
+ * kernel's shared-memory attributes (once each); make it before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race; serialise them.  A kernel
+ * whose bounded wait gave up reports MLZC_DEVERR_WAIT_TIMEOUT in a device word that
+ * mlzc_device_errors reads and clears (without allocating). */
 int mlzc_flash_attn_dev_noalloc(const mlzc_fa_desc* desc, void* stream);
 
 /* ------------------------------------------------ host-pointer (hook) level */

@@ -2,8 +2,10 @@
 
 The compute lives in ``libmlzc.so`` (CUDA kernels + C ABI, see include/mlzc.h); this
 package is the host-side mirror of the reference's dispatch interface over that ABI.
-Importing it loads the library and fails if it has not been built -- there is no CPU
-fallback.
+The library is loaded by the first call that needs it (or by :func:`lib`), and that call
+raises ImportError if it has not been built -- there is no CPU fallback.  Importing the
+package alone maps no native code, so ``mlz_b200.synth`` (the seeded input generators)
+can be used by code that must not load the library.
 """
 from ._lib import (EXPORTS, FA_MODE_ALIBI, FA_MODE_GQA_BATCH, FA_MODE_SOFTCAP, LIB_PATH,
                    OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS, TYPE_F16, TYPE_F32, TYPE_Q4_K,
@@ -11,9 +13,8 @@ from ._lib import (EXPORTS, FA_MODE_ALIBI, FA_MODE_GQA_BATCH, FA_MODE_SOFTCAP, L
                    last_error, launch_count, lib, set_launch_overlap)
 from .ops import (Comm, Weight, device_errors, flash_attn_dispatch, flash_attn_workspace_bytes,
                   ggml_simd_try_flash_attn, ggml_simd_try_mul_mat, init, make_fa_desc, mul_mat,
-                  mul_mat_workspace_bytes, shutdown, tensor_view, weight_type_of)
-
-lib()  # load now: a missing or broken build is an import error, not a silent fallback
+                  mul_mat_workspace_bytes, selftest_wait_timeout, shutdown, tensor_view,
+                  weight_type_of)
 
 __all__ = [
     "EXPORTS", "FA_MODE_ALIBI", "FA_MODE_GQA_BATCH", "FA_MODE_SOFTCAP", "LIB_PATH", "OVERLAP_OFF",
@@ -21,6 +22,6 @@ __all__ = [
     "TYPE_F32", "TYPE_Q4_K", "UNIQUE_ID_BYTES", "FaDesc", "MlzcError", "TensorView", "check",
     "last_error", "launch_count", "lib", "Comm", "Weight", "device_errors", "flash_attn_dispatch",
     "flash_attn_workspace_bytes", "ggml_simd_try_flash_attn", "ggml_simd_try_mul_mat", "init",
-    "make_fa_desc", "mul_mat", "mul_mat_workspace_bytes", "shutdown", "tensor_view",
+    "make_fa_desc", "mul_mat", "mul_mat_workspace_bytes", "selftest_wait_timeout", "shutdown", "tensor_view",
     "weight_type_of",
 ]

@@ -24,6 +24,7 @@ UNIQUE_ID_BYTES = 128
 # every symbol include/mlzc.h declares (checked by the CPU test suite)
 EXPORTS = (
     "mlzc_launch_count", "mlzc_last_error", "mlzc_version", "mlzc_init", "mlzc_shutdown", "mlzc_device_errors",
+    "mlzc_selftest_wait_timeout",
     "mlzc_set_launch_overlap", "mlzc_get_launch_overlap",
     "mlzc_mul_mat_workspace_bytes", "mlzc_mul_mat_dev",
     "mlzc_flash_attn_workspace_bytes", "mlzc_flash_attn_dev", "mlzc_flash_attn_dev_noalloc",
@@ -90,6 +91,7 @@ def _declare(L: C.CDLL) -> None:
     L.mlzc_init.argtypes = [i32]
     L.mlzc_shutdown.argtypes = []
     L.mlzc_device_errors.argtypes = [i32, C.POINTER(u32)]
+    L.mlzc_selftest_wait_timeout.argtypes = [i32, u32, C.POINTER(i32)]
     L.mlzc_mul_mat_workspace_bytes.argtypes = [i32, i64, i64, i64, psz]
     L.mlzc_mul_mat_dev.argtypes = [i32, vp, sz, i64, i64, vp, sz, i64, vp, sz, vp, sz, vp]
     L.mlzc_flash_attn_workspace_bytes.argtypes = [C.POINTER(FaDesc), psz]

@@ -39,6 +39,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <atomic>
 #include <mutex>
 
 #include "internal.h"
@@ -567,13 +568,16 @@ fa_combine_kernel(const __grid_constant__ FaParams p, int P) {
 
 // Resident CTAs of the decode kernel per SM on the current device (sets the kernel's
 // shared-memory attributes on first use).
+// The per-device cache is atomic: two host threads may make their first call at the same
+// time (on one device or on different ones); both then set the same attributes and store
+// the same value.
 template <int D>
 int fa_ctas_per_sm(int* out) {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64];
     int dev = 0;
     MLZC_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(MLZC_ERR_INVALID, "flash_attn: device %d beyond 64", dev);
-    if (!cached[dev]) {
+    if (!cached[dev].load(std::memory_order_acquire)) {
         constexpr size_t smem = FaCfg<D>::kSmemBytes;
         for (auto* k : {fa_decode_kernel<D, false>, fa_decode_kernel<D, true>}) {
             MLZC_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -587,9 +591,9 @@ int fa_ctas_per_sm(int* out) {
         int sms = 0;
         MLZC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         if (occ < 1) return fail(MLZC_ERR_CUDA, "flash_attn: decode kernel does not fit on an SM");
-        cached[dev] = occ * sms;
+        cached[dev].store(occ * sms, std::memory_order_release);
     }
-    *out = cached[dev];
+    *out = cached[dev].load(std::memory_order_acquire);
     return MLZC_OK;
 }
 

@@ -51,16 +51,17 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Slow path of mbar_wait: polls until the phase completes, gives up after kWaitNs (setting
-// the error word and `abort_flag`) or as soon as another thread of the CTA set `abort_flag`.
+// Slow path of mbar_wait: polls until the phase completes, gives up after `limit_ns`
+// (kWaitNs for every kernel; setting the error word and `abort_flag`) or as soon as
+// another thread of the CTA set `abort_flag`.
 __device__ __noinline__ inline bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                   unsigned int* err) {
+                                                   unsigned int* err, uint64_t limit_ns = kWaitNs) {
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 31) == 0) {
             if (*abort_flag) return false;
-            if (global_ns() - t0 > kWaitNs) {
+            if (global_ns() - t0 > limit_ns) {
                 atomicOr(err, MLZC_DEVERR_WAIT_TIMEOUT);
                 *abort_flag = 1;
                 return false;

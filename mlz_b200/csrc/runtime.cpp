@@ -254,15 +254,24 @@ extern "C" int mlzc_shutdown(void) {
 
 extern "C" int mlzc_device_errors(int device, uint32_t* out_bits) {
     if (!out_bits) return fail(MLZC_ERR_INVALID, "null out_bits");
-    DeviceCtx* c = device_ctx(device);
-    if (!c) return MLZC_ERR_CUDA;
+    // No context is created here: a process that only used the allocation-free entry
+    // point has none, and reading its error word must not allocate either.
+    DeviceCtx* c = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_ctx_mu);
+        int ndev = 0;
+        cudaError_t e = cudaGetDeviceCount(&ndev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+        if (device < 0 || device >= ndev) return fail(MLZC_ERR_INVALID, "device %d out of range (%d devices)", device, ndev);
+        if (device < (int)g_ctx.size()) c = g_ctx[device].get();
+    }
     int prev = 0;
     cudaGetDevice(&prev);
     MLZC_CUDA_TRY(cudaSetDevice(device));
     unsigned int v = 0, vs = 0;
     cudaError_t e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemcpy(&v, c->err, sizeof v, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof v);
+    if (c && e == cudaSuccess) e = cudaMemcpy(&v, c->err, sizeof v, cudaMemcpyDeviceToHost);
+    if (c && e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof v);
     int st = e == cudaSuccess ? fa_take_static_errors(&vs) : MLZC_OK;
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "mlzc_device_errors");

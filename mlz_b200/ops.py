@@ -200,6 +200,15 @@ def device_errors(device: int = 0) -> int:
     return v.value
 
 
+def selftest_wait_timeout(device: int = 0, limit_us: int = 20000) -> bool:
+    """Runs the bounded-wait failure path once (mlzc_selftest_wait_timeout): a kernel waits
+    on an mbarrier nothing arrives on and must give up after ``limit_us``.  Returns True
+    when it gave up; the device error word then holds MLZC_DEVERR_WAIT_TIMEOUT."""
+    v = C.c_int32(0)
+    check(lib().mlzc_selftest_wait_timeout(device, limit_us, C.byref(v)))
+    return bool(v.value)
+
+
 class Weight:
     """Device-resident weight matrix for host-pointer calls (mlzc_weight)."""
 

@@ -35,9 +35,17 @@ FA_MODE_SOFTCAP = 0x10
 FA_MODE_GQA_BATCH = 0x04
 
 
+# The reference checkout this recipe compiles oracle/_ref from (read in place, never
+# copied); MLZ_REF_SIMD overrides it.  Where it is absent the prebuilt _ref is used.
+_REF_SIMD = os.environ.get("MLZ_REF_SIMD", "/root/reference/src/simd")
+
+
 def build(quiet: bool = True) -> None:
     """Compile liboracle.so (and oracle/_ref when the reference tree exists)."""
-    out = subprocess.run(["make", "-C", _HERE], capture_output=True, text=True)
+    args = ["make", "-C", _HERE]
+    if os.path.isdir(_REF_SIMD):
+        args.append("REF_SIMD=" + _REF_SIMD)
+    out = subprocess.run(args, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:
@@ -311,6 +319,22 @@ def ref_matmul_f32_small(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     assert M * N * K < 512
     c = np.full((M, N), np.nan, dtype=np.float32)
     ref().simd_matmul_f32(_p(a), _p(b), _p(c), M, N, K, 0, 1)
+    return c
+
+
+def ref_matmul_f16_small(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """The reference's simd_matmul_f16 (src/simd/simd_matmul.cpp:428-480): f16 A (M x K)
+    and B (K x N) widened to f32, simd_matmul_f32's scalar i-k-j loop (fp32, k ascending,
+    below M*N*K < 512: :217-223), C rounded to f16 (F16C round-to-nearest-even in chunks
+    of 8, :378-384; the scalar tail loop :387-406 truncates, so callers keep M*N a
+    multiple of 8).  Returns C's f16 bits (M x N)."""
+    a_bits = np.ascontiguousarray(a_bits, dtype=np.uint16)
+    b_bits = np.ascontiguousarray(b_bits, dtype=np.uint16)
+    M, K = a_bits.shape
+    N = b_bits.shape[1]
+    assert M * N * K < 512 and (M * N) % 8 == 0
+    c = np.full((M, N), 0x7E00, dtype=np.uint16)
+    ref().simd_matmul_f16(_p(a_bits), _p(b_bits), _p(c), M, N, K, 0, 1)
     return c
 
 

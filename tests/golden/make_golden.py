@@ -10,6 +10,10 @@ they were made).
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
 * matmul_reference.npz -- tiny row-major matmuls through the reference's simd_matmul_f32
                        scalar path (src/simd/simd_matmul.cpp:196-223).
+* matmul_f16_reference.npz -- tiny F16 matmuls through the reference's own F16 GEMM,
+                       simd_matmul_f16 (src/simd/simd_matmul.cpp:428-480): f16 operands,
+                       fp32 accumulation, f16 result.  A is an F16 weight block (M x K),
+                       B the activations already rounded to f16 (K x N).
 
 Usage: python tests/golden/make_golden.py
 """
@@ -94,6 +98,29 @@ def matmul_fixture() -> None:
     np.savez_compressed(os.path.join(HERE, "matmul_reference.npz"), **cases)
 
 
+def matmul_f16_fixture() -> None:
+    g = np.random.Generator(np.random.PCG64(17))
+    cases = {}
+    # (M, N, K), all with M*N*K < 512 (the scalar path) and M*N % 8 == 0 (the F16C
+    # rounding of the result).  K = 56 / 16 / 24 keep 16-byte rows, so the GPU takes its
+    # vectorised GEMV (N = 1), skinny tensor-core (N = 4, 8) and tcgen05 GEMM (N >= 17)
+    # kernels on them; K = 63 / 31 / 15 / 7 take the unaligned paths.
+    shapes = [(8, 1, 56), (1, 8, 56), (2, 4, 56), (1, 24, 16), (1, 32, 15), (4, 2, 63),
+              (8, 1, 63), (2, 4, 63), (8, 2, 31), (2, 8, 31), (4, 8, 15), (8, 8, 7)]
+    for i, (M, N, K) in enumerate(shapes):
+        a = (g.standard_normal((M, K)) * 0.5).astype(np.float16)
+        b = g.standard_normal((K, N)).astype(np.float16)
+        if i == 0:  # zeros, signed zeros, a subnormal and large finite values
+            a[0, :4] = np.array([0.0, -0.0, 6e-8, 1000.0], dtype=np.float16)
+            b[:4, 0] = np.array([-0.0, 5.0, 3000.0, -0.25], dtype=np.float16)
+        c = oracle.ref_matmul_f16_small(a.view(np.uint16), b.view(np.uint16))
+        cases[f"a{i}"] = a.view(np.uint16)
+        cases[f"b{i}"] = b.view(np.uint16)
+        cases[f"c{i}"] = c
+    assert oracle.ref_stub_hits() == 0
+    np.savez_compressed(os.path.join(HERE, "matmul_f16_reference.npz"), **cases)
+
+
 if __name__ == "__main__":
     oracle.build()
     if not oracle.ref_available():
@@ -101,4 +128,5 @@ if __name__ == "__main__":
     q4k_fixture()
     fa_fixture()
     matmul_fixture()
+    matmul_f16_fixture()
     print("fixtures written to", HERE)

@@ -127,3 +127,18 @@ def test_hook_threads_agree_on_fallback_without_gpu():
             t.join(timeout=30)
         assert all(not t.is_alive() for t in ts)
         assert results == [0] * nth
+
+
+def test_init_and_error_word_without_a_gpu_fail_with_a_status():
+    """On a host without a usable GPU the runtime entry points return a status (no abort),
+    with a message naming the failing CUDA call."""
+    import torch
+    if torch.cuda.is_available():
+        return  # the GPU failure tests cover a real device
+    L = mlz_b200.lib()
+    assert L.mlzc_init(0) == -3                               # MLZC_ERR_CUDA
+    assert "cudaGetDeviceCount" in mlz_b200.last_error()
+    v = C.c_uint32(0)
+    assert L.mlzc_device_errors(0, C.byref(v)) == -3
+    g = C.c_int32(0)
+    assert L.mlzc_selftest_wait_timeout(0, 1000, C.byref(g)) == -3

@@ -87,3 +87,46 @@ def test_power_of_two_scaling_is_exact_full_size(dev, N):
     torch.cuda.synchronize()
     assert torch.equal(y4, 4.0 * y)
     assert torch.isfinite(y).all()
+
+
+def test_f16_matches_reference_simd_matmul_f16(dev, golden):
+    """GPU F16 mul_mat against the reference's own F16 GEMM, simd_matmul_f16
+    (src/simd/simd_matmul.cpp:428-480, f16 operands, fp32 accumulation, f16 result), on
+    the committed fixture: the GPU's f32 result rounded to f16 is within 1 ulp of the
+    reference's f16 result.  The cases reach the GEMV (N = 1), skinny tensor-core
+    (N = 4, 8), tcgen05 GEMM (N >= 17) and unaligned kernels."""
+    f = golden("matmul_f16_reference.npz")
+    n = len([k for k in f.files if k.startswith("a")])
+    for i in range(n):
+        a, b, c = f[f"a{i}"], f[f"b{i}"], f[f"c{i}"]
+        x = np.ascontiguousarray(b.T.view(np.float16).astype(np.float32))
+        y = _run(dev, a.view(np.float16), x, y_pad=1)
+        got = y.astype(np.float16).view(np.int16).astype(np.int32)
+        want = c.T.view(np.int16).astype(np.int32)
+        # ulp distance on the sign-magnitude f16 encoding
+        to_ord = lambda v: np.where(v < 0, -(v & 0x7FFF), v)
+        assert np.abs(to_ord(got) - to_ord(want)).max() <= 1, f"case {i}: {a.shape} x {b.shape}"
+
+
+C5_MATS = [("gate", 28672, 8192), ("down", 8192, 28672)]
+
+
+@pytest.mark.parametrize("N", [1, 256])
+@pytest.mark.parametrize("name,M,K", C5_MATS)
+def test_f16_llama3_70b_ffn_full_shape(dev, name, M, K, N):
+    """Llama-3-70B FFN shapes at full size (gate/up 28672x8192, down 8192x28672) for
+    N = 1 (GEMV) and N = 256 (tcgen05 GEMM): every column of 48 rows spread over all of M
+    (both ends included) against the fp64 oracle."""
+    import torch
+    gen = torch.Generator(device=dev).manual_seed(7000 + M + N)
+    w = synth.f16_weights_dev(gen, M, K, dev)
+    x = torch.randn((N, K), generator=gen, device=dev)
+    y = mlz_b200.mul_mat(w, x)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([np.linspace(0, M - 1, 46).astype(np.int64), [1, M - 2]]))
+    rows_t = torch.from_numpy(rows).to(dev)
+    w_rows = w.index_select(0, rows_t).cpu().numpy()
+    want = oracle.mul_mat_f16(w_rows.view(np.uint16), x.cpu().numpy())
+    got = y.index_select(1, rows_t).cpu().numpy()
+    assert np.isfinite(got).all()
+    assert oracle.rel_err(got, want) <= TOL

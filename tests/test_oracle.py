@@ -26,6 +26,22 @@ def test_f16_narrowing_matches_ieee_rne():
     assert (oracle.f32_to_f16_bits(x) == want).all()
 
 
+def test_f16_mul_mat_matches_reference_simd_matmul_f16(golden):
+    """The oracle's F16 product (f16 weights x activations rounded to f16, accumulated in
+    fp64), rounded to f16, equals bit for bit the reference's own F16 GEMM
+    simd_matmul_f16 (src/simd/simd_matmul.cpp:428-480: f16 operands, fp32 accumulation,
+    f16 result) on every fixture case."""
+    f = golden("matmul_f16_reference.npz")
+    n = len([k for k in f.files if k.startswith("a")])
+    assert n >= 12
+    for i in range(n):
+        a, b, c = f[f"a{i}"], f[f"b{i}"], f[f"c{i}"]
+        x = b.T.view(np.float16).astype(np.float32)            # (N, K): ggml columns of X
+        y = oracle.mul_mat_f16(a, x)                           # (N, M), fp64
+        got = np.asarray(y, dtype=np.float64).astype(np.float16).view(np.uint16)
+        assert np.array_equal(got, c.T), f"case {i}: {a.shape} x {b.shape}"
+
+
 def test_q4k_dequant_matches_gguf_decoder(golden):
     f = golden("q4k_gguf.npz")
     got = oracle.q4k_dequant(f["blocks"], int(f["K"]))

@@ -56,6 +56,34 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(dev):
         assert np.max(np.abs(a - b)) / max(np.max(np.abs(a)), 1e-30) <= 1e-3
 
 
+def test_noalloc_batch_slices_reuse_the_scratch(dev):
+    """More than 1024 sequences: one call launches its batch in slices of 1024, each slice's
+    decode kernel rewriting the prefix table and partial records in the shared scratch
+    that the previous slice's combine kernel read.  Kept small enough to fit the scratch
+    (one kv head, D = 64, short sequences)."""
+    import torch
+    L = mlz_b200.lib()
+    B, Hq, Hkv, Lmax, D = 1100, 4, 1, 40, 64
+    q, k, v, kl = _inputs(dev, 950, B, Hq, Hkv, Lmax, D)
+    scale = 1.0 / np.sqrt(D)
+    out_ws = torch.full((B, Hq, 1, D), float("nan"), device=dev)
+    out_na = torch.full((B, Hq, 1, D), float("nan"), device=dev)
+    d_ws = _desc(q, k, v, out_ws, kl, scale)
+    d_na = _desc(q, k, v, out_na, kl, scale)
+    wsb = C.c_size_t(0)
+    mlz_b200.check(L.mlzc_flash_attn_workspace_bytes(C.byref(d_ws), C.byref(wsb)))
+    assert 0 < wsb.value <= 16 << 20
+    ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        mlz_b200.check(L.mlzc_flash_attn_dev(C.byref(d_ws), ws.data_ptr(), wsb.value, stream))
+        mlz_b200.check(L.mlzc_flash_attn_dev_noalloc(C.byref(d_na), stream))
+        torch.cuda.synchronize()
+        a, b = out_ws.cpu().numpy(), out_na.cpu().numpy()
+        assert np.isfinite(b).all()
+        assert np.max(np.abs(a - b)) / max(np.max(np.abs(a)), 1e-30) <= 1e-3
+
+
 def test_noalloc_rejects_calls_beyond_its_scratch(dev):
     import torch
     # 2048 sequences (launched 1024 at a time) x 8 kv heads: 1024 x 8 segment records of
