@@ -17,10 +17,14 @@
 //                 (M = 128, N = BN, K = 16) per K step, the MT M-tiles sharing the X tile,
 //                 fp32 accumulators in TMEM; commits free smem stages and publish
 //                 finished accumulators;
-//        warps 2-9 epilogue: tcgen05.ld 32 lanes x 32 columns, coalesced stores of
-//                 Y[n][m] (32 consecutive m per warp store); two warps per TMEM lane
-//                 quarter split the columns, which doubles the stores in flight (the
-//                 drain of an accumulator is store-bound).
+//        warps 2-9 epilogue: tcgen05.ld 32 lanes x 32 columns; each 32 x 32 block is
+//                 written to a per-warp shared-memory staging buffer in Y's own order
+//                 (32 consecutive m per column n) and stored with one TMA tensor store
+//                 (cp.async.bulk.tensor, bulk group), so a warp's drain costs 32 shared
+//                 stores per block instead of 32 global ones, and the TMEM accumulator is
+//                 released as soon as it has been read.  Two warps per TMEM lane quarter
+//                 split the columns.  Y without 16-byte alignment (and split-K partial
+//                 tiles) take plain coalesced global stores.
 //      When two accumulator sets fit in TMEM (2*MT*BN <= 512 columns) the epilogue of
 //      tile t overlaps the MMAs of tile t+1.  MT = 2 (256 x 256 per SM) needs 64 KB of
 //      operands per 1024 MMA cycles instead of 48 KB per 512 for 128 x 256, which is what
@@ -34,6 +38,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -45,7 +50,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;                       // one 128-byte swizzle atom of f16
 constexpr int kEpiWarps = 8;       // two warps per TMEM lane quarter, each draining half the columns
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemMax = 232448;             // dynamic shared memory per block (227 KB)
+constexpr int kSmemFixed = 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kStgBytes = 32 * 32 * 4;  // one 32 x 32 f32 staging block of the epilogue
 
 // ------------------------------------------------------------------ PTX wrappers
 
@@ -65,6 +72,27 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+
+// Tiled TMA store of a box from shared memory (one bulk group per call); elements outside
+// the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's bulk groups still read their shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -134,14 +162,20 @@ struct TileCfg {
     static constexpr uint32_t kABytes = (uint32_t)kRows * BK * 2;
     static constexpr uint32_t kBBytes = (uint32_t)BN * BK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (kSmemBudget - 2048) / kStageBytes > 12 ? 12 : (kSmemBudget - 2048) / kStageBytes;
+    // epilogue staging: two blocks per warp when that still leaves three pipeline stages
+    static constexpr int kStgBufs = (kSmemMax - kSmemFixed - 2 * kEpiWarps * (int)kStgBytes) / (int)kStageBytes >= 3 ? 2 : 1;
+    static constexpr uint32_t kStgTotal = (uint32_t)kEpiWarps * kStgBufs * kStgBytes;
+    static constexpr int kStagesFit = (kSmemMax - kSmemFixed - (int)kStgTotal) / (int)kStageBytes;
+    static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
     static constexpr int kAccCols = MT * BN;                           // one accumulator set
     static constexpr int kBufs = 2 * kAccCols <= 512 ? 2 : 1;          // double-buffered when TMEM allows
     static constexpr uint32_t kTmemCols = kBufs * kAccCols < 32 ? 32u
                                           : (kBufs * kAccCols <= 64 ? 64u
                                           : (kBufs * kAccCols <= 128 ? 128u
                                           : (kBufs * kAccCols <= 256 ? 256u : 512u)));
-    static constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kStgTotal + kSmemFixed;
+    static_assert(kStages >= 2, "pipeline needs two stages");
+    static_assert(kSmemBytes <= (size_t)kSmemMax, "shared memory");
 };
 
 struct GemmArgs {
@@ -156,11 +190,12 @@ struct GemmArgs {
     float* part;          // [splits][tiles][BN][128*MT] partial accumulators (splits > 1)
     int* tile_count;      // per tile: splits finished (zeroed by the narrowing kernel)
     unsigned int* err;
+    int tma_store;        // 1: Y is written through tmY (16-byte aligned Y and column stride)
 };
 
 template <int BN, int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
+gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmY, GemmArgs g) {
     using C = TileCfg<BN, MT>;
     constexpr int STAGES = C::kStages;
     constexpr int NBUF = C::kBufs;
@@ -169,7 +204,8 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smA = smem;
     uint8_t* smB = smem + STAGES * C::kABytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes);
+    float* stg_all = reinterpret_cast<float*>(smem + STAGES * C::kStageBytes);   // epilogue staging
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStageBytes + C::kStgTotal);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
@@ -193,6 +229,7 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         tma_prefetch_desc(&tmA);
+        if (g.tma_store) tma_prefetch_desc(&tmY);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -213,8 +250,10 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
     auto work_coords = [&](int w, int& m0, int& n0, int& kb0, int& kb1) {
         const int tile = w % tiles;
         const int split = w / tiles;
-        m0 = (tile % g.num_m) * ROWS;
-        n0 = (tile / g.num_m) * BN;
+        // N-tiles fastest: the CTAs in flight share each W tile (read from DRAM once per
+        // round, by all its N-tiles together) and all of X stays in L2
+        m0 = (tile / g.num_n) * ROWS;
+        n0 = (tile % g.num_n) * BN;
         kb0 = split * kper;
         kb1 = min(kb0 + kper, g.kblocks);
     };
@@ -305,6 +344,11 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
         constexpr int kChunks = BN < 32 ? 1 : BN / 32;
         // chunk groups of G go round-robin to the NSUB warps of a quarter
         constexpr int G = kChunks >= 2 * NSUB ? 2 : 1;
+        constexpr int NSTG = C::kStgBufs;
+        float* stg = stg_all + (size_t)(warp - 2) * NSTG * (kStgBytes / 4);
+        // TMA stores: full 32 x 32 blocks, whole tiles (no split partials)
+        const bool tma_out = (kCols == 32) && g.tma_store && g.splits == 1;
+        uint32_t nst = 0;                        // staging blocks this warp has stored
         uint32_t t = 0;
         for (int w = blockIdx.x; w < g.num_work; w += gridDim.x, ++t) {
             int m0, n0, kb0, kb1;
@@ -338,7 +382,21 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
                     for (int gg = 0; gg < G; ++gg) {
                         if (c0 + gg >= kChunks) continue;
                         const int c = (c0 + gg) * 32;
-                        if (g.splits == 1) {
+                        if (tma_out) {
+                            // block (32 rows of this lane quarter x 32 columns) -> staging in
+                            // Y's order (column-major over m), then one tensor store
+                            float* buf = stg + (nst % NSTG) * (kStgBytes / 4);
+                            if (nst >= (uint32_t)NSTG) {
+                                if (lane == 0) bulk_wait_read<NSTG - 1>();
+                                __syncwarp();
+                            }
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = __uint_as_float(r[gg][j]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) tma_store_2d(&tmY, smem_u32(buf), m0 + i * BM + quarter * 32, n0 + c);
+                            ++nst;
+                        } else if (g.splits == 1) {
                             if (m < g.M) {
 #pragma unroll
                                 for (int j = 0; j < kCols; ++j) {
@@ -418,6 +476,8 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmArgs g) {
         }
     }
 
+    // the epilogue's tensor stores read shared memory until they complete
+    if (warp >= 2 && lane == 0) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -486,6 +546,21 @@ int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, 
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MLZC_OK;
+}
+
+// 2-D f32 tensor map of Y (ggml dst: N columns of M floats, y_cs bytes apart), 32 x 32
+// boxes, no swizzle: the epilogue's staging blocks.
+int make_y_map(CUtensorMap* map, float* y, uint64_t M, uint64_t N, uint64_t y_cs) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {M, N};
+    const cuuint64_t strides[1] = {y_cs};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MLZC_ERR_CUDA, "cuTensorMapEncodeTiled (Y) failed (%d)", (int)r);
     return MLZC_OK;
 }
 
@@ -567,7 +642,7 @@ int current_sm_count() {
 }
 
 template <int BN, int MT>
-int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, GemmArgs g, cudaStream_t s) {
+int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& ty, GemmArgs g, cudaStream_t s) {
     using Cfg = TileCfg<BN, MT>;
     static bool attr_set[64] = {};
     const int dev = c->device < 64 ? c->device : 63;
@@ -577,7 +652,7 @@ int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, GemmArgs g, cudaStrea
         attr_set[dev] = true;
     }
     const int grid = std::min(g.num_work, c->sm_count);
-    MLZC_CUDA_TRY(launch_pdl(gemm_f16_tc_kernel<BN, MT>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, s, ta, g));
+    MLZC_CUDA_TRY(launch_pdl(gemm_f16_tc_kernel<BN, MT>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, s, ta, ty, g));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;
@@ -636,14 +711,22 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
     g.x16t = x16t;
     g.part = partials;
     g.tile_count = counters;
-    if (pl.MT == 2) return BN == 192 ? launch_tile<192, 2>(c, ta, g, s) : launch_tile<256, 2>(c, ta, g, s);
+    // Y through TMA stores: base and column stride 16-byte aligned (the tensor-map rules)
+    CUtensorMap ty;
+    std::memset(&ty, 0, sizeof ty);
+    g.tma_store = ((uintptr_t)y % 16 == 0 && y_col_bytes % 16 == 0 && pl.splits == 1 && pl.BN >= 32) ? 1 : 0;
+    if (g.tma_store) {
+        st = make_y_map(&ty, y, (uint64_t)M, (uint64_t)N, y_col_bytes);
+        if (st != MLZC_OK) return st;
+    }
+    if (pl.MT == 2) return BN == 192 ? launch_tile<192, 2>(c, ta, ty, g, s) : launch_tile<256, 2>(c, ta, ty, g, s);
     switch (BN) {
-        case 16: return launch_tile<16, 1>(c, ta, g, s);
-        case 32: return launch_tile<32, 1>(c, ta, g, s);
-        case 64: return launch_tile<64, 1>(c, ta, g, s);
-        case 96: return launch_tile<96, 1>(c, ta, g, s);
-        case 128: return launch_tile<128, 1>(c, ta, g, s);
-        default: return launch_tile<256, 1>(c, ta, g, s);
+        case 16: return launch_tile<16, 1>(c, ta, ty, g, s);
+        case 32: return launch_tile<32, 1>(c, ta, ty, g, s);
+        case 64: return launch_tile<64, 1>(c, ta, ty, g, s);
+        case 96: return launch_tile<96, 1>(c, ta, ty, g, s);
+        case 128: return launch_tile<128, 1>(c, ta, ty, g, s);
+        default: return launch_tile<256, 1>(c, ta, ty, g, s);
     }
 }
 

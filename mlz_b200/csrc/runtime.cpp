@@ -29,6 +29,7 @@ namespace mlzc {
 
 namespace {
 thread_local std::string g_last_error;
+thread_local int g_last_status = MLZC_OK;   // status of the calling thread's last fail()
 
 std::mutex g_ctx_mu;
 std::vector<std::unique_ptr<DeviceCtx>> g_ctx;   // indexed by device id
@@ -65,6 +66,7 @@ int fail(int status, const char* fmt, ...) {
     vsnprintf(buf, sizeof buf, fmt, ap);
     va_end(ap);
     g_last_error = buf;
+    g_last_status = status;
     return status;
 }
 
@@ -228,8 +230,9 @@ extern "C" int mlzc_get_launch_overlap(int* out_mode) {
 }
 
 extern "C" int mlzc_init(int device) {
+    g_last_status = MLZC_OK;
     DeviceCtx* c = device_ctx(device);
-    if (!c) return MLZC_ERR_CUDA;
+    if (!c) return g_last_status != MLZC_OK ? g_last_status : MLZC_ERR_CUDA;
     g_hook_device = device;
     return MLZC_OK;
 }
