@@ -13,6 +13,8 @@ Workloads (synthetic seeded inputs of the named shapes; random-init weights):
   c4  flash-attention decode, 16 sequences, L ~ U{512..8192}, 32 q / 8 kv heads, D = 128
   c5  Llama-3-70B FFN (gate/up 28672x8192, down 8192x28672) row-sharded over the ranks with
       NCCL all-gather of the output slices, N in {1, 256}
+  c6  Q6_K decode mul_mat on the Llama-3.1-8B shapes of c3, batch N (Q4_K_M files carry
+      Q6_K tensors; the reference hook routes them with Q4_K)
 
 A step is one pass of the hot path over one batch.  `value` is whole-job throughput with
 inputs resident in HBM; `e2e` is the same metric through the reference-facing plugin
@@ -57,12 +59,14 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c6"])
     ap.add_argument("--n", "--size", dest="n", type=int, default=None,
                     help="activation columns / tokens / batch (--size under torchrun, whose parser takes --n)")
     ap.add_argument("--impl", default="mlz", choices=["mlz", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-rows", action="store_true",
+                    help="measure the headline workload only (no rows of the other configurations)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU sample length")
     ap.add_argument("--no-graph", action="store_true",
                     help="time the eager launches instead of a CUDA-graph replay of the K steps")
@@ -75,8 +79,8 @@ def parse_args():
     return ap.parse_args()
 
 
-DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 256}
-DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16"}
+DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 256, "c6": 4}
+DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32"}
 
 
 def metric_name(cfg: str, n: int, world: int) -> str:
@@ -89,6 +93,8 @@ def metric_name(cfg: str, n: int, world: int) -> str:
         return f"decode Q4_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
     if cfg == "c4":
         return f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
+    if cfg == "c6":
+        return f"decode Q6_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
     return (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
             f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, NCCL all-gather)")
 
@@ -114,6 +120,8 @@ def workload_name(cfg: str, n: int, world: int) -> str:
         return f"c3 Q4_K mul_mat Llama-3.1-8B shapes, batch {n}"
     if cfg == "c4":
         return f"c4 FA decode GQA, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
+    if cfg == "c6":
+        return f"c6 Q6_K mul_mat Llama-3.1-8B shapes, batch {n}"
     return f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}"
 
 
@@ -314,6 +322,43 @@ class C3(Workload):
                 sum(y.numel() * 4 for y in ys))
 
 
+class C6(C3):
+    """Q6_K decode mul_mat on the shapes of c3 (210-byte blocks)."""
+    dtype = "q6_k/f32"
+
+    def roofline_kernel(self, j):
+        m, k = self.SHAPES[j]
+        return f"q6k_mma_kernel<{2 if self.N > 8 else 1}>, {m}x{k} (one call)"
+
+    def __init__(self, n, dev, gen):
+        import torch
+        from mlz_b200 import synth
+        self.N = n
+        self.metric = metric_name("c6", n, 1)
+        per_step = sum(m * k // 256 * 210 for m, k in self.SHAPES)
+        self.R = _rot_copies(per_step)
+        self.W = [[synth.q6k_blocks_dev(gen, m, k, dev) for (m, k) in self.SHAPES] for _ in range(self.R)]
+        self.X = [synth.f32_acts_dev(gen, n, k, dev) for (_, k) in self.SHAPES]
+        self.Y = [torch.empty((n, m), dtype=torch.float32, device=dev) for (m, _) in self.SHAPES]
+        self.ws = None
+        self.config = {"workload": workload_name("c6", n, 1), "batch": n,
+                       "shapes": "4096x4096, 14336x4096, 4096x14336",
+                       "l2": f"rotates {self.R} weight sets ({self.R * per_step / 1e6:.0f} MB >= 4x L2)"}
+
+    def _bytes(self, m, k):
+        return m * k // 256 * 210 + 4 * k * self.N + 4 * m * self.N
+
+    def launches(self, i):
+        import mlz_b200
+        Ws = self.W[i % self.R]
+        return [(lambda j=j: mlz_b200.mul_mat(Ws[j], self.X[j], out=self.Y[j], w_type=mlz_b200.TYPE_Q6_K),
+                 self._bytes(m, k)) for j, (m, k) in enumerate(self.SHAPES)]
+
+    def host_weights(self):
+        self.hW = [w.cpu().numpy() for w in self.W[0]]
+        return [(w, 14, k) for w, (_, k) in zip(self.hW, self.SHAPES)]
+
+
 class C4(Workload):
     unit = "GB/s"
     bound = "hbm"
@@ -477,12 +522,16 @@ class CpuStep:
             self.kernel = lambda w, x: oracle.base_mul_mat_f16(w, x, self.nth)
             self.flops = cfg == "c2" or (cfg == "c5" and n > 1)
             self.what = "convert-then-GEMM restatement"
-        elif cfg == "c3":
+        elif cfg in ("c3", "c6"):
+            q6 = cfg == "c6"
             for (M, K) in C3_SHAPES:
-                self.parts.append((M, K, synth.q4k_blocks(g, min(M, 4096), K), synth.f32_acts(g, n, K)))
-            self.kernel = lambda w, x: oracle.base_mul_mat_q4k(w, x, self.nth)
+                blk = (synth.q6k_blocks if q6 else synth.q4k_blocks)(g, min(M, 4096), K)
+                self.parts.append((M, K, blk, synth.f32_acts(g, n, K)))
+            self.kernel = ((lambda w, x: oracle.base_mul_mat_q6k(w, x, self.nth)) if q6 else
+                           (lambda w, x: oracle.base_mul_mat_q4k(w, x, self.nth)))
             self.flops = False
-            self.what = "Q8_K quantise + Q4_K x Q8_K dot restatement"
+            self.block_bytes = 210 if q6 else 144
+            self.what = f"Q8_K quantise + {'Q6_K' if q6 else 'Q4_K'} x Q8_K dot restatement"
         elif cfg == "c4":
             self.kl = c4_lengths(n)
             self.slots = 4
@@ -512,8 +561,8 @@ class CpuStep:
                 self.kernel(w[:r], x)
             if self.flops:
                 units += 2.0 * M * K * n
-            elif self.cfg == "c3":
-                units += M * (K // 256) * 144 + 4 * K * n + 4 * M * n
+            elif self.cfg in ("c3", "c6"):
+                units += M * (K // 256) * self.block_bytes + 4 * K * n + 4 * M * n
             else:
                 units += 2.0 * M * K + 4 * K * n + 4 * M * n
         return units
@@ -555,7 +604,8 @@ def reference_arm(a):
     if rank != 0:
         return
     n = a.n or DEFAULT_N[a.config]
-    unit = {"c1": "GB/s", "c2": "TFLOP/s", "c3": "GB/s", "c4": "GB/s", "c5": "GB/s" if n == 1 else "TFLOP/s"}[a.config]
+    unit = {"c1": "GB/s", "c2": "TFLOP/s", "c3": "GB/s", "c4": "GB/s", "c5": "GB/s" if n == 1 else "TFLOP/s",
+            "c6": "GB/s"}[a.config]
     import oracle
     oracle.build()
     per_step = max(a.cpu_seconds / max(a.steps, 1), 0.5)
@@ -581,6 +631,186 @@ def reference_arm(a):
     print(json.dumps(line), flush=True)
 
 
+def make_workload(cfg: str, n: int, dev, rank: int, world: int, comm):
+    import torch
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + 100 * int(cfg[1]) + n + rank)
+    wl = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c6": C6}.get(cfg)
+    return wl(n, dev, gen) if wl else C5(n, dev, gen, rank, world, comm)
+
+
+def time_workload(w, a, world, K: int, warmup: int, use_graph: bool):
+    """Warm-up, then K steps timed on the device: a CUDA-graph replay of the K steps (or the
+    eager launches), and each call's K repetitions replayed as their own graph for the
+    roofline.  Returns a dict of the timings (milliseconds, this rank)."""
+    import torch
+    import mlz_b200
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        for f, _ in w.launches(i):
+            f()
+    torch.cuda.synchronize()
+    units_l = [u for _, u in w.launches(0)]
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in units_l]
+          for _ in range(K)]
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    # Hold the GPU with a short spin (torch.cuda._sleep) while the host queues the K steps
+    # and their events, so the per-launch events time the kernels rather than the host's
+    # launch cadence.  The spin is enqueued before t0 and is not part of the timed region.
+    t_host = time.perf_counter()
+    for f, _ in w.launches(0):
+        f()
+    torch.cuda.synchronize()
+    host_per_step = time.perf_counter() - t_host
+    torch.cuda._sleep(int(min(2e9, max(2e6, 3.0 * host_per_step * K * 2.0e9))))
+    n0 = mlz_b200.launch_count()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s_ in range(K):
+        for j, (f, _) in enumerate(w.launches(s_)):
+            ev[s_][j][0].record(stream)
+            f()
+            ev[s_][j][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    out = {"n_launch": mlz_b200.launch_count() - n0, "ms_eager": t0.elapsed_time(t1),
+           "per_launch_ms": [sum(ev[s_][j][0].elapsed_time(ev[s_][j][1]) for s_ in range(K)) / K
+                             for j in range(len(units_l))],
+           "timing": "eager launches", "call_timing": "eager events around each call", "units_l": units_l}
+    out["ms_local"] = out["ms_eager"]
+    # The same K steps captured once as a CUDA graph and replayed: the decode kernels are
+    # shorter than the host's per-call launch cost, so the eager loop would time Python.
+    if use_graph:
+        gs = torch.cuda.Stream()
+        gs.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        n0 = mlz_b200.launch_count()
+        try:
+            with torch.cuda.graph(graph, stream=gs):
+                for s_ in range(K):
+                    for f, _ in w.launches(s_):
+                        f()
+        except Exception as exc:  # a call that cannot be captured: keep the eager timing
+            use_graph = False
+            out["timing"] = f"eager launches ({type(exc).__name__} in graph capture)"
+            del graph
+            torch.cuda.synchronize()
+    if use_graph:
+        out["n_launch"] = mlz_b200.launch_count() - n0       # kernels the replay runs
+        with torch.cuda.stream(gs):
+            graph.replay()                                     # untimed first replay
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(gs):
+            g0.record(gs)
+            graph.replay()
+            g1.record(gs)
+        torch.cuda.synchronize()
+        out["ms_local"] = g0.elapsed_time(g1)
+        out["timing"] = "CUDA graph replay of the K steps"
+        del graph
+        # Per-call device times for the roofline: each call's K repetitions (the same
+        # inputs and weight rotation as in the steps) captured as their own graph and timed
+        # by events around its replay -- event nodes inside a graph would add microseconds
+        # to every call.  The sharded calls wait on their peers, so every rank replays
+        # every call's graph in the same order.
+        try:
+            per = []
+            for j in range(len(units_l)):
+                gj = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gj, stream=gs):
+                    for s_ in range(K):
+                        w.launches(s_)[j][0]()
+                with torch.cuda.stream(gs):
+                    gj.replay()                                # untimed first replay
+                torch.cuda.synchronize()
+                c0 = torch.cuda.Event(enable_timing=True)
+                c1 = torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(gs):
+                    c0.record(gs)
+                    gj.replay()
+                    c1.record(gs)
+                torch.cuda.synchronize()
+                per.append(c0.elapsed_time(c1) / K)
+                del gj
+            out["per_launch_ms"] = per
+            out["call_timing"] = "each call's K repetitions replayed as a CUDA graph, timed by events"
+        except Exception as exc:  # keep the eager per-call events
+            out["call_timing"] = f"eager events around each call ({type(exc).__name__} with per-call graphs)"
+    return out
+
+
+def roofline_of(w, t, peaks, clocks, ms):
+    """Roofline of the dominant call (largest average device time); c2 pools its 7 calls."""
+    units_l, per = t["units_l"], t["per_launch_ms"]
+    jdom = max(range(len(units_l)), key=lambda j: per[j])
+    if isinstance(w, C2):  # all 7 projections run the same GEMM kernel: pool them
+        ach = sum(units_l) / (sum(per) * 1e-3) * 1e-12
+    else:
+        ach = units_l[jdom] / (per[jdom] * 1e-3) * w.unit_scale()
+    # tensor peak: the sustained (power-capped) figure when the timed region ran under the
+    # power cap or for over a second -- the regime that figure was measured in -- else burst
+    power_capped = "sw_power_cap" in ((clocks or {}).get("reasons") or [])
+    long_run = ms * 1e-3 > 1.0 or power_capped
+    if w.bound == "hbm":
+        peak, peak_name = peaks["hbm_gbs"], "hbm_gbs"
+    else:
+        peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
+        peak_name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
+    r = {"bound": w.bound, "achieved": ach, "peak": peak, "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s",
+         "frac": ach / peak, "traffic": None,
+         "peak_source": f"{peaks['source']} {peak_name}" + (" (sw_power_cap active in the timed region)"
+                                                            if power_capped and w.bound != "hbm" else ""),
+         "kernel": w.roofline_kernel(jdom), "call_timing": t["call_timing"]}
+    if w.bound != "hbm":
+        r["frac_of_burst"] = ach / peaks["bf16_tflops"]
+    return r
+
+
+# Measured rows that the default line carries besides its headline workload, so that one
+# run records every configuration: (config, N).  On several GPUs only the other c5 size.
+EXTRA_ROWS_1GPU = [("c2", 2048), ("c2", 512), ("c1", 1), ("c1", 8), ("c1", 32), ("c3", 1), ("c3", 4), ("c3", 16),
+                   ("c4", 16), ("c5", 256), ("c6", 1), ("c6", 4), ("c6", 16)]
+
+
+def extra_rows(a, n_head, dev, rank, world, comm, peaks):
+    import torch
+    rows_cfg = EXTRA_ROWS_1GPU if world == 1 else [("c5", 256 if n_head == 1 else 1)]
+    rows = []
+    for cfg, n in rows_cfg:
+        if cfg == a.config and n == n_head:
+            continue
+        try:
+            w = make_workload(cfg, n, dev, rank, world, comm if cfg == "c5" else None)
+            t = time_workload(w, a, world, max(5, min(a.steps, 20)), 3, not a.no_graph)
+            ms = max_over_ranks(t["ms_local"], world)
+            K = max(5, min(a.steps, 20))
+            units = w.work_units()
+            job = units if isinstance(w, C5) else units * world
+            row = {"workload": w.config["workload"], "metric": w.metric, "unit": w.unit,
+                   "value": job * K / (ms * 1e-3) * w.unit_scale(), "ms_per_step": ms / K,
+                   "roofline": roofline_of(w, t, peaks, None, ms), "gpu_launches": t["n_launch"]}
+            if rank == 0 and world == 1 and not a.no_cpu_baseline:
+                v, desc, nth = cpu_sample(cfg, n, 1.0)
+                row["cpu_baseline"] = {"value": v, "unit": w.unit, "cores": nth, "kind": "port", "sample": desc}
+            rows.append(row)
+            del w
+        except Exception as exc:  # a row is reported, never required
+            rows.append({"workload": f"{cfg} N={n}", "error": f"{type(exc).__name__}: {exc}"[:300]})
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return rows
+
+
 def mlz_arm(a):
     import torch
     import mlz_b200
@@ -598,19 +828,16 @@ def mlz_arm(a):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    comm = None
-    if a.config == "c5" and world > 1:
-        import torch.distributed as dist
+    comm = None   # one GPU runs c5 unsharded (the plain mul_mat): nothing to gather
+    if world > 1 and (a.config == "c5" or not a.no_rows):
         obj = [mlz_b200.Comm.unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
+        if world > 1:
+            import torch.distributed as dist
+            dist.broadcast_object_list(obj, src=0)
         comm = mlz_b200.Comm(world, rank, local, obj[0], timeout_ms=60000)
 
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1000 + 100 * int(a.config[1]) + n + rank)
-    wl = {"c1": C1, "c2": C2, "c3": C3, "c4": C4}.get(a.config)
-    w = wl(n, dev, gen) if wl else C5(n, dev, gen, rank, world, comm)
+    w = make_workload(a.config, n, dev, rank, world, comm)
     peaks = load_peaks()
-    stream = torch.cuda.current_stream()
 
     # warm-up (first calls also create contexts / workspaces outside the timed region)
     for i in range(a.warmup if a.profile_run else max(a.warmup, 3)):
@@ -631,147 +858,27 @@ def mlz_arm(a):
     torch.cuda.synchronize()
 
     K = a.steps
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in w.launches(0)]
-          for _ in range(K)]
-    units_l = [u for _, u in w.launches(0)]
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    torch.cuda.synchronize()
-    # Hold the GPU with a short spin (torch.cuda._sleep) while the host queues the K steps
-    # and their events, so the per-launch events time the kernels rather than the host's
-    # launch cadence.  The spin is enqueued before t0 and is not part of the timed region.
-    t_host = time.perf_counter()
-    for f, _ in w.launches(0):
-        f()
-    torch.cuda.synchronize()
-    host_per_step = time.perf_counter() - t_host
-    torch.cuda._sleep(int(min(2e9, max(2e6, 3.0 * host_per_step * K * 2.0e9))))
-    n0 = mlz_b200.launch_count()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for s in range(K):
-        for j, (f, _) in enumerate(w.launches(s)):
-            ev[s][j][0].record(stream)
-            f()
-            ev[s][j][1].record(stream)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    n_launch = mlz_b200.launch_count() - n0
-    ms_eager = t0.elapsed_time(t1)
-    per_launch_ms = [sum(ev[s][j][0].elapsed_time(ev[s][j][1]) for s in range(K)) / K for j in range(len(units_l))]
-
-    # The same K steps captured once as a CUDA graph and replayed: the decode kernels are
-    # shorter than the host's per-call launch cost, so the eager loop would time Python.
-    use_graph = not a.no_graph and not a.profile_run
-    timing = "eager launches"
-    call_timing = "eager events around each call"
-    if use_graph:
-        gs = torch.cuda.Stream()
-        gs.wait_stream(torch.cuda.current_stream())
-        graph = torch.cuda.CUDAGraph()
-        n0 = mlz_b200.launch_count()
-        try:
-            with torch.cuda.graph(graph, stream=gs):
-                for s_ in range(K):
-                    for f, _ in w.launches(s_):
-                        f()
-        except Exception as exc:  # a call that cannot be captured: keep the eager timing
-            use_graph = False
-            timing = f"eager launches ({type(exc).__name__} in graph capture)"
-            del graph
-            torch.cuda.synchronize()
-    if use_graph:
-        n_launch = mlz_b200.launch_count() - n0       # kernels the replay runs
-        with torch.cuda.stream(gs):
-            graph.replay()                              # untimed first replay
-        torch.cuda.synchronize()
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-        torch.cuda.synchronize()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(gs):
-            g0.record(gs)
-            graph.replay()
-            g1.record(gs)
-        torch.cuda.synchronize()
-        ms_local = g0.elapsed_time(g1)
-        timing = "CUDA graph replay of the K steps"
-        del graph
-        # Per-call device times for the roofline: each call's K repetitions (the same
-        # inputs and weight rotation as in the steps) captured as their own graph and timed
-        # by events around its replay -- event nodes inside a graph would add microseconds
-        # to every call.
-        try:
-            per = []
-            for j in range(len(units_l)):
-                gj = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gj, stream=gs):
-                    for s_ in range(K):
-                        w.launches(s_)[j][0]()
-                with torch.cuda.stream(gs):
-                    gj.replay()                         # untimed first replay
-                torch.cuda.synchronize()
-                c0 = torch.cuda.Event(enable_timing=True)
-                c1 = torch.cuda.Event(enable_timing=True)
-                with torch.cuda.stream(gs):
-                    c0.record(gs)
-                    gj.replay()
-                    c1.record(gs)
-                torch.cuda.synchronize()
-                per.append(c0.elapsed_time(c1) / K)
-                del gj
-            per_launch_ms = per
-            call_timing = "each call's K repetitions replayed as a CUDA graph, timed by events"
-        except Exception as exc:  # keep the eager per-call events
-            call_timing = f"eager events around each call ({type(exc).__name__} with per-call graphs)"
-    else:
-        ms_local = ms_eager
+    t = time_workload(w, a, world, K, 0, not a.no_graph and not a.profile_run)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
     clocks = sampler.stop()
-    ms = max_over_ranks(ms_local, world)
-    max_ms_eager = max_over_ranks(ms_eager, world)
+    ms = max_over_ranks(t["ms_local"], world)
+    max_ms_eager = max_over_ranks(t["ms_eager"], world)
 
     units = w.work_units()
     job_units = units if isinstance(w, C5) else units * world
     value = job_units * K / (ms * 1e-3) * w.unit_scale()
-
-    # roofline of the dominant launch (largest average device time)
-    jdom = max(range(len(units_l)), key=lambda j: per_launch_ms[j])
-    if isinstance(w, C2):  # all 7 projections run the same GEMM kernel: pool them
-        ach = sum(units_l) / (sum(per_launch_ms) * 1e-3) * 1e-12
-    else:
-        ach = units_l[jdom] / (per_launch_ms[jdom] * 1e-3) * w.unit_scale()
-    # tensor peak: the sustained (power-capped) figure when the timed region ran under the
-    # power cap or for over a second -- the regime that figure was measured in -- else burst
-    power_capped = "sw_power_cap" in (clocks.get("reasons") or [])
-    long_run = ms * 1e-3 > 1.0 or power_capped
-    if w.bound == "hbm":
-        peak, peak_name = peaks["hbm_gbs"], "hbm_gbs"
-    else:
-        peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
-        peak_name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
-    roofline = {"bound": w.bound, "achieved": ach, "peak": peak,
-                "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s", "frac": ach / peak, "traffic": None,
-                "peak_source": f"{peaks['source']} {peak_name}" + (" (sw_power_cap active in the timed region)"
-                                                                      if power_capped and w.bound != "hbm" else ""),
-                "kernel": w.roofline_kernel(jdom), "call_timing": call_timing}
-    if w.bound != "hbm":
-        roofline["frac_of_burst"] = ach / peaks["bf16_tflops"]
+    roofline = roofline_of(w, t, peaks, clocks, ms)
     tr = NCU_TRAFFIC.get((a.config, n))
     if tr is not None and not isinstance(w, C2):
         roofline["traffic"] = tr[0]
         roofline["traffic_source"] = tr[1]
 
-    # end to end through the plugin entry point with pinned host buffers
+    # end to end through the public API with host buffers
     e2e = None
-    if not a.no_e2e and not a.profile_run and not isinstance(w, C5):
-        e2e = run_e2e(w, a, world, value)
+    if not a.no_e2e and not a.profile_run:
+        e2e = run_e2e_sharded(w, a, world) if isinstance(w, C5) else run_e2e(w, a, world, value)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile_run:
@@ -781,23 +888,67 @@ def mlz_arm(a):
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "unit": w.unit, "cores": None, "kind": "port", "sample": f"failed: {exc}"}
 
+    head = {"metric": w.metric, "unit": w.unit, "scaling": w.scaling, "dtype": w.dtype, "config": dict(w.config)}
+    rows = None
+    if not a.no_rows and not a.profile_run:
+        del w
+        torch.cuda.empty_cache()
+        rows = extra_rows(a, n, dev, rank, world, comm, peaks)
+
     if rank == 0:
-        cfg = dict(w.config)
+        cfg = head["config"]
         cfg["parallelism"] = cfg.get("parallelism", f"replicas x{world}" if world > 1 else "single GPU")
-        cfg["timing"] = timing
+        cfg["timing"] = t["timing"]
         cfg["launch_overlap"] = a.overlap
         cfg["eager_ms_per_step"] = max_ms_eager / K
-        line = {"metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world, "steps": K,
-                "warmup": a.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": w.scaling,
-                "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded), random-init weights",
-                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": n_launch, "clocks": clocks}
+        line = {"metric": head["metric"], "value": value, "unit": head["unit"], "n_gpus": world, "steps": K,
+                "warmup": a.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": head["scaling"],
+                "vs_baseline": None, "dtype": head["dtype"], "data": "synthetic (seeded), random-init weights",
+                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": t["n_launch"],
+                "clocks": clocks}
+        if rows is not None:
+            line["rows"] = rows
         print(json.dumps(line), flush=True)
     if comm is not None:
         comm.destroy()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_e2e_sharded(w, a, world):
+    """c5 end to end through the public device API with host buffers: every step copies the
+    three activation matrices from page-locked host memory to the device, runs the three
+    row-sharded calls (mlzc_mul_mat_sharded_dev) and reads the three gathered outputs back
+    to page-locked host memory, then synchronises.  Host wall clock, max over ranks."""
+    import torch
+    hx = [x.cpu().pin_memory() for x in w.X]
+    hy = [torch.empty(y.shape, dtype=torch.float32).pin_memory() for y in w.Y]
+    calls = w.launches(0)
+
+    def step():
+        for x, h in zip(w.X, hx):
+            x.copy_(h, non_blocking=True)
+        for f, _ in calls:
+            f()
+        for y, h in zip(w.Y, hy):
+            h.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for _ in range(max(a.warmup, 2)):
+        step()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    K = max(3, min(a.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = max_over_ranks((time.perf_counter() - t0) / K, world)
+    h2d = sum(x.numel() * 4 for x in hx)
+    d2h = sum(y.numel() * 4 for y in hy)
+    return {"value": w.work_units() / dt * w.unit_scale(), "unit": w.unit, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "path": "mlzc_mul_mat_sharded_dev with host copies",
+            "host_buffers": "page-locked", "ms_per_step": 1e3 * dt}
 
 
 def run_e2e(w, a, world, value_dev):
@@ -823,36 +974,52 @@ def run_e2e(w, a, world, value_dev):
     else:
         hws = w.host_weights()
         calls, h2d, d2h = w.e2e_calls(pinned)
-        views = []
-        for (j, x, y) in calls:
-            hw, t, K = hws[j]
-            views.append((mlz_b200.tensor_view(hw if t != 1 else hw.view(np.uint16), t, ne0=K),
-                          mlz_b200.TensorView(), mlz_b200.TensorView()))
-            sv = views[-1]
-            for tv, arr in ((sv[1], x), (sv[2], y)):
-                tv.type = 0
-                tv.ne[:] = [arr.shape[1], arr.shape[0], 1, 1]
-                tv.nb[:] = [4, arr.stride(0) * 4, arr.stride(0) * 4 * arr.shape[0], arr.stride(0) * 4 * arr.shape[0]]
-                tv.data = arr.data_ptr()
 
-        def step():
-            r = 1
-            for (s0, s1, d) in views:
-                r &= mlz_b200.ggml_simd_try_mul_mat(s0, s1, d)
-            return r
-    for _ in range(max(a.warmup, 2)):
-        if step() != 1:
-            raise RuntimeError("plugin entry point declined the workload: " + mlz_b200.last_error())
-    torch.cuda.synchronize()
-    K = max(3, min(a.steps, 10))
-    t0 = time.perf_counter()
-    for _ in range(K):
-        step()
-    dt = max_over_ranks(time.perf_counter() - t0, world)
+        def make_step(pairs):
+            views = []
+            for (j, x, y) in pairs:
+                hw, t, K = hws[j]
+                views.append((mlz_b200.tensor_view(hw if t != 1 else hw.view(np.uint16), t, ne0=K),
+                              mlz_b200.TensorView(), mlz_b200.TensorView()))
+                sv = views[-1]
+                for tv, arr in ((sv[1], x), (sv[2], y)):
+                    tv.type = 0
+                    tv.ne[:] = [arr.shape[1], arr.shape[0], 1, 1]
+                    tv.nb[:] = [4, arr.stride(0) * 4, arr.stride(0) * 4 * arr.shape[0],
+                                arr.stride(0) * 4 * arr.shape[0]]
+                    tv.data = arr.data_ptr()
+
+            def step_fn():
+                r = 1
+                for (s0, s1, d) in views:
+                    r &= mlz_b200.ggml_simd_try_mul_mat(s0, s1, d)
+                return r
+            return step_fn
+        step = make_step(calls)
+        # the same calls with pageable (not page-locked) host buffers, as a ggml buffer is
+        # unless the integration registers it (mlzc_host_register)
+        pageable = [(j, x.clone(), y.clone()) for (j, x, y) in calls]
+        step_pageable = make_step(pageable)
+
+    def timed(fn):
+        for _ in range(max(a.warmup, 2)):
+            if fn() != 1:
+                raise RuntimeError("plugin entry point declined the workload: " + mlz_b200.last_error())
+        torch.cuda.synchronize()
+        K = max(3, min(a.steps, 10))
+        t0 = time.perf_counter()
+        for _ in range(K):
+            fn()
+        return max_over_ranks(time.perf_counter() - t0, world) / K
     units = w.work_units() * world
-    return {"value": units * K / dt * w.unit_scale(), "unit": w.unit, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "path": "mlzc_try_flash_attn" if isinstance(w, C4) else "mlzc_try_mul_mat",
-            "ms_per_step": 1e3 * dt / K}
+    dt = timed(step)
+    out = {"value": units / dt * w.unit_scale(), "unit": w.unit, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h), "path": "mlzc_try_flash_attn" if isinstance(w, C4) else "mlzc_try_mul_mat",
+           "host_buffers": "page-locked", "ms_per_step": 1e3 * dt}
+    if not isinstance(w, C4):
+        dtp = timed(step_pageable)
+        out["pageable"] = {"value": units / dtp * w.unit_scale(), "ms_per_step": 1e3 * dtp}
+    return out
 
 
 def main():

@@ -20,11 +20,13 @@
  *     (column n at x + n*x_col_bytes), Y has ne = [M, N] (element (m, n) at
  *     y + n*y_col_bytes + 4*m).  This is the contract ggml_compute_forward_mul_mat
  *     asserts (src/simd/ggml-cpu-simd.c:1273-1288 in the MLz tree).
- *   - Type ids are ggml_type values: F32 = 0, F16 = 1, Q4_K = 12.
+ *   - Type ids are ggml_type values: F32 = 0, F16 = 1, Q4_K = 12, Q6_K = 14.
  *   - F16 weights: activations are narrowed to f16 (round-to-nearest-even) and the
  *     products are accumulated in fp32, which is the contract of the reference's
  *     F16 path (type_traits_cpu[F16].vec_dot_type = F16, ggml-cpu-simd.c:215-220).
- *     F32 and Q4_K weights: activations stay f32, fp32 accumulation.
+ *     F32 weights: activations stay f32, fp32 accumulation.  Q4_K / Q6_K weights:
+ *     activations rounded to f16 once, exact f16 dequant of the quants, fp32 accumulation
+ *     (within 2e-3 of the dequantised-F32 product).
  *   - The first call that touches a device creates its context (a small device
  *     allocation); make that call, or mlzc_init(), before any stream capture.
  */
@@ -50,7 +52,7 @@ enum mlzc_status {
     MLZC_ERR_COMM = -6          /* NCCL failure or timeout */
 };
 
-enum mlzc_type { MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_K = 12 };
+enum mlzc_type { MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_K = 12, MLZC_TYPE_Q6_K = 14 };
 
 /* Attention mode bits; same values as FA_MODE_* (src/simd/flash_attention.h:43-49). */
 #define MLZC_FA_MODE_GQA_BATCH 0x04u
@@ -114,12 +116,24 @@ int mlzc_mul_mat_workspace_bytes(int w_type, int64_t M, int64_t K, int64_t N, si
  * upstream F16 vec_dot path the hook falls back to (src/simd/ggml-cpu-simd.c:1314-1465).
  * Pointers and strides need only their element alignment; 16-byte aligned W and X with
  * 16-byte multiple strides take the vectorised kernels, anything else a slower exact
- * path.  Q4_K needs K % 256 == 0 and 16-byte aligned blocks and activation columns.
+ * path.  Q4_K needs K % 256 == 0 and 16-byte aligned blocks and activation columns;
+ * Q6_K (210-byte blocks, ggml_simd_hook.cpp:282-288 routes them with Q4_K) needs
+ * K % 256 == 0, a 4-byte aligned W with an even row stride, and 16-byte aligned
+ * activation columns.
  * `workspace` may be NULL when the query above returned 0. */
 int mlzc_mul_mat_dev(int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                      const float* x, size_t x_col_bytes, int64_t N,
                      float* y, size_t y_col_bytes,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* F32 activations -> Q8_K blocks, on `stream`: column n of X (K floats at
+ * x + n*x_col_bytes, K % 256 == 0) becomes K/256 blocks of 292 bytes at
+ * out + n*out_col_bytes (f32 d = amax/127, 256 int8 q = round(x/d), 16 int16 sums of 16
+ * consecutive q).  Bit-identical to the reference on finite inputs.
+ * Replaces: quantize_row_q8_k_reference (src/simd/ggml_simd_hook.cpp:109-148), run by the
+ * hook on each activation column before the Q4_K dot products (:197-204, :244-251). */
+int mlzc_quantize_q8k_dev(const float* x, size_t x_col_bytes, int64_t K, int64_t N, void* out,
+                          size_t out_col_bytes, void* stream);
 
 /* One flash-attention call.  Field names and meaning follow flash_attn_config_t
  * (src/simd/flash_attention.h:65-114); pointers are DEVICE pointers for
@@ -205,11 +219,22 @@ typedef struct mlzc_weight_s* mlzc_weight;
 int mlzc_weight_upload(int device, int w_type, const void* host, size_t row_bytes,
                        int64_t M, int64_t K, mlzc_weight* out);
 int mlzc_weight_free(mlzc_weight w);
-/* Y = W . X with X, Y in HOST memory (pinned or pageable).  Synchronous. */
+/* Y = W . X with X, Y in HOST memory (pinned or pageable).  Synchronous.  Calls with
+ * N >= 256 columns are cut into up to 4 column chunks whose uploads, compute and
+ * downloads overlap on three streams. */
 int mlzc_mul_mat(mlzc_weight w, const float* x, size_t x_col_bytes, int64_t N,
                  float* y, size_t y_col_bytes);
 /* Drop every weight cached by mlzc_try_mul_mat (e.g. when a model is unloaded). */
 int mlzc_weight_cache_clear(void);
+
+/* Page-lock an existing host range (e.g. ggml's compute buffer, which holds every src1 and
+ * dst the hook sees) so the host-pointer calls copy it by DMA, overlapping the upload of
+ * one column chunk with the compute and download of the others; pageable memory is copied
+ * through a driver staging buffer, one direction at a time.  Idempotent; unregister
+ * before freeing the range.  No counterpart in the reference (its buffers never leave the
+ * host). */
+int mlzc_host_register(void* ptr, size_t bytes);
+int mlzc_host_unregister(void* ptr);
 
 /* ---------------------------------------------------- multi-GPU (one node) */
 

@@ -16,7 +16,7 @@ STATUS_NAMES = {
     0: "MLZC_OK", -1: "MLZC_ERR_INVALID", -2: "MLZC_ERR_UNSUPPORTED", -3: "MLZC_ERR_CUDA",
     -4: "MLZC_ERR_NOMEM", -5: "MLZC_ERR_DEVICE", -6: "MLZC_ERR_COMM",
 }
-TYPE_F32, TYPE_F16, TYPE_Q4_K = 0, 1, 12
+TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 12, 14
 FA_MODE_GQA_BATCH, FA_MODE_ALIBI, FA_MODE_SOFTCAP = 0x04, 0x08, 0x10
 OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS = 0, 1, 2
 UNIQUE_ID_BYTES = 128
@@ -26,10 +26,11 @@ EXPORTS = (
     "mlzc_launch_count", "mlzc_last_error", "mlzc_version", "mlzc_init", "mlzc_shutdown", "mlzc_device_errors",
     "mlzc_selftest_wait_timeout",
     "mlzc_set_launch_overlap", "mlzc_get_launch_overlap",
-    "mlzc_mul_mat_workspace_bytes", "mlzc_mul_mat_dev",
+    "mlzc_mul_mat_workspace_bytes", "mlzc_mul_mat_dev", "mlzc_quantize_q8k_dev",
     "mlzc_flash_attn_workspace_bytes", "mlzc_flash_attn_dev", "mlzc_flash_attn_dev_noalloc",
     "mlzc_try_mul_mat", "mlzc_try_flash_attn",
     "mlzc_weight_upload", "mlzc_weight_free", "mlzc_mul_mat", "mlzc_weight_cache_clear",
+    "mlzc_host_register", "mlzc_host_unregister",
     "mlzc_comm_unique_id", "mlzc_comm_init", "mlzc_comm_destroy",
     "mlzc_mul_mat_sharded_workspace_bytes", "mlzc_mul_mat_sharded_dev",
 )
@@ -94,6 +95,7 @@ def _declare(L: C.CDLL) -> None:
     L.mlzc_selftest_wait_timeout.argtypes = [i32, u32, C.POINTER(i32)]
     L.mlzc_mul_mat_workspace_bytes.argtypes = [i32, i64, i64, i64, psz]
     L.mlzc_mul_mat_dev.argtypes = [i32, vp, sz, i64, i64, vp, sz, i64, vp, sz, vp, sz, vp]
+    L.mlzc_quantize_q8k_dev.argtypes = [vp, sz, i64, i64, vp, sz, vp]
     L.mlzc_flash_attn_workspace_bytes.argtypes = [C.POINTER(FaDesc), psz]
     L.mlzc_flash_attn_dev.argtypes = [C.POINTER(FaDesc), vp, sz, vp]
     L.mlzc_flash_attn_dev_noalloc.argtypes = [C.POINTER(FaDesc), vp]
@@ -103,6 +105,8 @@ def _declare(L: C.CDLL) -> None:
     L.mlzc_weight_free.argtypes = [vp]
     L.mlzc_mul_mat.argtypes = [vp, vp, sz, i64, vp, sz]
     L.mlzc_weight_cache_clear.argtypes = []
+    L.mlzc_host_register.argtypes = [vp, sz]
+    L.mlzc_host_unregister.argtypes = [vp]
     L.mlzc_comm_unique_id.argtypes = [vp]
     L.mlzc_comm_init.argtypes = [i32, i32, i32, vp, i32, C.POINTER(vp)]
     L.mlzc_comm_destroy.argtypes = [vp]

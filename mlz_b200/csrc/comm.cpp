@@ -14,17 +14,22 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
+#include <algorithm>
+#include <vector>
 #include <cstring>
 #include <mutex>
 #include <thread>
 
 #include "internal.h"
+#include "peer.h"
 
 namespace mlzc {
 namespace {
 
 struct NcclApi {
     void* handle = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
     ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
@@ -56,9 +61,10 @@ const NcclApi* nccl() {
         sym(h, "ncclCommAbort", g_nccl.CommAbort);
         sym(h, "ncclCommGetAsyncError", g_nccl.CommGetAsyncError);
         sym(h, "ncclAllGather", g_nccl.AllGather);
+        sym(h, "ncclAllReduce", g_nccl.AllReduce);
         sym(h, "ncclGetErrorString", g_nccl.GetErrorString);
         g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRankConfig && g_nccl.CommDestroy && g_nccl.CommAbort &&
-                    g_nccl.CommGetAsyncError && g_nccl.AllGather && g_nccl.GetErrorString;
+                    g_nccl.CommGetAsyncError && g_nccl.AllGather && g_nccl.AllReduce && g_nccl.GetErrorString;
     });
     return g_nccl.ok ? &g_nccl : nullptr;
 }
@@ -77,6 +83,12 @@ struct mlzc_comm_s {
     int nranks = 0, rank = 0, device = 0;
     int timeout_ms = 0;
     bool broken = false;
+    // peer-memory all-gather (peer.cu): this rank's exchange region and every rank's, as
+    // mapped in this process (peer regions opened from their CUDA IPC handles)
+    bool peer_ok = false;
+    void* region = nullptr;
+    char* base[mlzc::kPeerMaxRanks] = {};
+    size_t slot_bytes = 0;
 };
 
 namespace {
@@ -102,6 +114,95 @@ int wait_comm(const NcclApi* api, mlzc_comm c, const char* what) {
         const auto us = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
         if (us > 100) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
+}
+
+}  // namespace
+
+namespace {
+
+// Enqueue-and-wait helpers for the set-up collectives (non-blocking communicator).
+int enq_done(const NcclApi* api, mlzc_comm c, ncclResult_t r, const char* what) {
+    if (r != ncclSuccess && r != ncclInProgress) {
+        c->broken = true;
+        return nccl_fail(api, r, what);
+    }
+    return r == ncclInProgress ? wait_comm(api, c, what) : MLZC_OK;
+}
+
+void peer_release(mlzc_comm c) {
+    for (int r = 0; r < c->nranks && r < kPeerMaxRanks; ++r)
+        if (r != c->rank && c->base[r]) cudaIpcCloseMemHandle(c->base[r]);
+    if (c->region) cudaFree(c->region);
+    c->region = nullptr;
+    for (auto& b : c->base) b = nullptr;
+    c->peer_ok = false;
+}
+
+// Symmetric exchange region for the peer-memory all-gather: allocated here, its CUDA IPC
+// handle all-gathered over the communicator, every peer's region opened (peer access over
+// NVLink), and the outcome agreed on by all ranks (an all-reduce of the local result), so
+// every rank takes the same gather path.  MLZ_SHARDED_GATHER=nccl keeps NCCL's all-gather;
+// MLZ_PEER_SLOT_MB sets the slot size (64 MB per parity by default).
+int peer_setup(const NcclApi* api, mlzc_comm c) {
+    const char* mode = getenv("MLZ_SHARDED_GATHER");
+    if ((mode && std::strcmp(mode, "nccl") == 0) || c->nranks > kPeerMaxRanks) return MLZC_OK;   // same on every rank
+    const char* mb = getenv("MLZ_PEER_SLOT_MB");
+    c->slot_bytes = (size_t)(mb ? std::max(1, atoi(mb)) : 64) << 20;
+    cudaStream_t s = nullptr;
+    MLZC_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    int local_ok = 1;
+    cudaIpcMemHandle_t mine{};
+    if (cudaMalloc(&c->region, kPeerHeaderBytes + 2 * c->slot_bytes) != cudaSuccess ||
+        cudaMemset(c->region, 0, kPeerHeaderBytes) != cudaSuccess || cudaIpcGetMemHandle(&mine, c->region) != cudaSuccess) {
+        cudaGetLastError();
+        local_ok = 0;
+    }
+    // handles of all ranks (64 bytes each) through a device buffer
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    char* dh = nullptr;
+    int* dflag = nullptr;
+    int st = MLZC_OK;
+    std::vector<char> all((size_t)c->nranks * hb);
+    if (cudaMalloc(&dh, hb * (size_t)(c->nranks + 1)) != cudaSuccess || cudaMalloc(&dflag, sizeof(int)) != cudaSuccess) {
+        cudaGetLastError();
+        st = fail(MLZC_ERR_NOMEM, "peer exchange set-up: device buffers");
+    }
+    if (st == MLZC_OK && cudaMemcpy(dh + (size_t)c->nranks * hb, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess)
+        st = fail(MLZC_ERR_CUDA, "peer exchange set-up: copy of the handle");
+    if (st == MLZC_OK)
+        st = enq_done(api, c, api->AllGather(dh + (size_t)c->nranks * hb, dh, hb, ncclUint8, c->comm, s), "ncclAllGather (handles)");
+    if (st == MLZC_OK && (cudaStreamSynchronize(s) != cudaSuccess ||
+                          cudaMemcpy(all.data(), dh, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess))
+        st = fail(MLZC_ERR_CUDA, "peer exchange set-up: handle read-back");
+    if (st == MLZC_OK) {
+        c->base[c->rank] = static_cast<char*>(c->region);
+        for (int r = 0; r < c->nranks && local_ok; ++r) {
+            if (r == c->rank) continue;
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, all.data() + (size_t)r * hb, hb);
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                local_ok = 0;
+            } else {
+                c->base[r] = static_cast<char*>(p);
+            }
+        }
+        // every rank must agree: minimum of the local outcomes
+        int agreed = 0;
+        if (cudaMemcpy(dflag, &local_ok, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+            st = fail(MLZC_ERR_CUDA, "peer exchange set-up: flag copy");
+        if (st == MLZC_OK) st = enq_done(api, c, api->AllReduce(dflag, dflag, 1, ncclInt32, ncclMin, c->comm, s), "ncclAllReduce (peer set-up)");
+        if (st == MLZC_OK && (cudaStreamSynchronize(s) != cudaSuccess ||
+                              cudaMemcpy(&agreed, dflag, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess))
+            st = fail(MLZC_ERR_CUDA, "peer exchange set-up: flag read-back");
+        c->peer_ok = st == MLZC_OK && agreed == 1;
+    }
+    if (dh) cudaFree(dh);
+    if (dflag) cudaFree(dflag);
+    cudaStreamDestroy(s);
+    if (!c->peer_ok) peer_release(c);
+    return st;
 }
 
 }  // namespace
@@ -147,12 +248,28 @@ extern "C" int mlzc_comm_init(int nranks, int rank, int device, const void* uniq
         delete c;
         return st;
     }
+    st = peer_setup(api, c);
+    if (st != MLZC_OK) {
+        api->CommAbort(c->comm);
+        delete c;
+        return st;
+    }
     *out = c;
     return MLZC_OK;
 }
 
 extern "C" int mlzc_comm_destroy(mlzc_comm c) {
     if (!c) return MLZC_OK;
+    if (c->peer_ok) {
+        // this rank's kernels are done with the exchange (every peer's push into this
+        // region completed before this rank's last wait kernel could finish)
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(c->device);
+        cudaDeviceSynchronize();
+        peer_release(c);
+        cudaSetDevice(prev);
+    }
     const NcclApi* api = nccl();
     if (api && c->comm) {
         if (c->broken) api->CommAbort(c->comm);
@@ -202,6 +319,15 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
     st = mul_mat_run(ctx, w_type, w_shard, w_row_bytes, m_loc, K, x, x_col_bytes, N, slice, (size_t)m_loc * 4,
                      ws, mm, s);
     if (st != MLZC_OK) return st;
+    if (c->peer_ok && (size_t)c->nranks * slice_bytes <= c->slot_bytes) {
+        PeerView pv{};
+        for (int r = 0; r < c->nranks; ++r) pv.base[r] = c->base[r];
+        pv.G = c->nranks;
+        pv.rank = c->rank;
+        pv.slot_bytes = c->slot_bytes;
+        pv.slice_stride = slice_bytes;
+        return launch_peer_allgather(pv, slice, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
+    }
     const bool direct = (N == 1);  // one column: slices land at their final place in y
     ncclResult_t r = api->AllGather(slice, direct ? static_cast<void*>(y) : static_cast<void*>(gathered),
                                     (size_t)N * m_loc, ncclFloat32, c->comm, s);

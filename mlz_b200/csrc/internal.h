@@ -29,7 +29,11 @@ struct DeviceCtx {
     int device = -1;
     int sm_count = 0;
     unsigned int* err = nullptr;      // kernel error word (MLZC_DEVERR_* bits)
-    cudaStream_t stream = nullptr;    // stream of the host-pointer entry points
+    cudaStream_t stream = nullptr;    // stream of the host-pointer entry points (compute)
+    cudaStream_t h2d = nullptr;       // host -> device copies of the host-pointer calls
+    cudaStream_t d2h = nullptr;       // device -> host copies of the host-pointer calls
+    static constexpr int kEvents = 8;
+    cudaEvent_t ev[kEvents] = {};     // chunk hand-offs between the three streams
 };
 
 // Context of `device` (creating it if needed); nullptr + last error on failure.
@@ -112,6 +116,19 @@ size_t mul_mat_workspace(int w_type, int64_t M, int64_t K, int64_t N);
 // ggml [N][M] layout.
 int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,
                           int64_t m_loc, cudaStream_t s);
+
+// Q4_K / Q6_K: 256-weight super-blocks of 144 / 210 bytes.
+inline bool is_kquant(int w_type) { return w_type == MLZC_TYPE_Q4_K || w_type == MLZC_TYPE_Q6_K; }
+// Bytes of one dense row of K weights of type w_type.
+inline size_t dense_row_bytes(int w_type, int64_t K) {
+    if (w_type == MLZC_TYPE_Q4_K) return (size_t)(K / 256) * 144;
+    if (w_type == MLZC_TYPE_Q6_K) return (size_t)(K / 256) * 210;
+    return (size_t)K * (w_type == MLZC_TYPE_F16 ? 2 : 4);
+}
+
+// Q6_K dequant-dot on the tensor cores (mma.sync), any N; no workspace.
+int launch_q6k(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+               size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s);
 
 // Shape / type gate shared by the device entry point and the hook.
 int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,

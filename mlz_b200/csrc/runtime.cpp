@@ -92,6 +92,10 @@ DeviceCtx* device_ctx(int device) {
     ok = ok && cudaMalloc(&c->err, sizeof(unsigned int)) == cudaSuccess;
     ok = ok && cudaMemset(c->err, 0, sizeof(unsigned int)) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&c->h2d, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&c->d2h, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; ok && i < DeviceCtx::kEvents; ++i)
+        ok = cudaEventCreateWithFlags(&c->ev[i], cudaEventDisableTiming) == cudaSuccess;
     cudaSetDevice(prev);
     if (!ok) { fail(MLZC_ERR_CUDA, "creating the context of device %d failed: %s", device, cudaGetErrorString(cudaGetLastError())); return nullptr; }
     g_ctx[device] = std::move(c);
@@ -108,20 +112,24 @@ DeviceCtx* current_ctx() {
 int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                        const float* x, size_t x_col_bytes, int64_t N, const float* y,
                        size_t y_col_bytes) {
-    if (w_type != MLZC_TYPE_F16 && w_type != MLZC_TYPE_F32 && w_type != MLZC_TYPE_Q4_K)
-        return fail(MLZC_ERR_UNSUPPORTED, "mul_mat: weight type %d not handled (F32=0, F16=1, Q4_K=12)", w_type);
+    if (w_type != MLZC_TYPE_F16 && w_type != MLZC_TYPE_F32 && w_type != MLZC_TYPE_Q4_K && w_type != MLZC_TYPE_Q6_K)
+        return fail(MLZC_ERR_UNSUPPORTED, "mul_mat: weight type %d not handled (F32=0, F16=1, Q4_K=12, Q6_K=14)",
+                    w_type);
     if (M < 0 || K < 0 || N < 0) return fail(MLZC_ERR_INVALID, "mul_mat: negative dimension");
     if (M == 0 || N == 0) return MLZC_OK;
     if (K > 0 && (!w || !x)) return fail(MLZC_ERR_INVALID, "mul_mat: null W or X");
     if (!y) return fail(MLZC_ERR_INVALID, "mul_mat: null Y");
+    // alignment the kernels need of W and its row stride: the element (f16 / f32), a
+    // 4-byte word for the quantised blocks (Q6_K rows themselves are 2-byte multiples)
     const size_t esz = w_type == MLZC_TYPE_F16 ? 2 : 4;
-    const size_t min_row = w_type == MLZC_TYPE_Q4_K ? (size_t)(K / 256) * 144 : (size_t)K * esz;
-    if (w_type == MLZC_TYPE_Q4_K && K % 256 != 0)
-        return fail(MLZC_ERR_INVALID, "mul_mat: Q4_K needs K %% 256 == 0 (K=%lld)", (long long)K);
+    const size_t rs_align = w_type == MLZC_TYPE_Q6_K ? 2 : esz;
+    const size_t min_row = dense_row_bytes(w_type, K);
+    if (is_kquant(w_type) && K % 256 != 0)
+        return fail(MLZC_ERR_INVALID, "mul_mat: Q4_K / Q6_K need K %% 256 == 0 (K=%lld)", (long long)K);
     if (w_row_bytes < min_row) return fail(MLZC_ERR_INVALID, "mul_mat: w_row_bytes %zu < row size %zu", w_row_bytes, min_row);
     if (x_col_bytes < (size_t)K * 4) return fail(MLZC_ERR_INVALID, "mul_mat: x_col_bytes %zu < 4*K", x_col_bytes);
     if (y_col_bytes < (size_t)M * 4 || y_col_bytes % 4) return fail(MLZC_ERR_INVALID, "mul_mat: y_col_bytes %zu must be >= 4*M and a multiple of 4", y_col_bytes);
-    if ((uintptr_t)y % 4 || (uintptr_t)x % 4 || (uintptr_t)w % esz || x_col_bytes % 4 || w_row_bytes % esz)
+    if ((uintptr_t)y % 4 || (uintptr_t)x % 4 || (uintptr_t)w % esz || x_col_bytes % 4 || w_row_bytes % rs_align)
         return fail(MLZC_ERR_INVALID, "mul_mat: pointers / strides not aligned to their element size");
     return MLZC_OK;
 }
@@ -175,6 +183,11 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
         return MLZC_OK;
     }
     if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
+    if (w_type == MLZC_TYPE_Q6_K) {
+        if ((uintptr_t)x % 16 || x_cs % 16)
+            return fail(MLZC_ERR_INVALID, "mul_mat (Q6_K): activation columns must be 16-byte aligned");
+        return launch_q6k(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
+    }
     if (w_type == MLZC_TYPE_F16 && gemv_f16_mma_applicable(M, K, N, w, w_rs, x, x_cs))
         return launch_gemv_f16_mma(w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
     if (use_gemm(w_type, M, K, N, w, w_rs, x, x_cs, y, y_cs))
@@ -248,6 +261,10 @@ extern "C" int mlzc_shutdown(void) {
         if (!c) continue;
         cudaSetDevice(c->device);
         if (c->stream) cudaStreamDestroy(c->stream);
+        if (c->h2d) cudaStreamDestroy(c->h2d);
+        if (c->d2h) cudaStreamDestroy(c->d2h);
+        for (cudaEvent_t e : c->ev)
+            if (e) cudaEventDestroy(e);
         if (c->err) cudaFree(c->err);
     }
     g_ctx.clear();
@@ -411,8 +428,7 @@ extern "C" int mlzc_weight_upload(int device, int w_type, const void* host, size
     if (!c) return MLZC_ERR_CUDA;
     DeviceGuard g(device);
     if (!g.ok) return fail(MLZC_ERR_CUDA, "cudaSetDevice(%d) failed", device);
-    const size_t esz = w_type == MLZC_TYPE_F16 ? 2 : 4;
-    const size_t dense = w_type == MLZC_TYPE_Q4_K ? (size_t)(K / 256) * 144 : (size_t)K * esz;
+    const size_t dense = dense_row_bytes(w_type, K);
     // keep rows 16-byte aligned on the device so the vector paths apply
     const size_t dev_row = (dense + 15) / 16 * 16;
     auto w = std::make_unique<mlzc_weight_s>();
@@ -447,6 +463,11 @@ extern "C" int mlzc_weight_free(mlzc_weight w) {
     return MLZC_OK;
 }
 
+namespace {
+constexpr int kPipeChunks = 4;          // column chunks of a wide host-pointer call
+constexpr int64_t kPipeMinCols = 128;   // no chunk narrower than this
+}  // namespace
+
 extern "C" int mlzc_mul_mat(mlzc_weight w, const float* x, size_t x_col_bytes, int64_t N, float* y,
                             size_t y_col_bytes) {
     if (!w) return fail(MLZC_ERR_INVALID, "null weight handle");
@@ -466,16 +487,54 @@ extern "C" int mlzc_mul_mat(mlzc_weight w, const float* x, size_t x_col_bytes, i
     int st;
     if ((st = a->x.ensure(xb * (size_t)N + 16)) != MLZC_OK) return st;
     if ((st = a->y.ensure(yb * (size_t)N + 16)) != MLZC_OK) return st;
-    const size_t wsb = mul_mat_ws(w->type, M, K, N);
+    // Column chunks flow through three streams: copy in (h2d), compute (stream), copy out
+    // (d2h).  Chunk i + 1 uploads while chunk i computes and chunk i - 1 downloads; PCIe
+    // carries both directions at once.  Narrow calls (decode) are one chunk.
+    const int64_t nc = N >= 2 * kPipeMinCols ? std::max<int64_t>(kPipeMinCols, (N + kPipeChunks - 1) / kPipeChunks) : N;
+    const int nchunks = (int)((N + nc - 1) / nc);
+    const size_t wsb = mul_mat_ws(w->type, M, K, nc);
     if ((st = a->ws.ensure(wsb)) != MLZC_OK) return st;
-    cudaStream_t s = c->stream;
-    if ((st = h2d_cols(a->x.ptr, x, xb, x_col_bytes, N, s)) != MLZC_OK) return st;
-    // dense device columns: pad the column stride to 16 bytes for the vector paths
-    st = mul_mat_dispatch(c, w->type, w->dev, w->row_bytes, M, K, static_cast<const float*>(a->x.ptr), xb, N,
-                          static_cast<float*>(a->y.ptr), yb, a->ws.ptr, a->ws.bytes, s);
-    if (st != MLZC_OK) return st;
-    if ((st = d2h_cols(y, y_col_bytes, a->y.ptr, yb, N, s)) != MLZC_OK) return st;
-    MLZC_CUDA_TRY(cudaStreamSynchronize(s));
+    char* xd = static_cast<char*>(a->x.ptr);
+    char* yd = static_cast<char*>(a->y.ptr);
+    const char* xh = reinterpret_cast<const char*>(x);
+    char* yh = reinterpret_cast<char*>(y);
+    for (int i = 0; i < nchunks; ++i) {
+        const int64_t c0 = (int64_t)i * nc, n = std::min(nc, N - c0);
+        cudaEvent_t up = c->ev[(2 * i) % DeviceCtx::kEvents], done = c->ev[(2 * i + 1) % DeviceCtx::kEvents];
+        if ((st = h2d_cols(xd + c0 * xb, xh + c0 * x_col_bytes, xb, x_col_bytes, n, c->h2d)) != MLZC_OK) return st;
+        MLZC_CUDA_TRY(cudaEventRecord(up, c->h2d));
+        MLZC_CUDA_TRY(cudaStreamWaitEvent(c->stream, up, 0));
+        // dense device columns: the column stride is K floats
+        st = mul_mat_dispatch(c, w->type, w->dev, w->row_bytes, M, K, reinterpret_cast<const float*>(xd + c0 * xb), xb,
+                              n, reinterpret_cast<float*>(yd + c0 * yb), yb, a->ws.ptr, a->ws.bytes, c->stream);
+        if (st != MLZC_OK) return st;
+        MLZC_CUDA_TRY(cudaEventRecord(done, c->stream));
+        MLZC_CUDA_TRY(cudaStreamWaitEvent(c->d2h, done, 0));
+        if ((st = d2h_cols(yh + c0 * y_col_bytes, y_col_bytes, yd + c0 * yb, yb, n, c->d2h)) != MLZC_OK) return st;
+    }
+    MLZC_CUDA_TRY(cudaStreamSynchronize(c->d2h));
+    return MLZC_OK;
+}
+
+extern "C" int mlzc_host_register(void* ptr, size_t bytes) {
+    if (!ptr || !bytes) return fail(MLZC_ERR_INVALID, "host_register: null or empty range");
+    const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterPortable);
+    if (e == cudaErrorHostMemoryAlreadyRegistered) {
+        cudaGetLastError();
+        return MLZC_OK;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostRegister");
+    return MLZC_OK;
+}
+
+extern "C" int mlzc_host_unregister(void* ptr) {
+    if (!ptr) return fail(MLZC_ERR_INVALID, "host_unregister: null pointer");
+    const cudaError_t e = cudaHostUnregister(ptr);
+    if (e == cudaErrorHostMemoryNotRegistered) {
+        cudaGetLastError();
+        return MLZC_OK;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostUnregister");
     return MLZC_OK;
 }
 
@@ -544,8 +603,7 @@ uint64_t fingerprint(const void* data, size_t bytes) {
 
 mlzc_weight cached_weight(const mlzc_tensor* src0, int device, int* status) {
     const WeightKey key{src0->data, src0->type, src0->ne[0], src0->ne[1], src0->nb[1], device};
-    const size_t row = src0->type == MLZC_TYPE_Q4_K ? (size_t)(src0->ne[0] / 256) * 144
-                                                     : (size_t)src0->ne[0] * (src0->type == MLZC_TYPE_F16 ? 2 : 4);
+    const size_t row = dense_row_bytes(src0->type, src0->ne[0]);
     const size_t bytes = src0->ne[1] > 0 ? (size_t)(src0->ne[1] - 1) * src0->nb[1] + row : 0;
     const uint64_t fp = bytes ? fingerprint(src0->data, bytes) : 0;
     std::lock_guard<std::mutex> lk(g_wcache_mu);
@@ -568,14 +626,15 @@ mlzc_weight cached_weight(const mlzc_tensor* src0, int device, int* status) {
 bool mul_mat_gate(const mlzc_tensor* s0, const mlzc_tensor* s1, const mlzc_tensor* d) {
     if (!s0 || !s1 || !d || !s0->data || !s1->data || !d->data) return false;
     if (d->type != MLZC_TYPE_F32 || s1->type != MLZC_TYPE_F32) return false;
-    if (s0->type != MLZC_TYPE_F32 && s0->type != MLZC_TYPE_F16 && s0->type != MLZC_TYPE_Q4_K) return false;
+    if (s0->type != MLZC_TYPE_F32 && s0->type != MLZC_TYPE_F16 && !is_kquant(s0->type)) return false;
     if (s1->ne[0] != s0->ne[0]) return false;
     if (d->ne[0] != s0->ne[1] || d->ne[1] != s1->ne[1]) return false;
     for (int i = 2; i < 4; i++)
         if (s0->ne[i] != 1 || s1->ne[i] != 1 || d->ne[i] != 1) return false;
-    const size_t esz0 = s0->type == MLZC_TYPE_F16 ? 2 : (s0->type == MLZC_TYPE_F32 ? 4 : 144);
+    // nb[0] of a quantised ggml tensor is its block size in bytes
+    const size_t esz0 = s0->type == MLZC_TYPE_F16 ? 2 : (s0->type == MLZC_TYPE_F32 ? 4 : dense_row_bytes(s0->type, 256));
     if (s0->nb[0] != esz0 || s1->nb[0] != 4 || d->nb[0] != 4) return false;
-    if (s0->type == MLZC_TYPE_Q4_K && s0->ne[0] % 256 != 0) return false;
+    if (is_kquant(s0->type) && s0->ne[0] % 256 != 0) return false;
     return true;
 }
 

@@ -20,7 +20,7 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_Q4_K, FaDesc,
+from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, FaDesc,
                    MlzcError, TensorView, check, lib)
 
 QK_K = 256
@@ -40,7 +40,8 @@ def _stream_handle(stream) -> int:
 
 
 def weight_type_of(w) -> int:
-    """ggml type id of a weight tensor: f16 -> F16, f32 -> F32, uint8 -> Q4_K blocks."""
+    """ggml type id of a weight tensor: f16 -> F16, f32 -> F32, uint8 -> Q4_K blocks (pass
+    w_type=TYPE_Q6_K to the calls for Q6_K blocks)."""
     torch = _torch()
     if w.dtype == torch.float16:
         return TYPE_F16
@@ -57,14 +58,16 @@ def mul_mat_workspace_bytes(w_type: int, M: int, K: int, N: int) -> int:
     return out.value
 
 
-def mul_mat(w, x, *, out=None, workspace=None, stream=None):
+def mul_mat(w, x, *, out=None, workspace=None, stream=None, w_type=None):
     """y[n, m] = sum_k W[m, k] x[n, k] on the GPU (ggml mul_mat, dst = [M, N]).
 
-    w: (M, K) float16 / float32, or (M, K/256*144) uint8 Q4_K super-blocks.
+    w: (M, K) float16 / float32, or uint8 super-blocks: (M, K/256*144) Q4_K (the default
+    for uint8) or (M, K/256*210) Q6_K with w_type=TYPE_Q6_K.
     x: (N, K) float32 (row stride may exceed K).  Returns y: (N, M) float32.
     """
     torch = _torch()
-    w_type = weight_type_of(w)
+    if w_type is None:
+        w_type = weight_type_of(w)
     M = w.shape[0]
     N, K = x.shape
     if x.dtype != torch.float32:
@@ -83,6 +86,21 @@ def mul_mat(w, x, *, out=None, workspace=None, stream=None):
         x.data_ptr(), x.stride(0) * 4, N, out.data_ptr(), out.stride(0) * 4,
         workspace.data_ptr() if workspace is not None else None,
         workspace.numel() if workspace is not None else 0, _stream_handle(stream)))
+    return out
+
+
+Q8K_BYTES = 292
+
+
+def quantize_q8k(x, *, out=None, stream=None):
+    """F32 activations (N, K) on the device -> Q8_K blocks (N, K/256*292) uint8
+    (mlzc_quantize_q8k_dev; the reference's quantize_row_q8_k_reference per column)."""
+    torch = _torch()
+    N, K = x.shape
+    if out is None:
+        out = torch.empty((N, K // QK_K * Q8K_BYTES), dtype=torch.uint8, device=x.device)
+    check(lib().mlzc_quantize_q8k_dev(x.data_ptr(), x.stride(0) * 4, K, N, out.data_ptr(),
+                                      out.stride(0) * out.element_size(), _stream_handle(stream)))
     return out
 
 
@@ -158,8 +176,8 @@ def flash_attn_dispatch(q, k, v, scale: float, *, kv_len=None, mask=None, softca
 # ----------------------------------------------------------------- host level
 
 def tensor_view(arr: np.ndarray, ggml_type: int, ne0: Optional[int] = None) -> TensorView:
-    """mlzc_tensor for a host numpy array whose dims are ggml's reversed.  For Q4_K pass
-    the logical row length ne0 (arr is then (M, ne0/256*144) uint8)."""
+    """mlzc_tensor for a host numpy array whose dims are ggml's reversed.  For Q4_K / Q6_K
+    pass the logical row length ne0 (arr is then (M, ne0/256*144) or (M, ne0/256*210) uint8)."""
     t = TensorView()
     t.type = ggml_type
     shape = list(arr.shape[::-1]) + [1] * (4 - arr.ndim)
@@ -169,6 +187,8 @@ def tensor_view(arr: np.ndarray, ggml_type: int, ne0: Optional[int] = None) -> T
     nb = list(arr.strides[::-1]) + [0] * (4 - arr.ndim)
     if ggml_type == TYPE_Q4_K:
         nb[0] = Q4K_BYTES
+    elif ggml_type == TYPE_Q6_K:
+        nb[0] = 210
     for i in range(arr.ndim, 4):
         nb[i] = nb[i - 1] * shape[i - 1] if i > 0 else 0
     t.nb[:] = nb
@@ -287,5 +307,5 @@ __all__ = [
     "mul_mat", "mul_mat_workspace_bytes", "flash_attn_dispatch", "flash_attn_workspace_bytes",
     "make_fa_desc", "tensor_view", "ggml_simd_try_mul_mat", "ggml_simd_try_flash_attn", "init",
     "shutdown", "device_errors", "Weight", "Comm", "MlzcError", "weight_type_of",
-    "TYPE_F16", "TYPE_F32", "TYPE_Q4_K",
+    "TYPE_F16", "TYPE_F32", "TYPE_Q4_K", "TYPE_Q6_K",
 ]

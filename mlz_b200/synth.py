@@ -46,6 +46,20 @@ def q4k_blocks(g: np.random.Generator, M: int, K: int) -> np.ndarray:
     return blk.reshape(M, nb * Q4K_BYTES)
 
 
+Q6K_BYTES = 210
+
+
+def q6k_blocks(g: np.random.Generator, M: int, K: int) -> np.ndarray:
+    """(M, K/256*210) uint8 Q6_K super-blocks: random ql / qh bits, int8 scales uniform in
+    -128..127, d = f16(|N(0, 0.001)|)."""
+    assert K % QK_K == 0
+    nb = K // QK_K
+    blk = g.integers(0, 256, size=(M, nb, Q6K_BYTES), dtype=np.uint8)
+    d = np.abs(g.standard_normal((M, nb, 1), dtype=np.float32) * 0.001).astype(np.float16)
+    blk[:, :, 208:210] = d.view(np.uint8).reshape(M, nb, 2)
+    return blk.reshape(M, nb * Q6K_BYTES)
+
+
 def fa_inputs(g: np.random.Generator, B: int, Hq: int, Hkv: int, L: int, D: int, NQ: int = 1):
     """q (B, Hq, NQ, D) f32; k, v (B, Hkv, L, D) f16."""
     s = 1.0 / np.sqrt(D)
@@ -69,6 +83,15 @@ def f16_weights_dev(gen, M: int, K: int, device, std: float = 0.02):
 def f32_acts_dev(gen, N: int, K: int, device):
     import torch
     return torch.randn((N, K), generator=gen, device=device, dtype=torch.float32)
+
+
+def q6k_blocks_dev(gen, M: int, K: int, device):
+    import torch
+    nb = K // QK_K
+    blk = torch.randint(0, 256, (M, nb, Q6K_BYTES), generator=gen, device=device, dtype=torch.uint8)
+    d = (torch.randn((M, nb, 1), generator=gen, device=device) * 0.001).abs().to(torch.float16)
+    blk[:, :, 208:210] = d.view(torch.uint8).reshape(M, nb, 2)
+    return blk.reshape(M, nb * Q6K_BYTES)
 
 
 def q4k_blocks_dev(gen, M: int, K: int, device):

@@ -30,6 +30,7 @@ _REF = os.path.join(_HERE, "_ref", "libmlzref.so")
 QK_K = 256
 Q4K_BYTES = 144
 Q8K_BYTES = 292
+Q6K_BYTES = 210
 FA_MODE_ALIBI = 0x08
 FA_MODE_SOFTCAP = 0x10
 FA_MODE_GQA_BATCH = 0x04
@@ -133,6 +134,9 @@ def _declare(L: C.CDLL) -> None:
     L.ora_mul_mat_f32.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
     L.ora_q4k_dequant_row.argtypes = [vp, i64, vp]
     L.ora_mul_mat_q4k.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
+    L.ora_q6k_dequant_row.argtypes = [vp, i64, vp]
+    L.ora_mul_mat_q6k.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
+    L.base_mul_mat_q6k.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp, i32]
     L.ora_quantize_row_q8k.argtypes = [vp, i64, vp]
     L.ora_vec_dot_q4k_q8k.argtypes = [i64, vp, vp]
     L.ora_vec_dot_q4k_q8k.restype = C.c_float
@@ -211,6 +215,27 @@ def mul_mat_q4k(blocks: np.ndarray, x: np.ndarray) -> np.ndarray:
     N = x.shape[0]
     y = np.empty((N, M), dtype=np.float64)
     lib().ora_mul_mat_q4k(_p(blocks), row_bytes, M, K, _p(x), K * 4, N, _p(y))
+    return y
+
+
+def q6k_dequant(blocks: np.ndarray, K: int) -> np.ndarray:
+    """Dequantise Q6_K rows: blocks is (M, K/256*210) uint8 -> (M, K) f32."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    M = blocks.shape[0]
+    out = np.empty((M, K), dtype=np.float32)
+    for m in range(M):
+        lib().ora_q6k_dequant_row(blocks[m].ctypes.data, K, out[m].ctypes.data)
+    return out
+
+
+def mul_mat_q6k(blocks: np.ndarray, x: np.ndarray) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, row_bytes = blocks.shape
+    K = row_bytes // Q6K_BYTES * QK_K
+    N = x.shape[0]
+    y = np.empty((N, M), dtype=np.float64)
+    lib().ora_mul_mat_q6k(_p(blocks), row_bytes, M, K, _p(x), K * 4, N, _p(y))
     return y
 
 
@@ -360,6 +385,17 @@ def base_mul_mat_q4k(blocks, x, nth: int) -> np.ndarray:
     N = x.shape[0]
     y = np.empty((N, M), dtype=np.float32)
     lib().base_mul_mat_q4k(_p(blocks), row_bytes, M, K, _p(x), K * 4, N, _p(y), nth)
+    return y
+
+
+def base_mul_mat_q6k(blocks, x, nth: int) -> np.ndarray:
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, row_bytes = blocks.shape
+    K = row_bytes // Q6K_BYTES * QK_K
+    N = x.shape[0]
+    y = np.empty((N, M), dtype=np.float32)
+    lib().base_mul_mat_q6k(_p(blocks), row_bytes, M, K, _p(x), K * 4, N, _p(y), nth)
     return y
 
 

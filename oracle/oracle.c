@@ -167,6 +167,7 @@ void ora_mul_mat_f32(const float* W, size_t w_row_bytes, int64_t M, int64_t K,
 #define ORA_QK_K 256
 #define ORA_Q4K_BYTES 144
 #define ORA_Q8K_BYTES 292
+#define ORA_Q6K_BYTES 210
 
 /* 6-bit scale/min unpack of sub-block j, as the AVX2 kernel does it
  * (vec_dot_q4_k_q8_k_avx2.asm:101-150). */
@@ -218,6 +219,53 @@ void ora_mul_mat_q4k(const uint8_t* W, size_t w_row_bytes, int64_t M, int64_t K,
     float* wf = (float*)malloc(sizeof(float) * (size_t)K);
     for (int64_t m = 0; m < M; m++) {
         ora_q4k_dequant_row(W + m * w_row_bytes, K, wf);
+        for (int64_t n = 0; n < N; n++) {
+            const float* xc = (const float*)((const char*)X + n * x_col_bytes);
+            double acc = 0.0;
+            for (int64_t k = 0; k < K; k++) acc += (double)wf[k] * (double)xc[k];
+            Y[n * M + m] = acc;
+        }
+    }
+    free(wf);
+}
+
+/* Q6_K (GGUF, 210 bytes per 256 weights): ql[128] @0 (low 4 bits), qh[64] @128 (high 2
+ * bits), 16 int8 scales @192 (one per 16 weights), f16 d @208.  Element p of a block
+ * (h = p / 128, r = p % 128, l = r % 32, k = r / 32): low bits = nibble k / 2 of
+ * ql[64h + 32 (k % 2) + l], high bits = bits 2k, 2k+1 of qh[32h + l]; q = (lo | hi << 4)
+ * - 32; w = (d * scales[p / 16]) * q in f32 -- the layout and arithmetic of the gguf
+ * 0.19.0 decoder (gguf/quants.py Q6_K.dequantize_blocks), bit for bit.  The reference
+ * hook routes Q6_K weights like Q4_K (src/simd/ggml_simd_hook.cpp:282-288; block size
+ * src/bench_simd.zig:34-40). */
+void ora_q6k_dequant_row(const uint8_t* blocks, int64_t K, float* out) {
+    const int64_t nb = K / ORA_QK_K;
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = blocks + b * ORA_Q6K_BYTES;
+        const uint8_t* ql = blk;
+        const uint8_t* qh = blk + 128;
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        uint16_t dh;
+        memcpy(&dh, blk + 208, 2);
+        const float d = ora_f16_to_f32(dh);
+        float* o = out + b * ORA_QK_K;
+        for (int p = 0; p < ORA_QK_K; p++) {
+            const int h = p / 128, r = p % 128, l = r % 32, k = r / 32;
+            const int lo = (ql[64 * h + 32 * (k % 2) + l] >> (4 * (k / 2))) & 0x0F;
+            const int hi = (qh[32 * h + l] >> (2 * k)) & 0x03;
+            const int q = (lo | (hi << 4)) - 32;
+            const float ds = d * (float)sc[p / 16];
+            o[p] = ds * (float)q;
+        }
+    }
+}
+
+/* Q6_K weight x f32 activation, fp64 accumulation of the dequantised f32 weights (the
+ * dequantised-F32 product the Q6_K parity gate is defined against). */
+void ora_mul_mat_q6k(const uint8_t* W, size_t w_row_bytes, int64_t M, int64_t K,
+                     const float* X, size_t x_col_bytes, int64_t N, double* Y) {
+    float* wf = (float*)malloc(sizeof(float) * (size_t)K);
+    for (int64_t m = 0; m < M; m++) {
+        ora_q6k_dequant_row(W + m * w_row_bytes, K, wf);
         for (int64_t n = 0; n < N; n++) {
             const float* xc = (const float*)((const char*)X + n * x_col_bytes);
             double acc = 0.0;
@@ -659,6 +707,66 @@ void base_mul_mat_q4k(const uint8_t* W, size_t w_row_bytes, int64_t M, int64_t K
                       const float* X, size_t x_col_bytes, int64_t N, float* Y, int nth) {
     base_q4k_task_t t = {W, w_row_bytes, M, K, X, x_col_bytes, N, Y};
     base_parallel(base_q4k_worker, &t, nth);
+}
+
+/* Q6_K . Q8_K super-block dot: sum_b y.d * d * sum_g sc_g * sum_{i in g} (q_i - 32) q8_i,
+ * the math of vec_dot_q6_k_q8_k (src/simd/kernels/x86/vec/vec_dot_q6_k_q8_k_avx2.asm),
+ * with GGUF's element order; integer sums per group of 16, one float scale per block. */
+static float base_vec_dot_q6k_q8k(int64_t K, const uint8_t* vx, const uint8_t* vy) {
+    const int64_t nb = K / ORA_QK_K;
+    float sum = 0.0f;
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = vx + b * ORA_Q6K_BYTES;
+        const uint8_t* yb = vy + b * ORA_Q8K_BYTES;
+        float yd;
+        memcpy(&yd, yb, 4);
+        const int8_t* q8 = (const int8_t*)(yb + 4);
+        const uint8_t* ql = blk;
+        const uint8_t* qh = blk + 128;
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        uint16_t dh;
+        memcpy(&dh, blk + 208, 2);
+        int8_t q6[256];
+        for (int h = 0; h < 2; h++)
+            for (int l = 0; l < 32; l++) {
+                const uint8_t a = ql[64 * h + l], c = ql[64 * h + 32 + l], e = qh[32 * h + l];
+                q6[128 * h + l] = (int8_t)(((a & 0x0F) | ((e & 3) << 4)) - 32);
+                q6[128 * h + 32 + l] = (int8_t)(((c & 0x0F) | (((e >> 2) & 3) << 4)) - 32);
+                q6[128 * h + 64 + l] = (int8_t)(((a >> 4) | (((e >> 4) & 3) << 4)) - 32);
+                q6[128 * h + 96 + l] = (int8_t)(((c >> 4) | (((e >> 6) & 3) << 4)) - 32);
+            }
+        int isum = 0;
+        for (int g = 0; g < 16; g++) {
+            int gs = 0;
+            for (int i = 0; i < 16; i++) gs += (int)q6[16 * g + i] * (int)q8[16 * g + i];
+            isum += (int)sc[g] * gs;
+        }
+        sum += yd * ora_f16_to_f32(dh) * (float)isum;
+    }
+    return sum;
+}
+
+static void base_q6k_worker(void* p, int ith, int nth) {
+    base_q4k_task_t* t = (base_q4k_task_t*)p;
+    const int64_t mpt = (t->M + nth - 1) / nth;
+    const int64_t m0 = (int64_t)ith * mpt < t->M ? (int64_t)ith * mpt : t->M;
+    const int64_t m1 = m0 + mpt < t->M ? m0 + mpt : t->M;
+    if (m0 >= m1) return;
+    const size_t qrow = (size_t)(t->K / ORA_QK_K) * ORA_Q8K_BYTES;
+    uint8_t* q8 = (uint8_t*)malloc(qrow * (size_t)t->N);
+    for (int64_t n = 0; n < t->N; n++)
+        ora_quantize_row_q8k((const float*)((const char*)t->X + n * t->x_col_bytes), t->K, q8 + n * qrow);
+    for (int64_t m = m0; m < m1; m++) {
+        const uint8_t* wr = t->W + m * t->w_row_bytes;
+        for (int64_t n = 0; n < t->N; n++) t->Y[n * t->M + m] = base_vec_dot_q6k_q8k(t->K, wr, q8 + n * qrow);
+    }
+    free(q8);
+}
+
+void base_mul_mat_q6k(const uint8_t* W, size_t w_row_bytes, int64_t M, int64_t K,
+                      const float* X, size_t x_col_bytes, int64_t N, float* Y, int nth) {
+    base_q4k_task_t t = {W, w_row_bytes, M, K, X, x_col_bytes, N, Y};
+    base_parallel(base_q6k_worker, &t, nth);
 }
 
 /* --- Flash-attention decode, F16 K/V ------------------------------------ */

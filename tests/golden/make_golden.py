@@ -5,6 +5,7 @@ they were made).
 * q4k_gguf.npz      -- Q4_K super-blocks and their dequantisation by the gguf 0.19.0
                        Python decoder (gguf.quants.dequantize), the published GGUF
                        algorithm the reference's Q4_K kernels implement.
+* q6k_gguf.npz      -- Q6_K super-blocks and their dequantisation by the same gguf decoder.
 * fa_reference.npz  -- flash-attention decode cases and the outputs of the reference's
                        own flash_attn_quantized (src/simd/flash_attention.cpp:291-410),
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
@@ -48,6 +49,27 @@ def q4k_fixture() -> None:
     blk = blk.reshape(M, nb * 144)
     deq = quants.dequantize(blk, GGMLQuantizationType.Q4_K).astype(np.float32)
     np.savez_compressed(os.path.join(HERE, "q4k_gguf.npz"), blocks=blk, dequant=deq, K=K)
+
+
+def q6k_fixture() -> None:
+    from gguf import GGMLQuantizationType, quants
+    g = np.random.Generator(np.random.PCG64(9))
+    M, K = 6, 512
+    nb = K // 256
+    blk = g.integers(0, 256, size=(M, nb, 210), dtype=np.uint8)
+    d = np.abs(g.standard_normal((M, nb)) * 0.001).astype(np.float16)
+    # edge values for d: zero, a subnormal, the largest finite half, negative
+    d[0, 0] = np.float16(0.0)
+    d[1, 1] = np.float16(6e-8)
+    d[2, 0] = np.float16(65504.0)
+    d[3, 1] = np.float16(-0.5)
+    blk[:, :, 208:210] = d.view(np.uint8).reshape(M, nb, 2)
+    blk[4, 0, 192:208] = np.array([-128, 127] * 8, dtype=np.int8).view(np.uint8)   # extreme scales
+    blk[4, 1, :192] = 0xFF                                                        # q = 31 everywhere
+    blk[5, 0, :192] = 0x00                                                        # q = -32 everywhere
+    blk = blk.reshape(M, nb * 210)
+    deq = quants.dequantize(blk, GGMLQuantizationType.Q6_K).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "q6k_gguf.npz"), blocks=blk, dequant=deq, K=K)
 
 
 def fa_fixture() -> None:
@@ -126,6 +148,7 @@ if __name__ == "__main__":
     if not oracle.ref_available():
         sys.exit("oracle/_ref/libmlzref.so is missing: run `make -C oracle` where the reference tree exists")
     q4k_fixture()
+    q6k_fixture()
     fa_fixture()
     matmul_fixture()
     matmul_f16_fixture()

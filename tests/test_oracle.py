@@ -50,6 +50,32 @@ def test_q4k_dequant_matches_gguf_decoder(golden):
     assert same.all()
 
 
+def test_q6k_dequant_matches_gguf_decoder(golden):
+    f = golden("q6k_gguf.npz")
+    got = oracle.q6k_dequant(f["blocks"], int(f["K"]))
+    want = f["dequant"]
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all()
+
+
+def test_q6k_known_answer():
+    # ql low nibbles 5, high nibbles 1, qh all 2 (bits 10 per element), every scale 3,
+    # d = 0.25: low-nibble elements q = 5 + 32 - 32 = 5, high-nibble q = 1 -> known row dot
+    K = 256
+    blk = np.zeros((1, 210), dtype=np.uint8)
+    blk[0, :128] = 0x15
+    blk[0, 128:192] = 0xAA
+    blk[0, 192:208] = 3
+    blk[0, 208:210] = np.array([0.25], dtype=np.float16).view(np.uint8)
+    w = oracle.q6k_dequant(blk, K)[0]
+    p = np.arange(256)
+    low = ((p % 128) // 32) < 2          # elements k = 0, 1 read the low nibble
+    assert np.all(w[low] == 0.75 * 5) and np.all(w[~low] == 0.75 * 1)
+    x = np.random.default_rng(2).standard_normal((1, K)).astype(np.float32)
+    np.testing.assert_allclose(oracle.mul_mat_q6k(blk, x)[0, 0], float(np.dot(w.astype(np.float64), x[0])),
+                               rtol=1e-12)
+
+
 def test_q4k_known_answer():
     # every nibble 1, sc = 1, m = 0, d = 0.5, dmin arbitrary: row dot = d * sum(x)
     K = 512
