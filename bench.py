@@ -8,11 +8,13 @@ Workloads (synthetic seeded inputs of the named shapes; random-init weights):
   c1  F16 mul_mat, Llama-3.2-3B FFN up-proj: W 8192x3072 f16, X 3072xN f32, N in {1,8,32}
   c2  prefill GEMM of one Llama-3.2-3B layer: 7 F16 projections (Q 3072^2, K/V 1024x3072,
       O 3072^2, gate/up 8192x3072, down 3072x8192) over M tokens, M in {512, 2048}
-      (default workload: c2, M = 2048)
   c3  Q4_K decode mul_mat on Llama-3.1-8B shapes 4096x4096, 14336x4096, 4096x14336, batch N
   c4  flash-attention decode, 16 sequences, L ~ U{512..8192}, 32 q / 8 kv heads, D = 128
-  c5  Llama-3-70B FFN (gate/up 28672x8192, down 8192x28672) row-sharded over the ranks with
-      NCCL all-gather of the output slices, N in {1, 256}
+  c5  Llama-3-70B FFN (gate/up 28672x8192, down 8192x28672) row-sharded over the ranks, the
+      output slices all-gathered through NVLink peer memory, N in {1, 256}
+      (default workload: c5, N = 1, the decode GB/s of the configuration quoted at 1/2/4/8
+      GPUs; the line carries measured rows of the other configurations -- every one on one
+      GPU, the other c5 size on several)
   c6  Q6_K decode mul_mat on the Llama-3.1-8B shapes of c3, batch N (Q4_K_M files carry
       Q6_K tensors; the reference hook routes them with Q4_K)
 
@@ -59,7 +61,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c6"])
+    ap.add_argument("--config", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "c6"])
     ap.add_argument("--n", "--size", dest="n", type=int, default=None,
                     help="activation columns / tokens / batch (--size under torchrun, whose parser takes --n)")
     ap.add_argument("--impl", default="mlz", choices=["mlz", "reference"])
@@ -79,7 +81,7 @@ def parse_args():
     return ap.parse_args()
 
 
-DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 256, "c6": 4}
+DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 1, "c6": 4}
 DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32"}
 
 
@@ -96,7 +98,7 @@ def metric_name(cfg: str, n: int, world: int) -> str:
     if cfg == "c6":
         return f"decode Q6_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
     return (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
-            f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, NCCL all-gather)")
+            f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, all-gather of the slices)")
 
 
 C2_PROJ = [("q", 3072, 3072, 0), ("k", 1024, 3072, 0), ("v", 1024, 3072, 0), ("o", 3072, 3072, 1),
@@ -421,7 +423,9 @@ class C5(Workload):
                max(mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_F16, m, k, n) for (_, m, k) in self.mats))
         self.ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
         self.config = {"workload": workload_name("c5", n, world), "N": n,
-                       "parallelism": f"row-shard x{world} + all-gather", "l2": "inputs larger than L2"}
+                       "parallelism": (f"row-shard x{world}, slices all-gathered through NVLink peer memory"
+                                       if world > 1 else "single GPU (unsharded)"),
+                       "l2": "inputs larger than L2"}
 
     def work_units(self):  # whole-job units (all ranks together), reported once
         if self.N == 1:
@@ -845,15 +849,20 @@ def mlz_arm(a):
             f()
     torch.cuda.synchronize()
 
+    # about a second of load for the clock sampler; the same number of steps on every rank
+    # (the sharded calls are collective)
+    t_step = time.perf_counter()
+    for f, _ in w.launches(0):
+        f()
+    torch.cuda.synchronize()
+    n_load = 0 if a.profile_run else int(max_over_ranks(min(20000.0, max(8.0, 1.0 / max(time.perf_counter() - t_step,
+                                                                                          1e-5))), world))
     sampler = ClockSampler(local)
     sampler.start()
-    t_load = time.perf_counter()
-    i = 0
-    while not a.profile_run and time.perf_counter() - t_load < 1.0:  # load for the clock sampler
+    for i in range(n_load):
         for f, _ in w.launches(i):
             f()
-        i += 1
-        if i % 8 == 0:
+        if i % 8 == 7:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
 

@@ -315,19 +315,27 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
     const size_t slice_bytes = ((size_t)N * m_loc * 4 + 255) / 256 * 256;
     float* slice = reinterpret_cast<float*>(ws + mm);
     float* gathered = reinterpret_cast<float*>(ws + mm + slice_bytes);
-    // This rank's slice, dense [N][m_loc].
-    st = mul_mat_run(ctx, w_type, w_shard, w_row_bytes, m_loc, K, x, x_col_bytes, N, slice, (size_t)m_loc * 4,
-                     ws, mm, s);
-    if (st != MLZC_OK) return st;
-    if (c->peer_ok && (size_t)c->nranks * slice_bytes <= c->slot_bytes) {
-        PeerView pv{};
+    const bool peer = c->peer_ok && (size_t)c->nranks * slice_bytes <= c->slot_bytes;
+    PeerView pv{};
+    if (peer) {
         for (int r = 0; r < c->nranks; ++r) pv.base[r] = c->base[r];
         pv.G = c->nranks;
         pv.rank = c->rank;
         pv.slot_bytes = c->slot_bytes;
         pv.slice_stride = slice_bytes;
-        return launch_peer_allgather(pv, slice, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
+        // decode (one column, F16): one kernel computes the slice and stores it into every
+        // rank's slot over NVLink as it goes; then the wait-and-copy kernel
+        if (N == 1 && w_type == MLZC_TYPE_F16) {
+            st = launch_gemv_f16_peer(w_shard, w_row_bytes, m_loc, K, x, pv, s);
+            if (st == MLZC_OK) return launch_peer_wait(pv, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
+            if (st != MLZC_ERR_UNSUPPORTED) return st;
+        }
     }
+    // This rank's slice, dense [N][m_loc].
+    st = mul_mat_run(ctx, w_type, w_shard, w_row_bytes, m_loc, K, x, x_col_bytes, N, slice, (size_t)m_loc * 4,
+                     ws, mm, s);
+    if (st != MLZC_OK) return st;
+    if (peer) return launch_peer_allgather(pv, slice, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
     const bool direct = (N == 1);  // one column: slices land at their final place in y
     ncclResult_t r = api->AllGather(slice, direct ? static_cast<void*>(y) : static_cast<void*>(gathered),
                                     (size_t)N * m_loc, ncclFloat32, c->comm, s);

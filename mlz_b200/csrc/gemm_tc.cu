@@ -28,7 +28,7 @@
 //      When two accumulator sets fit in TMEM (2*MT*BN <= 512 columns) the epilogue of
 //      tile t overlaps the MMAs of tile t+1.  MT = 2 (256 x 256 per SM) needs 64 KB of
 //      operands per 1024 MMA cycles instead of 48 KB per 512 for 128 x 256, which is what
-//      bounds this kernel (no TMA multicast is used anywhere).  Every mbarrier wait is
+//      bounds this kernel (every TMA copy fills only its own CTA).  Every mbarrier wait is
 //      bounded (MLZC_DEVERR_WAIT_TIMEOUT).
 // Small tile counts split K across CTAs: each split stores its partial tile to the
 // workspace and the split that finishes a tile last sums the partials in split order, so
@@ -155,7 +155,7 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // MT M-tiles of 128 rows share one BN-column X tile per stage: an SM computes a
 // (128*MT) x BN output tile with MT UMMAs per K step.  The per-SM operand feed per MMA
 // cycle falls with MT (48 KB per 512 MMA cycles for 128x256, 64 KB per 1024 for 256x256),
-// which is what bounds this kernel without cross-SM multicast.
+// which is what bounds this kernel with per-CTA operand loads.
 template <int BN, int MT>
 struct TileCfg {
     static constexpr int kRows = BM * MT;
@@ -586,10 +586,13 @@ constexpr ShapeCost kShapeCosts[] = {
     {1, 128, 581.0, 5909.0},   {1, 96, 596.0, 8882.0},
 };
 constexpr double kSplitBytesPerCycle = 10.0;
+// K splits for wide problems: few tiles over a long K (the row shards of the sharded FFN,
+// e.g. 1024 x 28672 at 256 tokens) measured fastest with 4 to 8 splits.
+constexpr int kMaxWideSplits = 8;
 
 // Tile shape (MT M-tiles of 128 rows x BN columns per CTA) and K split for a problem.
 // Wide problems (N >= 128) minimise rounds x measured unit cost over the candidates, with
-// at most two K splits (a split's partial tile goes through the workspace); narrow ones
+// at most kMaxWideSplits K splits (a split's partial tile goes through the workspace); narrow ones
 // (decode) use the narrowest BN that holds N and split K to occupy the SMs.
 GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
     GemmPlan p{};
@@ -599,7 +602,7 @@ GemmPlan plan_gemm(int64_t M, int64_t K, int64_t N, int sm_count) {
     if (N >= 128) {
         double best = 1e300;
         for (const ShapeCost& sc : kShapeCosts)
-            for (int sp = 1; sp <= 2; ++sp) {
+            for (int sp = 1; sp <= kMaxWideSplits; ++sp) {
                 if (sp > 1 && p.kblocks / sp < 4) break;
                 const long tiles = (long)((M + BM * sc.mt - 1) / (BM * sc.mt)) * ((N + sc.bn - 1) / sc.bn);
                 const long rounds = (tiles * sp + sm_count - 1) / sm_count;

@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "internal.h"
+#include "peer.h"
 #include "ptx.cuh"
 
 namespace mlzc {
@@ -72,17 +73,29 @@ struct WF32 {
 // Each lane keeps ROWS x U 16-byte weight loads in flight (U chunks 32 apart), which is
 // what hides the HBM latency: ~128 KB in flight per SM at ROWS = 2, U = 4.
 // early != 0 (f16 weights only): the first weight loads are issued before pdl_wait().
-template <class WT, int NB, int ROWS, int U>
+// KW = 1: each warp owns ROWS rows over all of K.  KW = kWarps (few rows: too few warps
+// to keep enough loads in flight): the CTA's 8 warps share ROWS rows, warp w takes every
+// 8th group of 32 * U chunks, and the CTA sums the 8 partial rows in warp order.
+// PEER (row-sharded mul_mat, one column): instead of Y, every output row goes to this
+// rank's slice in the epoch's slot of every rank's exchange region (peer memory over
+// NVLink); the wait kernel that follows on the stream signals and gathers.
+template <class WT, int NB, int ROWS, int U, int KW, bool PEER>
 __global__ void __launch_bounds__(kThreads)
 gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
                 const char* X, size_t x_cs, int ncols,
-                char* __restrict__ Y, size_t y_cs, int early) {
+                char* __restrict__ Y, size_t y_cs, int early, PeerView pv) {
     constexpr int CH = WT::kPerChunk;
     const int lane = threadIdx.x & 31;
-    const int64_t row0 = ((int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5)) * ROWS;
+    const int warp = threadIdx.x >> 5;
+    const int64_t row0 = KW == 1 ? ((int64_t)blockIdx.x * kWarps + warp) * ROWS : (int64_t)blockIdx.x * ROWS;
+    const int kw = KW == 1 ? 0 : warp;
     ptx::pdl_launch_dependents();
-    if (row0 >= M) return;
-    if (!(WT::kNcWeights && early)) ptx::pdl_wait();
+    if (KW == 1 && row0 >= M) return;   // (KW > 1: the grid covers M exactly by ROWS-row groups)
+    bool waited = false;
+    if (!(WT::kNcWeights && early)) {
+        ptx::pdl_wait();
+        waited = true;
+    }
 
     const char* wrow[ROWS];
 #pragma unroll
@@ -95,7 +108,7 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
         for (int n = 0; n < NB; n++) acc[r][n] = 0.0f;
 
     const int64_t nchunk = K / CH;
-    for (int64_t base = 0; base < nchunk; base += 32 * U) {
+    for (int64_t base = (int64_t)kw * 32 * U; base < nchunk; base += (int64_t)32 * U * KW) {
         uint4 wv[ROWS][U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
@@ -106,7 +119,10 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
         }
         // the first weight loads are in flight while the previous kernel finishes; the
         // activations (and every write) come after it
-        if (base == 0) ptx::pdl_wait();
+        if (!waited) {
+            ptx::pdl_wait();
+            waited = true;
+        }
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int64_t c = base + lane + 32 * u;
@@ -136,14 +152,43 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
             }
         }
     }
-#pragma unroll
-    for (int r = 0; r < ROWS; r++)
-#pragma unroll
-        for (int n = 0; n < NB; n++) {
-            const float v = warp_sum(acc[r][n]);
-            if (lane == 0 && n < ncols && row0 + r < M)
-                reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row0 + r] = v;
+    if (!waited) ptx::pdl_wait();
+    uint32_t e = 0;
+    if (PEER) e = peer_epoch(pv);   // after the wait: the previous call's wait kernel advanced it
+    auto put = [&](int n, int64_t row, float v) {
+        if (PEER) {
+            const size_t off = peer_slice_offset(pv, e) + (size_t)row * 4;   // [N = 1][m_loc]
+            for (int r = 0; r < pv.G; ++r) *reinterpret_cast<float*>(pv.base[r] + off) = v;
+        } else {
+            reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row] = v;
         }
+    };
+    if (KW == 1) {
+#pragma unroll
+        for (int r = 0; r < ROWS; r++)
+#pragma unroll
+            for (int n = 0; n < NB; n++) {
+                const float v = warp_sum(acc[r][n]);
+                if (lane == 0 && n < ncols && row0 + r < M) put(n, row0 + r, v);
+            }
+    } else {
+        __shared__ float red[kWarps][ROWS * NB];
+#pragma unroll
+        for (int r = 0; r < ROWS; r++)
+#pragma unroll
+            for (int n = 0; n < NB; n++) {
+                const float v = warp_sum(acc[r][n]);
+                if (lane == 0) red[warp][r * NB + n] = v;
+            }
+        __syncthreads();
+        if (threadIdx.x < ROWS * NB) {
+            const int r = threadIdx.x / NB, n = threadIdx.x % NB;
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) v += red[w][threadIdx.x];
+            if (n < ncols && row0 + r < M) put(n, row0 + r, v);
+        }
+    }
 }
 
 // Scalar kernel for any alignment / K: one warp per row, columns in sequence.
@@ -169,15 +214,27 @@ gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K
     }
 }
 
-template <class WT, int NB>
+// Rows below which the warps of a CTA split K instead of taking rows of their own: with
+// fewer than ~2 CTAs of 16 rows per SM the loads in flight cannot cover the HBM latency
+// (e.g. the 1024 x 28672 and 3584 x 8192 row shards of the sharded FFN).
+constexpr int64_t kKSplitMaxRows = 2 * 148 * kWarps * 2;
+
+template <class WT, int NB, bool PEER = false>
 int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
-               int ncols, char* y, size_t y_cs, cudaStream_t s) {
+               int ncols, char* y, size_t y_cs, cudaStream_t s, const PeerView& pv = PeerView{}) {
     constexpr int ROWS = 2;
     constexpr int U = NB <= 2 ? 4 : 2;
-    const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
-    const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U>, dim3(grid), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs,
-                             ncols, y, y_cs, weights_before_wait() ? 1 : 0));
+    const int early = weights_before_wait() ? 1 : 0;
+    if (M < kKSplitMaxRows && K / WT::kPerChunk >= (int64_t)32 * U * kWarps) {
+        const unsigned grid = (unsigned)((M + ROWS - 1) / ROWS);
+        MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U, kWarps, PEER>, dim3(grid), dim3(kThreads), 0, s, w,
+                                 w_rs, M, K, x, x_cs, ncols, y, y_cs, early, pv));
+    } else {
+        const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
+        const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
+        MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U, 1, PEER>, dim3(grid), dim3(kThreads), 0, s, w, w_rs,
+                                 M, K, x, x_cs, ncols, y, y_cs, early, pv));
+    }
     count_launch();
     return MLZC_OK;
 }
@@ -211,6 +268,16 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
     return MLZC_OK;
 }
 
+// F16 decode GEMV whose outputs go straight to every rank's exchange slot (see PEER).
+int gemv_f16_peer(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, const PeerView& pv,
+                  cudaStream_t s) {
+    const bool aligned = ((uintptr_t)w % 16 == 0) && ((uintptr_t)x % 16 == 0) && (w_rs % 16 == 0) &&
+                         (K % WF16::kPerChunk == 0);
+    if (!aligned || M < 1 || K < 1) return MLZC_ERR_UNSUPPORTED;   // caller takes the two-kernel path
+    return launch_vec<WF16, 1, true>(static_cast<const char*>(w), w_rs, M, K, reinterpret_cast<const char*>(x),
+                                     (size_t)K * 4, 1, nullptr, 0, s, pv);
+}
+
 // gathered [G][N][m_loc] -> dst [N][G * m_loc] (column stride dst_cs bytes): one CTA row per
 // (rank slice r, column n) -- blockIdx.y = r * N + n -- threads over m, float4 when the
 // slices and the destination are 16-byte aligned.
@@ -233,6 +300,11 @@ __global__ void gather_permute_kernel(const float* src, char* __restrict__ dst, 
 }
 
 }  // namespace
+
+int launch_gemv_f16_peer(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                         const PeerView& pv, cudaStream_t s) {
+    return gemv_f16_peer(w, w_row_bytes, M, K, x, pv, s);
+}
 
 int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,
                           int64_t m_loc, cudaStream_t s) {

@@ -43,7 +43,9 @@ def test_f16_llama32_3b_up_proj(dev, N):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 64, 1), (5, 3080, 2), (33, 256, 3), (130, 520, 31), (64, 1024, 33),
-                                   (17, 100, 4), (9, 7, 5), (3, 2056, 9)])
+                                   (17, 100, 4), (9, 7, 5), (3, 2056, 9),
+                                   # few rows over a long K: the warps of a CTA split K
+                                   (1024, 28672, 1), (37, 16384, 2), (3584, 8192, 1), (515, 8200, 3)])
 def test_f16_edge_shapes(dev, M, K, N):
     g = synth.rng(100 + M + K + N)
     w = synth.f16_weights(g, M, K)
@@ -52,7 +54,7 @@ def test_f16_edge_shapes(dev, M, K, N):
     assert oracle.rel_err(y, oracle.mul_mat_f16(w.view(np.uint16), x)) <= TOL
 
 
-@pytest.mark.parametrize("M,K,N", [(256, 512, 1), (100, 36, 3), (64, 4096, 8), (7, 5, 2)])
+@pytest.mark.parametrize("M,K,N", [(256, 512, 1), (100, 36, 3), (64, 4096, 8), (7, 5, 2), (100, 8192, 3)])
 def test_f32_weights(dev, M, K, N):
     g = synth.rng(200 + M + N)
     w = g.standard_normal((M, K), dtype=np.float32) * 0.02

@@ -35,9 +35,12 @@ def test_single_rank_equals_unsharded(dev, comm):
             assert torch.equal(y, ref), (rep, M, K, N)
 
 
-def test_single_rank_graph_replay(dev, comm):
+@pytest.mark.parametrize("N", [1, 4])
+def test_single_rank_graph_replay(dev, comm, N):
+    """N = 1 takes the fused decode GEMV (outputs stored straight into the exchange slots),
+    N = 4 the slice + push kernels."""
     import torch
-    M, K, N = 2048, 1024, 4
+    M, K = 2048, 1024
     gen = torch.Generator(device=dev).manual_seed(700)
     ws_ = [synth.f16_weights_dev(gen, M, K, dev) for _ in range(3)]
     x = torch.randn((N, K), generator=gen, device=dev)
