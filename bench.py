@@ -17,6 +17,7 @@ Workloads (synthetic seeded inputs of the named shapes; random-init weights):
       GPU, the other c5 size on several)
   c6  Q6_K decode mul_mat on the Llama-3.1-8B shapes of c3, batch N (Q4_K_M files carry
       Q6_K tensors; the reference hook routes them with Q4_K)
+  c7  flash-attention decode of c4 over a Q8_0 KV cache
 
 A step is one pass of the hot path over one batch.  `value` is whole-job throughput with
 inputs resident in HBM; `e2e` is the same metric through the reference-facing plugin
@@ -48,8 +49,6 @@ NCU_TRAFFIC = {
     ("c1", 4): (50.39e6 + 0.07e6, "ncu capture: gemv_f16_mma_kernel, 8192x3072, N=4"),
     ("c1", 8): (50.44e6 + 0.01e6, "ncu capture: gemv_f16_mma_kernel<1, 1, 4>, 8192x3072, N=8"),
     ("c4", 16): (250.80e6 + 5.98e6, "ncu capture: fa_decode_kernel of the c4 call (16 sequences)"),
-    ("c3", 1): (33.07e6, "ncu capture: q4k_ring_kernel, 14336x4096 launch (the 4096x14336 launch reads the "
-                         "same block bytes)"),
     ("c3", 8): (33.29e6, "ncu capture: q4k_ring_xs_kernel, 4096x14336 launch, batch 8 (the 14336x4096 launch "
                          "reads the same block bytes)"),
     ("c3", 16): (33.31e6, "ncu capture: q4k_mma_kernel, 14336x4096 launch, batch 16"),
@@ -61,7 +60,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "c6"])
+    ap.add_argument("--config", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "c6", "c7"])
     ap.add_argument("--n", "--size", dest="n", type=int, default=None,
                     help="activation columns / tokens / batch (--size under torchrun, whose parser takes --n)")
     ap.add_argument("--impl", default="mlz", choices=["mlz", "reference"])
@@ -81,8 +80,9 @@ def parse_args():
     return ap.parse_args()
 
 
-DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 1, "c6": 4}
-DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32"}
+DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 1, "c6": 4, "c7": 16}
+DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32",
+         "c7": "q8_0 kv / f32"}
 
 
 def metric_name(cfg: str, n: int, world: int) -> str:
@@ -97,6 +97,8 @@ def metric_name(cfg: str, n: int, world: int) -> str:
         return f"flash-attention decode GB/s (F16 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
     if cfg == "c6":
         return f"decode Q6_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
+    if cfg == "c7":
+        return f"flash-attention decode GB/s (Q8_0 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
     return (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
             f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, all-gather of the slices)")
 
@@ -124,6 +126,8 @@ def workload_name(cfg: str, n: int, world: int) -> str:
         return f"c4 FA decode GQA, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
     if cfg == "c6":
         return f"c6 Q6_K mul_mat Llama-3.1-8B shapes, batch {n}"
+    if cfg == "c7":
+        return f"c7 FA decode GQA over a Q8_0 KV cache, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
     return f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}"
 
 
@@ -271,9 +275,9 @@ class C3(Workload):
     def roofline_kernel(self, j):
         m, k = self.SHAPES[j]
         n = self.N
-        # the library's dispatch (q4k_ring_applicable, q4k_ring_xs_applicable, launch_q4k_mma)
-        if n <= 2 or (n <= 4 and m >= 8192 and k <= 4096):
-            kern = "q4k_ring_kernel"
+        # the library's dispatch (q4k_i8_applicable, q4k_ring_xs_applicable, launch_q4k_mma)
+        if n <= 4:
+            kern = "q4k_i8_prep_kernel + q4k_i8_kernel"
         elif n <= 8 and (n >= 5 or m >= 8192 or k > 4096):
             kern = "q4k_prep_kernel + q4k_ring_xs_kernel"
         elif n <= 8:
@@ -401,6 +405,59 @@ class C4(Workload):
         import mlz_b200
         return [(lambda: mlz_b200.flash_attn_dispatch(self.q, self.k, self.v, 1.0 / math.sqrt(self.D),
                                                       kv_len=self.kv_len, out=self.out, workspace=self.ws),
+                 self.work_units())]
+
+
+class C7(Workload):
+    """c4's batch and lengths over a Q8_0 KV cache (34-byte blocks of 32 values)."""
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = "q8_0 kv / f32"
+
+    def roofline_kernel(self, j):
+        return "one flash-attention call: fa_quant_kernel<128, Q8_0> + fa_quant_combine_kernel"
+
+    def __init__(self, n, dev, gen):
+        import torch
+        import mlz_b200
+        from mlz_b200.ops import _nb
+        self.B, self.Hq, self.Hkv, self.D = n, 32, 8, 128
+        self.kv_len_np = c4_lengths(n)
+        self.L = 8192
+        self.rb = self.D // 32 * 34
+        s = 1.0 / math.sqrt(self.D)
+        self.q = torch.randn((n, self.Hq, 1, self.D), generator=gen, device=dev) * s
+        self.k = self._rows(gen, dev)
+        self.v = self._rows(gen, dev)
+        self.kv_len = torch.from_numpy(self.kv_len_np).to(dev)
+        self.out = torch.empty((n, self.Hq, 1, self.D), dtype=torch.float32, device=dev)
+        desc = mlz_b200.make_fa_desc(self.q.data_ptr(), _nb(self.q, 4), self.k.data_ptr(), (34,) + _nb(self.k, 1)[1:],
+                                     self.v.data_ptr(), (34,) + _nb(self.v, 1)[1:], self.out.data_ptr(),
+                                     _nb(self.out, 4), (n, self.Hq, 1, self.Hkv, self.L, self.D), s,
+                                     kv_len_ptr=self.kv_len.data_ptr(), kv_type=mlz_b200.TYPE_Q8_0)
+        self.ws = torch.empty(max(mlz_b200.flash_attn_workspace_bytes(desc), 1), dtype=torch.uint8, device=dev)
+        self.metric = metric_name("c7", n, 1)
+        self.config = {"workload": workload_name("c7", n, 1), "batch": n, "sum_kv_len": int(self.kv_len_np.sum()),
+                       "l2": "inputs larger than L2 (KV cache 285 MB)"}
+
+    def _rows(self, gen, dev):
+        import torch
+        nb = self.D // 32
+        r = torch.randint(-127, 128, (self.B, self.Hkv, self.L, nb, 34), generator=gen, device=dev,
+                          dtype=torch.int16).to(torch.int8).view(torch.uint8)
+        d = (torch.randn((self.B, self.Hkv, self.L, nb, 1), generator=gen, device=dev).abs() /
+             (64.0 * math.sqrt(self.D))).to(torch.float16)
+        r[..., 0:2] = d.view(torch.uint8)
+        return r.reshape(self.B, self.Hkv, self.L, nb * 34)
+
+    def work_units(self):
+        return 2 * self.Hkv * self.rb * float(self.kv_len_np.sum()) + 2 * self.B * self.Hq * self.D * 4
+
+    def launches(self, i):
+        import mlz_b200
+        return [(lambda: mlz_b200.flash_attn_dispatch_quant(self.q, self.k, self.v, 1.0 / math.sqrt(self.D),
+                                                            mlz_b200.TYPE_Q8_0, kv_len=self.kv_len, out=self.out,
+                                                            workspace=self.ws),
                  self.work_units())]
 
 
@@ -536,12 +593,19 @@ class CpuStep:
             self.flops = False
             self.block_bytes = 210 if q6 else 144
             self.what = f"Q8_K quantise + {'Q6_K' if q6 else 'Q4_K'} x Q8_K dot restatement"
-        elif cfg == "c4":
+        elif cfg in ("c4", "c7"):
             self.kl = c4_lengths(n)
             self.slots = 4
             self.q, self.k, self.v = synth.fa_inputs(g, self.slots, 32, 8, int(self.kl.max()), 128)
             self.flops = False
-            self.what = "FA2 skeleton restatement"
+            self.kv_type = 1
+            self.row_bytes = 256
+            if cfg == "c7":
+                self.kv_type = 8
+                self.row_bytes = 136
+                self.k = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, 8)
+                self.v = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, 8)
+            self.what = "FA2 skeleton restatement" + (" (Q8_0 K/V dequantised per row)" if cfg == "c7" else "")
         else:
             raise ValueError(cfg)
 
@@ -550,12 +614,16 @@ class CpuStep:
         import oracle
         n = self.n
         units = 0.0
-        if self.cfg == "c4":
+        if self.cfg in ("c4", "c7"):
             for b in range(len(self.kl)):
                 j = b % self.slots
-                oracle.base_flash_attn(self.q[j:j + 1], self.k[j:j + 1], self.v[j:j + 1], 1 / math.sqrt(128),
-                                       kv_len=self.kl[b:b + 1], nth=self.nth)
-                units += 4096.0 * int(self.kl[b]) + 2 * 32 * 128 * 4
+                if self.kv_type == 1:
+                    oracle.base_flash_attn(self.q[j:j + 1], self.k[j:j + 1], self.v[j:j + 1], 1 / math.sqrt(128),
+                                           kv_len=self.kl[b:b + 1], nth=self.nth)
+                else:
+                    oracle.base_flash_attn_q(self.q[j:j + 1], self.k[j:j + 1], self.v[j:j + 1], 1 / math.sqrt(128),
+                                             self.kv_type, kv_len=self.kl[b:b + 1], nth=self.nth)
+                units += 2 * 8 * self.row_bytes * float(int(self.kl[b])) + 2 * 32 * 128 * 4
             return units
         for (M, K, w, x) in self.parts:
             reps, r = divmod(M, w.shape[0])
@@ -609,7 +677,7 @@ def reference_arm(a):
         return
     n = a.n or DEFAULT_N[a.config]
     unit = {"c1": "GB/s", "c2": "TFLOP/s", "c3": "GB/s", "c4": "GB/s", "c5": "GB/s" if n == 1 else "TFLOP/s",
-            "c6": "GB/s"}[a.config]
+            "c6": "GB/s", "c7": "GB/s"}[a.config]
     import oracle
     oracle.build()
     per_step = max(a.cpu_seconds / max(a.steps, 1), 0.5)
@@ -639,7 +707,7 @@ def make_workload(cfg: str, n: int, dev, rank: int, world: int, comm):
     import torch
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000 + 100 * int(cfg[1]) + n + rank)
-    wl = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c6": C6}.get(cfg)
+    wl = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c6": C6, "c7": C7}.get(cfg)
     return wl(n, dev, gen) if wl else C5(n, dev, gen, rank, world, comm)
 
 
@@ -770,20 +838,24 @@ def roofline_of(w, t, peaks, clocks, ms):
     else:
         peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
         peak_name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
+    # a row-sharded call's work is the whole matrix, spread over the ranks: its roof is the
+    # per-GPU peak times the ranks
+    shards = getattr(w, "world", 1) if isinstance(w, C5) else 1
+    peak *= shards
     r = {"bound": w.bound, "achieved": ach, "peak": peak, "unit": "GB/s" if w.bound == "hbm" else "TFLOP/s",
          "frac": ach / peak, "traffic": None,
-         "peak_source": f"{peaks['source']} {peak_name}" + (" (sw_power_cap active in the timed region)"
-                                                            if power_capped and w.bound != "hbm" else ""),
+         "peak_source": f"{peaks['source']} {peak_name}" + (f" x {shards} GPUs" if shards > 1 else "")
+                        + (" (sw_power_cap active in the timed region)" if power_capped and w.bound != "hbm" else ""),
          "kernel": w.roofline_kernel(jdom), "call_timing": t["call_timing"]}
     if w.bound != "hbm":
-        r["frac_of_burst"] = ach / peaks["bf16_tflops"]
+        r["frac_of_burst"] = ach / (peaks["bf16_tflops"] * shards)
     return r
 
 
 # Measured rows that the default line carries besides its headline workload, so that one
 # run records every configuration: (config, N).  On several GPUs only the other c5 size.
 EXTRA_ROWS_1GPU = [("c2", 2048), ("c2", 512), ("c1", 1), ("c1", 8), ("c1", 32), ("c3", 1), ("c3", 4), ("c3", 16),
-                   ("c4", 16), ("c5", 256), ("c6", 1), ("c6", 4), ("c6", 16)]
+                   ("c4", 16), ("c5", 256), ("c6", 1), ("c6", 4), ("c6", 16), ("c7", 16)]
 
 
 def extra_rows(a, n_head, dev, rank, world, comm, peaks):
@@ -966,18 +1038,25 @@ def run_e2e(w, a, world, value_dev):
     import torch
     import mlz_b200
     pinned = []
-    if isinstance(w, C4):
+    fa = isinstance(w, (C4, C7))
+    if fa:
         q = w.q.cpu().pin_memory()
         k = w.k.cpu().pin_memory()
         v = w.v.cpu().pin_memory()
         kl = torch.from_numpy(w.kv_len_np).pin_memory()
         o = torch.empty(w.out.shape, dtype=torch.float32).pin_memory()
         nb = lambda t, e: tuple(s * e for s in t.stride()[::-1])
-        desc = mlz_b200.make_fa_desc(q.data_ptr(), nb(q, 4), k.data_ptr(), nb(k, 2), v.data_ptr(), nb(v, 2),
+        if isinstance(w, C7):   # rows of 34-byte Q8_0 blocks (nb[0] = block bytes)
+            kv_nb = lambda t: (34,) + nb(t, 1)[1:]
+            kv_type = mlz_b200.TYPE_Q8_0
+        else:
+            kv_nb = lambda t: nb(t, 2)
+            kv_type = mlz_b200.TYPE_F16
+        desc = mlz_b200.make_fa_desc(q.data_ptr(), nb(q, 4), k.data_ptr(), kv_nb(k), v.data_ptr(), kv_nb(v),
                                      o.data_ptr(), nb(o, 4), (w.B, w.Hq, 1, w.Hkv, w.L, w.D),
-                                     1.0 / math.sqrt(w.D), kv_len_ptr=kl.data_ptr())
+                                     1.0 / math.sqrt(w.D), kv_len_ptr=kl.data_ptr(), kv_type=kv_type)
         # the hook copies the whole cache view it is given: here only the live keys count
-        h2d = q.numel() * 4 + (k.numel() + v.numel()) * 2 + kl.numel() * 4
+        h2d = q.numel() * 4 + (k.numel() * k.element_size() + v.numel() * v.element_size()) + kl.numel() * 4
         d2h = o.numel() * 4
         step = lambda: mlz_b200.ggml_simd_try_flash_attn(desc)
     else:
@@ -1023,9 +1102,9 @@ def run_e2e(w, a, world, value_dev):
     units = w.work_units() * world
     dt = timed(step)
     out = {"value": units / dt * w.unit_scale(), "unit": w.unit, "h2d_bytes_per_step": int(h2d),
-           "d2h_bytes_per_step": int(d2h), "path": "mlzc_try_flash_attn" if isinstance(w, C4) else "mlzc_try_mul_mat",
+           "d2h_bytes_per_step": int(d2h), "path": "mlzc_try_flash_attn" if fa else "mlzc_try_mul_mat",
            "host_buffers": "page-locked", "ms_per_step": 1e3 * dt}
-    if not isinstance(w, C4):
+    if not fa:
         dtp = timed(step_pageable)
         out["pageable"] = {"value": units / dtp * w.unit_scale(), "ms_per_step": 1e3 * dtp}
     return out

@@ -17,6 +17,7 @@ STATUS_NAMES = {
     -4: "MLZC_ERR_NOMEM", -5: "MLZC_ERR_DEVICE", -6: "MLZC_ERR_COMM",
 }
 TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 12, 14
+TYPE_Q4_0, TYPE_Q8_0 = 2, 8
 FA_MODE_GQA_BATCH, FA_MODE_ALIBI, FA_MODE_SOFTCAP = 0x04, 0x08, 0x10
 OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS = 0, 1, 2
 UNIQUE_ID_BYTES = 128

@@ -666,7 +666,19 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t D, int64_t n_kv, i
 
 }  // namespace
 
+namespace {
+int current_sms() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        sms = 148;
+    }
+    return sms;
+}
+}  // namespace
+
 int fa_workspace_bytes(const mlzc_fa_desc* d, size_t* out) {
+    if (d->k_type != MLZC_TYPE_F16) return faq_workspace_bytes(d, current_sms(), out);
     FaPlan pl;
     const int st = make_plan(d, &pl);
     *out = st == MLZC_OK ? pl.ws_bytes : 0;
@@ -723,6 +735,7 @@ int fa_take_static_errors(unsigned int* out) {
 }
 
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (d->k_type != MLZC_TYPE_F16) return launch_flash_attn_quant(c ? c->sm_count : current_sms(), d, ws, ws_bytes, s);
     FaPlan pl;
     int st = make_plan(d, &pl);
     if (st != MLZC_OK) return st;

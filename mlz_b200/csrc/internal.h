@@ -76,6 +76,13 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
                    void* ws, size_t ws_bytes, cudaStream_t s);
 // Decode-shaped Q4_K, N <= 2 (N <= 4 with many short rows): persistent kernel fed by a TMA
 // ring, activations converted once per CTA into shared memory.
+// Q4_K, 1 <= N <= 4: int8 tensor-core path (activations quantised to int8 hi + lo per
+// block by a prep launch), stream-K over 16-row x 8-block units.
+bool q4k_i8_applicable(int64_t M, int64_t K, int64_t N);
+size_t q4k_i8_workspace_bytes(int64_t K, int64_t N);
+int launch_q4k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                  size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                  cudaStream_t s);
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                     const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
@@ -98,6 +105,15 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
 // Flash-attention decode (persistent stream-K over key tiles + combine).  The workspace
 // size depends on the current device (its resident CTA count).
 int fa_workspace_bytes(const mlzc_fa_desc* d, size_t* out);
+// Quantised KV cache (Q8_0 / Q4_0 K and V): split-K CUDA-core decode + combine (fa_quant.cu).
+int faq_workspace_bytes(const mlzc_fa_desc* d, int sm_count, size_t* out);
+int launch_flash_attn_quant(int sm_count, const mlzc_fa_desc* d, void* ws, size_t ws_bytes, cudaStream_t s);
+// Bytes of one K or V row of head_dim values of ggml type `type` (F16, Q8_0, Q4_0).
+inline size_t fa_row_bytes(int32_t type, int64_t head_dim) {
+    if (type == MLZC_TYPE_Q8_0) return (size_t)(head_dim / 32) * 34;
+    if (type == MLZC_TYPE_Q4_0) return (size_t)(head_dim / 32) * 18;
+    return (size_t)head_dim * 2;
+}
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
                       cudaStream_t s);
 

@@ -136,8 +136,10 @@ int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M,
 
 int check_fa_args(const mlzc_fa_desc* d) {
     if (!d) return fail(MLZC_ERR_INVALID, "flash_attn: null descriptor");
-    if (d->k_type != MLZC_TYPE_F16 || d->v_type != MLZC_TYPE_F16)
-        return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V types %d/%d (F16/F16 only)", d->k_type, d->v_type);
+    const bool quant = d->k_type == MLZC_TYPE_Q8_0 || d->k_type == MLZC_TYPE_Q4_0;
+    if ((d->k_type != MLZC_TYPE_F16 && !quant) || d->v_type != d->k_type)
+        return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V types %d/%d (F16/F16, Q8_0/Q8_0 or Q4_0/Q4_0)", d->k_type,
+                    d->v_type);
     if (d->head_dim_k != d->head_dim_v) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: DK != DV");
     if (d->head_dim_k != 64 && d->head_dim_k != 128 && d->head_dim_k != 256)
         return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: head_dim %lld (64, 128, 256 supported)", (long long)d->head_dim_k);
@@ -149,9 +151,17 @@ int check_fa_args(const mlzc_fa_desc* d) {
     if (!d->q || !d->dst || (d->n_kv > 0 && (!d->k || !d->v))) return fail(MLZC_ERR_INVALID, "flash_attn: null tensor");
     if ((uintptr_t)d->q % 16 || d->q_nb[1] % 16 || d->q_nb[2] % 16 || d->q_nb[3] % 16 || d->q_nb[0] != 4)
         return fail(MLZC_ERR_INVALID, "flash_attn: q rows must be contiguous f32 on 16-byte boundaries");
-    if ((uintptr_t)d->k % 16 || (uintptr_t)d->v % 16 || d->k_nb[1] % 16 || d->v_nb[1] % 16 || d->k_nb[2] % 16 ||
-        d->v_nb[2] % 16 || d->k_nb[3] % 16 || d->v_nb[3] % 16 || d->k_nb[0] != 2 || d->v_nb[0] != 2)
+    if (quant) {
+        // rows of blocks (nb[0] = block bytes, ggml's convention), 4-byte aligned
+        const size_t bb = d->k_type == MLZC_TYPE_Q8_0 ? 34 : 18;
+        if ((uintptr_t)d->k % 4 || (uintptr_t)d->v % 4 || d->k_nb[1] % 4 || d->v_nb[1] % 4 || d->k_nb[2] % 4 ||
+            d->v_nb[2] % 4 || d->k_nb[3] % 4 || d->v_nb[3] % 4 || d->k_nb[0] != bb || d->v_nb[0] != bb)
+            return fail(MLZC_ERR_INVALID, "flash_attn: quantised K/V rows must be contiguous blocks on 4-byte boundaries");
+    } else if ((uintptr_t)d->k % 16 || (uintptr_t)d->v % 16 || d->k_nb[1] % 16 || d->v_nb[1] % 16 ||
+               d->k_nb[2] % 16 || d->v_nb[2] % 16 || d->k_nb[3] % 16 || d->v_nb[3] % 16 || d->k_nb[0] != 2 ||
+               d->v_nb[0] != 2) {
         return fail(MLZC_ERR_INVALID, "flash_attn: K/V rows must be contiguous f16 on 16-byte boundaries");
+    }
     if (d->dst_nb[0] != 4 || (uintptr_t)d->dst % 4) return fail(MLZC_ERR_INVALID, "flash_attn: dst rows must be contiguous f32");
     if (d->mask && (d->mask_nb[0] % 4 || (uintptr_t)d->mask % 4)) return fail(MLZC_ERR_INVALID, "flash_attn: mask must be f32-aligned");
     if ((d->mode & MLZC_FA_MODE_SOFTCAP) && d->logit_softcap == 0.0f)
@@ -682,8 +692,10 @@ extern "C" int mlzc_try_flash_attn(const mlzc_fa_desc* desc, int ith, int nth) {
         std::lock_guard<std::mutex> lk(a->mu);
         const mlzc_fa_desc& d = *desc;
         const size_t qb = extent(d.head_dim_k, 4, d.n_queries, d.q_nb[1], d.n_head_q, d.q_nb[2], d.batch_size, d.q_nb[3]);
-        const size_t kb = extent(d.head_dim_k, 2, d.n_kv, d.k_nb[1], d.n_head_kv, d.k_nb[2], d.batch_size, d.k_nb[3]);
-        const size_t vb = extent(d.head_dim_v, 2, d.n_kv, d.v_nb[1], d.n_head_kv, d.v_nb[2], d.batch_size, d.v_nb[3]);
+        const size_t kb = extent((int64_t)fa_row_bytes(d.k_type, d.head_dim_k), 1, d.n_kv, d.k_nb[1], d.n_head_kv,
+                                 d.k_nb[2], d.batch_size, d.k_nb[3]);
+        const size_t vb = extent((int64_t)fa_row_bytes(d.v_type, d.head_dim_v), 1, d.n_kv, d.v_nb[1], d.n_head_kv,
+                                 d.v_nb[2], d.batch_size, d.v_nb[3]);
         const size_t db = extent(d.head_dim_v, 4, d.n_queries, d.dst_nb[1], d.n_head_q, d.dst_nb[2], d.batch_size, d.dst_nb[3]);
         const size_t mb = d.mask ? extent(d.n_kv, 4, d.n_queries, d.mask_nb[1], d.n_head_q, d.mask_nb[2], d.batch_size, d.mask_nb[3]) : 0;
         if (d.mask && d.mask_nb[0] != 4) return 0;

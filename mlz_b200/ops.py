@@ -20,7 +20,8 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, FaDesc,
+from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0,
+                   FaDesc,
                    MlzcError, TensorView, check, lib)
 
 QK_K = 256
@@ -116,8 +117,9 @@ def _nb(t, esz: int):
 
 def make_fa_desc(q_ptr, q_nb, k_ptr, k_nb, v_ptr, v_nb, dst_ptr, dst_nb, dims, scale,
                  mask_ptr=None, mask_nb=(0, 0, 0, 0), kv_len_ptr=None, softcap=0.0,
-                 alibi=False, max_bias=0.0) -> FaDesc:
-    """dims = (B, Hq, NQ, Hkv, NKV, D)."""
+                 alibi=False, max_bias=0.0, kv_type=TYPE_F16) -> FaDesc:
+    """dims = (B, Hq, NQ, Hkv, NKV, D); kv_type: TYPE_F16, or TYPE_Q8_0 / TYPE_Q4_0 for a
+    quantised cache (k_nb / v_nb then in bytes with nb[0] = the block size)."""
     B, Hq, NQ, Hkv, NKV, D = dims
     d = FaDesc()
     d.head_dim_k = d.head_dim_v = D
@@ -138,7 +140,7 @@ def make_fa_desc(q_ptr, q_nb, k_ptr, k_nb, v_ptr, v_nb, dst_ptr, dst_nb, dims, s
     d.v_nb[:] = v_nb
     d.dst_nb[:] = dst_nb
     d.mask_nb[:] = mask_nb
-    d.k_type = d.v_type = TYPE_F16
+    d.k_type = d.v_type = kv_type
     d.kv_len = kv_len_ptr
     return d
 
@@ -164,6 +166,37 @@ def flash_attn_dispatch(q, k, v, scale: float, *, kv_len=None, mask=None, softca
                         mask.data_ptr() if mask is not None else None,
                         _nb(mask, 4) if mask is not None else (0, 0, 0, 0),
                         kv_len.data_ptr() if kv_len is not None else None, softcap, alibi)
+    wsb = flash_attn_workspace_bytes(desc)
+    if wsb and workspace is None:
+        workspace = torch.empty(wsb, dtype=torch.uint8, device=q.device)
+    check(lib().mlzc_flash_attn_dev(C.byref(desc), workspace.data_ptr() if workspace is not None else None,
+                                    workspace.numel() if workspace is not None else 0,
+                                    _stream_handle(stream)))
+    return out
+
+
+KV_BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
+
+
+def flash_attn_dispatch_quant(q, k, v, scale: float, kv_type: int, *, kv_len=None, mask=None,
+                              softcap: float = 0.0, alibi: bool = False, out=None, workspace=None,
+                              stream=None):
+    """Flash-attention over a quantised KV cache on device tensors: q (B, Hq, NQ, D) f32;
+    k, v (B, Hkv, L, D/32*block_bytes) uint8 rows of Q8_0 (34-byte) or Q4_0 (18-byte)
+    blocks (any strides with contiguous rows).  Returns out (B, Hq, NQ, D) f32."""
+    torch = _torch()
+    B, Hq, NQ, D = q.shape
+    _, Hkv, L, _ = k.shape
+    bb = KV_BLOCK_BYTES[kv_type]
+    if out is None:
+        out = torch.empty((B, Hq, NQ, D), dtype=torch.float32, device=q.device)
+    knb = (bb,) + tuple(_nb(k, 1)[1:])
+    vnb = (bb,) + tuple(_nb(v, 1)[1:])
+    desc = make_fa_desc(q.data_ptr(), _nb(q, 4), k.data_ptr(), knb, v.data_ptr(), vnb,
+                        out.data_ptr(), _nb(out, 4), (B, Hq, NQ, Hkv, L, D), scale,
+                        mask.data_ptr() if mask is not None else None,
+                        _nb(mask, 4) if mask is not None else (0, 0, 0, 0),
+                        kv_len.data_ptr() if kv_len is not None else None, softcap, alibi, kv_type=kv_type)
     wsb = flash_attn_workspace_bytes(desc)
     if wsb and workspace is None:
         workspace = torch.empty(wsb, dtype=torch.uint8, device=q.device)

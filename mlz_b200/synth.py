@@ -69,6 +69,21 @@ def fa_inputs(g: np.random.Generator, B: int, Hq: int, Hkv: int, L: int, D: int,
     return q, k, v
 
 
+KV_QUANT = {8: (34, 64.0), 2: (18, 4.0)}   # ggml type -> (block bytes, typical |q|)
+
+
+def kv_quant_rows(g: np.random.Generator, shape, D: int, kv_type: int) -> np.ndarray:
+    """Quantised K/V rows (Q8_0 = 8 or Q4_0 = 2): uint8 array of shape + (D/32*block_bytes,),
+    random quants, block scales d = f16(|N(0, 1)| / (typical |q| * sqrt(D))) so that the
+    values have the spread of N(0, 1)/sqrt(D)."""
+    bb, qmag = KV_QUANT[kv_type]
+    nb = D // 32
+    rows = g.integers(0, 256, size=tuple(shape) + (nb, bb), dtype=np.uint8)
+    d = (np.abs(g.standard_normal(tuple(shape) + (nb, 1), dtype=np.float32)) / (qmag * np.sqrt(D))).astype(np.float16)
+    rows[..., 0:2] = d.view(np.uint8)
+    return rows.reshape(tuple(shape) + (nb * bb,))
+
+
 def kv_lengths(g: np.random.Generator, B: int, lo: int, hi: int) -> np.ndarray:
     return g.integers(lo, hi + 1, size=B, dtype=np.int64).astype(np.int32)
 

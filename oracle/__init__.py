@@ -100,6 +100,7 @@ class OraFA(C.Structure):
         ("q_nb", C.c_size_t * 4), ("k_nb", C.c_size_t * 4), ("v_nb", C.c_size_t * 4),
         ("mask_nb", C.c_size_t * 4), ("dst_nb", C.c_size_t * 4),
         ("kv_len", C.c_void_p),
+        ("kv_type", C.c_int32),
     ]
 
 
@@ -133,6 +134,7 @@ def _declare(L: C.CDLL) -> None:
     L.ora_mul_mat_f16.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp, i32]
     L.ora_mul_mat_f32.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
     L.ora_q4k_dequant_row.argtypes = [vp, i64, vp]
+    L.ora_kv_row.argtypes = [vp, i64, i32, vp]
     L.ora_mul_mat_q4k.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
     L.ora_q6k_dequant_row.argtypes = [vp, i64, vp]
     L.ora_mul_mat_q6k.argtypes = [vp, sz, i64, i64, vp, sz, i64, vp]
@@ -264,9 +266,10 @@ def _nb(a: np.ndarray) -> tuple:
 
 
 def _fa_struct(q, k_bits, v_bits, out, scale, mask=None, kv_len=None,
-               softcap=0.0, max_bias=0.0, mode=0) -> OraFA:
+               softcap=0.0, max_bias=0.0, mode=0, kv_type=1) -> OraFA:
     B, Hq, NQ, D = q.shape
-    _, Hkv, NKV, DV = v_bits.shape
+    Hkv, NKV = v_bits.shape[1], v_bits.shape[2]
+    DV = out.shape[-1]
     c = OraFA()
     c.head_dim_k, c.head_dim_v, c.n_queries, c.n_kv = D, DV, NQ, NKV
     c.n_head_q, c.n_head_kv, c.batch_size = Hq, Hkv, B
@@ -280,6 +283,7 @@ def _fa_struct(q, k_bits, v_bits, out, scale, mask=None, kv_len=None,
     if mask is not None:
         c.mask_nb[:] = _nb(mask)
     c.kv_len = _p(kv_len) if kv_len is not None else None
+    c.kv_type = kv_type
     return c
 
 
@@ -298,6 +302,54 @@ def flash_attn(q, k_bits, v_bits, scale, mask=None, kv_len=None, softcap=0.0,
     out = np.zeros((B, Hq, NQ, v_bits.shape[-1]), dtype=np.float32)
     c = _fa_struct(q, k_bits, v_bits, out, scale, mask, kv_len, softcap, max_bias, mode)
     lib().ora_flash_attn(C.byref(c))
+    return out
+
+
+KV_BLOCK = {8: (34, 32), 2: (18, 32)}   # ggml type id -> (bytes, values) per block
+
+
+def flash_attn_q(q, k_blocks, v_blocks, scale, kv_type, mask=None, kv_len=None, softcap=0.0,
+                 max_bias=0.0, mode=0) -> np.ndarray:
+    """Exact decode attention over a quantised KV cache (kv_type 8 = Q8_0, 2 = Q4_0):
+    k/v_blocks: (B, Hkv, NKV, D/32*block_bytes) uint8 rows of blocks; every element is
+    dequantised with GGUF's rule (ora_kv_elem) and the attention runs in fp64."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k_blocks = np.ascontiguousarray(k_blocks, dtype=np.uint8)
+    v_blocks = np.ascontiguousarray(v_blocks, dtype=np.uint8)
+    if mask is not None:
+        mask = np.ascontiguousarray(mask, dtype=np.float32)
+    if kv_len is not None:
+        kv_len = np.ascontiguousarray(kv_len, dtype=np.int32)
+    B, Hq, NQ, D = q.shape
+    out = np.zeros((B, Hq, NQ, D), dtype=np.float32)
+    c = _fa_struct(q, k_blocks, v_blocks, out, scale, mask, kv_len, softcap, max_bias, mode, kv_type)
+    c.head_dim_k = c.head_dim_v = D
+    lib().ora_flash_attn(C.byref(c))
+    return out
+
+
+def kv_dequant(rows: np.ndarray, D: int, kv_type: int) -> np.ndarray:
+    """Dequantise (..., D/32*block_bytes) uint8 K/V rows of kv_type to (..., D) f32."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    lead = rows.shape[:-1]
+    flat = rows.reshape(-1, rows.shape[-1])
+    out = np.empty((flat.shape[0], D), dtype=np.float32)
+    for i in range(flat.shape[0]):
+        lib().ora_kv_row(flat[i].ctypes.data, D, kv_type, out[i].ctypes.data)
+    return out.reshape(*lead, D)
+
+
+def base_flash_attn_q(q, k_blocks, v_blocks, scale, kv_type, kv_len=None, nth: int = 1) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k_blocks = np.ascontiguousarray(k_blocks, dtype=np.uint8)
+    v_blocks = np.ascontiguousarray(v_blocks, dtype=np.uint8)
+    if kv_len is not None:
+        kv_len = np.ascontiguousarray(kv_len, dtype=np.int32)
+    B, Hq, NQ, D = q.shape
+    out = np.zeros((B, Hq, NQ, D), dtype=np.float32)
+    c = _fa_struct(q, k_blocks, v_blocks, out, scale, None, kv_len, kv_type=kv_type)
+    c.head_dim_k = c.head_dim_v = D
+    lib().base_flash_attn(C.byref(c), nth)
     return out
 
 

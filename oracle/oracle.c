@@ -360,7 +360,59 @@ typedef struct {
     float* dst;                     /* f32 */
     size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
     const int32_t* kv_len;          /* per batch element, NULL = n_kv for all */
+    int32_t kv_type;                /* K/V element type: 1 F16, 8 Q8_0, 2 Q4_0 (ggml ids) */
 } ora_fa_t;
+
+/* Element d of a K or V row of type `type` as f32.
+ *   F16  : the half at d.
+ *   Q8_0 : 34-byte blocks of 32 values (f16 d, 32 int8 q); value d * q in f32 (the
+ *          dequant of flash_attn_q8_0_avx512.asm:40-70 and of the gguf decoder).
+ *   Q4_0 : 18-byte blocks of 32 values (f16 d, 16 bytes: value i < 16 in the low nibble of
+ *          byte i, value i >= 16 in the high nibble of byte i - 16); value d * (q - 8) in f32
+ *          (the gguf 0.19.0 decoder, gguf/quants.py Q4_0.dequantize_blocks). */
+static float ora_kv_elem(const char* row, int64_t d, int32_t type) {
+    if (type == 8) {
+        const char* b = row + (d / 32) * 34;
+        uint16_t h;
+        memcpy(&h, b, 2);
+        return ora_f16_to_f32(h) * (float)(int8_t)b[2 + d % 32];
+    }
+    if (type == 2) {
+        const char* b = row + (d / 32) * 18;
+        uint16_t h;
+        memcpy(&h, b, 2);
+        const int i = (int)(d % 32);
+        const uint8_t byte = (uint8_t)b[2 + (i % 16)];
+        const int q = (i < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
+        return ora_f16_to_f32(h) * (float)q;
+    }
+    uint16_t h;
+    memcpy(&h, row + 2 * d, 2);
+    return ora_f16_to_f32(h);
+}
+
+/* A whole K/V row of type `type` (dv values) as f32, block by block (the same products as
+ * ora_kv_elem, so the same bits). */
+void ora_kv_row(const char* row, int64_t dv, int32_t type, float* out) {
+    if (type == 8 || type == 2) {
+        const int64_t bb = type == 8 ? 34 : 18;
+        for (int64_t b = 0; b < dv / 32; b++) {
+            const unsigned char* blk = (const unsigned char*)row + b * bb;
+            const float d = ora_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            float* o = out + 32 * b;
+            if (type == 8) {
+                for (int i = 0; i < 32; i++) o[i] = d * (float)(int8_t)blk[2 + i];
+            } else {
+                for (int i = 0; i < 16; i++) {
+                    o[i] = d * (float)((int)(blk[2 + i] & 0x0F) - 8);
+                    o[16 + i] = d * (float)((int)(blk[2 + i] >> 4) - 8);
+                }
+            }
+        }
+        return;
+    }
+    for (int64_t d = 0; d < dv; d++) out[d] = ora_kv_elem(row, d, type);
+}
 
 static double ora_alibi_slope(int64_t h, int64_t n_heads, float max_bias) {
     /* flash_attention.cpp:278-285 fixes max_bias at 8 (base 2^(-8/n)); the
@@ -386,9 +438,9 @@ void ora_flash_attn(const ora_fa_t* c) {
                 float* dr = (float*)((char*)c->dst + iq * c->dst_nb[1] + ihq * c->dst_nb[2] + ib * c->dst_nb[3]);
                 double mx = -INFINITY;
                 for (int64_t j = 0; j < L; j++) {
-                    const uint16_t* kr = (const uint16_t*)((const char*)c->k + j * c->k_nb[1] + ihkv * c->k_nb[2] + ib * c->k_nb[3]);
+                    const char* kr = (const char*)c->k + j * c->k_nb[1] + ihkv * c->k_nb[2] + ib * c->k_nb[3];
                     double dot = 0.0;
-                    for (int64_t d = 0; d < DK; d++) dot += (double)qr[d] * (double)ora_f16_to_f32(kr[d]);
+                    for (int64_t d = 0; d < DK; d++) dot += (double)qr[d] * (double)ora_kv_elem(kr, d, c->kv_type);
                     double sj = dot * (double)c->scale;
                     if (c->mask) {
                         sj += (double)*(const float*)((const char*)c->mask + iq * c->mask_nb[1] + j * c->mask_nb[0]);
@@ -404,8 +456,8 @@ void ora_flash_attn(const ora_fa_t* c) {
                     for (int64_t j = 0; j < L; j++) {
                         const double p = exp(s[j] - mx);
                         l += p;
-                        const uint16_t* vr = (const uint16_t*)((const char*)c->v + j * c->v_nb[1] + ihkv * c->v_nb[2] + ib * c->v_nb[3]);
-                        for (int64_t d = 0; d < DV; d++) o[d] += p * (double)ora_f16_to_f32(vr[d]);
+                        const char* vr = (const char*)c->v + j * c->v_nb[1] + ihkv * c->v_nb[2] + ib * c->v_nb[3];
+                        for (int64_t d = 0; d < DV; d++) o[d] += p * (double)ora_kv_elem(vr, d, c->kv_type);
                     }
                 }
                 for (int64_t d = 0; d < DV; d++) dr[d] = l > 0.0 ? (float)(o[d] / l) : 0.0f;
@@ -829,6 +881,57 @@ static void base_fa_item_avx512(const ora_fa_t* c, int64_t ib, int64_t ihq, int6
 }
 #endif
 
+#if defined(__x86_64__)
+/* The same FA2 loop for quantised K/V (Q8_0, Q4_0): each key / value row is first
+ * dequantised to f32 (the DEQUANT_K_DOT_BLOCK / DEQUANT_V_ACCUM_BLOCK steps of
+ * flash_attn_q8_0_avx512.asm / flash_attn_q4_0_avx512.asm), then dotted / accumulated. */
+__attribute__((target("avx512f,avx512bw,fma")))
+static void base_fa_item_q_avx512(const ora_fa_t* c, int64_t ib, int64_t ihq, int64_t iq) {
+    enum { TILE = 64 };
+    const int64_t DK = c->head_dim_k, DV = c->head_dim_v;
+    const int64_t ihkv = ihq * c->n_head_kv / c->n_head_q;
+    const int64_t L = c->kv_len ? c->kv_len[ib] : c->n_kv;
+    const float* qr = (const float*)((const char*)c->q + iq * c->q_nb[1] + ihq * c->q_nb[2] + ib * c->q_nb[3]);
+    const char* kb = (const char*)c->k + ihkv * c->k_nb[2] + ib * c->k_nb[3];
+    const char* vb = (const char*)c->v + ihkv * c->v_nb[2] + ib * c->v_nb[3];
+    float* dr = (float*)((char*)c->dst + iq * c->dst_nb[1] + ihq * c->dst_nb[2] + ib * c->dst_nb[3]);
+    float O[256] __attribute__((aligned(64)));
+    float row[256] __attribute__((aligned(64)));
+    float sc[TILE];
+    for (int64_t d = 0; d < DV; d++) O[d] = 0.0f;
+    float mx = -INFINITY, sum = 0.0f;
+    for (int64_t t0 = 0; t0 < L; t0 += TILE) {
+        const int64_t t1 = t0 + TILE < L ? t0 + TILE : L;
+        float tmax = -INFINITY;
+        for (int64_t j = t0; j < t1; j++) {
+            ora_kv_row(kb + j * c->k_nb[1], DK, c->kv_type, row);
+            __m512 acc = _mm512_setzero_ps();
+            for (int64_t d = 0; d < DK; d += 16) acc = _mm512_fmadd_ps(_mm512_load_ps(row + d), _mm512_loadu_ps(qr + d), acc);
+            float s = _mm512_reduce_add_ps(acc) * c->scale;
+            if (c->mask) s += *(const float*)((const char*)c->mask + iq * c->mask_nb[1] + j * c->mask_nb[0]);
+            sc[j - t0] = s;
+            if (s > tmax) tmax = s;
+        }
+        const float nmx = mx > tmax ? mx : tmax;
+        const float corr = expf(mx - nmx);
+        sum *= corr;
+        mx = nmx;
+        const __m512 cv = _mm512_set1_ps(corr);
+        for (int64_t d = 0; d < DV; d += 16) _mm512_store_ps(O + d, _mm512_mul_ps(cv, _mm512_load_ps(O + d)));
+        for (int64_t j = t0; j < t1; j++) {
+            const float p = expf(sc[j - t0] - mx);
+            sum += p;
+            ora_kv_row(vb + j * c->v_nb[1], DV, c->kv_type, row);
+            const __m512 pv = _mm512_set1_ps(p);
+            for (int64_t d = 0; d < DV; d += 16)
+                _mm512_store_ps(O + d, _mm512_fmadd_ps(pv, _mm512_load_ps(row + d), _mm512_load_ps(O + d)));
+        }
+    }
+    const float inv = sum != 0.0f ? 1.0f / sum : 0.0f;
+    for (int64_t d = 0; d < DV; d++) dr[d] = sum != 0.0f ? O[d] * inv : 0.0f;
+}
+#endif
+
 static void base_fa_worker(void* p, int ith, int nth) {
     const ora_fa_t* c = ((base_fa_task_t*)p)->c;
     const int64_t nqh = c->n_queries * c->n_head_q;
@@ -840,7 +943,8 @@ static void base_fa_worker(void* p, int ith, int nth) {
         const int64_t ihq = rem / c->n_queries, iq = rem % c->n_queries;
 #if defined(__x86_64__)
         if (base_has_avx512() && c->head_dim_k % 16 == 0 && c->head_dim_v % 16 == 0 && c->head_dim_v <= 256) {
-            base_fa_item_avx512(c, ib, ihq, iq);
+            if (c->kv_type == 1) base_fa_item_avx512(c, ib, ihq, iq);
+            else base_fa_item_q_avx512(c, ib, ihq, iq);
             continue;
         }
 #endif

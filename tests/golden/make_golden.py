@@ -6,6 +6,8 @@ they were made).
                        Python decoder (gguf.quants.dequantize), the published GGUF
                        algorithm the reference's Q4_K kernels implement.
 * q6k_gguf.npz      -- Q6_K super-blocks and their dequantisation by the same gguf decoder.
+* kv_gguf.npz       -- Q8_0 and Q4_0 blocks (the quantised KV-cache formats) and their
+                       dequantisation by the same gguf decoder.
 * fa_reference.npz  -- flash-attention decode cases and the outputs of the reference's
                        own flash_attn_quantized (src/simd/flash_attention.cpp:291-410),
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
@@ -70,6 +72,24 @@ def q6k_fixture() -> None:
     blk = blk.reshape(M, nb * 210)
     deq = quants.dequantize(blk, GGMLQuantizationType.Q6_K).astype(np.float32)
     np.savez_compressed(os.path.join(HERE, "q6k_gguf.npz"), blocks=blk, dequant=deq, K=K)
+
+
+def kv_fixture() -> None:
+    from gguf import GGMLQuantizationType, quants
+    g = np.random.Generator(np.random.PCG64(21))
+    out = {}
+    for name, qt, bb in (("q8_0", GGMLQuantizationType.Q8_0, 34), ("q4_0", GGMLQuantizationType.Q4_0, 18)):
+        rows = g.integers(0, 256, size=(6, 4, bb), dtype=np.uint8)
+        d = (np.abs(g.standard_normal((6, 4))) * 0.02).astype(np.float16)
+        d[0, 0] = np.float16(0.0)
+        d[1, 1] = np.float16(6e-8)
+        d[2, 2] = np.float16(65504.0)
+        d[3, 3] = np.float16(-0.5)
+        rows[:, :, 0:2] = d.view(np.uint8).reshape(6, 4, 2)
+        rows = rows.reshape(6, 4 * bb)
+        out[name + "_rows"] = rows
+        out[name + "_dequant"] = quants.dequantize(rows, qt).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "kv_gguf.npz"), **out)
 
 
 def fa_fixture() -> None:
@@ -149,6 +169,7 @@ if __name__ == "__main__":
         sys.exit("oracle/_ref/libmlzref.so is missing: run `make -C oracle` where the reference tree exists")
     q4k_fixture()
     q6k_fixture()
+    kv_fixture()
     fa_fixture()
     matmul_fixture()
     matmul_f16_fixture()

@@ -76,6 +76,37 @@ def test_q6k_known_answer():
                                rtol=1e-12)
 
 
+@pytest.mark.parametrize("name,kv_type", [("q8_0", 8), ("q4_0", 2)])
+def test_kv_dequant_matches_gguf_decoder(golden, name, kv_type):
+    """The quantised KV-cache element rule of the oracle (Q8_0, Q4_0) equals the gguf
+    decoder bit for bit on blocks with edge scales."""
+    f = golden("kv_gguf.npz")
+    got = oracle.kv_dequant(f[name + "_rows"], 128, kv_type)
+    want = f[name + "_dequant"]
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all()
+
+
+def test_fa_quant_oracle_equals_f16_oracle_on_exact_values():
+    """Q8_0 blocks whose values are exact in f16 (d a power of two, small q): the quantised
+    attention oracle equals the F16 one on the same values."""
+    g = synth.rng(44)
+    B, Hq, Hkv, L, D = 2, 8, 2, 70, 64
+    q = synth.fa_inputs(g, B, Hq, Hkv, L, D)[0]
+    kq = synth.kv_quant_rows(g, (B, Hkv, L), D, 8)
+    vq = synth.kv_quant_rows(g, (B, Hkv, L), D, 8)
+    for rows in (kq, vq):
+        r = rows.reshape(B, Hkv, L, D // 32, 34)
+        r[..., 0:2] = np.array([2.0 ** -7], dtype=np.float16).view(np.uint8)
+        r[..., 2:] = (r[..., 2:].view(np.int8) // 16).view(np.uint8)
+    kf = oracle.kv_dequant(kq, D, 8).astype(np.float16)
+    vf = oracle.kv_dequant(vq, D, 8).astype(np.float16)
+    kl = np.array([70, 33], dtype=np.int32)
+    a = oracle.flash_attn_q(q, kq, vq, 0.125, 8, kv_len=kl)
+    b = oracle.flash_attn(q, kf.view(np.uint16), vf.view(np.uint16), 0.125, kv_len=kl)
+    assert np.array_equal(a, b)
+
+
 def test_q4k_known_answer():
     # every nibble 1, sc = 1, m = 0, d = 0.5, dmin arbitrary: row dot = d * sum(x)
     K = 512

@@ -34,5 +34,6 @@ def test_two_rank_sharded_mul_mat(tmp_path):
         for c in res["cases"]:
             tol = 1e-3 if c["kind"] == "f16" else 2e-3
             assert c["finite"], c
-            assert c["vs_single"] <= 1e-5, c
+            # the shard's K-split plan can differ from the whole matrix's: same terms, other order
+            assert c["vs_single"] <= 1e-4, c
             assert c["vs_oracle"] <= tol, c
