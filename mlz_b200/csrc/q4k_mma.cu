@@ -385,6 +385,7 @@ Q4kWs q4k_ws(int64_t K, int64_t N) {
 }  // namespace
 
 size_t q4k_workspace_bytes(int64_t K, int64_t N) {
+    if (q4k_i8_applicable(1, K, N)) return q4k_i8_workspace_bytes(K, N);
     // prepared activations: the batched kernel (N > 8) and the shared-X ring (3 <= N <= 8;
     // for N = 3..4 on small short-row shapes the register decode kernel runs and the
     // workspace goes unused -- the size cannot depend on M)
@@ -404,6 +405,8 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
+    if (q4k_i8_applicable(M, K, N))
+        return launch_q4k_i8(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s);
     if (q4k_ring_applicable(M, K, N))
         return launch_q4k_ring(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
     const bool xstream = q4k_ring_xs_applicable(M, K, N);

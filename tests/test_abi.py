@@ -54,12 +54,16 @@ def test_launch_overlap_mode():
 
 
 def test_q4k_workspace_follows_the_dispatch():
-    """Host arithmetic only: the Q4_K paths that read prepared activations (the shared-X
-    ring, 3 <= N <= 8; the batched kernel, N > 8) get a workspace; N <= 2 needs none."""
+    """Host arithmetic only: every Q4_K path reads prepared activations from the workspace.
+    N <= 4 (int8 path): per 8 blocks a record of 2 int8 vectors (2080 B each), 8 scales and
+    8 x 2 f16 sub-block sums per column (columns padded to 1, 2 or 4); independent of M."""
     ws = lambda M, K, N: mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q4_K, M, K, N)
-    for N in (1, 2):
-        assert ws(4096, 4096, N) == 0 and ws(4096, 14336, N) == 0
-    for N in (3, 4, 5, 8, 9, 16, 256):
+    for N, nct in ((1, 1), (2, 2), (3, 4), (4, 4)):
+        for K in (256, 4096, 14336):
+            rec = (K // 256 + 7) // 8 * (2 * nct * 2080 + nct * 32 + 8 * 2 * nct * 16)
+            assert ws(4096, K, N) >= rec
+            assert ws(1, K, N) == ws(14336, K, N)
+    for N in (5, 8, 9, 16, 256):
         for K in (256, 4096, 14336):
             # f16 fragments (512 B per column and block) + sums (32 B); columns padded to a
             # whole 8-column tile, or pairs of them above 8

@@ -66,9 +66,45 @@ def test_known_answer_block(dev):
     np.testing.assert_allclose(y[:, 0], want, rtol=1e-5, atol=1e-5)
 
 
+def _int8_model(x):
+    """The activations as the N <= 4 path carries them: per 256-value block one scale
+    s = max|x| / 127 and two int8 vectors, x ~= s (hi + lo / 254)."""
+    xb = x.astype(np.float32).reshape(x.shape[0], -1, 256)
+    amax = np.abs(xb).max(axis=2, keepdims=True)
+    s = (amax / np.float32(127.0)).astype(np.float32)
+    inv = np.where(amax > 0, np.float32(127.0) / np.where(amax > 0, amax, 1), 0).astype(np.float32)
+    hi = np.rint((xb * inv).astype(np.float32))
+    r = (xb.astype(np.float64) - s.astype(np.float64) * hi).astype(np.float32)
+    lo = np.clip(np.rint(((r * inv).astype(np.float32) * np.float32(254.0)).astype(np.float32)), -127, 127)
+    return s.astype(np.float64), hi.astype(np.float64), lo.astype(np.float64)
+
+
+@pytest.mark.parametrize("N", [1, 2, 4])
+def test_known_answer_block_int8_path(dev, N):
+    """Every weight 0.5 (as in the test above) with N <= 4 columns, where the activations
+    are carried as int8 hi + lo per block: the exact answer is 0.5 sum_b s_b (sum hi + sum lo / 254)."""
+    K = 512
+    blk = np.zeros((1, 2, 144), dtype=np.uint8)
+    blk[0, :, 0:2] = np.array([0.5], dtype=np.float16).view(np.uint8)
+    blk[0, :, 2:4] = np.array([0.25], dtype=np.float16).view(np.uint8)
+    blk[0, :, 4:8] = 1
+    blk[0, :, 12:16] = 0x01
+    blk[0, :, 16:] = 0x11
+    blk = blk.reshape(1, -1)
+    x = synth.f32_acts(synth.rng(9 + N), N, K)
+    y = _run(dev, blk, x)
+    s, hi, lo = _int8_model(x)
+    want = 0.5 * (s[:, :, 0] * (hi.sum(axis=2) + lo.sum(axis=2) / 254.0)).sum(axis=1)
+    np.testing.assert_allclose(y[:, 0], want, rtol=1e-5, atol=1e-6)
+    # and the quantisation error itself is far inside the parity tolerance
+    assert np.abs(y[:, 0] - 0.5 * x.sum(axis=1)).max() <= 1e-3 * np.abs(0.5 * x.sum(axis=1)).max() + 1e-4
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 256, 1), (3, 512, 2), (37, 768, 5), (300, 256, 17), (8, 1024, 33),
                                    (17, 2304, 3), (2053, 4352, 7), (64, 14336, 4), (40, 14336, 8), (16, 256, 8),
-                                   (8200, 512, 3), (8197, 4096, 8), (100, 11520, 3), (33, 11520, 6)])
+                                   (8200, 512, 3), (8197, 4096, 8), (100, 11520, 3), (33, 11520, 6),
+                                   (8197, 4096, 1), (8197, 4096, 2), (5000, 2048, 4), (20, 18432, 1),
+                                   (129, 6144, 2), (7, 256, 4)])
 def test_edge_shapes(dev, M, K, N):
     g = synth.rng(300 + M + K + N)
     blocks = synth.q4k_blocks(g, M, K)
