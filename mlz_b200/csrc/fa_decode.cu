@@ -118,19 +118,9 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
 }
 
 using ptx::mma16816;
+using ptx::movtrans;
+using ptx::split_h2;
 
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// f16 hi + lo split of two floats: x ~= hi + lo with |x - hi - lo| ~ 2^-22 |x|.
-__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const float2 hf = __half22float2(h);
-    hi = *reinterpret_cast<const uint32_t*>(&h);
-    lo = pack_h2(x0 - hf.x, x1 - hf.y);
-}
 
 // Address of the 16-byte chunk `chunk` (of 8 dims) of key row `key` in a tile operand
 // stored as kBoxes boxes of [64 keys][128 bytes] with the TMA 128-byte swizzle.
@@ -138,13 +128,6 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int chunk)
     return base + (uint32_t)((chunk >> 3) * (kTile * 128) + key * 128 + (((chunk & 7) ^ (key & 7)) << 4));
 }
 
-// Transposes an 8x8 f16 matrix held as the standard mma fragment (lane: row lane/4,
-// columns 2*(lane%4) and +1).
-__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
-    uint32_t y;
-    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-    return y;
-}
 
 __device__ __forceinline__ int seq_len(const FaParams& p, int b) {
     return p.kv_len ? min(max(ptx::ld_act(p.kv_len + p.b_base + b), 0), p.n_kv) : p.n_kv;

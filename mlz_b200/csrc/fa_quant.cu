@@ -8,21 +8,29 @@
 // 32) = f16 d * (nibble - 8), values 0-15 in the low nibbles, 16-31 in the high ones.  The
 // score order is the F16 kernel's: s = <q * scale, k> + mask, softcap, + ALiBi.
 //
-// Design (split-K flash decoding on the CUDA cores; the rows are 136 / 72 bytes for
+// Design (split-K flash decoding on the tensor cores; the rows are 136 / 72 bytes for
 // D = 128, not 16-byte multiples, so no TMA map describes them):
-//   - a CTA (128 threads) owns one segment -- one sequence, one KV head, up to 8 query rows
-//     sharing it (GQA packing, as the F16 kernel) -- and one contiguous range of its
-//     64-key tiles (grid.x = splits);
-//   - per tile the CTA copies the 64 raw K and V rows into shared memory with 4-byte loads
-//     (coalesced over each row), thread t scores key t % 64 for rows t / 64, +2, +4, +6
-//     (int8 / nibble -> f32 per element, block scale once per 32), each warp updates the
-//     online softmax of two rows, and thread t accumulates output dims t (+128) of every
-//     row from the dequantised V;
-//   - each CTA writes one partial record (m, l, O) per row; a combine kernel merges a
-//     segment's records in split order (results repeat bit for bit).
+//   - a CTA (four warps) owns one segment -- one sequence, one KV head, up to 8 query rows
+//     sharing it (GQA packing, as the F16 kernel) -- and one contiguous range of up to
+//     tiles_per_split 64-key tiles (grid.x = splits; CTAs past a sequence's end only write
+//     an empty record);
+//   - the raw K and V rows of each tile stream into a 3-stage shared-memory ring with
+//     cp.async (16-byte chunks when a head's rows are contiguous, else 8- or 4-byte
+//     pieces per row; rows past the sequence's end are zero-filled);
+//   - warp w owns keys 16 w .. 16 w + 15 of every tile, with its own online softmax.
+//     Scores S^T = K . Q^T and the update O^T += V^T . P^T run on mma.sync m16n8k16 (keys
+//     on M for S, dims on M for O, up to 8 query rows on N), Q and P split into f16 hi + lo
+//     as in the F16 kernel.  The quantised values enter as exact f16 (int8 or nibble - 8,
+//     one LOP3 + PRMT + HSUB2 per pair) and the f16 block scales d are applied in f32: per
+//     key and 32-dim block on the score partial sums, and per key and block on P before
+//     the V^T . P^T step -- the reference's own order (q . (d k) as (q . k) d per block);
+//   - at the end the four warps' (max, sum, O) states are merged through shared memory into
+//     one partial record per row and a combine kernel merges a segment's records in split
+//     order (results repeat bit for bit).
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "internal.h"
@@ -54,200 +62,380 @@ struct FaqParams {
     int b_base, nB;
     float scale, softcap, alibi_p2inv;
     int use_softcap;
+    int kcopy, vcopy;          // copy width of a tile's rows: 16 (contiguous rows), 8 or 4
 };
+
+using ptx::mma16816;
+using ptx::movtrans;
+using ptx::split_h2;
 
 template <int TYPE>
 struct KvFormat;
 template <>
-struct KvFormat<8> {   // Q8_0
+struct KvFormat<8> {   // Q8_0: f16 d, 32 int8
     static constexpr int kBlockBytes = 34;
-    __device__ __forceinline__ static float elem(const unsigned char* blk, int i) {
-        return (float)(int)(signed char)blk[2 + i];
-    }
 };
 template <>
-struct KvFormat<2> {   // Q4_0
+struct KvFormat<2> {   // Q4_0: f16 d, 16 bytes of nibbles (values 0-15 low, 16-31 high)
     static constexpr int kBlockBytes = 18;
-    __device__ __forceinline__ static float elem(const unsigned char* blk, int i) {
-        const unsigned b = blk[2 + (i & 15)];
-        return (float)((int)(i < 16 ? (b & 15u) : (b >> 4)) - 8);
-    }
 };
 
-__device__ __forceinline__ float blk_scale(const unsigned char* blk) {
-    return __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+constexpr int kQStages = 3;
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds_f16(uint32_t a) { return __half2float(__ushort_as_half((unsigned short)lds_u16(a))); }
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Two int8 values (bytes 0 and 1 of x) -> exact f16 pair: bias to unsigned, place under the
+// 1024 exponent (0x64 bytes), subtract 1024 + 128.
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t x) {
+    const uint32_t u = __byte_perm(x ^ 0x8080u, 0x6464u, 0x5140u);
+    return h2_bits(__hsub2(bits_h2(u), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480))));
+}
+// Two nibbles (low nibbles of bytes 0, 1 of x when HI = false, high nibbles when true) ->
+// exact f16 pair (nibble - 8).
+template <bool HI>
+__device__ __forceinline__ uint32_t nib2_to_h2(uint32_t x) {
+    const uint32_t u = __byte_perm(x, 0x6464u, 0x5140u);
+    if constexpr (!HI) {
+        return h2_bits(__hsub2(bits_h2(u & 0xFF0FFF0Fu), __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408))));
+    } else {
+        // 1024 + 16 q -> q - 8
+        const __half2 k = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));      // 1/16
+        const __half2 c = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));      // -72
+        return h2_bits(__hfma2(bits_h2(u & 0xFFF0FFF0u), k, c));
+    }
+}
+// Column pair (bytes 0 of a and b) and (bytes 1 of a and b) of two keys' u16 loads.
+__device__ __forceinline__ void pair_cols(uint32_t a, uint32_t b, uint32_t& c0, uint32_t& c1) {
+    const uint32_t z = __byte_perm(a, b, 0x5410u);   // a.b0 a.b1 b.b0 b.b1
+    c0 = __byte_perm(z, 0x6464u, 0x4240u);           // a.b0 64 b.b0 64
+    c1 = __byte_perm(z, 0x6464u, 0x4341u);           // a.b1 64 b.b1 64
 }
 
-// Copies `rows` rows of `rb` bytes (row j at src + j * stride, 4-byte aligned) into shared
-// memory at dst + j * rb; rows past `valid` are zero.
-__device__ __forceinline__ void copy_rows(unsigned char* dst, const char* src, int64_t stride, int rb, int valid) {
-    const int wpr = rb / 4;
-    for (int i = threadIdx.x; i < kQTile * wpr; i += kQThreads) {
-        const int j = i / wpr, w = i - j * wpr;
-        uint32_t v = 0;
-        if (j < valid) v = ptx::ld_act(reinterpret_cast<const int*>(src + (int64_t)j * stride) + w);
-        reinterpret_cast<uint32_t*>(dst + j * rb)[w] = v;
+__device__ __forceinline__ void cp_async(uint32_t dst, const void* src, int bytes, int src_bytes) {
+    if (bytes == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+    else if (bytes == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Issues the copies of `valid` rows (of RB bytes, row j at src + j * stride) into dst
+// (rows packed at RB); rows valid..63 are zero-filled.  mode 16: the 64 rows are one
+// contiguous 16-byte-aligned range; 8 / 4: per-row pieces of that width.
+template <int RB>
+__device__ __forceinline__ void copy_tile(uint32_t dst, const char* src, int64_t stride, int valid, int mode) {
+    if (mode == 16) {
+        constexpr int kChunks = kQTile * RB / 16;
+        const int vb = valid * RB;
+        for (int c = threadIdx.x; c < kChunks; c += kQThreads) {
+            const int off = 16 * c;
+            const int n = min(16, max(0, vb - off));
+            cp_async(dst + off, src + (n > 0 ? off : 0), 16, n);
+        }
+    } else {
+        const int w = mode;
+        const int per = RB / w;
+        for (int i = threadIdx.x; i < kQTile * per; i += kQThreads) {
+            const int j = i / per, c = i - j * per;
+            const bool ok = j < valid;
+            cp_async(dst + j * RB + c * w, src + (ok ? (int64_t)j * stride + c * w : 0), w, ok ? w : 0);
+        }
     }
 }
 
-template <int D, int TYPE>
+template <int D, int TYPE, bool GEN>
 __global__ void __launch_bounds__(kQThreads)
 fa_quant_kernel(const FaqParams p) {
     using F = KvFormat<TYPE>;
     constexpr int NB = D / 32;                  // blocks per row
     constexpr int RB = NB * F::kBlockBytes;     // bytes per row
-    constexpr int DU = D / kQThreads;           // output dims per thread (1 or 2)
-    static_assert(D % kQThreads == 0 || D == 64, "head dim");
+    constexpr int KS = D / 16;                  // 16-dim steps
+    constexpr uint32_t kTileBytes = kQTile * RB;
     extern __shared__ __align__(16) unsigned char fq_smem[];
-    float* q_s = reinterpret_cast<float*>(fq_smem);                   // [kQRows][D], * scale
-    float* p_s = q_s + kQRows * D;                                    // [kQRows][kQTile]
-    float* st_s = p_s + kQRows * kQTile;                              // [kQRows][3]: m, l, corr
-    unsigned char* k_s = reinterpret_cast<unsigned char*>(st_s + kQRows * 4);
-    unsigned char* v_s = k_s + kQTile * RB;
+    // [stage][K, V] raw tiles (the merge area [4 warps][8 rows][D + 2] once they are done),
+    // then the Q^T fragment table [KS][32 lanes] x uint4 (hi0, hi1, lo0, lo1)
+    constexpr uint32_t kRing = kQStages * 2 * kTileBytes;
+    constexpr uint32_t kMerge = 4 * kQRows * (D + 2) * 4;
+    const uint32_t ring = ptx::smem_u32(fq_smem);
+    uint4* qtab = reinterpret_cast<uint4*>(fq_smem + (kRing > kMerge ? kRing : kMerge));
+    float* mrg = reinterpret_cast<float*>(fq_smem);   // after the last tile (ring drained)
 
-    ptx::pdl_launch_dependents();
-    ptx::pdl_wait();
-    const int t = threadIdx.x;
-    const int split = blockIdx.x;
-    const int seg = blockIdx.y;
-    const int ib = p.b_base + blockIdx.z;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31, g = lane >> 2, q4 = lane & 3;
+    const int split = blockIdx.x, seg = blockIdx.y, ib = p.b_base + blockIdx.z;
     const int hidx = seg / p.n_rgroups, rg = seg % p.n_rgroups;
     const int head_base = p.packed ? hidx * p.G : hidx;
     const int ihkv = p.packed ? hidx : hidx * p.n_head_kv / p.n_head_q;
     const int r0 = rg * kQRows;
     const int nrows = min(kQRows, p.rows_total - r0);
-    const int L = p.kv_len ? min(p.kv_len[ib], p.n_kv) : p.n_kv;
 
-    // query rows of the segment, scaled
-    for (int i = t; i < kQRows * D; i += kQThreads) {
-        const int r = i / D, d = i - r * D;
-        float v = 0.0f;
-        if (r < nrows) {
-            const int rr = r0 + r, iq = rr / p.G, ihq = head_base + rr % p.G;
-            v = ptx::ld_act(reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3) + d) * p.scale;
-        }
-        q_s[i] = v;
-    }
-    if (t < kQRows) {
-        st_s[t * 4 + 0] = -INFINITY;
-        st_s[t * 4 + 1] = 0.0f;
-    }
-    float O[kQRows][DU > 0 ? DU : 1];
-#pragma unroll
-    for (int r = 0; r < kQRows; ++r)
-#pragma unroll
-        for (int u = 0; u < (DU > 0 ? DU : 1); ++u) O[r][u] = 0.0f;
-
-    const char* kbase = p.k + ihkv * p.k_nb2 + ib * p.k_nb3;
-    const char* vbase = p.v + ihkv * p.v_nb2 + ib * p.v_nb3;
+    ptx::pdl_launch_dependents();
+    ptx::pdl_wait();
+    const int L = p.kv_len ? min(max(ptx::ld_act(p.kv_len + ib), 0), p.n_kv) : p.n_kv;
     const int tile0 = split * p.tiles_per_split;
     const int tile1 = min(tile0 + p.tiles_per_split, (L + kQTile - 1) / kQTile);
-    const int warp = t >> 5, lane = t & 31;
-    for (int tile = tile0; tile < tile1; ++tile) {
+    float* rec = p.part + ((((size_t)blockIdx.z * p.HR + seg) * p.splits + split) * kQRows) * (D + 2);
+    if (tile0 >= tile1) {
+        // no key of this split: an empty record (the combine skips it)
+        if (t < kQRows) { rec[t * (D + 2)] = -INFINITY; rec[t * (D + 2) + 1] = 0.0f; }
+        return;
+    }
+    const char* kbase = p.k + ihkv * p.k_nb2 + ib * p.k_nb3;
+    const char* vbase = p.v + ihkv * p.v_nb2 + ib * p.v_nb3;
+    auto load_tile = [&](int tile, int stage) {
         const int j0 = tile * kQTile;
         const int valid = min(kQTile, L - j0);
-        __syncthreads();   // the previous tile's K/V/P are no longer read
-        copy_rows(k_s, kbase + (int64_t)j0 * p.k_nb1, p.k_nb1, RB, valid);
-        copy_rows(v_s, vbase + (int64_t)j0 * p.v_nb1, p.v_nb1, RB, valid);
-        __syncthreads();
-        // scores: key jj = t % 64, rows t / 64 + 2 i
-        {
-            const int jj = t & (kQTile - 1);
-            const int rbase = t / kQTile;               // 0 or 1
-            float acc[kQRows / 2];
+        const uint32_t dk = ring + (uint32_t)stage * 2 * kTileBytes;
+        copy_tile<RB>(dk, kbase + (int64_t)j0 * p.k_nb1, p.k_nb1, valid, p.kcopy);
+        copy_tile<RB>(dk + kTileBytes, vbase + (int64_t)j0 * p.v_nb1, p.v_nb1, valid, p.vcopy);
+    };
+    const int ntiles = tile1 - tile0;
 #pragma unroll
-            for (int i = 0; i < kQRows / 2; ++i) acc[i] = 0.0f;
-            const unsigned char* krow = k_s + jj * RB;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                const unsigned char* blk = krow + b * F::kBlockBytes;
-                float part[kQRows / 2];
-#pragma unroll
-                for (int i = 0; i < kQRows / 2; ++i) part[i] = 0.0f;
-#pragma unroll 8
-                for (int e = 0; e < 32; ++e) {
-                    const float kv = F::elem(blk, e);
-#pragma unroll
-                    for (int i = 0; i < kQRows / 2; ++i) part[i] = fmaf(q_s[(rbase + 2 * i) * D + b * 32 + e], kv, part[i]);
-                }
-                const float ds = blk_scale(blk);
-#pragma unroll
-                for (int i = 0; i < kQRows / 2; ++i) acc[i] = fmaf(ds, part[i], acc[i]);
-            }
-            const int j = j0 + jj;
-#pragma unroll
-            for (int i = 0; i < kQRows / 2; ++i) {
-                const int r = rbase + 2 * i;
-                float a = acc[i];
-                if (j < L && r < nrows) {
-                    const int rr = r0 + r, iq = rr / p.G, ihq = head_base + rr % p.G;
-                    if (p.mask)
-                        a += ptx::ld_act(reinterpret_cast<const float*>(p.mask + iq * p.m_nb1 + (int64_t)j * p.m_nb0 +
-                                                                        ihq * p.m_nb2 + ib * p.m_nb3));
-                    if (p.use_softcap) a = p.softcap * tanhf(a / p.softcap);
-                    if (p.alibi_p2inv != 0.0f) a += exp2f(p.alibi_p2inv * (float)(ihq + 1)) * (float)(j - iq);
-                } else {
-                    a = -INFINITY;
-                }
-                p_s[r * kQTile + jj] = a;
-            }
+    for (int i = 0; i < kQStages - 1; ++i) {
+        if (i < ntiles) load_tile(tile0 + i, i);
+        cp_commit();
+    }
+    // Q^T fragments (scaled, f16 hi + lo): entry (ks, lane) = row g, dims 16 ks + {2 q4, +1, +8, +9}
+    for (int e = t; e < KS * 32; e += kQThreads) {
+        const int ks = e >> 5, l = e & 31, gr = l >> 2, qq = l & 3;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (gr < nrows) {
+            const int rr = r0 + gr, iq = rr / p.G, ihq = head_base + rr % p.G;
+            const float* qr = reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3);
+            const int d0 = 16 * ks + 2 * qq;
+            x[0] = ptx::ld_act(qr + d0) * p.scale;
+            x[1] = ptx::ld_act(qr + d0 + 1) * p.scale;
+            x[2] = ptx::ld_act(qr + d0 + 8) * p.scale;
+            x[3] = ptx::ld_act(qr + d0 + 9) * p.scale;
         }
-        __syncthreads();
-        // online softmax: warp w updates rows w and w + 4
+        uint4 f;
+        split_h2(x[0], x[1], f.x, f.z);
+        split_h2(x[2], x[3], f.y, f.w);
+        qtab[e] = f;
+    }
+    // per-lane row state: rows 2 q4 and 2 q4 + 1
+    int iq_r[2], ihq_r[2];
+    bool row_ok[2];
+    float slope[2], m_row[2], l_row[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = 2 * q4 + h;
+        row_ok[h] = r < nrows;
+        const int rr = r0 + (row_ok[h] ? r : 0);
+        iq_r[h] = rr / p.G;
+        ihq_r[h] = head_base + rr % p.G;
+        slope[h] = p.alibi_p2inv != 0.0f ? exp2f(p.alibi_p2inv * (float)(ihq_r[h] + 1)) : 0.0f;
+        m_row[h] = -INFINITY;
+        l_row[h] = 0.0f;
+    }
+    float o[KS][4];
+#pragma unroll
+    for (int d = 0; d < KS; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+    const int kw = warp * 16;
+    const uint32_t qtab_u = ptx::smem_u32(qtab) + (uint32_t)lane * 16;
+
+    for (int i = 0; i < ntiles; ++i) {
+        cp_wait<kQStages - 2>();
+        __syncthreads();   // tile i has landed for every thread; stage (i - 1) % S is free
+        if (i + kQStages - 1 < ntiles) load_tile(tile0 + i + kQStages - 1, (i + kQStages - 1) % kQStages);
+        cp_commit();
+        const uint32_t kb = ring + (uint32_t)(i % kQStages) * 2 * kTileBytes;
+        const uint32_t vb = kb + kTileBytes;
+        const int j0 = (tile0 + i) * kQTile;
+        // ---- S^T (keys kw + g, kw + g + 8; rows 2 q4, +1): per block, two 16-dim steps
+        const uint32_t kr0 = kb + (uint32_t)(kw + g) * RB, kr1 = kr0 + 8 * RB;
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t o0 = kr0 + b * F::kBlockBytes + 2, o1 = kr1 + b * F::kBlockBytes + 2;
+            if constexpr (TYPE == 8) {
+#pragma unroll
+                for (int st = 0; st < 2; ++st) {
+                    const uint32_t a0 = i8x2_to_h2(lds_u16(o0 + 16 * st + 2 * q4));
+                    const uint32_t a1 = i8x2_to_h2(lds_u16(o1 + 16 * st + 2 * q4));
+                    const uint32_t a2 = i8x2_to_h2(lds_u16(o0 + 16 * st + 2 * q4 + 8));
+                    const uint32_t a3 = i8x2_to_h2(lds_u16(o1 + 16 * st + 2 * q4 + 8));
+                    const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b + st) * 512);
+                    mma16816(th, a0, a1, a2, a3, qf.x, qf.y);
+                    mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
+                }
+            } else {
+                const uint32_t w0 = lds_u16(o0 + 2 * q4), w1 = lds_u16(o1 + 2 * q4);
+                const uint32_t w2 = lds_u16(o0 + 2 * q4 + 8), w3 = lds_u16(o1 + 2 * q4 + 8);
+                {
+                    const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b) * 512);
+                    const uint32_t a0 = nib2_to_h2<false>(w0), a1 = nib2_to_h2<false>(w1);
+                    const uint32_t a2 = nib2_to_h2<false>(w2), a3 = nib2_to_h2<false>(w3);
+                    mma16816(th, a0, a1, a2, a3, qf.x, qf.y);
+                    mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
+                }
+                {
+                    const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b + 1) * 512);
+                    const uint32_t a0 = nib2_to_h2<true>(w0), a1 = nib2_to_h2<true>(w1);
+                    const uint32_t a2 = nib2_to_h2<true>(w2), a3 = nib2_to_h2<true>(w3);
+                    mma16816(th, a0, a1, a2, a3, qf.x, qf.y);
+                    mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
+                }
+            }
+            const float d0 = lds_f16(kr0 + b * F::kBlockBytes), d1 = lds_f16(kr1 + b * F::kBlockBytes);
+            sacc[0] = fmaf(d0, th[0] + tl[0], sacc[0]);
+            sacc[1] = fmaf(d0, th[1] + tl[1], sacc[1]);
+            sacc[2] = fmaf(d1, th[2] + tl[2], sacc[2]);
+            sacc[3] = fmaf(d1, th[3] + tl[3], sacc[3]);
+        }
+        // ---- mask / softcap / ALiBi / validity; element e: key g + 8 (e >> 1), row 2 q4 + (e & 1)
+        float sc[4], tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int h = e & 1;
+            const int j = j0 + kw + g + 8 * (e >> 1);
+            float a = sacc[e];
+            if (j < L && row_ok[h]) {
+                if constexpr (GEN) {
+                    if (p.mask)
+                        a += ptx::ld_act(reinterpret_cast<const float*>(p.mask + iq_r[h] * p.m_nb1 + (int64_t)j * p.m_nb0 +
+                                                                        ihq_r[h] * p.m_nb2 + ib * p.m_nb3));
+                    if (p.use_softcap) a = p.softcap * tanhf(a / p.softcap);
+                    if (p.alibi_p2inv != 0.0f) a += slope[h] * (float)(j - iq_r[h]);
+                }
+            } else {
+                a = -INFINITY;
+            }
+            sc[e] = a;
+            tmax[h] = fmaxf(tmax[h], a);
+        }
+        float corr[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int r = warp + 4 * h;
-            const float a0 = p_s[r * kQTile + lane], a1 = p_s[r * kQTile + lane + 32];
-            float mx = fmaxf(a0, a1);
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 4));
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 8));
+            tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 16));
+            const float mnew = fmaxf(m_row[h], tmax[h]);
+            corr[h] = (mnew == -INFINITY) ? 1.0f : __expf(m_row[h] - mnew);
+            m_row[h] = mnew;
+            l_row[h] *= corr[h];
+        }
+        if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float m_old = st_s[r * 4 + 0];
-            const float m_new = fmaxf(m_old, mx);
-            // a row with no visible key so far keeps m = -inf and p = 0
-            const float corr = m_new == -INFINITY ? 1.0f : __expf(m_old - m_new);
-            const float e0 = m_new == -INFINITY ? 0.0f : __expf(a0 - m_new);
-            const float e1 = m_new == -INFINITY ? 0.0f : __expf(a1 - m_new);
-            p_s[r * kQTile + lane] = e0;
-            p_s[r * kQTile + lane + 32] = e1;
-            float sum = e0 + e1;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) {
-                st_s[r * 4 + 0] = m_new;
-                st_s[r * 4 + 1] = st_s[r * 4 + 1] * corr + sum;
-                st_s[r * 4 + 2] = corr;
+            for (int d = 0; d < KS; ++d) {
+                o[d][0] *= corr[0]; o[d][1] *= corr[1];
+                o[d][2] *= corr[0]; o[d][3] *= corr[1];
             }
         }
-        __syncthreads();
-        // O[r][d] = O[r][d] * corr[r] + sum_j p[r][j] * v[j][d]
+        float pe[4];
 #pragma unroll
-        for (int u = 0; u < (DU > 0 ? DU : 1); ++u) {
-            const int d = t + u * kQThreads;
-            if (D == 64 && d >= 64) break;
-            const int b = d / 32, e = d % 32;
+        for (int e = 0; e < 4; ++e) {
+            const int h = e & 1;
+            pe[e] = (sc[e] == -INFINITY) ? 0.0f : __expf(sc[e] - m_row[h]);
+            l_row[h] += pe[e];
+        }
+        // ---- O^T += V^T . (P d_V)^T, per 32-dim block.  Within a 16-dim output tile, MMA
+        // row g is dim 2 g and row g + 8 dim 2 g + 1 (so a lane's pair of loads feeds both).
+        const uint32_t vk0 = vb + (uint32_t)(kw + 2 * q4) * RB;    // keys 2 q4, 2 q4 + 1
+        const uint32_t vk8 = vk0 + 8 * RB;                          // keys 2 q4 + 8, + 9
+        const uint32_t vd0 = vb + (uint32_t)(kw + g) * RB, vd8 = vd0 + 8 * RB;   // keys g, g + 8 (scales)
 #pragma unroll
-            for (int r = 0; r < kQRows; ++r) O[r][u] *= st_s[r * 4 + 2];
-            for (int jj = 0; jj < valid; ++jj) {
-                const unsigned char* blk = v_s + jj * RB + b * F::kBlockBytes;
-                const float vv = blk_scale(blk) * F::elem(blk, e);
+        for (int b = 0; b < NB; ++b) {
+            const float dv0 = lds_f16(vd0 + b * F::kBlockBytes), dv8 = lds_f16(vd8 + b * F::kBlockBytes);
+            uint32_t h0, l0, h1, l1;
+            split_h2(pe[0] * dv0, pe[1] * dv0, h0, l0);   // key g
+            split_h2(pe[2] * dv8, pe[3] * dv8, h1, l1);   // key g + 8
+            const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1), bl0 = movtrans(l0), bl1 = movtrans(l1);
+            const uint32_t base0 = vk0 + b * F::kBlockBytes + 2 + 2 * g, base8 = vk8 + b * F::kBlockBytes + 2 + 2 * g;
+            if constexpr (TYPE == 8) {
 #pragma unroll
-                for (int r = 0; r < kQRows; ++r) O[r][u] = fmaf(p_s[r * kQTile + jj], vv, O[r][u]);
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t c00, c01, c80, c81;
+                    pair_cols(lds_u16(base0 + 16 * hf) ^ 0x8080u, lds_u16(base0 + RB + 16 * hf) ^ 0x8080u, c00, c01);
+                    pair_cols(lds_u16(base8 + 16 * hf) ^ 0x8080u, lds_u16(base8 + RB + 16 * hf) ^ 0x8080u, c80, c81);
+                    const __half2 k = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+                    const uint32_t a0 = h2_bits(__hsub2(bits_h2(c00), k)), a1 = h2_bits(__hsub2(bits_h2(c01), k));
+                    const uint32_t a2 = h2_bits(__hsub2(bits_h2(c80), k)), a3 = h2_bits(__hsub2(bits_h2(c81), k));
+                    mma16816(o[2 * b + hf], a0, a1, a2, a3, bh0, bh1);
+                    mma16816(o[2 * b + hf], a0, a1, a2, a3, bl0, bl1);
+                }
+            } else {
+                uint32_t c00, c01, c80, c81;
+                pair_cols(lds_u16(base0), lds_u16(base0 + RB), c00, c01);
+                pair_cols(lds_u16(base8), lds_u16(base8 + RB), c80, c81);
+                const __half2 k8 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+                const __half2 k16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
+                const __half2 c72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));
+                // low nibbles: dims 0-15 of the block
+                {
+                    const uint32_t a0 = h2_bits(__hsub2(bits_h2(c00 & 0xFF0FFF0Fu), k8));
+                    const uint32_t a1 = h2_bits(__hsub2(bits_h2(c01 & 0xFF0FFF0Fu), k8));
+                    const uint32_t a2 = h2_bits(__hsub2(bits_h2(c80 & 0xFF0FFF0Fu), k8));
+                    const uint32_t a3 = h2_bits(__hsub2(bits_h2(c81 & 0xFF0FFF0Fu), k8));
+                    mma16816(o[2 * b], a0, a1, a2, a3, bh0, bh1);
+                    mma16816(o[2 * b], a0, a1, a2, a3, bl0, bl1);
+                }
+                // high nibbles: dims 16-31
+                {
+                    const uint32_t a0 = h2_bits(__hfma2(bits_h2(c00 & 0xFFF0FFF0u), k16, c72));
+                    const uint32_t a1 = h2_bits(__hfma2(bits_h2(c01 & 0xFFF0FFF0u), k16, c72));
+                    const uint32_t a2 = h2_bits(__hfma2(bits_h2(c80 & 0xFFF0FFF0u), k16, c72));
+                    const uint32_t a3 = h2_bits(__hfma2(bits_h2(c81 & 0xFFF0FFF0u), k16, c72));
+                    mma16816(o[2 * b + 1], a0, a1, a2, a3, bh0, bh1);
+                    mma16816(o[2 * b + 1], a0, a1, a2, a3, bl0, bl1);
+                }
             }
+        }
+    }
+    cp_wait<0>();
+    // ---- merge the four warps' states into one record per row
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 4);
+        l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 8);
+        l_row[h] += __shfl_xor_sync(0xffffffffu, l_row[h], 16);
+    }
+    __syncthreads();   // the ring and the Q table are no longer read
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        float* mr = mrg + (warp * kQRows + 2 * q4 + h) * (D + 2);
+        if (g == 0) { mr[0] = m_row[h]; mr[1] = l_row[h]; }
+        // tile d: MMA rows g, g + 8 = dims 16 d + 2 g, + 1
+#pragma unroll
+        for (int d = 0; d < KS; ++d) {
+            mr[2 + 16 * d + 2 * g] = o[d][h];
+            mr[2 + 16 * d + 2 * g + 1] = o[d][2 + h];
         }
     }
     __syncthreads();
-    // partial record per row: m, l, O[D]
-    float* rec = p.part + ((((size_t)blockIdx.z * p.HR + seg) * p.splits + split) * kQRows) * (D + 2);
+    for (int e = t; e < kQRows * (D + 2); e += kQThreads) {
+        const int r = e / (D + 2), c = e - r * (D + 2);
+        float M = -INFINITY;
 #pragma unroll
-    for (int u = 0; u < (DU > 0 ? DU : 1); ++u) {
-        const int d = t + u * kQThreads;
-        if (D == 64 && d >= 64) break;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, mrg[(w * kQRows + r) * (D + 2)]);
+        float v;
+        if (c == 0) {
+            v = M;
+        } else {
+            v = 0.0f;
 #pragma unroll
-        for (int r = 0; r < kQRows; ++r) rec[r * (D + 2) + 2 + d] = O[r][u];
-    }
-    if (t < kQRows) {
-        rec[t * (D + 2) + 0] = st_s[t * 4 + 0];
-        rec[t * (D + 2) + 1] = st_s[t * 4 + 1];
+            for (int w = 0; w < 4; ++w) {
+                const float m = mrg[(w * kQRows + r) * (D + 2)];
+                if (m != -INFINITY) v += __expf(m - M) * mrg[(w * kQRows + r) * (D + 2) + c];
+            }
+        }
+        rec[e] = v;
     }
 }
 
@@ -305,30 +493,38 @@ int faq_plan(const mlzc_fa_desc* d, int sm_count, FaqPlan* out) {
     p.HR = p.n_hidx * p.n_rgroups;
     pl.slice = (int)std::min<int64_t>(d->batch_size, 65535);
     const int tiles = std::max(1, (p.n_kv + kQTile - 1) / kQTile);
-    // about 4 CTAs per SM over the launch, at least 2 tiles per split where possible
+    // Splits of 4..64 tiles, sized for ~8 CTAs per SM over the launch if every sequence had
+    // n_kv keys: ragged batches then still fill several waves (CTAs past a sequence's end
+    // exit at once), and the partial records stay a few percent of the K/V bytes.
     const int64_t segs = (int64_t)pl.slice * p.HR;
-    int splits = (int)std::min<int64_t>(tiles, std::max<int64_t>(1, (4LL * sm_count + segs - 1) / segs));
-    p.tiles_per_split = (tiles + splits - 1) / splits;
+    const int64_t want = (int64_t)tiles * segs / std::max<int64_t>(1, 8LL * sm_count);
+    p.tiles_per_split = (int)std::min<int64_t>(std::max<int64_t>(4, want), 64);
+    p.tiles_per_split = std::min(p.tiles_per_split, tiles);
     p.splits = (tiles + p.tiles_per_split - 1) / p.tiles_per_split;
+    if (p.splits > 65535) return fail(MLZC_ERR_INVALID, "flash_attn: too many key tiles");
     const int RB = (int)fa_row_bytes(d->k_type, D);
-    pl.smem = (size_t)(kQRows * D + kQRows * kQTile + kQRows * 4) * 4 + 2 * (size_t)kQTile * RB;
+    // the merge area of the four warps reuses the ring
+    const size_t ring = (size_t)kQStages * 2 * kQTile * RB;
+    pl.smem = std::max(ring, (size_t)4 * kQRows * (D + 2) * 4) + (size_t)(D / 16) * 32 * 16;
     pl.ws_bytes = (size_t)pl.slice * p.HR * p.splits * kQRows * (D + 2) * 4;
     *out = pl;
     return MLZC_OK;
 }
 
-template <int D, int TYPE>
+template <int D, int TYPE, bool GEN>
 int faq_launch(const FaqPlan& pl, cudaStream_t s) {
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};
     int dev = 0;
     MLZC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev >= 0 && dev < 64 && !attr[dev]) {
-        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_quant_kernel<D, TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (dev < 0 || dev >= 64 || !attr[dev].load()) {
+        // the largest dynamic size any call of this instantiation asks for (the ring and
+        // table depend on D and the type only)
+        MLZC_CUDA_TRY(cudaFuncSetAttribute(fa_quant_kernel<D, TYPE, GEN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)pl.smem));
-        attr[dev] = true;
+        if (dev >= 0 && dev < 64) attr[dev].store(true);
     }
     const dim3 g((unsigned)pl.p.splits, (unsigned)pl.p.HR, (unsigned)pl.p.nB);
-    MLZC_CUDA_TRY(launch_pdl(fa_quant_kernel<D, TYPE>, g, dim3(kQThreads), pl.smem, s, pl.p));
+    MLZC_CUDA_TRY(launch_pdl(fa_quant_kernel<D, TYPE, GEN>, g, dim3(kQThreads), pl.smem, s, pl.p));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     const dim3 gc((unsigned)kQRows, (unsigned)pl.p.HR, (unsigned)pl.p.nB);
@@ -338,11 +534,20 @@ int faq_launch(const FaqPlan& pl, cudaStream_t s) {
     return MLZC_OK;
 }
 
-template <int TYPE>
+template <int TYPE, bool GEN>
 int faq_dispatch(const FaqPlan& pl, int D, cudaStream_t s) {
-    if (D == 64) return faq_launch<64, TYPE>(pl, s);
-    if (D == 128) return faq_launch<128, TYPE>(pl, s);
-    return faq_launch<256, TYPE>(pl, s);
+    if (D == 64) return faq_launch<64, TYPE, GEN>(pl, s);
+    if (D == 128) return faq_launch<128, TYPE, GEN>(pl, s);
+    return faq_launch<256, TYPE, GEN>(pl, s);
+}
+
+// Widest cp.async piece every row of a tile can be copied with: 16 when a head's rows are
+// contiguous and 16-byte aligned (a tile is then one range), else 8 or 4 per row.
+int copy_mode(const void* base, int64_t nb1, int64_t nb2, int64_t nb3, int rb) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(base);
+    if (nb1 == rb && a % 16 == 0 && nb2 % 16 == 0 && nb3 % 16 == 0) return 16;
+    if (rb % 8 == 0 && a % 8 == 0 && nb1 % 8 == 0 && nb2 % 8 == 0 && nb3 % 8 == 0) return 8;
+    return 4;
 }
 
 }  // namespace
@@ -385,10 +590,17 @@ int launch_flash_attn_quant(int sm_count, const mlzc_fa_desc* d, void* ws, size_
         p.alibi_p2inv = 0.0f;
     }
     const int D = (int)d->head_dim_k;
+    const int RB = (int)fa_row_bytes(d->k_type, D);
+    p.kcopy = copy_mode(d->k, d->k_nb[1], d->k_nb[2], d->k_nb[3], RB);
+    p.vcopy = copy_mode(d->v, d->v_nb[1], d->v_nb[2], d->v_nb[3], RB);
+    const bool gen = p.mask != nullptr || p.use_softcap || p.alibi_p2inv != 0.0f;
     for (int64_t b0 = 0; b0 < d->batch_size; b0 += pl.slice) {
         p.b_base = (int)b0;
         p.nB = (int)std::min<int64_t>(pl.slice, d->batch_size - b0);
-        st = d->k_type == MLZC_TYPE_Q8_0 ? faq_dispatch<8>(pl, D, s) : faq_dispatch<2>(pl, D, s);
+        if (d->k_type == MLZC_TYPE_Q8_0)
+            st = gen ? faq_dispatch<8, true>(pl, D, s) : faq_dispatch<8, false>(pl, D, s);
+        else
+            st = gen ? faq_dispatch<2, true>(pl, D, s) : faq_dispatch<2, false>(pl, D, s);
         if (st != MLZC_OK) return st;
     }
     return MLZC_OK;

@@ -2,6 +2,8 @@
 // bulk (TMA engine) copies into shared memory.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include <cstdint>
 
 #include "internal.h"
@@ -96,6 +98,27 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
         "{%0, %1, %2, %3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// f16 hi + lo split of two floats: x ~= hi + lo with |x - hi - lo| ~ 2^-22 |x|.
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_h2(x0 - hf.x, x1 - hf.y);
+}
+
+// Transposes an 8x8 f16 matrix held as the standard mma fragment (lane: row lane/4,
+// columns 2*(lane%4) and +1).
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 
 // Programmatic dependent launch: a kernel launched with the programmatic-serialization
