@@ -277,7 +277,7 @@ class C3(Workload):
         n = self.N
         # the library's dispatch (q4k_i8_applicable, q4k_ring_xs_applicable, launch_q4k_mma)
         if n <= 4:
-            kern = "q4k_i8_prep_kernel + q4k_i8_kernel"
+            kern = "act_i8::prep_kernel<8> + q4k_i8_kernel"
         elif n <= 8 and (n >= 5 or m >= 8192 or k > 4096):
             kern = "q4k_prep_kernel + q4k_ring_xs_kernel"
         elif n <= 8:
@@ -334,6 +334,8 @@ class C6(C3):
 
     def roofline_kernel(self, j):
         m, k = self.SHAPES[j]
+        if self.N <= 4 and k % 1024 == 0:
+            return f"act_i8::prep_kernel<16> + q6k_i8_kernel, {m}x{k} (one call)"
         return f"q6k_mma_kernel<{2 if self.N > 8 else 1}>, {m}x{k} (one call)"
 
     def __init__(self, n, dev, gen):

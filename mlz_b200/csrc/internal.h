@@ -83,6 +83,12 @@ size_t q4k_i8_workspace_bytes(int64_t K, int64_t N);
 int launch_q4k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                   cudaStream_t s);
+// Q6_K, 1 <= N <= 4, K a multiple of 1024: the same int8 path (q6k_i8.cu).
+bool q6k_i8_applicable(int64_t M, int64_t K, int64_t N);
+size_t q6k_i8_workspace_bytes(int64_t K, int64_t N);
+int launch_q6k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                  size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                  cudaStream_t s);
 bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
                     const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,

@@ -26,7 +26,7 @@
 // units of all row tiles are numbered tile-major and every CTA takes an equal contiguous
 // range of them (stream-K), so no SM idles while another finishes a tile.  A producer warp
 // fills a shared-memory ring with each unit's weight box plus, by one bulk copy, the unit's
-// prepared activation record (q4k_i8_prep_kernel writes one record per 8 blocks).  Eight
+// prepared activation record (act_i8::prep_kernel writes one record per 8 blocks).  Eight
 // consumer warps each take one block of a unit.  At the end of a tile (or of the CTA's
 // range) the warps' partial rows are summed in warp order through shared memory and added
 // into Y (zeroed by the prep kernel) with red.global.add.  The grid is capped so that every
@@ -53,6 +53,7 @@
 #include "internal.h"
 #include "ptx.cuh"
 #include "q4k.cuh"
+#include "act_i8.cuh"
 
 namespace mlzc {
 namespace {
@@ -64,15 +65,11 @@ constexpr int kThreads = (kWarps + 1) * 32;                // + the producer war
 constexpr int kTileRows = 16;
 constexpr uint32_t kBoxBytes = kTileRows * kWarps * kBlk;  // 18432: one unit's weights
 constexpr int kU64PerBlock = kBlk / 8;                     // 18
-constexpr int kVarStride = 2080;                           // bytes per int8 vector in a record (2048 + 32)
-
-// Prepared activation record of one unit (8 blocks) for NCT columns (NV = 2 NCT vectors):
-//   [NV][2080] int8: vector 2n = hi, 2n + 1 = lo of column n, block w at 256 w
-//   [NCT][8] f32: the scale s of each (column, block)
-//   [8 blocks][NV][8] f16: sub-block sums S_j, the hi part in vector 2n, lo part in 2n + 1
-__host__ __device__ constexpr uint32_t rec_bytes(int nct) { return (uint32_t)(2 * nct * kVarStride + nct * 32 + 8 * 2 * nct * 16); }
-__host__ __device__ constexpr uint32_t rec_scale_off(int nct) { return (uint32_t)(2 * nct * kVarStride); }
-__host__ __device__ constexpr uint32_t rec_sum_off(int nct) { return rec_scale_off(nct) + (uint32_t)(nct * 32); }
+// activation records: act_i8.cuh with 8 sums (32-value sub-blocks) per block
+using act_i8::kVarStride;
+__host__ __device__ constexpr uint32_t rec_bytes(int nct) { return act_i8::rec_bytes(nct, 8); }
+__host__ __device__ constexpr uint32_t rec_scale_off(int nct) { return act_i8::rec_scale_off(nct); }
+__host__ __device__ constexpr uint32_t rec_sum_off(int nct) { return act_i8::rec_sum_off(nct); }
 
 __host__ __device__ constexpr int stages_for(int nct) { return nct <= 2 ? 4 : 2; }
 
@@ -141,68 +138,6 @@ __device__ __forceinline__ uint32_t box_off(int r, int o) {
 
 // CTA c's units [first_unit(c), first_unit(c + 1)).
 __device__ __forceinline__ long long first_unit(long long c, long long U, long long G) { return c * U / G; }
-
-// ------------------------------------------------------------------ activation prep
-// One warp per (block kb < nst * 8, column n < NCT): quantises the block's 256 values to
-// (s, hi, lo), sums its eight sub-blocks, and writes them into unit kb / 8's record (zeros
-// for blocks past the row and columns past N).  Also zeroes Y (M rows of N columns), which
-// the main kernel adds its pieces into.
-__global__ void __launch_bounds__(256) q4k_i8_prep_kernel(const char* __restrict__ x, size_t x_cs, int N, int nct,
-                                                          int nblk, int nst, uint32_t rbytes, char* __restrict__ rec,
-                                                          char* __restrict__ y, size_t y_cs, int M) {
-    ptx::pdl_launch_dependents();
-    ptx::pdl_wait();   // x comes from, and the records and Y may still be read by, the previous kernel
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)M * N;
-         i += (long long)gridDim.x * blockDim.x)
-        reinterpret_cast<float*>(y + (size_t)(i / M) * y_cs)[i % M] = 0.0f;
-    const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-    if (item >= nst * 8 * nct) return;
-    const int kb = item / nct, n = item % nct;
-    float v[8];
-    if (kb < nblk && n < N) {
-        const float4* p = reinterpret_cast<const float4*>(x + (size_t)n * x_cs) + (size_t)kb * (kQK / 4) + 2 * lane;
-        const float4 a = ptx::ld_act(p), b = ptx::ld_act(p + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-    }
-    float amax = 0.0f, sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        amax = fmaxf(amax, fabsf(v[i]));
-        sum += v[i];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);   // lanes 4j..4j+3: S_j
-    const float s = amax / 127.0f;
-    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
-    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int h = __float2int_rn(v[i] * inv);
-        const float r = fmaf(-s, (float)h, v[i]);
-        const int l = max(-127, min(127, __float2int_rn(r * inv * 254.0f)));
-        hw[i >> 2] |= ((uint32_t)h & 0xFFu) << (8 * (i & 3));
-        lw[i >> 2] |= ((uint32_t)l & 0xFFu) << (8 * (i & 3));
-    }
-    char* r = rec + (size_t)(kb >> 3) * rbytes;
-    const int w = kb & 7;
-    *reinterpret_cast<uint2*>(r + (2 * n) * kVarStride + w * kQK + 8 * lane) = make_uint2(hw[0], hw[1]);
-    *reinterpret_cast<uint2*>(r + (2 * n + 1) * kVarStride + w * kQK + 8 * lane) = make_uint2(lw[0], lw[1]);
-    if (lane == 0) reinterpret_cast<float*>(r + 2 * nct * kVarStride)[n * 8 + w] = s;
-    if ((lane & 3) == 0) {
-        const __half sh = __float2half_rn(sum);
-        const __half sl = __float2half_rn(sum - __half2float(sh));
-        __half* sp = reinterpret_cast<__half*>(r + 2 * nct * kVarStride + nct * 32);
-        sp[(w * 2 * nct + 2 * n) * 8 + (lane >> 2)] = sh;
-        sp[(w * 2 * nct + 2 * n + 1) * 8 + (lane >> 2)] = sl;
-    }
-}
 
 // ------------------------------------------------------------------ main kernel
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
@@ -364,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4k_i8_kernel(const __grid_consta
                 acc_o[2] += d[2] * sob;
                 acc_o[3] += d[3] * sob;
             }
-            // min term: sum_j m_j S_j (rows y0, y1; S as f16 hi + lo in columns 2t, 2t + 1)
+            // min term: sum_j m_j S_j (rows y0, y1; S as f16 hi + lo / 2048 in columns 2t, 2t + 1)
             const uint32_t m03a = h0.z & 0x3F3F3F3Fu, m03b = h1.z & 0x3F3F3F3Fu;
             const uint32_t m47a = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
             const uint32_t m47b = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
@@ -376,8 +311,8 @@ __global__ void __launch_bounds__(kThreads, 2) q4k_i8_kernel(const __grid_consta
             const float f = sb * (1.0f / 16.0f);
             const float hi0 = (float)(acc_e[0] * 16 + acc_o[0]), lo0 = (float)(acc_e[1] * 16 + acc_o[1]);
             const float hi1 = (float)(acc_e[2] * 16 + acc_o[2]), lo1 = (float)(acc_e[3] * 16 + acc_o[3]);
-            ya0 += dd0.x * f * fmaf(lo0, 1.0f / 254.0f, hi0) - dd0.y * (mn[0] + mn[1]);
-            ya1 += dd1.x * f * fmaf(lo1, 1.0f / 254.0f, hi1) - dd1.y * (mn[2] + mn[3]);
+            ya0 += dd0.x * f * fmaf(lo0, 1.0f / 254.0f, hi0) - dd0.y * fmaf(mn[1], 1.0f / 2048.0f, mn[0]);
+            ya1 += dd1.x * f * fmaf(lo1, 1.0f / 254.0f, hi1) - dd1.y * fmaf(mn[3], 1.0f / 2048.0f, mn[2]);
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
@@ -522,7 +457,7 @@ int launch_q4k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t
         // one warp per record item; at least enough threads to zero Y in a few passes
         const long long zero_ctas = std::min<long long>(148, ((long long)M * N + 2047) / 2048);
         const unsigned pg = (unsigned)std::max<long long>((items + 7) / 8, zero_ctas);
-        MLZC_CUDA_TRY(launch_pdl(q4k_i8_prep_kernel, dim3(pg), dim3(256), 0, s,
+        MLZC_CUDA_TRY(launch_pdl(act_i8::prep_kernel<8>, dim3(pg), dim3(256), 0, s,
                                  reinterpret_cast<const char*>(x), x_col_bytes, (int)N, nct, p.nblk, p.nst, q.rbytes,
                                  wsc, p.y, p.y_cs, p.M));
         count_launch();

@@ -196,6 +196,10 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
     if (w_type == MLZC_TYPE_Q6_K) {
         if ((uintptr_t)x % 16 || x_cs % 16)
             return fail(MLZC_ERR_INVALID, "mul_mat (Q6_K): activation columns must be 16-byte aligned");
+        // decode shapes with 16-byte rows: the int8 path; the rest (and rows only 2-byte
+        // aligned) the f16 tensor-core kernel
+        if (q6k_i8_applicable(M, K, N) && (uintptr_t)w % 16 == 0 && w_rs % 16 == 0)
+            return launch_q6k_i8(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
         return launch_q6k(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, s);
     }
     if (w_type == MLZC_TYPE_F16 && gemv_f16_mma_applicable(M, K, N, w, w_rs, x, x_cs))
@@ -207,6 +211,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
 
 size_t mul_mat_ws(int w_type, int64_t M, int64_t K, int64_t N) {
     if (w_type == MLZC_TYPE_Q4_K) return K % 256 == 0 ? q4k_workspace_bytes(K, N) : 0;
+    if (w_type == MLZC_TYPE_Q6_K) return q6k_i8_applicable(M, K, N) ? q6k_i8_workspace_bytes(K, N) : 0;
     // N in [8, 16] normally takes the skinny tensor-core path (no workspace), but the
     // tcgen05 GEMM it falls back to for unaligned operands needs one
     if (w_type == MLZC_TYPE_F16 && N >= kGemmMinN) return gemm_f16_workspace_bytes(M, K, N);

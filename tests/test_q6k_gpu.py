@@ -61,10 +61,13 @@ def test_llama31_8b_shapes(dev, MK, B):
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 256, 1), (3, 512, 2), (37, 768, 5), (300, 256, 17), (8, 1024, 33),
-                                   (17, 2304, 3), (2053, 4352, 7), (64, 14336, 4), (33, 11520, 9), (16, 256, 8)])
+                                   (17, 2304, 3), (2053, 4352, 7), (64, 14336, 4), (33, 11520, 9), (16, 256, 8),
+                                   (8197, 4096, 1), (100, 1024, 2), (37, 3072, 3), (16, 8192, 4), (5, 2048, 1),
+                                   (1000, 5120, 2)])
 def test_edge_shapes(dev, M, K, N):
     """Odd block counts (odd row strides: rows alternate between 4- and 2-byte alignment),
-    ragged row tiles, 1 .. 33 columns."""
+    ragged row tiles, 1 .. 33 columns; K a multiple of 1024 with N <= 4 takes the int8 path
+    (partial last unit at K = 1024, 3072, 5120)."""
     g = synth.rng(9300 + M + K + N)
     blocks = synth.q6k_blocks(g, M, K)
     x = synth.f32_acts(g, N, K)
@@ -84,7 +87,9 @@ def test_repeat_and_linearity_full_size(dev):
     y2 = mlz_b200.mul_mat(w, x, w_type=Q6)
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
-    assert torch.equal(y4, 4.0 * y)                    # powers of two commute with every rounding
+    # powers of two commute with every rounding except where an f16 part of an activation
+    # group sum is subnormal (the int8 path for N <= 4): 1e-6 of max |y|
+    assert ((y4 - 4.0 * y).abs().max() / (4.0 * y).abs().max()).item() <= 1e-6
     assert torch.equal(y2, y)
 
 
