@@ -49,6 +49,11 @@ NCU_TRAFFIC = {
     ("c1", 4): (50.39e6 + 0.07e6, "ncu capture: gemv_f16_mma_kernel, 8192x3072, N=4"),
     ("c1", 8): (50.44e6 + 0.01e6, "ncu capture: gemv_f16_mma_kernel<1, 1, 4>, 8192x3072, N=8"),
     ("c4", 16): (250.80e6 + 5.98e6, "ncu capture: fa_decode_kernel of the c4 call (16 sequences)"),
+    ("c3", 1): (33.14e6, "ncu capture: q4k_i8_kernel, 14336x4096 launch, batch 1 (the 4096x14336 launch reads the "
+                         "same block bytes)"),
+    ("c6", 1): (48.29e6 + 0.01e6, "ncu capture: q6k_i8_kernel, 14336x4096 launch, batch 1 (the 4096x14336 launch "
+                                  "reads the same block bytes)"),
+    ("c7", 16): (132.51e6 + 4.60e6, "ncu capture: fa_quant_kernel of the c7 call (16 sequences)"),
     ("c3", 8): (33.29e6, "ncu capture: q4k_ring_xs_kernel, 4096x14336 launch, batch 8 (the 14336x4096 launch "
                          "reads the same block bytes)"),
     ("c3", 16): (33.31e6, "ncu capture: q4k_mma_kernel, 14336x4096 launch, batch 16"),
@@ -874,9 +879,13 @@ def extra_rows(a, n_head, dev, rank, world, comm, peaks):
             K = max(5, min(a.steps, 20))
             units = w.work_units()
             job = units if isinstance(w, C5) else units * world
+            rl = roofline_of(w, t, peaks, None, ms)
+            tr = NCU_TRAFFIC.get((cfg, n))
+            if tr is not None and not isinstance(w, C2):
+                rl["traffic"], rl["traffic_source"] = tr
             row = {"workload": w.config["workload"], "metric": w.metric, "unit": w.unit,
                    "value": job * K / (ms * 1e-3) * w.unit_scale(), "ms_per_step": ms / K,
-                   "roofline": roofline_of(w, t, peaks, None, ms), "gpu_launches": t["n_launch"]}
+                   "roofline": rl, "gpu_launches": t["n_launch"]}
             if rank == 0 and world == 1 and not a.no_cpu_baseline:
                 v, desc, nth = cpu_sample(cfg, n, 1.0)
                 row["cpu_baseline"] = {"value": v, "unit": w.unit, "cores": nth, "kind": "port", "sample": desc}

@@ -330,6 +330,28 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
             if (st == MLZC_OK) return launch_peer_wait(pv, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
             if (st != MLZC_ERR_UNSUPPORTED) return st;
         }
+        // prefill (the tcgen05 GEMM): its epilogue stores every finished tile into its rows of Y
+        // and into this rank's slice of each other rank's slot, so the exchange overlaps the
+        // remaining tiles; the wait kernel then copies only the other ranks' slices
+        float* y_own = reinterpret_cast<float*>(reinterpret_cast<char*>(y) + (size_t)c->rank * m_loc * 4);
+        if (c->nranks - 1 <= 7 &&
+            mul_mat_uses_gemm(w_type, m_loc, K, N, w_shard, w_row_bytes, x, x_col_bytes, y_own, y_col_bytes)) {
+            GemmPeers gp{};
+            gp.npeer = c->nranks - 1;
+            gp.pcs = (size_t)m_loc * 4;
+            gp.epoch = &reinterpret_cast<const PeerHeader*>(c->base[c->rank])->epoch;
+            for (int par = 0; par < 2; ++par)
+                for (int r = 0, i = 0; r < c->nranks; ++r) {
+                    if (r == c->rank) continue;
+                    gp.slot[par][i++] = reinterpret_cast<float*>(c->base[r] + kPeerHeaderBytes + (size_t)par * c->slot_bytes +
+                                                                 (size_t)c->rank * slice_bytes);
+                }
+            st = launch_gemm_f16_peers(ctx, w_shard, w_row_bytes, m_loc, K, x, x_col_bytes, N, y_own, y_col_bytes, ws, mm,
+                                       gp, s);
+            if (st == MLZC_OK)
+                return launch_peer_wait(pv, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s, true);
+            if (st != MLZC_ERR_UNSUPPORTED) return st;
+        }
     }
     // This rank's slice, dense [N][m_loc].
     st = mul_mat_run(ctx, w_type, w_shard, w_row_bytes, m_loc, K, x, x_col_bytes, N, slice, (size_t)m_loc * 4,

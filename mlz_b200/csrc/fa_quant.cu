@@ -80,7 +80,7 @@ struct KvFormat<2> {   // Q4_0: f16 d, 16 bytes of nibbles (values 0-15 low, 16-
     static constexpr int kBlockBytes = 18;
 };
 
-constexpr int kQStages = 3;
+constexpr int kQStages = 2;
 
 __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
     uint16_t v;

@@ -73,15 +73,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Tiled TMA store of a box from shared memory (one bulk group per call); elements outside
-// the tensor are not written.
+// Tiled TMA store of a box from shared memory into the current bulk group (committed by
+// bulk_commit); elements outside the tensor are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
                  "r"(src), "r"(x), "r"(y)
                  : "memory");
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until at most N of this thread's bulk groups still read their shared memory.
 template <int N>
@@ -178,6 +178,8 @@ struct TileCfg {
     static_assert(kSmemBytes <= (size_t)kSmemMax, "shared memory");
 };
 
+constexpr int kGemmMaxPeers = 7;   // other ranks of an 8-GPU row-sharded call
+
 struct GemmArgs {
     float* y;
     size_t y_cs;          // bytes between output columns (tokens)
@@ -191,11 +193,24 @@ struct GemmArgs {
     int* tile_count;      // per tile: splits finished (zeroed by the narrowing kernel)
     unsigned int* err;
     int tma_store;        // 1: Y is written through tmY (16-byte aligned Y and column stride)
+    // Row-sharded mul_mat: every finished tile also goes to this rank's slice in the slot of
+    // the call's epoch parity of each other rank (peer memory over NVLink), so the exchange
+    // overlaps the remaining tiles.  npeer = 0: a plain GEMM.
+    int npeer;
+    float* pslot[2][kGemmMaxPeers];   // [parity][peer]: the slice, [N][M] with column stride pcs
+    size_t pcs;
+    const uint32_t* epoch;            // this rank's last completed epoch (the call's is + 1)
+};
+
+// The peers' slices as TMA store targets ([parity][peer], same box as tmY).
+struct PeerMaps {
+    CUtensorMap m[2][kGemmMaxPeers];
 };
 
 template <int BN, int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmY, GemmArgs g) {
+gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmY,
+                   const __grid_constant__ PeerMaps pm, GemmArgs g) {
     using C = TileCfg<BN, MT>;
     constexpr int STAGES = C::kStages;
     constexpr int NBUF = C::kBufs;
@@ -348,6 +363,9 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         float* stg = stg_all + (size_t)(warp - 2) * NSTG * (kStgBytes / 4);
         // TMA stores: full 32 x 32 blocks, whole tiles (no split partials)
         const bool tma_out = (kCols == 32) && g.tma_store && g.splits == 1;
+        // the call's epoch parity (the previous call's wait kernel advanced the epoch before
+        // this kernel's pdl_wait returned)
+        const int par = g.npeer ? (int)((*reinterpret_cast<const volatile uint32_t*>(g.epoch) + 1) & 1) : 0;
         uint32_t nst = 0;                        // staging blocks this warp has stored
         uint32_t t = 0;
         for (int w = blockIdx.x; w < g.num_work; w += gridDim.x, ++t) {
@@ -394,7 +412,12 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                             for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = __uint_as_float(r[gg][j]);
                             fence_proxy_async_smem();
                             __syncwarp();
-                            if (lane == 0) tma_store_2d(&tmY, smem_u32(buf), m0 + i * BM + quarter * 32, n0 + c);
+                            if (lane == 0) {
+                                const int bx = m0 + i * BM + quarter * 32, by = n0 + c;
+                                tma_store_2d(&tmY, smem_u32(buf), bx, by);
+                                for (int r = 0; r < g.npeer; ++r) tma_store_2d(&pm.m[par][r], smem_u32(buf), bx, by);
+                                bulk_commit();
+                            }
                             ++nst;
                         } else if (g.splits == 1) {
                             if (m < g.M) {
@@ -467,6 +490,12 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                 } else {
                                     const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
                                     for (int q = 0; q < 4 && mrow + q < g.M; ++q) dst[q] = a4[q];
+                                }
+                                for (int r = 0; r < g.npeer; ++r) {
+                                    // the slices are dense, 16-byte aligned [N][M] (M % 4 == 0)
+                                    float* pd = reinterpret_cast<float*>(reinterpret_cast<char*>(g.pslot[par][r]) +
+                                                                         (size_t)(n0 + cc) * g.pcs) + mrow;
+                                    *reinterpret_cast<float4*>(pd) = acc[u];
                                 }
                             }
                         }
@@ -645,7 +674,8 @@ int current_sm_count() {
 }
 
 template <int BN, int MT>
-int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& ty, GemmArgs g, cudaStream_t s) {
+int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& ty, const PeerMaps& pm, GemmArgs g,
+                cudaStream_t s) {
     using Cfg = TileCfg<BN, MT>;
     static bool attr_set[64] = {};
     const int dev = c->device < 64 ? c->device : 63;
@@ -655,7 +685,7 @@ int launch_tile(const DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& ty
         attr_set[dev] = true;
     }
     const int grid = std::min(g.num_work, c->sm_count);
-    MLZC_CUDA_TRY(launch_pdl(gemm_f16_tc_kernel<BN, MT>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, s, ta, ty, g));
+    MLZC_CUDA_TRY(launch_pdl(gemm_f16_tc_kernel<BN, MT>, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, s, ta, ty, pm, g));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;
@@ -673,9 +703,11 @@ bool gemm_f16_applicable(int64_t M, int64_t K, int64_t N, const void* w, size_t 
     return true;
 }
 
-int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
-                    cudaStream_t s) {
+namespace {
+
+int launch_gemm_f16_impl(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                         size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                         cudaStream_t s, const GemmPeers* peers) {
     const GemmPlan pl = plan_gemm(M, K, N, c->sm_count);
     const size_t need = pl.total();
     if (!ws || ws_bytes < need)
@@ -722,15 +754,48 @@ int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64
         st = make_y_map(&ty, y, (uint64_t)M, (uint64_t)N, y_col_bytes);
         if (st != MLZC_OK) return st;
     }
-    if (pl.MT == 2) return BN == 192 ? launch_tile<192, 2>(c, ta, ty, g, s) : launch_tile<256, 2>(c, ta, ty, g, s);
-    switch (BN) {
-        case 16: return launch_tile<16, 1>(c, ta, ty, g, s);
-        case 32: return launch_tile<32, 1>(c, ta, ty, g, s);
-        case 64: return launch_tile<64, 1>(c, ta, ty, g, s);
-        case 96: return launch_tile<96, 1>(c, ta, ty, g, s);
-        case 128: return launch_tile<128, 1>(c, ta, ty, g, s);
-        default: return launch_tile<256, 1>(c, ta, ty, g, s);
+    PeerMaps pm;
+    std::memset(&pm, 0, sizeof pm);
+    if (peers) {
+        // tiles reach the peers through the TMA stores or the split fix-up; the plain
+        // per-thread store path has no peer form
+        if (!g.tma_store && pl.splits == 1) return fail(MLZC_ERR_UNSUPPORTED, "GEMM peer stores: Y not TMA-storable");
+        if (peers->npeer > kGemmMaxPeers || M % 4 || peers->pcs % 16)
+            return fail(MLZC_ERR_UNSUPPORTED, "GEMM peer stores: layout not taken");
+        g.npeer = peers->npeer;
+        g.pcs = peers->pcs;
+        g.epoch = peers->epoch;
+        for (int par = 0; par < 2; ++par)
+            for (int r = 0; r < peers->npeer; ++r) {
+                g.pslot[par][r] = peers->slot[par][r];
+                if (g.tma_store && (st = make_y_map(&pm.m[par][r], peers->slot[par][r], (uint64_t)M, (uint64_t)N,
+                                                    peers->pcs)) != MLZC_OK)
+                    return st;
+            }
     }
+    if (pl.MT == 2) return BN == 192 ? launch_tile<192, 2>(c, ta, ty, pm, g, s) : launch_tile<256, 2>(c, ta, ty, pm, g, s);
+    switch (BN) {
+        case 16: return launch_tile<16, 1>(c, ta, ty, pm, g, s);
+        case 32: return launch_tile<32, 1>(c, ta, ty, pm, g, s);
+        case 64: return launch_tile<64, 1>(c, ta, ty, pm, g, s);
+        case 96: return launch_tile<96, 1>(c, ta, ty, pm, g, s);
+        case 128: return launch_tile<128, 1>(c, ta, ty, pm, g, s);
+        default: return launch_tile<256, 1>(c, ta, ty, pm, g, s);
+    }
+}
+
+}  // namespace
+
+int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                    cudaStream_t s) {
+    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, nullptr);
+}
+
+int launch_gemm_f16_peers(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                          size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                          const GemmPeers& peers, cudaStream_t s) {
+    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, &peers);
 }
 
 }  // namespace mlzc

@@ -76,6 +76,22 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
                    void* ws, size_t ws_bytes, cudaStream_t s);
 // Decode-shaped Q4_K, N <= 2 (N <= 4 with many short rows): persistent kernel fed by a TMA
 // ring, activations converted once per CTA into shared memory.
+// The tcgen05 GEMM of a row-sharded call that also stores every finished tile into this
+// rank's slice of each other rank's exchange slot (both parities given; the kernel picks
+// the call's by the device epoch).  MLZC_ERR_UNSUPPORTED when Y or the layout does not fit.
+struct GemmPeers {
+    int npeer;
+    float* slot[2][7];
+    size_t pcs;                 // column stride of the slices (bytes)
+    const uint32_t* epoch;      // this rank's completed-epoch counter
+};
+int launch_gemm_f16_peers(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
+                          size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
+                          const GemmPeers& peers, cudaStream_t s);
+// F16 mul_mat dispatch helpers shared with the sharded path.
+bool mul_mat_uses_gemm(int w_type, int64_t M, int64_t K, int64_t N, const void* w, size_t w_rs, const float* x,
+                       size_t x_cs, const float* y, size_t y_cs);
+
 // Q4_K, 1 <= N <= 4: int8 tensor-core path (activations quantised to int8 hi + lo per
 // block by a prep launch), stream-K over 16-row x 8-block units.
 bool q4k_i8_applicable(int64_t M, int64_t K, int64_t N);

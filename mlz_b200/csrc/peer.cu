@@ -31,6 +31,8 @@
 namespace mlzc {
 namespace {
 
+constexpr int kPeerPiece = 2048;   // floats per CTA pass of the slot -> Y copy
+
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -57,7 +59,7 @@ peer_push_kernel(const uint4* __restrict__ slice, size_t chunks, PeerView pv) {
 // rank's flag on every rank (a system-scope fence first orders those completed stores
 // before it), then every CTA waits for all G flags and copies the slots into Y.
 __global__ void __launch_bounds__(256)
-peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_cs, unsigned int* err) {
+peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_cs, unsigned int* err, int skip_self) {
     ptx::pdl_launch_dependents();
     ptx::pdl_wait();   // this rank's slice stores have completed; Y may be read by the previous kernel
     PeerHeader* me = reinterpret_cast<PeerHeader*>(pv.base[pv.rank]);
@@ -82,19 +84,25 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
     }
     __syncthreads();
     if (ok) {
-        // one (rank r, column n) row of m_loc floats per CTA pass: y[n][r*m_loc + m]
+        // pieces of kPeerPiece floats of the (rank r, column n) rows: y[n][r*m_loc + m]
         const char* slots = pv.base[pv.rank] + kPeerHeaderBytes + (size_t)(e & 1) * pv.slot_bytes;
-        const int rows = pv.G * N;
+        // skip_self: this rank's slice is already in Y (its GEMM stored it there)
+        const int nr = skip_self ? pv.G - 1 : pv.G;
+        const int per_row = (m_loc + kPeerPiece - 1) / kPeerPiece;
+        const int pieces = nr * N * per_row;
         const bool vec = (m_loc % 4 == 0) && (y_cs % 16 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
-        for (int rn = blockIdx.x; rn < rows; rn += gridDim.x) {
-            const int r = rn / N, n = rn - r * N;
+        for (int pc = blockIdx.x; pc < pieces; pc += gridDim.x) {
+            const int rn = pc / per_row, m0 = (pc - rn * per_row) * kPeerPiece;
+            const int ri = rn / N, n = rn - ri * N;
+            const int r = skip_self && ri >= pv.rank ? ri + 1 : ri;
+            const int m1 = min(m_loc, m0 + kPeerPiece);
             const float* src = reinterpret_cast<const float*>(slots + (size_t)r * pv.slice_stride) + (size_t)n * m_loc;
             float* dst = reinterpret_cast<float*>(reinterpret_cast<char*>(y) + (size_t)n * y_cs) + (size_t)r * m_loc;
             if (vec) {
-                for (int m4 = threadIdx.x; m4 < m_loc / 4; m4 += blockDim.x)
+                for (int m4 = m0 / 4 + threadIdx.x; m4 < m1 / 4; m4 += blockDim.x)
                     reinterpret_cast<float4*>(dst)[m4] = ptx::ld_act(reinterpret_cast<const float4*>(src) + m4);
             } else {
-                for (int m = threadIdx.x; m < m_loc; m += blockDim.x) dst[m] = ptx::ld_act(src + m);
+                for (int m = m0 + threadIdx.x; m < m1; m += blockDim.x) dst[m] = ptx::ld_act(src + m);
             }
         }
     }
@@ -112,11 +120,12 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
 }  // namespace
 
 int launch_peer_wait(const PeerView& pv, int N, int m_loc, float* y, size_t y_cs, unsigned int* err, int sm_count,
-                     cudaStream_t s) {
-    // one CTA pass per (rank, column) row of m_loc floats, at most 4 CTAs per SM
-    const int64_t rows = (int64_t)pv.G * N;
-    const int gw = (int)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)sm_count * 4));
-    MLZC_CUDA_TRY(launch_pdl(peer_wait_kernel, dim3(gw), dim3(256), 0, s, pv, N, m_loc, y, y_cs, err));
+                     cudaStream_t s, bool skip_self) {
+    // one CTA pass per piece of kPeerPiece floats (a multiple of 4) of each (rank, column) row,
+    // at most 4 CTAs per SM: a one-column gather spreads over many SMs
+    const int64_t pieces = (int64_t)(skip_self ? pv.G - 1 : pv.G) * N * ((m_loc + kPeerPiece - 1) / kPeerPiece);
+    const int gw = (int)std::max<int64_t>(1, std::min<int64_t>(pieces, (int64_t)sm_count * 4));
+    MLZC_CUDA_TRY(launch_pdl(peer_wait_kernel, dim3(gw), dim3(256), 0, s, pv, N, m_loc, y, y_cs, err, skip_self ? 1 : 0));
     MLZC_CUDA_TRY(cudaGetLastError());
     count_launch();
     return MLZC_OK;

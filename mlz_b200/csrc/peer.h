@@ -35,10 +35,11 @@ struct PeerView {
 int launch_peer_allgather(const PeerView& pv, const float* slice, int N, int m_loc, float* y, size_t y_cs,
                           unsigned int* err, int sm_count, cudaStream_t s);
 // The wait and copy half alone, after a kernel that stored this rank's slice into every
-// rank's slot itself (the push kernel, or the fused decode GEMV); it first releases this
-// rank's flag on every rank.
+// rank's slot itself (the push kernel, or the fused decode GEMV), or into the other ranks'
+// slots and its own rows of Y (the fused GEMM: skip_self); it first releases this rank's
+// flag on every rank.
 int launch_peer_wait(const PeerView& pv, int N, int m_loc, float* y, size_t y_cs, unsigned int* err, int sm_count,
-                     cudaStream_t s);
+                     cudaStream_t s, bool skip_self = false);
 
 #ifdef __CUDACC__
 // Epoch of the call in flight, read by every CTA of the kernels of one call.

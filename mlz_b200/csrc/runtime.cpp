@@ -179,6 +179,16 @@ bool use_gemm(int w_type, int64_t M, int64_t K, int64_t N, const void* w, size_t
     return w_type == MLZC_TYPE_F16 && N >= kGemmMinN && gemm_f16_applicable(M, K, N, w, w_rs, x, x_cs, y, y_cs);
 }
 
+}  // namespace
+
+bool mul_mat_uses_gemm(int w_type, int64_t M, int64_t K, int64_t N, const void* w, size_t w_rs, const float* x,
+                       size_t x_cs, const float* y, size_t y_cs) {
+    return w_type == MLZC_TYPE_F16 && !gemv_f16_mma_applicable(M, K, N, w, w_rs, x, x_cs) &&
+           use_gemm(w_type, M, K, N, w, w_rs, x, x_cs, y, y_cs);
+}
+
+namespace {
+
 int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64_t M, int64_t K,
                      const float* x, size_t x_cs, int64_t N, float* y, size_t y_cs, void* ws,
                      size_t ws_bytes, cudaStream_t s) {

@@ -35,10 +35,11 @@ def test_single_rank_equals_unsharded(dev, comm):
             assert torch.equal(y, ref), (rep, M, K, N)
 
 
-@pytest.mark.parametrize("N", [1, 4])
+@pytest.mark.parametrize("N", [1, 4, 64])
 def test_single_rank_graph_replay(dev, comm, N):
     """N = 1 takes the fused decode GEMV (outputs stored straight into the exchange slots),
-    N = 4 the slice + push kernels."""
+    N = 4 the slice + push kernels, N = 64 the tcgen05 GEMM that stores its tiles into its
+    rows of Y and into the other ranks' slots (none here) before the wait kernel."""
     import torch
     M, K = 2048, 1024
     gen = torch.Generator(device=dev).manual_seed(700)
