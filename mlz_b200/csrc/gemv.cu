@@ -73,9 +73,9 @@ struct WF32 {
 // Each lane keeps ROWS x U 16-byte weight loads in flight (U chunks 32 apart), which is
 // what hides the HBM latency: ~128 KB in flight per SM at ROWS = 2, U = 4.
 // early != 0 (f16 weights only): the first weight loads are issued before pdl_wait().
-// KW = 1: each warp owns ROWS rows over all of K.  KW = kWarps (few rows: too few warps
-// to keep enough loads in flight): the CTA's 8 warps share ROWS rows, warp w takes every
-// 8th group of 32 * U chunks, and the CTA sums the 8 partial rows in warp order.
+// KW = 1: each warp owns ROWS rows over all of K.  KW = 2, 4, 8: KW warps share a group of
+// ROWS rows, warp w of the group takes every KW-th stretch of 32 * U chunks, and the CTA sums
+// each group's KW partial rows in warp order -- more, shorter streams in flight per row.
 // PEER (row-sharded mul_mat, one column): instead of Y, every output row goes to this
 // rank's slice in the epoch's slot of every rank's exchange region (peer memory over
 // NVLink); the wait kernel that follows on the stream signals and gathers.
@@ -87,10 +87,12 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
     constexpr int CH = WT::kPerChunk;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int64_t row0 = KW == 1 ? ((int64_t)blockIdx.x * kWarps + warp) * ROWS : (int64_t)blockIdx.x * ROWS;
-    const int kw = KW == 1 ? 0 : warp;
+    // KW warps share a group of ROWS rows (KW = 1: a warp per group), kWarps / KW groups per CTA
+    const int grp = warp / KW;
+    const int64_t row0 = ((int64_t)blockIdx.x * (kWarps / KW) + grp) * ROWS;
+    const int kw = warp % KW;
     ptx::pdl_launch_dependents();
-    if (KW == 1 && row0 >= M) return;   // (KW > 1: the grid covers M exactly by ROWS-row groups)
+    if (KW == 1 && row0 >= M) return;   // (KW > 1: every warp takes the CTA barrier below)
     bool waited = false;
     if (!(WT::kNcWeights && early)) {
         ptx::pdl_wait();
@@ -181,12 +183,14 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
                 if (lane == 0) red[warp][r * NB + n] = v;
             }
         __syncthreads();
-        if (threadIdx.x < ROWS * NB) {
-            const int r = threadIdx.x / NB, n = threadIdx.x % NB;
+        if (threadIdx.x < (kWarps / KW) * ROWS * NB) {
+            const int gi = threadIdx.x / (ROWS * NB), e = threadIdx.x % (ROWS * NB);
+            const int r = e / NB, n = e % NB;
+            const int64_t rg = ((int64_t)blockIdx.x * (kWarps / KW) + gi) * ROWS;
             float v = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += red[w][threadIdx.x];
-            if (n < ncols && row0 + r < M) put(n, row0 + r, v);
+            for (int w = 0; w < KW; ++w) v += red[gi * KW + w][e];
+            if (n < ncols && rg + r < M) put(n, rg + r, v);
         }
     }
 }
@@ -214,10 +218,9 @@ gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K
     }
 }
 
-// Rows below which the warps of a CTA split K instead of taking rows of their own: with
-// fewer than ~2 CTAs of 16 rows per SM the loads in flight cannot cover the HBM latency
-// (e.g. the 1024 x 28672 and 3584 x 8192 row shards of the sharded FFN).
-constexpr int64_t kKSplitMaxRows = 2 * 148 * kWarps * 2;
+// KW warps of a CTA split the K of each row group whenever K is long enough for every warp
+// to keep its loads in flight: measured on B200 (us per call, KW = 8 / one warp per 2 rows):
+// 8192 x 28672 68.3 / 73.5, 28672 x 8192 65.0 / 74.6 (7.2 TB/s of weights).
 
 template <class WT, int NB, bool PEER = false>
 int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
@@ -225,16 +228,20 @@ int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, 
     constexpr int ROWS = 2;
     constexpr int U = NB <= 2 ? 4 : 2;
     const int early = weights_before_wait() ? 1 : 0;
-    if (M < kKSplitMaxRows && K / WT::kPerChunk >= (int64_t)32 * U * kWarps) {
-        const unsigned grid = (unsigned)((M + ROWS - 1) / ROWS);
-        MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U, kWarps, PEER>, dim3(grid), dim3(kThreads), 0, s, w,
-                                 w_rs, M, K, x, x_cs, ncols, y, y_cs, early, pv));
-    } else {
-        const int64_t rows_per_cta = (int64_t)kWarps * ROWS;
-        const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-        MLZC_CUDA_TRY(launch_pdl(gemv_vec_kernel<WT, NB, ROWS, U, 1, PEER>, dim3(grid), dim3(kThreads), 0, s, w, w_rs,
-                                 M, K, x, x_cs, ncols, y, y_cs, early, pv));
-    }
+    // the most warps per row group (KW) for which each still has a full set of loads in flight
+    const int64_t chunks = K / WT::kPerChunk;
+    const int kw = chunks >= (int64_t)32 * U * 8 ? 8 : chunks >= (int64_t)32 * U * 4 ? 4 : chunks >= (int64_t)32 * U * 2 ? 2 : 1;
+    const int64_t rows_per_cta = (int64_t)(kWarps / kw) * ROWS;
+    const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
+    auto go = [&](auto kern) {
+        return launch_pdl(kern, dim3(grid), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs, ncols, y, y_cs, early, pv);
+    };
+    cudaError_t e;
+    if (kw == 8) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 8, PEER>);
+    else if (kw == 4) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 4, PEER>);
+    else if (kw == 2) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 2, PEER>);
+    else e = go(gemv_vec_kernel<WT, NB, ROWS, U, 1, PEER>);
+    MLZC_CUDA_TRY(e);
     count_launch();
     return MLZC_OK;
 }

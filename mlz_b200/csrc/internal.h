@@ -105,10 +105,6 @@ size_t q6k_i8_workspace_bytes(int64_t K, int64_t N);
 int launch_q6k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                   cudaStream_t s);
-bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N);
-int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
-                    const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes,
-                    cudaStream_t s);
 // The same ring for 3 <= N <= 8 (where it wins), fed by activations prepared once per call
 // (q4k_prep_kernel's xf / xs) that travel with each stage.
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N);

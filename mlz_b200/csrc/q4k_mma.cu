@@ -82,125 +82,6 @@ __device__ __forceinline__ uint32_t word_of(const RowBlock& r, int wi) {
     }
 }
 
-// Decode form (N <= 8): as the main kernel below, with the activations rounded and summed
-// in the kernel itself (no prep launch, which would cost more than it saves at this size)
-// and the next block's weights prefetched into registers (one CTA per SM at ~250
-// registers; the prefetch, not occupancy, hides the load latency).
-__global__ void __launch_bounds__(kQThreads)
-q4k_gemv_kernel(const char* __restrict__ W, size_t w_rs, int M, int nblk, const char* X, size_t x_cs,
-               int N, char* __restrict__ Y, size_t y_cs, int early) {
-    __shared__ float red[kQWarps][kQRows * 8];
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int g = lane >> 2;
-    const int q4 = lane & 3;
-    const int m0 = blockIdx.y * kQRows;
-    const int n0 = blockIdx.x * 8;
-
-    // rows of this thread: tile t, half h -> m0 + 16 t + g + 8 h (clamped for loads)
-    const char* rowp[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = min(m0 + 16 * (i >> 1) + g + 8 * (i & 1), M - 1);
-        rowp[i] = W + (size_t)r * w_rs;
-    }
-    const bool col_ok = n0 + g < N;
-    const float* xcol = reinterpret_cast<const float*>(X + (size_t)(col_ok ? n0 + g : 0) * x_cs);
-
-    float y[2][4] = {};
-    RowBlock cur[4], nxt[4];
-    int kb = warp;
-    ptx::pdl_launch_dependents();
-    if (!early) ptx::pdl_wait();
-    if (kb < nblk) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) cur[i] = load_row_block(rowp[i] + (size_t)kb * kQ4KBytes, q4);
-    }
-    // Q4_K blocks are never an output of these kernels: with early != 0 the first block's
-    // loads overlap the previous kernel's tail; the activations and every write come after it
-    ptx::pdl_wait();
-    for (; kb < nblk; kb += kQWarps) {
-        const int kn = kb + kQWarps;
-        if (kn < nblk) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) nxt[i] = load_row_block(rowp[i] + (size_t)kn * kQ4KBytes, q4);
-        }
-        RowScales sc[4];   // rows g, g + 8 of tile 0, then of tile 1
-        q4k::row_scales2(cur[0].hdr, cur[1].hdr, q4, sc[0], sc[1]);
-        q4k::row_scales2(cur[2].hdr, cur[3].hdr, q4, sc[2], sc[3]);
-
-        float acc[2][4] = {};
-        float S[2] = {0.0f, 0.0f};
-        const float4* xb = reinterpret_cast<const float4*>(xcol + (size_t)kb * kQK + 64 * q4);
-#pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-            float4 xv[8];
-#pragma unroll
-            for (int wi = 0; wi < 8; ++wi) xv[wi] = col_ok ? ptx::ld_act(xb + 8 * hi + wi) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int wi = 0; wi < 8; ++wi) {
-                S[hi] += (xv[wi].x + xv[wi].y) + (xv[wi].z + xv[wi].w);
-                const uint32_t b0 = h2u(__floats2half2_rn(xv[wi].x, xv[wi].z));
-                const uint32_t b1 = h2u(__floats2half2_rn(xv[wi].y, xv[wi].w));
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const uint32_t w0 = word_of(cur[2 * t], wi), w1 = word_of(cur[2 * t + 1], wi);
-                    uint32_t a0, a1, a2, a3;
-                    if (hi == 0) {
-                        a0 = deq_lo(w0, sc[2 * t]);
-                        a1 = deq_lo(w1, sc[2 * t + 1]);
-                        a2 = deq_lo(w0 >> 8, sc[2 * t]);
-                        a3 = deq_lo(w1 >> 8, sc[2 * t + 1]);
-                    } else {
-                        a0 = deq_hi(w0, sc[2 * t]);
-                        a1 = deq_hi(w1, sc[2 * t + 1]);
-                        a2 = deq_hi(w0 >> 8, sc[2 * t]);
-                        a3 = deq_hi(w1 >> 8, sc[2 * t + 1]);
-                    }
-                    mma16816(acc[t], a0, a1, a2, a3, b0, b1);
-                }
-            }
-        }
-        // min term: sum_j m_j S_j with S as f16 hi + lo
-        const __half2 Sh = __floats2half2_rn(S[0], S[1]);
-        const float2 Shf = __half22float2(Sh);
-        const uint32_t bs_hi = h2u(Sh), bs_lo = h2u(__floats2half2_rn(S[0] - Shf.x, S[1] - Shf.y));
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            float mn[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(mn, sc[2 * t].mpair, sc[2 * t + 1].mpair, 0u, 0u, bs_hi, 0u);
-            mma16816(mn, sc[2 * t].mpair, sc[2 * t + 1].mpair, 0u, 0u, bs_lo, 0u);
-            // rows g (e = 0, 1) and g + 8 (e = 2, 3)
-            y[t][0] += sc[2 * t].d * acc[t][0] - sc[2 * t].dmin * mn[0];
-            y[t][1] += sc[2 * t].d * acc[t][1] - sc[2 * t].dmin * mn[1];
-            y[t][2] += sc[2 * t + 1].d * acc[t][2] - sc[2 * t + 1].dmin * mn[2];
-            y[t][3] += sc[2 * t + 1].d * acc[t][3] - sc[2 * t + 1].dmin * mn[3];
-        }
-        if (kn < nblk) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
-        }
-    }
-
-    // partial rows of every warp -> fixed-order sum
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const int r = 16 * t + g;
-        red[warp][r * 8 + 2 * q4] = y[t][0];
-        red[warp][r * 8 + 2 * q4 + 1] = y[t][1];
-        red[warp][(r + 8) * 8 + 2 * q4] = y[t][2];
-        red[warp][(r + 8) * 8 + 2 * q4 + 1] = y[t][3];
-    }
-    __syncthreads();
-    const int r = threadIdx.x % kQRows, cidx = threadIdx.x / kQRows;
-    if (m0 + r < M && n0 + cidx < N) {
-        float v = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kQWarps; ++w) v += red[w][r * 8 + cidx];
-        reinterpret_cast<float*>(Y + (size_t)(n0 + cidx) * y_cs)[m0 + r] = v;
-    }
-}
-
 // Activation prep: X (N x K f32) rounded to f16 once, in the order the B fragments use,
 // plus the sub-block sums as f16 hi + lo pairs.  One thread per (column, block, quad slot
 // q, k-step s = 8 hi + wi): the values e = 64q + 32 hi + 4 wi + {0, 2} go to b0 and {1, 3}
@@ -405,19 +286,10 @@ int launch_q4k_mma(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_
     const char* wc = static_cast<const char*>(w);
     const char* xc = reinterpret_cast<const char*>(x);
     char* yc = reinterpret_cast<char*>(y);
+    // N <= 4: the int8 path; 5 <= N <= 8: the shared-X ring; N > 8: the batched kernel
     if (q4k_i8_applicable(M, K, N))
         return launch_q4k_i8(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s);
-    if (q4k_ring_applicable(M, K, N))
-        return launch_q4k_ring(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, s);
     const bool xstream = q4k_ring_xs_applicable(M, K, N);
-    if (N <= 8 && !xstream) {
-        const dim3 grid(1u, (unsigned)((M + kQRows - 1) / kQRows));
-        if (grid.y > 65535u) return fail(MLZC_ERR_INVALID, "Q4_K: M=%lld beyond %d rows", (long long)M, 65535 * kQRows);
-        MLZC_CUDA_TRY(launch_pdl(q4k_gemv_kernel, grid, dim3(kQThreads), 0, s, wc, w_row_bytes, (int)M, (int)(K / kQK), xc,
-                                 x_col_bytes, (int)N, yc, y_col_bytes, weights_before_wait() ? 1 : 0));
-        count_launch();
-        return MLZC_OK;
-    }
     const Q4kWs q = q4k_ws(K, N);
     if (!ws || ws_bytes < q.xf_bytes + q.xs_bytes || (uintptr_t)ws % 16)
         return fail(MLZC_ERR_NOMEM, "Q4_K: workspace of %zu bytes needed, %zu given", q.xf_bytes + q.xs_bytes, ws_bytes);

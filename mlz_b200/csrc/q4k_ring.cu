@@ -1,9 +1,9 @@
-// q4k_ring.cu -- decode-shaped Q4_K mul_mat (N <= 8 activation columns) as persistent
-// kernels fed by a TMA ring: q4k_ring_kernel (N <= 2; N <= 4 with many short rows;
-// activations converted per CTA) and
-// q4k_ring_xs_kernel (3 <= N <= 8, activations prepared once per call, carried by the stages).
+// q4k_ring.cu -- decode-shaped Q4_K mul_mat for 5 <= N <= 8 activation columns as a
+// persistent kernel fed by a TMA ring (q4k_ring_xs_kernel): the activations are prepared once
+// per call (q4k_prep_kernel's f16 B fragments and sub-block sums) and each stage carries its
+// blocks' fragments next to the weight box.  (N <= 4 takes the int8 path, q4k_i8.cu.)
 //
-// Replaces, for the decode shapes, the Q4_K branch of ggml_simd_try_mul_mat
+// Replaces, for these shapes, the Q4_K branch of ggml_simd_try_mul_mat
 // (src/simd/ggml_simd_hook.cpp:188-231, 238-299): one simd_vec_dot_q4_k_q8_k
 // (src/simd/kernels/x86/vec/vec_dot_q4_k_q8_k_avx2.asm:38-266) per (row, column).  The
 // arithmetic is that of q4k_mma.cu (exact f16 sc*q dequant, f16 activations, fp32 MMA
@@ -12,17 +12,14 @@
 // Design (HBM-bound: every block byte is read once):
 //   - A tile is 16 weight rows (the MMA's M) times all of K.  Each CTA owns whole tiles
 //     (t = blockIdx.x, + gridDim.x, ...), so no partial row crosses CTAs and nothing is
-//     merged after the kernel; the grid is sized so every CTA gets the same tile count.
-//   - A producer warp streams the tile's blocks into a 4-stage shared-memory ring with TMA:
-//     a stage is 8 consecutive K blocks of the 16 rows, one 2-d box of 16 rows x 1152
-//     contiguous bytes (16 row requests per stage; 144-byte boxes, one per block, streamed
-//     at 3.7 instead of 4.8 TB/s).  Two CTAs per SM where shared memory allows.
+//     merged after the kernel.
+//   - A producer warp streams the tile's blocks into a 2-stage shared-memory ring with TMA:
+//     a stage is 8 consecutive K blocks of the 16 rows (one 2-d box of 16 rows x 1152
+//     contiguous bytes) plus those blocks' prepared activations (bulk copies from the
+//     workspace).  Two CTAs per SM.
 //   - Eight consumer warps each take one block of every stage: the header and their
 //     32-byte nibble chunk for rows g and g + 8, the (sc, m) unpack, LOP3 + HFMA2 dequant
-//     and 16 MMAs (four accumulator chains).
-//   - q4k_ring_kernel converts the activations once per CTA, before the main loop, into the
-//     MMA's f16 B fragments (in the permuted k order the dequant produces) and the sub-block
-//     sums (f16 hi + lo), kept in shared memory for the whole kernel.
+//     and the MMAs.
 //   - At the end of a tile the eight warps' partial rows are summed in warp order through
 //     shared memory (one named barrier per tile; double-buffered), so results repeat bit
 //     for bit.
@@ -56,9 +53,7 @@ constexpr int kTileRows = 16;                              // rows per tile (MMA
 constexpr int kStageBlocks = kRWarps;                      // K blocks per stage, one per consumer warp
 constexpr int kBoxBytes = kTileRows * q4k::kBlockBytes;    // 2304: one block of the tile's 16 rows
 constexpr uint32_t kStageBytes = kStageBlocks * kBoxBytes; // 18432
-constexpr int kStages = 4;
 constexpr int kU64PerBlock = q4k::kBlockBytes / 8;         // a block in the map's 8-byte elements
-constexpr int kRedFloats = kRWarps * kTileRows * 8;        // one set of the warps' partial tiles
 
 struct RingParams {
     const char* x;               // activations, column n at x + n * x_cs (f32)
@@ -72,12 +67,6 @@ struct RingParams {
     unsigned int* err;           // device error word (bounded waits)
     CUtensorMap tm_w;            // W as 8-byte elements: [M][nblk * 18], box 18 x 16
 };
-
-// Dynamic shared memory of the kernel for NCOL columns and nblk blocks per row.
-constexpr size_t ring_smem_bytes(int ncol, int nblk) {
-    return 1024 + (size_t)kStages * kStageBytes + (size_t)nblk * 8 * 4 * ncol * 16 + (size_t)nblk * 4 * ncol * 8 +
-           2 * (size_t)kRedFloats * 4 + 2 * kStages * 8 + 16;
-}
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile(
@@ -105,40 +94,6 @@ __device__ __forceinline__ uint32_t word_of(const uint4& a, const uint4& b, int 
         case 5: return b.y;
         case 6: return b.z;
         default: return b.w;
-    }
-}
-
-// Producer (one thread) of both ring kernels: the stages of this CTA's tiles (t =
-// blockIdx.x, + gridDim.x, ...), 16 rows x 8 blocks each, into the ring with TMA.
-template <int STAGES>
-__device__ __forceinline__ void ring_producer(const RingParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                              volatile int* abort_flag, int my_tiles, int nst) {
-    const int G = gridDim.x;
-    if (!p.early) ptx::pdl_wait();
-    const int total = my_tiles * nst;
-    int issued = 0;
-    for (int it = 0; it < total; ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (!ptx::mbar_wait(ptx::smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
-        // the consumers read the stage with generic loads: order them before the TMA
-        // (async proxy) overwrites it
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const int ti = it / nst, si = it % nst;
-        const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
-        const int kb0 = si * kStageBlocks;   // blocks past the row end are zero-filled by the map
-        const uint32_t fb = ptx::smem_u32(&full[s]);
-        const uint32_t st = ptx::smem_u32(ring + (size_t)s * kStageBytes);
-        ptx::mbar_expect_tx(fb, kStageBytes);
-        tma_load_2d(st, &p.tm_w, fb, kb0 * kU64PerBlock, m0);
-        issued = it + 1;
-    }
-    // no copy may still be landing when the CTA exits (consumers that gave up do not
-    // wait for theirs): the last fill of every slot has completed (bounded)
-    volatile int no_abort = 0;
-    for (int s = 0; s < STAGES && s < issued; ++s) {
-        const int last = s + (issued - 1 - s) / STAGES * STAGES;
-        ptx::mbar_wait(ptx::smem_u32(&full[s]), (last / STAGES) & 1, &no_abort, p.err);
     }
 }
 
@@ -183,177 +138,6 @@ __device__ __forceinline__ void ring_producer_xs(const RingParams& p, uint8_t* r
     for (int s = 0; s < kXsStages && s < issued; ++s) {
         const int last = s + (issued - 1 - s) / kXsStages * kXsStages;
         ptx::mbar_wait(ptx::smem_u32(&full[s]), (last / kXsStages) & 1, &no_abort, p.err);
-    }
-}
-
-// NCOL: activation columns held in shared memory (N rounded up to 1, 2, 4 or 8).
-template <int NCOL>
-__global__ void __launch_bounds__(kRThreads, 2)
-q4k_ring_kernel(const __grid_constant__ RingParams p) {
-    extern __shared__ uint8_t q4r_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q4r_smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* ring = smem;
-    // x fragments: [kb][k-step pair (8)][quad q (4)][column (NCOL)] uint4 = (b0, b1) of steps 2p, 2p+1
-    uint4* xfr = reinterpret_cast<uint4*>(smem + (size_t)kStages * kStageBytes);
-    // sub-block sums: [kb][q][column] uint2 = ((S_2q, S_2q+1) f16 hi, lo)
-    uint2* xsum = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(xfr) + (size_t)p.nblk * 8 * 4 * NCOL * 16);
-    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsum) + (size_t)p.nblk * 4 * NCOL * 8);
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRedFloats);
-    uint64_t* empty = full + kStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
-            ptx::mbar_init(ptx::smem_u32(&empty[s]), kRWarps);
-        }
-        *abort_flag = 0;
-        ptx::mbar_init_fence();
-    }
-    __syncthreads();
-    ptx::pdl_launch_dependents();
-
-    const int G = gridDim.x;
-    const int nst = (p.nblk + kStageBlocks - 1) / kStageBlocks;     // stages per tile
-    const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
-
-    if (warp == kRWarps) {
-        if (lane == 0) ring_producer<kStages>(p, ring, full, empty, abort_flag, my_tiles, nst);
-        return;
-    }
-
-    // ---------------- consumers
-    ptx::pdl_wait();   // the activations, and every write, come after the previous kernel
-    // Activations -> f16 B fragments + sub-block sums in shared memory.  Consumer warp w
-    // consumes exactly the blocks kb = w (mod 8), so it converts those itself (no barrier).
-    // Per (block, column) 64 items (quad q, k-step st = 8 hi + wi), two per lane: the values
-    // e = 64 q + 32 hi + 4 wi + {0, 2} go to b0 and {1, 3} to b1, and the 16 lanes sharing
-    // (block, column, q) sum S_2q (hi = 0) and S_2q+1 (hi = 1) by shuffles.  Columns past N
-    // are zero.  Loads are issued kPrepBatch (block, column) pairs at a time.
-    {
-        constexpr int kPrepBatch = 4;
-        const int mine = (p.nblk - warp + kRWarps - 1) / kRWarps;     // blocks of this warp
-        const int pairs = mine * NCOL;
-        for (int pb = 0; pb < pairs; pb += kPrepBatch) {
-            float4 v[kPrepBatch][2];
-#pragma unroll
-            for (int u = 0; u < kPrepBatch; ++u) {
-                const int pi = pb + u;
-                const int kb = warp + (pi / NCOL) * kRWarps, n = pi % NCOL;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int item = lane + 32 * h, st = item & 15, q = item >> 4;
-                    v[u][h] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (pi < pairs && n < p.N)
-                        v[u][h] = ptx::ld_act(reinterpret_cast<const float4*>(p.x + (size_t)n * p.x_cs) +
-                                              (size_t)kb * (q4k::kQK / 4) + 16 * q + 8 * (st >> 3) + (st & 7));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kPrepBatch; ++u) {
-                const int pi = pb + u;
-                if (pi >= pairs) break;   // warp-uniform
-                const int kb = warp + (pi / NCOL) * kRWarps, n = pi % NCOL;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int item = lane + 32 * h, st = item & 15, q = item >> 4;
-                    const float4 x4 = v[u][h];
-                    const uint2 b = make_uint2(h2u(__floats2half2_rn(x4.x, x4.z)), h2u(__floats2half2_rn(x4.y, x4.w)));
-                    reinterpret_cast<uint2*>(xfr + ((kb * 8 + (st >> 1)) * 4 + q) * NCOL + n)[st & 1] = b;
-                    float S = (x4.x + x4.y) + (x4.z + x4.w);
-                    S += __shfl_xor_sync(0xffffffffu, S, 1);
-                    S += __shfl_xor_sync(0xffffffffu, S, 2);
-                    S += __shfl_xor_sync(0xffffffffu, S, 4);
-                    const float S1 = __shfl_down_sync(0xffffffffu, S, 8);   // lane st = 0 gets the hi = 1 sum
-                    if (st == 0) {
-                        const __half2 sh = __floats2half2_rn(S, S1);
-                        const float2 shf = __half22float2(sh);
-                        xsum[(kb * 4 + q) * NCOL + n] = make_uint2(h2u(sh), h2u(__floats2half2_rn(S - shf.x, S1 - shf.y)));
-                    }
-                }
-            }
-        }
-        __syncwarp();
-    }
-
-    const int g = lane >> 2;
-    const int q4 = lane & 3;
-    const bool colv = g < p.N;      // this lane's B column is a real one
-    const uint32_t ring_u32 = ptx::smem_u32(ring);
-    bool ok = true;
-    int it = 0;
-    for (int ti = 0; ti < my_tiles; ++ti) {
-        const int m0 = ((int)blockIdx.x + ti * G) * kTileRows;
-        float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;   // rows g (cols 2 q4, +1), g + 8 (same)
-        for (int si = 0; si < nst; ++si, ++it) {
-            const int s = it % kStages;
-            const uint32_t ph = (it / kStages) & 1;
-            if (ok && !ptx::mbar_wait(ptx::smem_u32(&full[s]), ph, abort_flag, p.err)) ok = false;
-            if (!ok) continue;
-            const int kb = si * kStageBlocks + warp;
-            if (kb < p.nblk) {
-                const uint32_t bb = ring_u32 + (uint32_t)s * kStageBytes + (uint32_t)warp * q4k::kBlockBytes;
-                const uint32_t r0 = bb + (uint32_t)g * (kStageBlocks * q4k::kBlockBytes), r1 = r0 + 8 * (kStageBlocks * q4k::kBlockBytes);
-                const uint4 h0 = lds128(r0), h1 = lds128(r1);
-                const uint4 a0w = lds128(r0 + 16 + 32 * q4), b0w = lds128(r0 + 32 + 32 * q4);
-                const uint4 a1w = lds128(r1 + 16 + 32 * q4), b1w = lds128(r1 + 32 + 32 * q4);
-                RowScales s0, s1;
-                q4k::row_scales2(h0, h1, q4, s0, s1);
-                const uint4* xb = xfr + ((size_t)kb * 8 * 4 + q4) * NCOL + (colv ? g : 0);
-                float acc[4][4] = {};
-#pragma unroll
-                for (int pr = 0; pr < 8; ++pr) {
-                    const uint4 xv = colv ? xb[pr * 4 * NCOL] : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        const int stp = 2 * pr + h2, wi = stp & 7;
-                        const uint32_t w0 = word_of(a0w, b0w, wi), w1 = word_of(a1w, b1w, wi);
-                        uint32_t a0, a1, a2, a3;
-                        if (stp < 8) {
-                            a0 = deq_lo(w0, s0);
-                            a1 = deq_lo(w1, s1);
-                            a2 = deq_lo(w0 >> 8, s0);
-                            a3 = deq_lo(w1 >> 8, s1);
-                        } else {
-                            a0 = deq_hi(w0, s0);
-                            a1 = deq_hi(w1, s1);
-                            a2 = deq_hi(w0 >> 8, s0);
-                            a3 = deq_hi(w1 >> 8, s1);
-                        }
-                        mma16816(acc[2 * (pr & 1) + h2], a0, a1, a2, a3, h2 ? xv.z : xv.x, h2 ? xv.w : xv.y);
-                    }
-                }
-                // min term: sum_j m_j S_j with S as f16 hi + lo
-                const uint2 sv = colv ? xsum[((size_t)kb * 4 + q4) * NCOL + g] : make_uint2(0u, 0u);
-                float mn[4] = {0.f, 0.f, 0.f, 0.f}, ml[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816(mn, s0.mpair, s1.mpair, 0u, 0u, sv.x, 0u);
-                mma16816(ml, s0.mpair, s1.mpair, 0u, 0u, sv.y, 0u);
-                y0 += s0.d * ((acc[0][0] + acc[1][0]) + (acc[2][0] + acc[3][0])) - s0.dmin * (mn[0] + ml[0]);
-                y1 += s0.d * ((acc[0][1] + acc[1][1]) + (acc[2][1] + acc[3][1])) - s0.dmin * (mn[1] + ml[1]);
-                y2 += s1.d * ((acc[0][2] + acc[1][2]) + (acc[2][2] + acc[3][2])) - s1.dmin * (mn[2] + ml[2]);
-                y3 += s1.d * ((acc[0][3] + acc[1][3]) + (acc[2][3] + acc[3][3])) - s1.dmin * (mn[3] + ml[3]);
-            }
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
-        }
-        // ---- the eight warps' partial tiles -> rows of Y, summed in warp order
-        float* rb = red + (ti & 1) * kRedFloats;
-        float* mine = rb + warp * (kTileRows * 8);
-        mine[g * 8 + 2 * q4] = y0;
-        mine[g * 8 + 2 * q4 + 1] = y1;
-        mine[(g + 8) * 8 + 2 * q4] = y2;
-        mine[(g + 8) * 8 + 2 * q4 + 1] = y3;
-        consumer_sync();
-        const int t = threadIdx.x;
-        if (ok && t < kTileRows * p.N && !*abort_flag) {
-            const int r = t & (kTileRows - 1), c = t >> 4;
-            float v = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kRWarps; ++w) v += rb[w * (kTileRows * 8) + r * 8 + c];
-            if (m0 + r < p.M) reinterpret_cast<float*>(p.y + (size_t)c * p.y_cs)[m0 + r] = v;
-        }
     }
 }
 
@@ -537,21 +321,6 @@ int ring_slots(Kern kernel, size_t smem, int* out) {
     return MLZC_OK;
 }
 
-template <int NCOL>
-int launch_ring(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
-    const size_t smem = ring_smem_bytes(NCOL, p.nblk);
-    int slots = 0;
-    const int st = ring_slots(q4k_ring_kernel<NCOL>, smem, &slots);
-    if (st != MLZC_OK) return st;
-    // one CTA per resident slot (or per tile): with two CTAs per SM this keeps the tiles per
-    // SM within one of each other
-    const int grid = std::min(p.tiles, slots);
-    p.err = c->err;
-    MLZC_CUDA_TRY(launch_pdl(q4k_ring_kernel<NCOL>, dim3((unsigned)grid), dim3(kRThreads), smem, s, p));
-    count_launch();
-    return MLZC_OK;
-}
-
 int launch_ring_xs(const DeviceCtx* c, RingParams& p, cudaStream_t s) {
     const size_t smem = ring_xs_smem_bytes();
     int slots = 0;
@@ -592,36 +361,10 @@ int make_ring_params(const void* w, size_t w_row_bytes, int64_t M, int64_t K, in
 
 }  // namespace
 
-bool q4k_ring_applicable(int64_t M, int64_t K, int64_t N) {
-    // Each CTA converts all of X itself (no prep launch): N <= 2 everywhere, N = 3..4 for many
-    // short rows (the C3 batch-4 step: 42.0 us with 14336 x 4096 here vs 43.8 us with it on
-    // the prepared-activation form below); more columns or longer rows: the form below
-    if (N < 1 || N > 4 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
-    if (N > 2 && (M < 8192 || K > 4096)) return false;
-    return ring_smem_bytes(N <= 1 ? 1 : N <= 2 ? 2 : 4, (int)(K / q4k::kQK)) <= 227 * 1024;
-}
-
-int launch_q4k_ring(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                    size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, cudaStream_t s) {
-    if (!q4k_ring_applicable(M, K, N)) return fail(MLZC_ERR_UNSUPPORTED, "Q4_K ring: shape not taken");
-    if ((uintptr_t)x % 16 || x_col_bytes % 16) return fail(MLZC_ERR_INVALID, "Q4_K: activations must be 16-byte aligned");
-    RingParams p;
-    const int st = make_ring_params(w, w_row_bytes, M, K, N, y, y_col_bytes, &p);
-    if (st != MLZC_OK) return st;
-    p.x = reinterpret_cast<const char*>(x);
-    p.x_cs = x_col_bytes;
-    if (N <= 1) return launch_ring<1>(c, p, s);
-    if (N <= 2) return launch_ring<2>(c, p, s);
-    return launch_ring<4>(c, p, s);
-}
-
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N) {
-    // Measured on B200 (us, this form / the best other): N = 8: 4096 x 4096 6.9 / 8.0,
-    // 14336 x 4096 16.4 / 19.4, 4096 x 14336 16.5 / 25.0; N = 4: 4096 x 14336 16.2 / 19.5,
-    // but 4096 x 4096 7.0 / 6.5 (the register decode kernel).  The launcher tries the ring
-    // above first, which takes N = 3..4 with many short rows.
-    if (N < 3 || N > 8 || K % q4k::kQK != 0 || M < 1 || M > (int64_t)1 << 30) return false;
-    return N >= 5 || M >= 8192 || K > 4096;
+    // Measured on B200 (us, this form / the register decode kernel it replaced): N = 8:
+    // 4096 x 4096 6.9 / 8.0, 14336 x 4096 16.4 / 19.4, 4096 x 14336 16.5 / 25.0.
+    return N >= 5 && N <= 8 && K % q4k::kQK == 0 && M >= 1 && M <= (int64_t)1 << 30;
 }
 
 int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
