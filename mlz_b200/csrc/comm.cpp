@@ -325,15 +325,17 @@ extern "C" int mlzc_mul_mat_sharded_dev(mlzc_comm c, int w_type, const void* w_s
         pv.slice_stride = slice_bytes;
         // decode (one column, F16): one kernel computes the slice and stores it into every
         // rank's slot over NVLink as it goes; then the wait-and-copy kernel
+        // this rank's rows of Y
+        float* y_own = reinterpret_cast<float*>(reinterpret_cast<char*>(y) + (size_t)c->rank * m_loc * 4);
         if (N == 1 && w_type == MLZC_TYPE_F16) {
-            st = launch_gemv_f16_peer(w_shard, w_row_bytes, m_loc, K, x, pv, s);
-            if (st == MLZC_OK) return launch_peer_wait(pv, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s);
+            st = launch_gemv_f16_peer(w_shard, w_row_bytes, m_loc, K, x, pv, y_own, s);
+            if (st == MLZC_OK)
+                return launch_peer_wait(pv, (int)N, (int)m_loc, y, y_col_bytes, ctx->err, ctx->sm_count, s, true);
             if (st != MLZC_ERR_UNSUPPORTED) return st;
         }
         // prefill (the tcgen05 GEMM): its epilogue stores every finished tile into its rows of Y
         // and into this rank's slice of each other rank's slot, so the exchange overlaps the
         // remaining tiles; the wait kernel then copies only the other ranks' slices
-        float* y_own = reinterpret_cast<float*>(reinterpret_cast<char*>(y) + (size_t)c->rank * m_loc * 4);
         if (c->nranks - 1 <= 7 &&
             mul_mat_uses_gemm(w_type, m_loc, K, N, w_shard, w_row_bytes, x, x_col_bytes, y_own, y_col_bytes)) {
             GemmPeers gp{};

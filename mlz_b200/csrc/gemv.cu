@@ -159,8 +159,12 @@ gemv_vec_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K,
     if (PEER) e = peer_epoch(pv);   // after the wait: the previous call's wait kernel advanced it
     auto put = [&](int n, int64_t row, float v) {
         if (PEER) {
+            // this rank's own rows straight into Y, the other ranks' slots over NVLink
             const size_t off = peer_slice_offset(pv, e) + (size_t)row * 4;   // [N = 1][m_loc]
-            for (int r = 0; r < pv.G; ++r) *reinterpret_cast<float*>(pv.base[r] + off) = v;
+            for (int r = 0; r < pv.G; ++r) {
+                if (r == pv.rank) reinterpret_cast<float*>(Y)[row] = v;
+                else *reinterpret_cast<float*>(pv.base[r] + off) = v;
+            }
         } else {
             reinterpret_cast<float*>(Y + (size_t)n * y_cs)[row] = v;
         }
@@ -277,12 +281,12 @@ int run_gemv(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, s
 
 // F16 decode GEMV whose outputs go straight to every rank's exchange slot (see PEER).
 int gemv_f16_peer(const void* w, size_t w_rs, int64_t M, int64_t K, const float* x, const PeerView& pv,
-                  cudaStream_t s) {
+                  float* y_own, cudaStream_t s) {
     const bool aligned = ((uintptr_t)w % 16 == 0) && ((uintptr_t)x % 16 == 0) && (w_rs % 16 == 0) &&
                          (K % WF16::kPerChunk == 0);
     if (!aligned || M < 1 || K < 1) return MLZC_ERR_UNSUPPORTED;   // caller takes the two-kernel path
     return launch_vec<WF16, 1, true>(static_cast<const char*>(w), w_rs, M, K, reinterpret_cast<const char*>(x),
-                                     (size_t)K * 4, 1, nullptr, 0, s, pv);
+                                     (size_t)K * 4, 1, reinterpret_cast<char*>(y_own), 0, s, pv);
 }
 
 // gathered [G][N][m_loc] -> dst [N][G * m_loc] (column stride dst_cs bytes): one CTA row per
@@ -309,8 +313,8 @@ __global__ void gather_permute_kernel(const float* src, char* __restrict__ dst, 
 }  // namespace
 
 int launch_gemv_f16_peer(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                         const PeerView& pv, cudaStream_t s) {
-    return gemv_f16_peer(w, w_row_bytes, M, K, x, pv, s);
+                         const PeerView& pv, float* y_own, cudaStream_t s) {
+    return gemv_f16_peer(w, w_row_bytes, M, K, x, pv, y_own, s);
 }
 
 int launch_gather_permute(const float* src, float* dst, size_t dst_col_bytes, int G, int64_t N,

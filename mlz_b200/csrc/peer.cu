@@ -69,17 +69,23 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
         __threadfence_system();
         for (int r = 0; r < pv.G; ++r) st_release_sys(&reinterpret_cast<PeerHeader*>(pv.base[r])->flag[e & 1][pv.rank], e);
     }
-    if (threadIdx.x == 0) {
-        ok = 1;
+    if (threadIdx.x < 32) {
+        // lane r polls rank r's flag: the G acquires overlap instead of taking one round trip
+        // each (bounded; every lane gives up together)
+        const int lane = threadIdx.x;
+        bool mine = lane >= pv.G;
         const uint64_t t0 = ptx::global_ns();
-        for (int r = 0; r < pv.G && ok; ++r) {
-            while (ld_acquire_sys(&me->flag[e & 1][r]) != e) {
-                if (ptx::global_ns() - t0 > ptx::kWaitNs) {
-                    atomicOr(err, MLZC_DEVERR_WAIT_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
+        bool timed_out = false;
+        while (!__all_sync(0xffffffffu, mine)) {
+            if (!mine) mine = ld_acquire_sys(&me->flag[e & 1][lane]) == e;
+            if (__any_sync(0xffffffffu, ptx::global_ns() - t0 > ptx::kWaitNs)) {
+                timed_out = true;
+                break;
             }
+        }
+        if (lane == 0) {
+            ok = timed_out ? 0 : 1;
+            if (timed_out) atomicOr(err, MLZC_DEVERR_WAIT_TIMEOUT);
         }
     }
     __syncthreads();

@@ -52,10 +52,11 @@ __device__ __forceinline__ size_t peer_slice_offset(const PeerView& pv, uint32_t
 }
 #endif
 
-// Decode GEMV (one activation column, F16 weights) that stores every output row into every
-// rank's slot (gemv.cu); MLZC_ERR_UNSUPPORTED when the operands do not fit its vectorised
-// form (the caller then takes the slice + push path).
+// Decode GEMV (one activation column, F16 weights) that stores every output row into this
+// rank's rows of Y (y_own) and into every other rank's slot (gemv.cu); MLZC_ERR_UNSUPPORTED
+// when the operands do not fit its vectorised form (the caller then takes the slice + push
+// path).
 int launch_gemv_f16_peer(const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
-                         const PeerView& pv, cudaStream_t s);
+                         const PeerView& pv, float* y_own, cudaStream_t s);
 
 }  // namespace mlzc
