@@ -8,17 +8,18 @@
 //         included) at offset rank * slice_stride -- 16-byte stores straight into peer
 //         memory.  For decode (one column) the GEMV itself does these stores (gemv.cu)
 //         and there is no push kernel;
-//   wait: its CTA 0 first releases this rank's epoch flag on every rank (after a
-//         system-scope fence: the kernel that stored the slice has completed), then one
-//         thread per CTA acquires the G flags of the epoch (bounded by %globaltimer:
+//   wait: its CTA 0 first releases this rank's epoch flag on every rank (release stores at
+//         system scope; the kernel that stored the slice has completed), then one warp per
+//         CTA acquires the G flags of the epoch (bounded by %globaltimer:
 //         MLZC_DEVERR_WAIT_TIMEOUT and no output on expiry), the CTAs copy the slots into
 //         Y in ggml order (y[n][r * m_loc + m] = slot[r][n][m]), and the last CTA to finish
 //         advances the epoch counter.
 // Epochs live in device memory (so a CUDA graph of the calls replays correctly); the two
 // slots alternate by epoch parity, which is safe because a rank pushes epoch e + 2 only
 // after its wait for e + 1, which needs every rank's push of e + 1, which each rank's
-// stream issues after its own wait (and copy) of e.  No TMA and no cluster-wide broadcast copy touch peer
-// memory: plain st.global / ld.global.
+// stream issues after its own wait (and copy) of e.  Peer memory is only ever written (plain
+// stores here and in the decode GEMV, TMA tensor stores in the prefill GEMM's epilogue) and
+// read back by its owner: no copy engine load or cluster-wide broadcast reads another GPU.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -37,6 +38,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -66,7 +73,10 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
     __shared__ int ok;
     const uint32_t e = peer_epoch(pv);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
-        __threadfence_system();
+        // message passing: the slice stores were completed by the kernel before this one (its
+        // grid finished before pdl_wait returned), and each flag is a release store at system
+        // scope; a reader acquires the flag before it reads the slot.  (A sequentially
+        // consistent system fence here measured 1.9 us per call and orders nothing more.)
         for (int r = 0; r < pv.G; ++r) st_release_sys(&reinterpret_cast<PeerHeader*>(pv.base[r])->flag[e & 1][pv.rank], e);
     }
     if (threadIdx.x < 32) {
@@ -114,8 +124,9 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();   // this CTA's read of the epoch happens before its count
-        const unsigned int done = atomicAdd(&me->wait_done, 1u);
+        // acq_rel: this CTA's read of the epoch happens before its count, and the last CTA's
+        // epoch store after every count
+        const unsigned int done = atom_add_acq_rel_gpu(&me->wait_done, 1u);
         if (done == gridDim.x - 1) {   // every CTA has read the epoch: advance it
             me->wait_done = 0;
             me->epoch = e;
