@@ -283,10 +283,8 @@ class C3(Workload):
         # the library's dispatch (q4k_i8_applicable, q4k_ring_xs_applicable, launch_q4k_mma)
         if n <= 4:
             kern = "act_i8::prep_kernel<8> + q4k_i8_kernel"
-        elif n <= 8 and (n >= 5 or m >= 8192 or k > 4096):
-            kern = "q4k_prep_kernel + q4k_ring_xs_kernel"
         elif n <= 8:
-            kern = "q4k_gemv_kernel"
+            kern = "q4k_prep_kernel + q4k_ring_xs_kernel"
         else:
             kern = "q4k_prep_kernel + q4k_mma_kernel"
         return f"{kern}, {m}x{k} (one call)"

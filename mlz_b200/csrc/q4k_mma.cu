@@ -267,10 +267,8 @@ Q4kWs q4k_ws(int64_t K, int64_t N) {
 
 size_t q4k_workspace_bytes(int64_t K, int64_t N) {
     if (q4k_i8_applicable(1, K, N)) return q4k_i8_workspace_bytes(K, N);
-    // prepared activations: the batched kernel (N > 8) and the shared-X ring (3 <= N <= 8;
-    // for N = 3..4 on small short-row shapes the register decode kernel runs and the
-    // workspace goes unused -- the size cannot depend on M)
-    if (N <= 2) return 0;
+    // prepared activations: the shared-X ring (5 <= N <= 8) and the batched kernel (N > 8,
+    // and any shape the int8 path does not take)
     const Q4kWs w = q4k_ws(K, N);
     return w.xf_bytes + w.xs_bytes;
 }

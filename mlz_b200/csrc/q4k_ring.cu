@@ -362,7 +362,7 @@ int make_ring_params(const void* w, size_t w_row_bytes, int64_t M, int64_t K, in
 }  // namespace
 
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N) {
-    // Measured on B200 (us, this form / the register decode kernel it replaced): N = 8:
+    // Measured on B200 (us, this form / a register-only decode kernel): N = 8:
     // 4096 x 4096 6.9 / 8.0, 14336 x 4096 16.4 / 19.4, 4096 x 14336 16.5 / 25.0.
     return N >= 5 && N <= 8 && K % q4k::kQK == 0 && M >= 1 && M <= (int64_t)1 << 30;
 }

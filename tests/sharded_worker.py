@@ -1,4 +1,4 @@
-"""One rank of the 2-GPU sharded mul_mat check (launched by tests/test_sharded_mgpu.py
+"""One rank of the multi-GPU sharded mul_mat check (launched by tests/test_sharded_mgpu.py
 through torchrun; not a test module itself).  Every rank builds the same full weights
 from a seed, keeps its M/G rows, runs mlzc_mul_mat_sharded_dev through NCCL, and compares
 the gathered Y with the single-GPU mul_mat of the full weights and with the oracle on
@@ -33,7 +33,7 @@ def main(out_path: str) -> None:
         # (gate/up 28672x8192 at N = 1, down 8192x28672 at N = 256; generated on the
         # device from one seed on every rank, so every rank holds the same full W)
         for (kind, M, K, N) in [("f16", 1024, 512, 1), ("f16", 2048, 1024, 4), ("f16", 512, 768, 33),
-                                ("f16", 1024, 256, 256), ("f16", 516, 256, 5), ("q4k", 1024, 1024, 1),
+                                ("f16", 1024, 256, 256), ("f16", 520, 256, 5), ("q4k", 1024, 1024, 1),
                                 ("q4k", 512, 512, 16), ("f16", 28672, 8192, 1), ("f16", 8192, 28672, 256)]:
             g = synth.rng(5000 + M + K + N)
             m_loc = M // world

@@ -1,5 +1,6 @@
-"""GPU, 2 ranks: the row-sharded mul_mat with the NCCL all-gather (config c5's path) against
-the single-GPU result (<= 1e-5) and the oracle (<= 1e-3 F16, 2e-3 Q4_K).  Needs two GPUs;
+"""GPU, 2 / 4 / 8 ranks: the row-sharded mul_mat (the 70B FFN's path: peer-memory exchange,
+NCCL all-gather where the peer path is not taken) against the single-GPU result (<= 1e-4)
+and the oracle (<= 1e-3 F16, 2e-3 Q4_K).  Each world size needs that many GPUs and is
 skipped on fewer.  NVLS is off (NCCL_NVLS_ENABLE=0): a plain ring/tree all-gather suffices."""
 import json
 import os
@@ -13,21 +14,22 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def test_two_rank_sharded_mul_mat(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_mul_mat(tmp_path, world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     out = str(tmp_path / "res")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(port),
            os.path.join(HERE, "sharded_worker.py"), out]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=300)
     assert r.returncode == 0, r.stderr[-3000:]
-    for rank in range(2):
+    for rank in range(world):
         with open(f"{out}.{rank}") as f:
             res = json.load(f)
         assert res["device_errors"] == 0
