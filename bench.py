@@ -57,7 +57,17 @@ NCU_TRAFFIC = {
     ("c3", 8): (33.29e6, "ncu capture: q4k_ring_xs_kernel, 4096x14336 launch, batch 8 (the 14336x4096 launch "
                          "reads the same block bytes)"),
     ("c3", 16): (33.31e6, "ncu capture: q4k_mma_kernel, 14336x4096 launch, batch 16"),
+    ("c5", 1): (469.85e6 + 3.33e6, "ncu capture: gemv_vec_kernel, 28672x8192 gate launch, N=1, one GPU (the "
+                                   "8192x28672 down launch reads the same weight bytes)"),
 }
+
+
+def traffic_of(cfg: str, n: int, w, world: int):
+    """The committed capture's DRAM bytes for this workload's dominant call, or None: none for
+    the pooled c2 calls, and the c5 captures hold one GPU's whole matrix, not a shard."""
+    if isinstance(w, C2) or (isinstance(w, C5) and world > 1):
+        return None
+    return NCU_TRAFFIC.get((cfg, n))
 
 
 def parse_args():
@@ -878,8 +888,8 @@ def extra_rows(a, n_head, dev, rank, world, comm, peaks):
             units = w.work_units()
             job = units if isinstance(w, C5) else units * world
             rl = roofline_of(w, t, peaks, None, ms)
-            tr = NCU_TRAFFIC.get((cfg, n))
-            if tr is not None and not isinstance(w, C2):
+            tr = traffic_of(cfg, n, w, world)
+            if tr is not None:
                 rl["traffic"], rl["traffic_source"] = tr
             row = {"workload": w.config["workload"], "metric": w.metric, "unit": w.unit,
                    "value": job * K / (ms * 1e-3) * w.unit_scale(), "ms_per_step": ms / K,
@@ -960,8 +970,8 @@ def mlz_arm(a):
     job_units = units if isinstance(w, C5) else units * world
     value = job_units * K / (ms * 1e-3) * w.unit_scale()
     roofline = roofline_of(w, t, peaks, clocks, ms)
-    tr = NCU_TRAFFIC.get((a.config, n))
-    if tr is not None and not isinstance(w, C2):
+    tr = traffic_of(a.config, n, w, world)
+    if tr is not None:
         roofline["traffic"] = tr[0]
         roofline["traffic_source"] = tr[1]
 

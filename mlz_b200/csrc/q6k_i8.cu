@@ -18,7 +18,9 @@
 // vector v (hi / lo) of the group-grp half of the quadrant's values and zeros in the other
 // half, so each accumulator column is one (group, hi / lo) sum.  A lane keeps the columns of
 // one group parity and scales them by that group's int8 scale with one IMAD each (|sum| <
-// 2^28 over a block).  The -32 offset is -32 d sum_g sc_g S_g with the group sums S_g of
+// 2^28 over a block).  One column fills half of the B columns, so there the other half carries
+// the next quadrant and quadrant pairs accumulate in one MMA chain (q6_block_spread: half the
+// scaling IMADs and scale extractions; 14.6 vs 15.0 us on 14336 x 4096).  The -32 offset is -32 d sum_g sc_g S_g with the group sums S_g of
 // the unquantised activations (f16 hi + lo / 2048) against the scales (exact f16) in one m16n8k16
 // MMA per block.  Per block the row gets d * s * (HI + LO / 254) - 32 d sum_g sc_g S_g.
 //
@@ -104,6 +106,16 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         "{%10, %10, %10, %10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// d += a . b (same fragments as mma_u8s8)
+__device__ __forceinline__ void mma_u8s8_acc(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWarps * 32) : "memory"); }
@@ -227,6 +239,90 @@ __device__ __forceinline__ void q6_block(uint32_t r0, uint32_t r1, uint32_t R, i
     }
 }
 
+// One activation column: the four B columns the column needs (2 groups x hi / lo) fill half
+// of an MMA, so the other half carries the next quadrant -- B column 4 qp + 2 grp + v holds
+// group grp of vector v for the quadrants qd % 2 == qp and zeros for the others -- and the
+// quadrant pairs (0, 1), (2, 3) of each half accumulate in one MMA chain.  Lane t's C columns
+// are then quadrant parity t / 2, group t % 2: its scale is byte t of one scale word, and it
+// scales one chain (4 IMADs) where the one-tile form scales every quadrant with lanes of zero
+// columns.  Accumulates this lane's share of rows y0, y1 into ya[0..1] (summed over the quad
+// at the flush; lane t = 0 carries the -32 offset).
+template <bool ODD>
+__device__ __forceinline__ void q6_block_spread(uint32_t r0, uint32_t r1, uint32_t R, int warp, int g, int t,
+                                                float (&ya)[2]) {
+    const int bqp = g >> 2, bgrp = (g >> 1) & 1, bvec = g & 1;
+    uint32_t sw0[4], sw1[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sw0[i] = ldw<ODD>(r0 + 192 + 4 * i);
+        sw1[i] = ldw<ODD>(r1 + 192 + 4 * i);
+    }
+    const uint32_t sel = (uint32_t)t | ((8u | t) << 4) | ((8u | t) << 8) | ((8u | t) << 12);
+    const uint32_t boff = R + (uint32_t)(bvec * kVarStride + warp * kQK + 16 * bgrp + 4 * t);
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t u00 = ldw<ODD>(r0 + 128 + 32 * h + 4 * t), u01 = ldw<ODD>(r0 + 128 + 32 * h + 16 + 4 * t);
+        const uint32_t u10 = ldw<ODD>(r1 + 128 + 32 * h + 4 * t), u11 = ldw<ODD>(r1 + 128 + 32 * h + 16 + 4 * t);
+        const uint32_t wa00 = ldw<ODD>(r0 + 64 * h + 4 * t), wa01 = ldw<ODD>(r0 + 64 * h + 16 + 4 * t);
+        const uint32_t wb00 = ldw<ODD>(r0 + 64 * h + 32 + 4 * t), wb01 = ldw<ODD>(r0 + 64 * h + 48 + 4 * t);
+        const uint32_t wa10 = ldw<ODD>(r1 + 64 * h + 4 * t), wa11 = ldw<ODD>(r1 + 64 * h + 16 + 4 * t);
+        const uint32_t wb10 = ldw<ODD>(r1 + 64 * h + 32 + 4 * t), wb11 = ldw<ODD>(r1 + 64 * h + 48 + 4 * t);
+        int d[2][4];
+        // chains c = quadrants (0, 1) and (2, 3), their MMAs interleaved
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int qd = 2 * c + jj;
+                auto q6 = [&](uint32_t wa, uint32_t wb, uint32_t u) -> uint32_t {
+                    const uint32_t w = (qd & 1) ? wb : wa;
+                    const uint32_t nib = (qd & 2) ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu);
+                    const uint32_t hb = (qd == 0 ? (u << 4) : qd == 1 ? (u << 2) : qd == 2 ? u : (u >> 2)) & 0x30303030u;
+                    return nib | hb;
+                };
+                const uint32_t a0 = q6(wa00, wb00, u00), a1 = q6(wa10, wb10, u10);
+                const uint32_t a2 = q6(wa01, wb01, u01), a3 = q6(wa11, wb11, u11);
+                const uint32_t bw = bqp == jj ? lds32(boff + (uint32_t)(128 * h + 32 * qd)) : 0u;
+                if (jj == 0)
+                    mma_u8s8(d[c], a0, a1, a2, a3, bgrp ? 0u : bw, bgrp ? bw : 0u);
+                else
+                    mma_u8s8_acc(d[c], a0, a1, a2, a3, bgrp ? 0u : bw, bgrp ? bw : 0u);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            // group 8 h + 2 (2 c + t / 2) + t % 2 = 8 h + 4 c + t: byte t of word 2 h + c
+            const int sc0 = prmt_sx(sw0[2 * h + c], sel), sc1 = prmt_sx(sw1[2 * h + c], sel);
+            acc[0] += d[c][0] * sc0;
+            acc[1] += d[c][1] * sc0;
+            acc[2] += d[c][2] * sc1;
+            acc[3] += d[c][3] * sc1;
+        }
+    }
+    // -32 d sum_g sc_g S_g as in q6_block (lane t = 0 holds column 0's pair)
+    const uint32_t swa0 = t < 2 ? sw0[0] : sw0[1], swb0 = t < 2 ? sw0[2] : sw0[3];
+    const uint32_t swa1 = t < 2 ? sw1[0] : sw1[1], swb1 = t < 2 ? sw1[2] : sw1[3];
+    const int sh = 16 * (t & 1);
+    const uint32_t ma0 = i8x2_to_h2(swa0 >> sh), ma2 = i8x2_to_h2(swb0 >> sh);
+    const uint32_t ma1 = i8x2_to_h2(swa1 >> sh), ma3 = i8x2_to_h2(swb1 >> sh);
+    uint32_t sb0 = 0u, sb1 = 0u;
+    if (g < 2) {
+        const uint32_t so = R + act_i8::rec_sum_off(1) + (uint32_t)((warp * 2 + g) * kGpb * 2 + 4 * t);
+        sb0 = lds32(so);
+        sb1 = lds32(so + 16);
+    }
+    float mn[4] = {0.f, 0.f, 0.f, 0.f};
+    ptx::mma16816(mn, ma0, ma1, ma2, ma3, sb0, sb1);
+    const float d0 = __half2float(__ushort_as_half((unsigned short)lds16(r0 + 208)));
+    const float d1 = __half2float(__ushort_as_half((unsigned short)lds16(r1 + 208)));
+    const float s = __uint_as_float(lds32(R + act_i8::rec_scale_off(1) + (uint32_t)warp * 4));
+    const float m0 = t == 0 ? 32.0f * fmaf(mn[1], 1.0f / 2048.0f, mn[0]) : 0.0f;
+    const float m1 = t == 0 ? 32.0f * fmaf(mn[3], 1.0f / 2048.0f, mn[2]) : 0.0f;
+    ya[0] += d0 * (s * fmaf((float)acc[1], 1.0f / 254.0f, (float)acc[0]) - m0);
+    ya[1] += d1 * (s * fmaf((float)acc[3], 1.0f / 254.0f, (float)acc[2]) - m1);
+}
+
 template <int NCT>
 __global__ void __launch_bounds__(kThreads, 2) q6k_i8_kernel(const __grid_constant__ I8Params p) {
     constexpr int S = stages_for(NCT);
@@ -311,10 +407,17 @@ __global__ void __launch_bounds__(kThreads, 2) q6k_i8_kernel(const __grid_consta
             const uint32_t W = box_base + (uint32_t)s * kBoxBytes;
             const uint32_t R = rec_base + (uint32_t)s * RB;
             const uint32_t r0 = W + (uint32_t)(g * kRowBytes + warp * kBlk), r1 = r0 + 8 * kRowBytes;
-            if (warp & 1)
-                q6_block<NCT, true>(r0, r1, R, warp, g, t, ya);
-            else
-                q6_block<NCT, false>(r0, r1, R, warp, g, t, ya);
+            if constexpr (NCT == 1) {
+                if (warp & 1)
+                    q6_block_spread<true>(r0, r1, R, warp, g, t, ya[0]);
+                else
+                    q6_block_spread<false>(r0, r1, R, warp, g, t, ya[0]);
+            } else {
+                if (warp & 1)
+                    q6_block<NCT, true>(r0, r1, R, warp, g, t, ya);
+                else
+                    q6_block<NCT, false>(r0, r1, R, warp, g, t, ya);
+            }
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&empty[s]));
@@ -325,14 +428,25 @@ __global__ void __launch_bounds__(kThreads, 2) q6k_i8_kernel(const __grid_consta
         // ---- flush: the warps' partial rows (two group parities each), summed in a fixed order
         float* rb = red + (flushes & 1) * (kWarps * kTileRows * NCT * 2);
         ++flushes;
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            const int n = 2 * j + (t >> 1);
-            if (n < NCT) {
-                rb[((warp * kTileRows + g) * NCT + n) * 2 + (t & 1)] = ya[j][0];
-                rb[((warp * kTileRows + g + 8) * NCT + n) * 2 + (t & 1)] = ya[j][1];
+        if constexpr (NCT == 1) {
+            // the quad's four shares of column 0: pairs (t, t + 2) here, the two sums below
+            const float v0 = ya[0][0] + __shfl_xor_sync(0xffffffffu, ya[0][0], 2);
+            const float v1 = ya[0][1] + __shfl_xor_sync(0xffffffffu, ya[0][1], 2);
+            if (t < 2) {
+                rb[(warp * kTileRows + g) * 2 + t] = v0;
+                rb[(warp * kTileRows + g + 8) * 2 + t] = v1;
             }
-            ya[j][0] = ya[j][1] = 0.0f;
+            ya[0][0] = ya[0][1] = 0.0f;
+        } else {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const int n = 2 * j + (t >> 1);
+                if (n < NCT) {
+                    rb[((warp * kTileRows + g) * NCT + n) * 2 + (t & 1)] = ya[j][0];
+                    rb[((warp * kTileRows + g + 8) * NCT + n) * 2 + (t & 1)] = ya[j][1];
+                }
+                ya[j][0] = ya[j][1] = 0.0f;
+            }
         }
         consumer_sync();
         const int r = tid & (kTileRows - 1), n = tid >> 4;
