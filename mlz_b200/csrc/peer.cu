@@ -61,10 +61,10 @@ peer_push_kernel(const uint4* __restrict__ slice, size_t chunks, PeerView pv) {
     }
 }
 
-// The kernel before this one on the stream (the push kernel, or the fused decode GEMV)
-// stored this rank's slice into every rank's slot and has completed: CTA 0 releases this
-// rank's flag on every rank (a system-scope fence first orders those completed stores
-// before it), then every CTA waits for all G flags and copies the slots into Y.
+// The kernel before this one on the stream (the push kernel, the fused decode GEMV or the
+// fused GEMM) stored this rank's slice into every rank's slot and has completed: G threads of
+// CTA 0 release this rank's flag on the G ranks, then every CTA waits for all G flags and
+// copies the slots into Y.
 __global__ void __launch_bounds__(256)
 peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_cs, unsigned int* err, int skip_self) {
     ptx::pdl_launch_dependents();
@@ -72,12 +72,14 @@ peer_wait_kernel(PeerView pv, int N, int m_loc, float* __restrict__ y, size_t y_
     PeerHeader* me = reinterpret_cast<PeerHeader*>(pv.base[pv.rank]);
     __shared__ int ok;
     const uint32_t e = peer_epoch(pv);
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (blockIdx.x == 0 && threadIdx.x < pv.G) {
         // message passing: the slice stores were completed by the kernel before this one (its
         // grid finished before pdl_wait returned), and each flag is a release store at system
-        // scope; a reader acquires the flag before it reads the slot.  (A sequentially
-        // consistent system fence here measured 1.9 us per call and orders nothing more.)
-        for (int r = 0; r < pv.G; ++r) st_release_sys(&reinterpret_cast<PeerHeader*>(pv.base[r])->flag[e & 1][pv.rank], e);
+        // scope; a reader acquires the flag before it reads the slot.  One thread per rank: a
+        // single thread's release stores would each wait for the previous remote store to
+        // complete (one NVLink round trip per rank).  (A sequentially consistent system fence
+        // here measured 1.9 us per call and orders nothing more.)
+        st_release_sys(&reinterpret_cast<PeerHeader*>(pv.base[threadIdx.x])->flag[e & 1][pv.rank], e);
     }
     if (threadIdx.x < 32) {
         // lane r polls rank r's flag: the G acquires overlap instead of taking one round trip
