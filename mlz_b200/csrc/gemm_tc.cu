@@ -200,6 +200,9 @@ struct GemmArgs {
     float* pslot[2][kGemmMaxPeers];   // [parity][peer]: the slice, [N][M] with column stride pcs
     size_t pcs;
     const uint32_t* epoch;            // this rank's last completed epoch (the call's is + 1)
+    // Optional per-row output scale (powers of two from the quantised-weight path, whose
+    // f16 rows may be stored scaled down); nullptr: none.
+    const float* row_scale;
 };
 
 // The peers' slices as TMA store targets ([parity][peer], same box as tmY).
@@ -383,6 +386,8 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                 const int row = i * BM + quarter * 32 + lane;   // row of the tile this thread owns
                 const int m = m0 + row;
                 char* ybase = reinterpret_cast<char*>(g.y) + (size_t)m * 4;
+                // whole tiles only (split partials are scaled in the fix-up below)
+                const float rsc = (g.row_scale && g.splits == 1 && m < g.M) ? ptx::ld_act(g.row_scale + m) : 1.0f;
 #pragma unroll 1
                 for (int c0 = sub * G; c0 < kChunks; c0 += NSUB * G) {
                     uint32_t r[G][32];
@@ -396,6 +401,12 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                           (c0 + gg) * 32,
                                       r[gg]);
                     tmem_ld_wait();
+                    if (rsc != 1.0f) {
+#pragma unroll
+                        for (int gg = 0; gg < G; ++gg)
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) r[gg][j] = __float_as_uint(__uint_as_float(r[gg][j]) * rsc);
+                    }
 #pragma unroll
                     for (int gg = 0; gg < G; ++gg) {
                         if (c0 + gg >= kChunks) continue;
@@ -461,6 +472,9 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                     const int ncols = min(BN, g.N - n0);
                     const int mrow = m0 + r4;
                     const bool vec_store = mrow + 3 < g.M && ((reinterpret_cast<uintptr_t>(g.y) | g.y_cs) % 16 == 0);
+                    float rs4[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+                    if (g.row_scale && mrow < g.M)
+                        for (int q = 0; q < 4 && mrow + q < g.M; ++q) rs4[q] = ptx::ld_act(g.row_scale + mrow + q);
                     if (mrow < g.M) {
 #pragma unroll 1
                         for (int c = cg; c < ncols; c += 4 * CG) {
@@ -479,6 +493,10 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
                                 for (int u = 0; u < 4; ++u) {
                                     acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
                                 }
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                acc[u].x *= rs4[0]; acc[u].y *= rs4[1]; acc[u].z *= rs4[2]; acc[u].w *= rs4[3];
                             }
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
@@ -707,7 +725,7 @@ namespace {
 
 int launch_gemm_f16_impl(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                          size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
-                         cudaStream_t s, const GemmPeers* peers) {
+                         cudaStream_t s, const GemmPeers* peers, const float* row_scale) {
     const GemmPlan pl = plan_gemm(M, K, N, c->sm_count);
     const size_t need = pl.total();
     if (!ws || ws_bytes < need)
@@ -746,6 +764,7 @@ int launch_gemm_f16_impl(const DeviceCtx* c, const void* w, size_t w_row_bytes, 
     g.x16t = x16t;
     g.part = partials;
     g.tile_count = counters;
+    g.row_scale = row_scale;
     // Y through TMA stores: base and column stride 16-byte aligned (the tensor-map rules)
     CUtensorMap ty;
     std::memset(&ty, 0, sizeof ty);
@@ -789,13 +808,22 @@ int launch_gemm_f16_impl(const DeviceCtx* c, const void* w, size_t w_row_bytes, 
 int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                     size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                     cudaStream_t s) {
-    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, nullptr);
+    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, nullptr,
+                                nullptr);
+}
+
+int launch_gemm_f16_row_scaled(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                               const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws,
+                               size_t ws_bytes, const float* row_scale, cudaStream_t s) {
+    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, nullptr,
+                                row_scale);
 }
 
 int launch_gemm_f16_peers(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                           size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                           const GemmPeers& peers, cudaStream_t s) {
-    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, &peers);
+    return launch_gemm_f16_impl(c, w, w_row_bytes, M, K, x, x_col_bytes, N, y, y_col_bytes, ws, ws_bytes, s, &peers,
+                                nullptr);
 }
 
 }  // namespace mlzc

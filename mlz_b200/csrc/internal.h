@@ -105,7 +105,15 @@ size_t q6k_i8_workspace_bytes(int64_t K, int64_t N);
 int launch_q6k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                   cudaStream_t s);
-// The same ring for 3 <= N <= 8 (where it wins), fed by activations prepared once per call
+// Q4_K / Q6_K with at least kQuantGemmMinN columns: the rows dequantised to f16 in the
+// workspace (read once), then the tcgen05 F16 GEMM (dequant.cu).
+constexpr int64_t kQuantGemmMinN = 64;
+bool quant_gemm_applicable(int w_type, int64_t M, int64_t K, int64_t N);
+size_t quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N);
+int launch_quant_gemm(const DeviceCtx* c, int w_type, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                      const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws,
+                      size_t ws_bytes, cudaStream_t s);
+// The same ring for 5 <= N <= 8 (where it wins), fed by activations prepared once per call
 // (q4k_prep_kernel's xf / xs) that travel with each stage.
 bool q4k_ring_xs_applicable(int64_t M, int64_t K, int64_t N);
 int launch_q4k_ring_xs(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
@@ -119,6 +127,10 @@ bool gemm_f16_applicable(int64_t M, int64_t K, int64_t N, const void* w, size_t 
 int launch_gemm_f16(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M,
                     int64_t K, const float* x, size_t x_col_bytes, int64_t N, float* y,
                     size_t y_col_bytes, void* ws, size_t ws_bytes, cudaStream_t s);
+// The same with Y row m multiplied by row_scale[m] (the quantised-weight path, dequant.cu).
+int launch_gemm_f16_row_scaled(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K,
+                               const float* x, size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws,
+                               size_t ws_bytes, const float* row_scale, cudaStream_t s);
 
 // Flash-attention decode (persistent stream-K over key tiles + combine).  The workspace
 // size depends on the current device (its resident CTA count).

@@ -202,6 +202,9 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
         }
         return MLZC_OK;
     }
+    // prefill-sized batches of quantised weights: dequantise once, then the tcgen05 GEMM
+    if (quant_gemm_applicable(w_type, M, K, N))
+        return launch_quant_gemm(c, w_type, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
     if (w_type == MLZC_TYPE_Q4_K) return launch_q4k_mma(c, w, w_rs, M, K, x, x_cs, N, y, y_cs, ws, ws_bytes, s);
     if (w_type == MLZC_TYPE_Q6_K) {
         if ((uintptr_t)x % 16 || x_cs % 16)
@@ -220,6 +223,7 @@ int mul_mat_dispatch(DeviceCtx* c, int w_type, const void* w, size_t w_rs, int64
 }
 
 size_t mul_mat_ws(int w_type, int64_t M, int64_t K, int64_t N) {
+    if (quant_gemm_applicable(w_type, M, K, N)) return quant_gemm_workspace_bytes(M, K, N);
     if (w_type == MLZC_TYPE_Q4_K) return K % 256 == 0 ? q4k_workspace_bytes(K, N) : 0;
     if (w_type == MLZC_TYPE_Q6_K) return q6k_i8_applicable(M, K, N) ? q6k_i8_workspace_bytes(K, N) : 0;
     // N in [8, 16] normally takes the skinny tensor-core path (no workspace), but the

@@ -63,12 +63,17 @@ def test_q4k_workspace_follows_the_dispatch():
             rec = (K // 256 + 7) // 8 * (2 * nct * 2080 + nct * 32 + 8 * 2 * nct * 16)
             assert ws(4096, K, N) >= rec
             assert ws(1, K, N) == ws(14336, K, N)
-    for N in (5, 8, 9, 16, 256):
+    for N in (5, 8, 9, 16, 63):
         for K in (256, 4096, 14336):
             # f16 fragments (512 B per column and block) + sums (32 B); columns padded to a
             # whole 8-column tile, or pairs of them above 8
             pad = 8 if N <= 8 else (N + 15) // 16 * 16
             assert ws(4096, K, N) >= pad * (K // 256) * (512 + 32)
+    for N in (64, 256):
+        for K in (256, 4096, 14336):
+            # prefill sizes: the rows dequantised to f16 (2 B per weight) + the GEMM's share
+            assert ws(4096, K, N) >= 4096 * K * 2
+            assert mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q6_K, 4096, K, N) >= 4096 * K * 2
 
 
 def test_argument_gates():

@@ -49,6 +49,28 @@ def test_gguf_golden_blocks(dev, golden):
     assert (np.abs(y - want) / den).max() <= TOL
 
 
+def test_prefill_dequant_is_f16_rounding_of_gguf(dev, golden):
+    """Prefill sizes (N = K = 512 here) dequantise to f16 once: with a one-hot X the GEMM
+    returns the stored f16 weights, which must be the RNE roundings of the decoder's f32
+    weights -- after a power-of-two row scale where |d| 945 + |dmin| 63 exceeds the f16
+    range (the golden blocks include d = 65504)."""
+    import math
+    f = golden("q4k_gguf.npz")
+    blocks, K = f["blocks"], int(f["K"])
+    y = _run(dev, blocks, np.eye(K, dtype=np.float32), y_pad=1)
+    dq = f["dequant"].astype(np.float32)
+    nb = K // 256
+    for m in range(blocks.shape[0]):
+        hdr = blocks[m].reshape(nb, 144)[:, 0:4].copy().view(np.float16).astype(np.float32)
+        bound = float((np.abs(hdr[:, 0]) * 945.0 + np.abs(hdr[:, 1]) * 63.0).max())
+        e = 0
+        if bound > 65504.0:
+            fr, e = math.frexp(bound / 65504.0)
+            e = e - 1 if fr == 0.5 else e
+        want = np.ldexp(dq[m], -e).astype(np.float16).astype(np.float32) * np.float32(2.0 ** e)
+        assert (y[:, m] == want).all(), m
+
+
 def test_known_answer_block(dev):
     K = 512
     blk = np.zeros((1, 2, 144), dtype=np.uint8)
@@ -132,3 +154,17 @@ def test_power_of_two_scaling_is_exact_full_size(dev, MK, B):
     assert torch.isfinite(y).all()
     assert ((y4 - 4.0 * y).abs().max() / (4.0 * y).abs().max()).item() <= 1e-6
     assert torch.equal(y2, y), "repeat is bitwise identical"
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1000, 2304, 100), (37, 768, 65),
+                                   (4096, 14336, 128)])
+def test_prefill_sizes_dequant_then_gemm(dev, M, K, N):
+    """64 columns and more: the blocks are dequantised to f16 once and the tcgen05 GEMM runs
+    (one pass over W instead of one per 16 columns).  Oracle on sampled rows, every column."""
+    g = synth.rng(700 + M + K + N)
+    blocks = synth.q4k_blocks(g, M, K)
+    x = synth.f32_acts(g, N, K)
+    y = _run(dev, blocks, x, y_pad=1)
+    rows = np.unique(np.concatenate([g.choice(M, size=min(M, 40), replace=False), [0, M - 1]]))
+    assert np.isfinite(y).all()
+    assert oracle.rel_err(y[:, rows], oracle.mul_mat_q4k(np.ascontiguousarray(blocks[rows]), x)) <= TOL

@@ -34,11 +34,40 @@ def _run(dev, blocks, x, y_pad=0):
 def test_dequant_bit_identical_to_gguf(dev, golden):
     f = golden("q6k_gguf.npz")
     blocks, K = f["blocks"], int(f["K"])
-    x = np.eye(K, dtype=np.float32)                  # column n = one-hot at k = n
-    y = _run(dev, blocks, x, y_pad=1)                # y[n, m] = w[m, n]
+    eye = np.eye(K, dtype=np.float32)                # column n = one-hot at k = n
     want = f["dequant"].T
-    # exact equality (a zero weight may come out as +0 where the decoder gives -0)
-    assert (y == want).all()
+    # decode-sized calls (32 columns at a time): the weights enter the MMAs exactly, so
+    # y[n, m] = w[m, n] bit for bit (a zero weight may come out as +0 where the decoder gives -0)
+    for n0 in range(0, K, 32):
+        y = _run(dev, blocks, eye[n0:n0 + 32], y_pad=1)
+        assert (y == want[n0:n0 + 32]).all()
+
+
+def _f16_row_image(dq, d_bound):
+    """What the prefill path stores for one row: f16(RNE) of w 2^-e, times 2^e, with e the
+    smallest exponent that brings the row's bound within 65504."""
+    import math
+    e = 0
+    if d_bound > 65504.0:
+        f, e = math.frexp(d_bound / 65504.0)
+        e = e - 1 if f == 0.5 else e
+    return (np.ldexp(dq, -e).astype(np.float16).astype(np.float32) * np.float32(2.0 ** e)).astype(np.float32)
+
+
+def test_prefill_dequant_is_f16_rounding_of_gguf(dev, golden):
+    """Prefill sizes (N = K = 512 here) dequantise to f16 once: with a one-hot X the GEMM
+    returns the stored f16 weights, which must be the RNE roundings of the decoder's f32
+    weights -- after a power-of-two row scale where |d| 4096 exceeds the f16 range (the
+    golden blocks include d = 65504)."""
+    f = golden("q6k_gguf.npz")
+    blocks, K = f["blocks"], int(f["K"])
+    y = _run(dev, blocks, np.eye(K, dtype=np.float32), y_pad=1)
+    dq = f["dequant"].astype(np.float32)
+    nb = K // 256
+    for m in range(blocks.shape[0]):
+        d = blocks[m].reshape(nb, 210)[:, 208:210].copy().view(np.float16).astype(np.float32).ravel()
+        want = _f16_row_image(dq[m], float(np.abs(d).max()) * 4096.0)
+        assert (y[:, m] == want).all(), m
 
 
 @pytest.mark.parametrize("MK", [(4096, 4096), (14336, 4096), (4096, 14336)])
@@ -104,3 +133,16 @@ def test_q6k_through_hook(dev):
     d = mlz_b200.tensor_view(y, mlz_b200.TYPE_F32)
     assert mlz_b200.ggml_simd_try_mul_mat(s0, s1, d, 0, 1) == 1
     assert oracle.rel_err(y, oracle.mul_mat_q6k(w, x)) <= TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1001, 2304, 100), (37, 768, 65)])
+def test_prefill_sizes_dequant_then_gemm(dev, M, K, N):
+    """64 columns and more: dequantised to f16 once (odd block counts: rows 2-byte aligned),
+    then the tcgen05 GEMM.  Oracle on sampled rows, every column."""
+    g = synth.rng(9700 + M + K + N)
+    blocks = synth.q6k_blocks(g, M, K)
+    x = synth.f32_acts(g, N, K)
+    y = _run(dev, blocks, x, y_pad=1)
+    rows = np.unique(np.concatenate([g.choice(M, size=min(M, 40), replace=False), [0, M - 1]]))
+    assert np.isfinite(y).all()
+    assert oracle.rel_err(y[:, rows], oracle.mul_mat_q6k(np.ascontiguousarray(blocks[rows]), x)) <= TOL
