@@ -105,8 +105,8 @@ size_t q6k_i8_workspace_bytes(int64_t K, int64_t N);
 int launch_q6k_i8(const DeviceCtx* c, const void* w, size_t w_row_bytes, int64_t M, int64_t K, const float* x,
                   size_t x_col_bytes, int64_t N, float* y, size_t y_col_bytes, void* ws, size_t ws_bytes,
                   cudaStream_t s);
-// Q4_K / Q6_K with at least kQuantGemmMinN columns: the rows dequantised to f16 in the
-// workspace (read once), then the tcgen05 F16 GEMM (dequant.cu).
+// Q4_K / Q6_K with at least kQuantGemmMinN columns and 4 M weights: the rows dequantised to
+// f16 in the workspace (read once), then the tcgen05 F16 GEMM (dequant.cu).
 constexpr int64_t kQuantGemmMinN = 64;
 bool quant_gemm_applicable(int w_type, int64_t M, int64_t K, int64_t N);
 size_t quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N);

@@ -70,8 +70,9 @@ def test_q4k_workspace_follows_the_dispatch():
             pad = 8 if N <= 8 else (N + 15) // 16 * 16
             assert ws(4096, K, N) >= pad * (K // 256) * (512 + 32)
     for N in (64, 256):
-        for K in (256, 4096, 14336):
-            # prefill sizes: the rows dequantised to f16 (2 B per weight) + the GEMM's share
+        for K in (1024, 4096, 14336):
+            # prefill sizes of matrices of >= 4 M weights: the rows dequantised to f16 (2 B per
+            # weight) + the GEMM's share
             assert ws(4096, K, N) >= 4096 * K * 2
             assert mlz_b200.mul_mat_workspace_bytes(mlz_b200.TYPE_Q6_K, 4096, K, N) >= 4096 * K * 2
 

@@ -57,10 +57,12 @@ def test_prefill_dequant_is_f16_rounding_of_gguf(dev, golden):
     import math
     f = golden("q4k_gguf.npz")
     blocks, K = f["blocks"], int(f["K"])
-    y = _run(dev, blocks, np.eye(K, dtype=np.float32), y_pad=1)
+    rep = 1366   # the golden rows tiled to 8196 x 512: over the 4 M weights the path needs
+    y = _run(dev, np.tile(blocks, (rep, 1)), np.eye(K, dtype=np.float32), y_pad=1)
     dq = f["dequant"].astype(np.float32)
     nb = K // 256
     for m in range(blocks.shape[0]):
+        assert all((y[:, m + 6 * i] == y[:, m]).all() for i in (1, rep // 2, rep - 1))
         hdr = blocks[m].reshape(nb, 144)[:, 0:4].copy().view(np.float16).astype(np.float32)
         bound = float((np.abs(hdr[:, 0]) * 945.0 + np.abs(hdr[:, 1]) * 63.0).max())
         e = 0
@@ -156,7 +158,7 @@ def test_power_of_two_scaling_is_exact_full_size(dev, MK, B):
     assert torch.equal(y2, y), "repeat is bitwise identical"
 
 
-@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1000, 2304, 100), (37, 768, 65),
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1000, 2304, 100), (37, 768, 65), (1001, 4352, 100),
                                    (4096, 14336, 128)])
 def test_prefill_sizes_dequant_then_gemm(dev, M, K, N):
     """64 columns and more: the blocks are dequantised to f16 once and the tcgen05 GEMM runs

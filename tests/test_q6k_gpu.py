@@ -61,10 +61,12 @@ def test_prefill_dequant_is_f16_rounding_of_gguf(dev, golden):
     golden blocks include d = 65504)."""
     f = golden("q6k_gguf.npz")
     blocks, K = f["blocks"], int(f["K"])
-    y = _run(dev, blocks, np.eye(K, dtype=np.float32), y_pad=1)
+    rep = 1366   # the golden rows tiled to 8196 x 512: over the 4 M weights the path needs
+    y = _run(dev, np.tile(blocks, (rep, 1)), np.eye(K, dtype=np.float32), y_pad=1)
     dq = f["dequant"].astype(np.float32)
     nb = K // 256
     for m in range(blocks.shape[0]):
+        assert all((y[:, m + 6 * i] == y[:, m]).all() for i in (1, rep // 2, rep - 1))
         d = blocks[m].reshape(nb, 210)[:, 208:210].copy().view(np.float16).astype(np.float32).ravel()
         want = _f16_row_image(dq[m], float(np.abs(d).max()) * 4096.0)
         assert (y[:, m] == want).all(), m
@@ -135,7 +137,7 @@ def test_q6k_through_hook(dev):
     assert oracle.rel_err(y, oracle.mul_mat_q6k(w, x)) <= TOL
 
 
-@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1001, 2304, 100), (37, 768, 65)])
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 64), (14336, 4096, 256), (1001, 2304, 100), (37, 768, 65), (1001, 4352, 100)])
 def test_prefill_sizes_dequant_then_gemm(dev, M, K, N):
     """64 columns and more: dequantised to f16 once (odd block counts: rows 2-byte aligned),
     then the tcgen05 GEMM.  Oracle on sampled rows, every column."""
