@@ -17,7 +17,8 @@ Workloads (synthetic seeded inputs of the named shapes; random-init weights):
       GPU, the other c5 size on several)
   c6  Q6_K decode mul_mat on the Llama-3.1-8B shapes of c3, batch N (Q4_K_M files carry
       Q6_K tensors; the reference hook routes them with Q4_K)
-  c7  flash-attention decode of c4 over a Q8_0 KV cache
+  c7  flash-attention decode of c4 over a quantised KV cache (Q8_0; --kv-type q4_0, q4_1,
+      q5_0, q5_1 or iq4_nl for the other block types)
 
 A step is one pass of the hot path over one batch.  `value` is whole-job throughput with
 inputs resident in HBM; `e2e` is the same metric through the reference-facing plugin
@@ -65,7 +66,7 @@ NCU_TRAFFIC = {
 def traffic_of(cfg: str, n: int, w, world: int):
     """The committed capture's DRAM bytes for this workload's dominant call, or None: none for
     the pooled c2 calls, and the c5 captures hold one GPU's whole matrix, not a shard."""
-    if isinstance(w, C2) or (isinstance(w, C5) and world > 1):
+    if isinstance(w, C2) or (isinstance(w, C5) and world > 1) or (cfg == "c7" and C7_TYPE["kv"] != "q8_0"):
         return None
     return NCU_TRAFFIC.get((cfg, n))
 
@@ -89,6 +90,8 @@ def parse_args():
     ap.add_argument("--overlap", default="weights", choices=["off", "safe", "weights"],
                     help="launch overlap of consecutive kernels (mlzc_set_launch_overlap); 'weights' "
                          "is valid here because no kernel of any workload writes the weights")
+    ap.add_argument("--kv-type", default="q8_0", choices=sorted(C7_KV),
+                    help="c7: the KV-cache block type")
     ap.add_argument("--profile-run", action="store_true",
                     help="for ncu launch lists: no clock-sampling load loop, no e2e, no CPU leg "
                          "(launch order = warm-up steps, then the timed steps)")
@@ -96,6 +99,9 @@ def parse_args():
 
 
 DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 1, "c6": 4, "c7": 16}
+# c7's KV-cache block types: name -> ggml type id (block layouts in mlz_b200.synth.KV_QUANT)
+C7_KV = {"q8_0": 8, "q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "iq4_nl": 20}
+C7_TYPE = {"kv": "q8_0"}   # set from --kv-type
 DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32",
          "c7": "q8_0 kv / f32"}
 
@@ -113,7 +119,8 @@ def metric_name(cfg: str, n: int, world: int) -> str:
     if cfg == "c6":
         return f"decode Q6_K mul_mat GB/s (Llama-3.1-8B 4096x4096, 14336x4096, 4096x14336; batch {n})"
     if cfg == "c7":
-        return f"flash-attention decode GB/s (Q8_0 KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
+        kv = C7_TYPE["kv"].upper()
+        return f"flash-attention decode GB/s ({kv} KV, {n} seqs, L~U[512,8192], 32q/8kv heads, D=128)"
     return (f"sharded FFN mul_mat {'GB/s' if n == 1 else 'TFLOP/s'} (Llama-3-70B gate/up 28672x8192, "
             f"down 8192x28672, F16, N={n}, row-sharded over {world} GPU, all-gather of the slices)")
 
@@ -142,7 +149,8 @@ def workload_name(cfg: str, n: int, world: int) -> str:
     if cfg == "c6":
         return f"c6 Q6_K mul_mat Llama-3.1-8B shapes, batch {n}"
     if cfg == "c7":
-        return f"c7 FA decode GQA over a Q8_0 KV cache, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
+        kv = C7_TYPE["kv"].upper()
+        return f"c7 FA decode GQA over a {kv} KV cache, {n} sequences, sum L = {int(c4_lengths(n).sum())}"
     return f"c5 Llama-3-70B FFN, N={n}, row-sharded x{world}"
 
 
@@ -424,46 +432,59 @@ class C4(Workload):
 
 
 class C7(Workload):
-    """c4's batch and lengths over a Q8_0 KV cache (34-byte blocks of 32 values)."""
+    """c4's batch and lengths over a quantised KV cache (32-value blocks; Q8_0 by default,
+    --kv-type for the others)."""
     unit = "GB/s"
     bound = "hbm"
-    dtype = "q8_0 kv / f32"
 
     def roofline_kernel(self, j):
-        return "one flash-attention call: fa_quant_kernel<128, Q8_0> + fa_quant_combine_kernel"
+        return f"one flash-attention call: fa_quant_kernel<128, {C7_TYPE['kv'].upper()}> + fa_quant_combine_kernel"
 
     def __init__(self, n, dev, gen):
         import torch
         import mlz_b200
         from mlz_b200.ops import _nb
+        from mlz_b200 import synth
         self.B, self.Hq, self.Hkv, self.D = n, 32, 8, 128
         self.kv_len_np = c4_lengths(n)
         self.L = 8192
-        self.rb = self.D // 32 * 34
+        self.kv_type = C7_KV[C7_TYPE["kv"]]
+        self.dtype = f"{C7_TYPE['kv']} kv / f32"
+        self.bb, self.qmag, self.moff = synth.KV_QUANT[self.kv_type]
+        self.rb = self.D // 32 * self.bb
         s = 1.0 / math.sqrt(self.D)
         self.q = torch.randn((n, self.Hq, 1, self.D), generator=gen, device=dev) * s
         self.k = self._rows(gen, dev)
         self.v = self._rows(gen, dev)
         self.kv_len = torch.from_numpy(self.kv_len_np).to(dev)
         self.out = torch.empty((n, self.Hq, 1, self.D), dtype=torch.float32, device=dev)
-        desc = mlz_b200.make_fa_desc(self.q.data_ptr(), _nb(self.q, 4), self.k.data_ptr(), (34,) + _nb(self.k, 1)[1:],
-                                     self.v.data_ptr(), (34,) + _nb(self.v, 1)[1:], self.out.data_ptr(),
-                                     _nb(self.out, 4), (n, self.Hq, 1, self.Hkv, self.L, self.D), s,
-                                     kv_len_ptr=self.kv_len.data_ptr(), kv_type=mlz_b200.TYPE_Q8_0)
+        desc = mlz_b200.make_fa_desc(self.q.data_ptr(), _nb(self.q, 4), self.k.data_ptr(),
+                                     (self.bb,) + _nb(self.k, 1)[1:], self.v.data_ptr(), (self.bb,) + _nb(self.v, 1)[1:],
+                                     self.out.data_ptr(), _nb(self.out, 4), (n, self.Hq, 1, self.Hkv, self.L, self.D), s,
+                                     kv_len_ptr=self.kv_len.data_ptr(), kv_type=self.kv_type)
         self.ws = torch.empty(max(mlz_b200.flash_attn_workspace_bytes(desc), 1), dtype=torch.uint8, device=dev)
         self.metric = metric_name("c7", n, 1)
         self.config = {"workload": workload_name("c7", n, 1), "batch": n, "sum_kv_len": int(self.kv_len_np.sum()),
-                       "l2": "inputs larger than L2 (KV cache 285 MB)"}
+                       "kv_type": C7_TYPE["kv"],
+                       "l2": f"inputs larger than L2 (KV cache {2 * n * self.Hkv * self.L * self.rb / 1e6:.0f} MB)"}
 
     def _rows(self, gen, dev):
+        """Random quants; block scales d with the spread of N(0, 1)/sqrt(D) values; block
+        minima m = offset * d * (1 + N(0, 0.1)) for the types that carry one."""
         import torch
-        nb = self.D // 32
-        r = torch.randint(-127, 128, (self.B, self.Hkv, self.L, nb, 34), generator=gen, device=dev,
-                          dtype=torch.int16).to(torch.int8).view(torch.uint8)
-        d = (torch.randn((self.B, self.Hkv, self.L, nb, 1), generator=gen, device=dev).abs() /
-             (64.0 * math.sqrt(self.D))).to(torch.float16)
-        r[..., 0:2] = d.view(torch.uint8)
-        return r.reshape(self.B, self.Hkv, self.L, nb * 34)
+        nb, bb = self.D // 32, self.bb
+        shape = (self.B, self.Hkv, self.L, nb)
+        if self.kv_type == 8:
+            r = torch.randint(-127, 128, shape + (bb,), generator=gen, device=dev,
+                              dtype=torch.int16).to(torch.int8).view(torch.uint8)
+        else:
+            r = torch.randint(0, 256, shape + (bb,), generator=gen, device=dev, dtype=torch.int16).to(torch.uint8)
+        d = torch.randn(shape + (1,), generator=gen, device=dev).abs() / (self.qmag * math.sqrt(self.D))
+        r[..., 0:2] = d.to(torch.float16).view(torch.uint8)
+        if self.moff is not None:
+            jit = 1.0 + 0.1 * torch.randn(shape + (1,), generator=gen, device=dev)
+            r[..., 2:4] = (self.moff * d * jit).to(torch.float16).view(torch.uint8)
+        return r.reshape(self.B, self.Hkv, self.L, nb * bb)
 
     def work_units(self):
         return 2 * self.Hkv * self.rb * float(self.kv_len_np.sum()) + 2 * self.B * self.Hq * self.D * 4
@@ -471,7 +492,7 @@ class C7(Workload):
     def launches(self, i):
         import mlz_b200
         return [(lambda: mlz_b200.flash_attn_dispatch_quant(self.q, self.k, self.v, 1.0 / math.sqrt(self.D),
-                                                            mlz_b200.TYPE_Q8_0, kv_len=self.kv_len, out=self.out,
+                                                            self.kv_type, kv_len=self.kv_len, out=self.out,
                                                             workspace=self.ws),
                  self.work_units())]
 
@@ -616,11 +637,12 @@ class CpuStep:
             self.kv_type = 1
             self.row_bytes = 256
             if cfg == "c7":
-                self.kv_type = 8
-                self.row_bytes = 136
-                self.k = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, 8)
-                self.v = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, 8)
-            self.what = "FA2 skeleton restatement" + (" (Q8_0 K/V dequantised per row)" if cfg == "c7" else "")
+                self.kv_type = C7_KV[C7_TYPE["kv"]]
+                self.row_bytes = 4 * synth.KV_QUANT[self.kv_type][0]
+                self.k = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, self.kv_type)
+                self.v = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, self.kv_type)
+            kv = C7_TYPE["kv"].upper()
+            self.what = "FA2 skeleton restatement" + (f" ({kv} K/V dequantised per row)" if cfg == "c7" else "")
         else:
             raise ValueError(cfg)
 
@@ -708,7 +730,7 @@ def reference_arm(a):
     line = {
         "impl": "reference", "metric": metric_name(a.config, n, world), "value": value, "unit": unit,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * wall / max(a.steps, 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE[a.config],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE[a.config] if a.config != "c7" else f"{C7_TYPE['kv']} kv / f32",
         "data": "synthetic (seeded), random-init weights",
         "config": {"workload": workload_name(a.config, n, world),
                    "implementation": "CPU restatement of the reference kernels (oracle/) on the host cores"},
@@ -1131,6 +1153,7 @@ def run_e2e(w, a, world, value_dev):
 
 def main():
     a = parse_args()
+    C7_TYPE["kv"] = a.kv_type
     if a.impl == "reference":
         reference_arm(a)
     else:

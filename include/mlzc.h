@@ -52,9 +52,10 @@ enum mlzc_status {
     MLZC_ERR_COMM = -6          /* NCCL failure or timeout */
 };
 
+/* ggml type ids (GGML_TYPE_*); Q4_1, Q5_0, Q5_1 and IQ4_NL are used as KV-cache types only. */
 enum mlzc_type {
-    MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_0 = 2, MLZC_TYPE_Q8_0 = 8,
-    MLZC_TYPE_Q4_K = 12, MLZC_TYPE_Q6_K = 14
+    MLZC_TYPE_F32 = 0, MLZC_TYPE_F16 = 1, MLZC_TYPE_Q4_0 = 2, MLZC_TYPE_Q4_1 = 3, MLZC_TYPE_Q5_0 = 6,
+    MLZC_TYPE_Q5_1 = 7, MLZC_TYPE_Q8_0 = 8, MLZC_TYPE_Q4_K = 12, MLZC_TYPE_Q6_K = 14, MLZC_TYPE_IQ4_NL = 20
 };
 
 /* Attention mode bits; same values as FA_MODE_* (src/simd/flash_attention.h:43-49). */
@@ -162,7 +163,7 @@ typedef struct {
     const float* mask;
     float* dst;
     size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
-    int32_t k_type, v_type;   /* both F16, both Q8_0 or both Q4_0 */
+    int32_t k_type, v_type;   /* both F16, or both one quantised KV type (Q8_0 Q4_0 Q4_1 Q5_0 Q5_1 IQ4_NL) */
     const int32_t* kv_len;    /* NULL or batch_size entries (device memory for _dev) */
 } mlzc_fa_desc;
 
@@ -175,10 +176,13 @@ int mlzc_flash_attn_workspace_bytes(const mlzc_fa_desc* desc, size_t* out_bytes)
  * skeleton flash_attn_fa2_skeleton_avx512.inc:394-842).
  * Requirements: DK == DV in {64, 128, 256}; contiguous f16 K/V rows whose strides
  * (nb[1..3]) are multiples of 16 bytes; contiguous, 16-byte aligned f32 q rows.
- * Quantised KV cache (the Q8_0 and Q4_0 branches of flash_attn_dispatch,
- * flash_attention.cpp:112-248): K and V rows of 34-byte Q8_0 or 18-byte Q4_0 blocks
- * (nb[0] = the block size, as ggml sets it), 4-byte aligned with 4-byte multiple strides;
- * element = f16 d * int8 q (Q8_0) or f16 d * (nibble - 8) (Q4_0). */
+ * Quantised KV cache (the Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 and IQ4_NL branches of
+ * flash_attn_dispatch, flash_attention.cpp:112-248 -> simd_flash_attn_<type>_avx512,
+ * kernels/x86/flash/flash_attn_<type>_avx512.asm): K and V rows of 32-value blocks in the
+ * GGUF layouts (nb[0] = the block size, as ggml sets it), 4-byte aligned with 4-byte
+ * multiple strides.  Element: Q8_0 (34 B) f16 d * int8 q; Q4_0 (18 B) d * (nibble - 8);
+ * Q4_1 (20 B) d * nibble + f16 m; Q5_0 (22 B) d * (q5 - 16); Q5_1 (24 B) d * q5 + m, q5 the
+ * nibble with its fifth bit from the block's 32-bit qh; IQ4_NL (18 B) d * table[nibble]. */
 int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t workspace_bytes,
                         void* stream);
 

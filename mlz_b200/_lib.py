@@ -18,6 +18,7 @@ STATUS_NAMES = {
 }
 TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 12, 14
 TYPE_Q4_0, TYPE_Q8_0 = 2, 8
+TYPE_Q4_1, TYPE_Q5_0, TYPE_Q5_1, TYPE_IQ4_NL = 3, 6, 7, 20   # quantised KV-cache types
 FA_MODE_GQA_BATCH, FA_MODE_ALIBI, FA_MODE_SOFTCAP = 0x04, 0x08, 0x10
 OVERLAP_OFF, OVERLAP_SAFE, OVERLAP_WEIGHTS = 0, 1, 2
 UNIQUE_ID_BYTES = 128

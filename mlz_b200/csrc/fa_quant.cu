@@ -69,16 +69,46 @@ using ptx::mma16816;
 using ptx::movtrans;
 using ptx::split_h2;
 
+// Block layouts (ggml type ids; 32 values per block, GGUF element order: value i < 16 in
+// the low nibble of quant byte i, value i >= 16 in the high nibble of byte i - 16; Q5_x:
+// bit i of the 32-bit qh is value i's fifth bit).  kQs / kQh: byte offsets of the quants and
+// of qh (-1: none); kMin: a block minimum m (f16 at offset 2) is added to every value.
 template <int TYPE>
 struct KvFormat;
 template <>
-struct KvFormat<8> {   // Q8_0: f16 d, 32 int8
-    static constexpr int kBlockBytes = 34;
+struct KvFormat<8> {   // Q8_0: f16 d, 32 int8; d * q
+    static constexpr int kBlockBytes = 34, kQs = 2, kQh = -1;
+    static constexpr bool kMin = false;
 };
 template <>
-struct KvFormat<2> {   // Q4_0: f16 d, 16 bytes of nibbles (values 0-15 low, 16-31 high)
-    static constexpr int kBlockBytes = 18;
+struct KvFormat<2> {   // Q4_0: f16 d, 16 bytes of nibbles; d * (q - 8)
+    static constexpr int kBlockBytes = 18, kQs = 2, kQh = -1;
+    static constexpr bool kMin = false;
 };
+template <>
+struct KvFormat<3> {   // Q4_1: f16 d, f16 m, 16 bytes of nibbles; d * q + m
+    static constexpr int kBlockBytes = 20, kQs = 4, kQh = -1;
+    static constexpr bool kMin = true;
+};
+template <>
+struct KvFormat<6> {   // Q5_0: f16 d, u32 qh, 16 bytes of nibbles; d * (q5 - 16)
+    static constexpr int kBlockBytes = 22, kQs = 6, kQh = 2;
+    static constexpr bool kMin = false;
+};
+template <>
+struct KvFormat<7> {   // Q5_1: f16 d, f16 m, u32 qh, 16 bytes of nibbles; d * q5 + m
+    static constexpr int kBlockBytes = 24, kQs = 8, kQh = 4;
+    static constexpr bool kMin = true;
+};
+template <>
+struct KvFormat<20> {  // IQ4_NL: f16 d, 16 bytes of 4-bit codes; d * kIq4nl[q]
+    static constexpr int kBlockBytes = 18, kQs = 2, kQh = -1;
+    static constexpr bool kMin = false;
+};
+
+// IQ4_NL's non-linear code book (the GGUF table, the LUT of
+// kernels/x86/flash/flash_attn_iq4_nl_avx512.asm:34-35).
+__constant__ int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
 constexpr int kQStages = 2;
 
@@ -102,20 +132,38 @@ __device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t x) {
     const uint32_t u = __byte_perm(x ^ 0x8080u, 0x6464u, 0x5140u);
     return h2_bits(__hsub2(bits_h2(u), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480))));
 }
-// Two nibbles (low nibbles of bytes 0, 1 of x when HI = false, high nibbles when true) ->
-// exact f16 pair (nibble - 8).
-template <bool HI>
-__device__ __forceinline__ uint32_t nib2_to_h2(uint32_t x) {
-    const uint32_t u = __byte_perm(x, 0x6464u, 0x5140u);
+// A nibble pair in f16 form -- u = (byte0, 0x64, byte1, 0x64) as two halves, from one key's
+// u16 load (prmt) or from two keys' (pair_cols) -- plus the pair's fifth bits already placed
+// (hb: bits 4 / 20 for low nibbles, 8 / 24 for high ones; 0 for 4-bit types) -> the exact
+// f16 pair of the type's integer values: q - 8 (Q4_0), q (Q4_1, Q5_1 with its fifth bit),
+// q5 - 16 (Q5_0).  Low nibbles read as 1024 + q, high ones as 1024 + 16 q.
+template <int TYPE, bool HI>
+__device__ __forceinline__ uint32_t nib_to_h2(uint32_t u, uint32_t hb) {
     if constexpr (!HI) {
-        return h2_bits(__hsub2(bits_h2(u & 0xFF0FFF0Fu), __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408))));
+        constexpr unsigned short kSub = TYPE == 2 ? 0x6408 : (TYPE == 6 ? 0x6410 : 0x6400);   // 1032 / 1040 / 1024
+        const __half2 k = __halves2half2(__ushort_as_half(kSub), __ushort_as_half(kSub));
+        return h2_bits(__hsub2(bits_h2((u & 0xFF0FFF0Fu) | hb), k));
     } else {
-        // 1024 + 16 q -> q - 8
-        const __half2 k = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));      // 1/16
-        const __half2 c = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));      // -72
-        return h2_bits(__hfma2(bits_h2(u & 0xFFF0FFF0u), k, c));
+        constexpr unsigned short kAdd = TYPE == 2 ? 0xD480 : (TYPE == 6 ? 0xD500 : 0xD400);   // -72 / -80 / -64
+        const __half2 k = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));   // 1/16
+        const __half2 c = __halves2half2(__ushort_as_half(kAdd), __ushort_as_half(kAdd));
+        return h2_bits(__hfma2(bits_h2((u & 0xFFF0FFF0u) | hb), k, c));
     }
 }
+// Fifth bits of a pair: bit s0 of x to bit t, bit s1 of y to bit t + 16.
+__device__ __forceinline__ uint32_t bits2(uint32_t x, int s0, uint32_t y, int s1, int t) {
+    return (((x >> s0) & 1u) << t) | (((y >> s1) & 1u) << (t + 16));
+}
+// The 32-bit qh of a block at a 2-byte-aligned shared address.
+__device__ __forceinline__ uint32_t lds_qh(uint32_t a) { return __byte_perm(lds_u16(a), lds_u16(a + 2), 0x5410); }
+// IQ4_NL: the f16 pair (value of the low nibble, value of the high nibble) of byte x, from
+// the 256-entry table at shared address tab.
+__device__ __forceinline__ uint32_t iq4_byte(uint32_t tab, uint32_t x) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(tab + 4 * x));
+    return v;
+}
+
 // Column pair (bytes 0 of a and b) and (bytes 1 of a and b) of two keys' u16 loads.
 __device__ __forceinline__ void pair_cols(uint32_t a, uint32_t b, uint32_t& c0, uint32_t& c1) {
     const uint32_t z = __byte_perm(a, b, 0x5410u);   // a.b0 a.b1 b.b0 b.b1
@@ -169,11 +217,15 @@ fa_quant_kernel(const FaqParams p) {
     constexpr uint32_t kTileBytes = kQTile * RB;
     extern __shared__ __align__(16) unsigned char fq_smem[];
     // [stage][K, V] raw tiles (the merge area [4 warps][8 rows][D + 2] once they are done),
-    // then the Q^T fragment table [KS][32 lanes] x uint4 (hi0, hi1, lo0, lo1)
+    // then the Q^T fragment table [KS][32 lanes] x uint4 (hi0, hi1, lo0, lo1), the block sums
+    // of the scaled query rows [NB][8] (types with a block minimum) and the IQ4_NL byte table
     constexpr uint32_t kRing = kQStages * 2 * kTileBytes;
     constexpr uint32_t kMerge = 4 * kQRows * (D + 2) * 4;
+    constexpr uint32_t kQtabOff = kRing > kMerge ? kRing : kMerge;
     const uint32_t ring = ptx::smem_u32(fq_smem);
-    uint4* qtab = reinterpret_cast<uint4*>(fq_smem + (kRing > kMerge ? kRing : kMerge));
+    uint4* qtab = reinterpret_cast<uint4*>(fq_smem + kQtabOff);
+    float* qsum = reinterpret_cast<float*>(fq_smem + kQtabOff + KS * 32 * 16);
+    uint32_t* iqtab = reinterpret_cast<uint32_t*>(fq_smem + kQtabOff + KS * 32 * 16 + 256);
     float* mrg = reinterpret_cast<float*>(fq_smem);   // after the last tile (ring drained)
 
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31, g = lane >> 2, q4 = lane & 3;
@@ -228,6 +280,27 @@ fa_quant_kernel(const FaqParams p) {
         split_h2(x[2], x[3], f.y, f.w);
         qtab[e] = f;
     }
+    if constexpr (F::kMin) {
+        // sum over each block's 32 dims of the scaled query: the block minimum m adds
+        // m * sum to a score (value = d q + m)
+        for (int e = t; e < NB * kQRows; e += kQThreads) {
+            const int b = e / kQRows, gr = e % kQRows;
+            float sum = 0.0f;
+            if (gr < nrows) {
+                const int rr = r0 + gr, iq = rr / p.G, ihq = head_base + rr % p.G;
+                const float* qr = reinterpret_cast<const float*>(p.q + iq * p.q_nb1 + ihq * p.q_nb2 + ib * p.q_nb3);
+                for (int d = 32 * b; d < 32 * b + 32; ++d) sum += ptx::ld_act(qr + d) * p.scale;
+            }
+            qsum[e] = sum;
+        }
+    }
+    if constexpr (TYPE == 20) {
+        // byte x -> f16 pair (code book value of its low nibble, of its high nibble)
+        for (int x = t; x < 256; x += kQThreads)
+            iqtab[x] = (uint32_t)__half_as_ushort(__float2half_rn((float)kIq4nl[x & 15])) |
+                       ((uint32_t)__half_as_ushort(__float2half_rn((float)kIq4nl[x >> 4])) << 16);
+    }
+    const uint32_t iqtab_u = ptx::smem_u32(iqtab);
     // per-lane row state: rows 2 q4 and 2 q4 + 1
     int iq_r[2], ihq_r[2];
     bool row_ok[2];
@@ -246,6 +319,11 @@ fa_quant_kernel(const FaqParams p) {
     float o[KS][4];
 #pragma unroll
     for (int d = 0; d < KS; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+    // block-minimum part of O (sum over this lane's keys of p * m per block and row; its
+    // lanes' sums are joined into o at the end)
+    float macc[F::kMin ? NB : 1][2];
+#pragma unroll
+    for (int b = 0; b < (F::kMin ? NB : 1); ++b) macc[b][0] = macc[b][1] = 0.0f;
     const int kw = warp * 16;
     const uint32_t qtab_u = ptx::smem_u32(qtab) + (uint32_t)lane * 16;
 
@@ -263,7 +341,7 @@ fa_quant_kernel(const FaqParams p) {
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
             float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t o0 = kr0 + b * F::kBlockBytes + 2, o1 = kr1 + b * F::kBlockBytes + 2;
+            const uint32_t o0 = kr0 + b * F::kBlockBytes + F::kQs, o1 = kr1 + b * F::kBlockBytes + F::kQs;
             if constexpr (TYPE == 8) {
 #pragma unroll
                 for (int st = 0; st < 2; ++st) {
@@ -276,21 +354,45 @@ fa_quant_kernel(const FaqParams p) {
                     mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
                 }
             } else {
-                const uint32_t w0 = lds_u16(o0 + 2 * q4), w1 = lds_u16(o1 + 2 * q4);
-                const uint32_t w2 = lds_u16(o0 + 2 * q4 + 8), w3 = lds_u16(o1 + 2 * q4 + 8);
+                // nibble types: low nibbles are dims 0-15 of the block, high nibbles dims 16-31;
+                // w0 / w2: key g, bytes 2 q4 (+1) / 2 q4 + 8 (+9); w1 / w3: key g + 8
+                const uint32_t w[4] = {lds_u16(o0 + 2 * q4), lds_u16(o1 + 2 * q4), lds_u16(o0 + 2 * q4 + 8),
+                                       lds_u16(o1 + 2 * q4 + 8)};
+                uint32_t lo[4], hi[4];
+                if constexpr (TYPE == 20) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t t0 = iq4_byte(iqtab_u, w[k] & 0xFFu), t1 = iq4_byte(iqtab_u, w[k] >> 8);
+                        lo[k] = __byte_perm(t0, t1, 0x5410u);
+                        hi[k] = __byte_perm(t0, t1, 0x7632u);
+                    }
+                } else {
+                    uint32_t hl[4] = {0u, 0u, 0u, 0u}, hh[4] = {0u, 0u, 0u, 0u};
+                    if constexpr (F::kQh >= 0) {
+                        // fifth bits of this lane's values: bits 2 q4 + {0, 1, 8, 9, 16, 17, 24, 25}
+                        const uint32_t h0 = lds_qh(kr0 + b * F::kBlockBytes + F::kQh) >> (2 * q4);
+                        const uint32_t h1 = lds_qh(kr1 + b * F::kBlockBytes + F::kQh) >> (2 * q4);
+                        hl[0] = bits2(h0, 0, h0, 1, 4); hl[1] = bits2(h1, 0, h1, 1, 4);
+                        hl[2] = bits2(h0, 8, h0, 9, 4); hl[3] = bits2(h1, 8, h1, 9, 4);
+                        hh[0] = bits2(h0, 16, h0, 17, 8); hh[1] = bits2(h1, 16, h1, 17, 8);
+                        hh[2] = bits2(h0, 24, h0, 25, 8); hh[3] = bits2(h1, 24, h1, 25, 8);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t u = __byte_perm(w[k], 0x6464u, 0x5140u);
+                        lo[k] = nib_to_h2<TYPE, false>(u, hl[k]);
+                        hi[k] = nib_to_h2<TYPE, true>(u, hh[k]);
+                    }
+                }
                 {
                     const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b) * 512);
-                    const uint32_t a0 = nib2_to_h2<false>(w0), a1 = nib2_to_h2<false>(w1);
-                    const uint32_t a2 = nib2_to_h2<false>(w2), a3 = nib2_to_h2<false>(w3);
-                    mma16816(th, a0, a1, a2, a3, qf.x, qf.y);
-                    mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
+                    mma16816(th, lo[0], lo[1], lo[2], lo[3], qf.x, qf.y);
+                    mma16816(tl, lo[0], lo[1], lo[2], lo[3], qf.z, qf.w);
                 }
                 {
                     const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b + 1) * 512);
-                    const uint32_t a0 = nib2_to_h2<true>(w0), a1 = nib2_to_h2<true>(w1);
-                    const uint32_t a2 = nib2_to_h2<true>(w2), a3 = nib2_to_h2<true>(w3);
-                    mma16816(th, a0, a1, a2, a3, qf.x, qf.y);
-                    mma16816(tl, a0, a1, a2, a3, qf.z, qf.w);
+                    mma16816(th, hi[0], hi[1], hi[2], hi[3], qf.x, qf.y);
+                    mma16816(tl, hi[0], hi[1], hi[2], hi[3], qf.z, qf.w);
                 }
             }
             const float d0 = lds_f16(kr0 + b * F::kBlockBytes), d1 = lds_f16(kr1 + b * F::kBlockBytes);
@@ -298,6 +400,14 @@ fa_quant_kernel(const FaqParams p) {
             sacc[1] = fmaf(d0, th[1] + tl[1], sacc[1]);
             sacc[2] = fmaf(d1, th[2] + tl[2], sacc[2]);
             sacc[3] = fmaf(d1, th[3] + tl[3], sacc[3]);
+            if constexpr (F::kMin) {
+                const float m0 = lds_f16(kr0 + b * F::kBlockBytes + 2), m1 = lds_f16(kr1 + b * F::kBlockBytes + 2);
+                const float2 qs = *reinterpret_cast<const float2*>(qsum + b * kQRows + 2 * q4);   // rows 2 q4, + 1
+                sacc[0] = fmaf(m0, qs.x, sacc[0]);
+                sacc[1] = fmaf(m0, qs.y, sacc[1]);
+                sacc[2] = fmaf(m1, qs.x, sacc[2]);
+                sacc[3] = fmaf(m1, qs.y, sacc[3]);
+            }
         }
         // ---- mask / softcap / ALiBi / validity; element e: key g + 8 (e >> 1), row 2 q4 + (e & 1)
         float sc[4], tmax[2] = {-INFINITY, -INFINITY};
@@ -337,6 +447,10 @@ fa_quant_kernel(const FaqParams p) {
                 o[d][0] *= corr[0]; o[d][1] *= corr[1];
                 o[d][2] *= corr[0]; o[d][3] *= corr[1];
             }
+            if constexpr (F::kMin) {
+#pragma unroll
+                for (int b = 0; b < NB; ++b) { macc[b][0] *= corr[0]; macc[b][1] *= corr[1]; }
+            }
         }
         float pe[4];
 #pragma unroll
@@ -357,7 +471,7 @@ fa_quant_kernel(const FaqParams p) {
             split_h2(pe[0] * dv0, pe[1] * dv0, h0, l0);   // key g
             split_h2(pe[2] * dv8, pe[3] * dv8, h1, l1);   // key g + 8
             const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1), bl0 = movtrans(l0), bl1 = movtrans(l1);
-            const uint32_t base0 = vk0 + b * F::kBlockBytes + 2 + 2 * g, base8 = vk8 + b * F::kBlockBytes + 2 + 2 * g;
+            const uint32_t base0 = vk0 + b * F::kBlockBytes + F::kQs + 2 * g, base8 = vk8 + b * F::kBlockBytes + F::kQs + 2 * g;
             if constexpr (TYPE == 8) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
@@ -371,34 +485,72 @@ fa_quant_kernel(const FaqParams p) {
                     mma16816(o[2 * b + hf], a0, a1, a2, a3, bl0, bl1);
                 }
             } else {
-                uint32_t c00, c01, c80, c81;
-                pair_cols(lds_u16(base0), lds_u16(base0 + RB), c00, c01);
-                pair_cols(lds_u16(base8), lds_u16(base8 + RB), c80, c81);
-                const __half2 k8 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-                const __half2 k16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));
-                const __half2 c72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));
-                // low nibbles: dims 0-15 of the block
-                {
-                    const uint32_t a0 = h2_bits(__hsub2(bits_h2(c00 & 0xFF0FFF0Fu), k8));
-                    const uint32_t a1 = h2_bits(__hsub2(bits_h2(c01 & 0xFF0FFF0Fu), k8));
-                    const uint32_t a2 = h2_bits(__hsub2(bits_h2(c80 & 0xFF0FFF0Fu), k8));
-                    const uint32_t a3 = h2_bits(__hsub2(bits_h2(c81 & 0xFF0FFF0Fu), k8));
-                    mma16816(o[2 * b], a0, a1, a2, a3, bh0, bh1);
-                    mma16816(o[2 * b], a0, a1, a2, a3, bl0, bl1);
+                // fragments (dims 2 g | 2 g + 1 of keys 2 q4, 2 q4 + 1 | 2 q4 + 8, 2 q4 + 9):
+                // low nibbles -> o[2 b] (dims 0-15 of the block), high nibbles -> o[2 b + 1]
+                uint32_t lo[4], hi[4];
+                if constexpr (TYPE == 20) {
+                    const uint32_t x[4] = {lds_u16(base0), lds_u16(base0 + RB), lds_u16(base8), lds_u16(base8 + RB)};
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr) {
+                        const uint32_t a = x[2 * pr], c = x[2 * pr + 1];
+                        const uint32_t ta0 = iq4_byte(iqtab_u, a & 0xFFu), ta1 = iq4_byte(iqtab_u, a >> 8);
+                        const uint32_t tc0 = iq4_byte(iqtab_u, c & 0xFFu), tc1 = iq4_byte(iqtab_u, c >> 8);
+                        lo[2 * pr] = __byte_perm(ta0, tc0, 0x5410u);
+                        lo[2 * pr + 1] = __byte_perm(ta1, tc1, 0x5410u);
+                        hi[2 * pr] = __byte_perm(ta0, tc0, 0x7632u);
+                        hi[2 * pr + 1] = __byte_perm(ta1, tc1, 0x7632u);
+                    }
+                } else {
+                    uint32_t c[4];
+                    pair_cols(lds_u16(base0), lds_u16(base0 + RB), c[0], c[1]);
+                    pair_cols(lds_u16(base8), lds_u16(base8 + RB), c[2], c[3]);
+                    uint32_t hl[4] = {0u, 0u, 0u, 0u}, hh[4] = {0u, 0u, 0u, 0u};
+                    if constexpr (F::kQh >= 0) {
+                        // fifth bits 2 g, 2 g + 1 (low) and 16 + 2 g, 17 + 2 g (high) of the four keys
+                        const uint32_t qa = lds_qh(vk0 + b * F::kBlockBytes + F::kQh) >> (2 * g);
+                        const uint32_t qb = lds_qh(vk0 + RB + b * F::kBlockBytes + F::kQh) >> (2 * g);
+                        const uint32_t qc = lds_qh(vk8 + b * F::kBlockBytes + F::kQh) >> (2 * g);
+                        const uint32_t qd = lds_qh(vk8 + RB + b * F::kBlockBytes + F::kQh) >> (2 * g);
+                        hl[0] = bits2(qa, 0, qb, 0, 4); hl[1] = bits2(qa, 1, qb, 1, 4);
+                        hl[2] = bits2(qc, 0, qd, 0, 4); hl[3] = bits2(qc, 1, qd, 1, 4);
+                        hh[0] = bits2(qa, 16, qb, 16, 8); hh[1] = bits2(qa, 17, qb, 17, 8);
+                        hh[2] = bits2(qc, 16, qd, 16, 8); hh[3] = bits2(qc, 17, qd, 17, 8);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        lo[k] = nib_to_h2<TYPE, false>(c[k], hl[k]);
+                        hi[k] = nib_to_h2<TYPE, true>(c[k], hh[k]);
+                    }
                 }
-                // high nibbles: dims 16-31
-                {
-                    const uint32_t a0 = h2_bits(__hfma2(bits_h2(c00 & 0xFFF0FFF0u), k16, c72));
-                    const uint32_t a1 = h2_bits(__hfma2(bits_h2(c01 & 0xFFF0FFF0u), k16, c72));
-                    const uint32_t a2 = h2_bits(__hfma2(bits_h2(c80 & 0xFFF0FFF0u), k16, c72));
-                    const uint32_t a3 = h2_bits(__hfma2(bits_h2(c81 & 0xFFF0FFF0u), k16, c72));
-                    mma16816(o[2 * b + 1], a0, a1, a2, a3, bh0, bh1);
-                    mma16816(o[2 * b + 1], a0, a1, a2, a3, bl0, bl1);
-                }
+                mma16816(o[2 * b], lo[0], lo[1], lo[2], lo[3], bh0, bh1);
+                mma16816(o[2 * b], lo[0], lo[1], lo[2], lo[3], bl0, bl1);
+                mma16816(o[2 * b + 1], hi[0], hi[1], hi[2], hi[3], bh0, bh1);
+                mma16816(o[2 * b + 1], hi[0], hi[1], hi[2], hi[3], bl0, bl1);
+            }
+            if constexpr (F::kMin) {
+                const float mv0 = lds_f16(vd0 + b * F::kBlockBytes + 2), mv8 = lds_f16(vd8 + b * F::kBlockBytes + 2);
+                macc[b][0] = fmaf(pe[0], mv0, fmaf(pe[2], mv8, macc[b][0]));
+                macc[b][1] = fmaf(pe[1], mv0, fmaf(pe[3], mv8, macc[b][1]));
             }
         }
     }
     cp_wait<0>();
+    if constexpr (F::kMin) {
+        // the block-minimum part: summed over the warp's keys (the lanes sharing q4), added to
+        // every dim of the block
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v = macc[b][h];
+                v += __shfl_xor_sync(0xffffffffu, v, 4);
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                o[2 * b][h] += v; o[2 * b][2 + h] += v;
+                o[2 * b + 1][h] += v; o[2 * b + 1][2 + h] += v;
+            }
+        }
+    }
     // ---- merge the four warps' states into one record per row
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -505,7 +657,8 @@ int faq_plan(const mlzc_fa_desc* d, int sm_count, FaqPlan* out) {
     const int RB = (int)fa_row_bytes(d->k_type, D);
     // the merge area of the four warps reuses the ring
     const size_t ring = (size_t)kQStages * 2 * kQTile * RB;
-    pl.smem = std::max(ring, (size_t)4 * kQRows * (D + 2) * 4) + (size_t)(D / 16) * 32 * 16;
+    // + the Q^T fragment table, the query block sums (256 bytes) and the IQ4_NL byte table (1 KB)
+    pl.smem = std::max(ring, (size_t)4 * kQRows * (D + 2) * 4) + (size_t)(D / 16) * 32 * 16 + 256 + 1024;
     pl.ws_bytes = (size_t)pl.slice * p.HR * p.splits * kQRows * (D + 2) * 4;
     *out = pl;
     return MLZC_OK;
@@ -597,10 +750,17 @@ int launch_flash_attn_quant(int sm_count, const mlzc_fa_desc* d, void* ws, size_
     for (int64_t b0 = 0; b0 < d->batch_size; b0 += pl.slice) {
         p.b_base = (int)b0;
         p.nB = (int)std::min<int64_t>(pl.slice, d->batch_size - b0);
-        if (d->k_type == MLZC_TYPE_Q8_0)
-            st = gen ? faq_dispatch<8, true>(pl, D, s) : faq_dispatch<8, false>(pl, D, s);
-        else
-            st = gen ? faq_dispatch<2, true>(pl, D, s) : faq_dispatch<2, false>(pl, D, s);
+        switch (d->k_type) {
+            case MLZC_TYPE_Q8_0: st = gen ? faq_dispatch<8, true>(pl, D, s) : faq_dispatch<8, false>(pl, D, s); break;
+            case MLZC_TYPE_Q4_0: st = gen ? faq_dispatch<2, true>(pl, D, s) : faq_dispatch<2, false>(pl, D, s); break;
+            case MLZC_TYPE_Q4_1: st = gen ? faq_dispatch<3, true>(pl, D, s) : faq_dispatch<3, false>(pl, D, s); break;
+            case MLZC_TYPE_Q5_0: st = gen ? faq_dispatch<6, true>(pl, D, s) : faq_dispatch<6, false>(pl, D, s); break;
+            case MLZC_TYPE_Q5_1: st = gen ? faq_dispatch<7, true>(pl, D, s) : faq_dispatch<7, false>(pl, D, s); break;
+            case MLZC_TYPE_IQ4_NL:
+                st = gen ? faq_dispatch<20, true>(pl, D, s) : faq_dispatch<20, false>(pl, D, s);
+                break;
+            default: return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V type %d", d->k_type);
+        }
         if (st != MLZC_OK) return st;
     }
     return MLZC_OK;

@@ -139,10 +139,21 @@ int fa_workspace_bytes(const mlzc_fa_desc* d, size_t* out);
 int faq_workspace_bytes(const mlzc_fa_desc* d, int sm_count, size_t* out);
 int launch_flash_attn_quant(int sm_count, const mlzc_fa_desc* d, void* ws, size_t ws_bytes, cudaStream_t s);
 // Bytes of one K or V row of head_dim values of ggml type `type` (F16, Q8_0, Q4_0).
+// Bytes of one 32-value block of a quantised KV-cache type (GGUF layouts), 0 for other types.
+inline size_t kv_block_bytes(int32_t type) {
+    switch (type) {
+        case MLZC_TYPE_Q8_0: return 34;
+        case MLZC_TYPE_Q4_0: return 18;
+        case MLZC_TYPE_Q4_1: return 20;
+        case MLZC_TYPE_Q5_0: return 22;
+        case MLZC_TYPE_Q5_1: return 24;
+        case MLZC_TYPE_IQ4_NL: return 18;
+        default: return 0;
+    }
+}
 inline size_t fa_row_bytes(int32_t type, int64_t head_dim) {
-    if (type == MLZC_TYPE_Q8_0) return (size_t)(head_dim / 32) * 34;
-    if (type == MLZC_TYPE_Q4_0) return (size_t)(head_dim / 32) * 18;
-    return (size_t)head_dim * 2;
+    const size_t bb = kv_block_bytes(type);
+    return bb ? (size_t)(head_dim / 32) * bb : (size_t)head_dim * 2;
 }
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
                       cudaStream_t s);

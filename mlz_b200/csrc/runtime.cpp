@@ -136,9 +136,10 @@ int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M,
 
 int check_fa_args(const mlzc_fa_desc* d) {
     if (!d) return fail(MLZC_ERR_INVALID, "flash_attn: null descriptor");
-    const bool quant = d->k_type == MLZC_TYPE_Q8_0 || d->k_type == MLZC_TYPE_Q4_0;
+    const bool quant = kv_block_bytes(d->k_type) != 0;
     if ((d->k_type != MLZC_TYPE_F16 && !quant) || d->v_type != d->k_type)
-        return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: K/V types %d/%d (F16/F16, Q8_0/Q8_0 or Q4_0/Q4_0)", d->k_type,
+        return fail(MLZC_ERR_UNSUPPORTED,
+                    "flash_attn: K/V types %d/%d (both F16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 or IQ4_NL)", d->k_type,
                     d->v_type);
     if (d->head_dim_k != d->head_dim_v) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: DK != DV");
     if (d->head_dim_k != 64 && d->head_dim_k != 128 && d->head_dim_k != 256)
@@ -153,7 +154,7 @@ int check_fa_args(const mlzc_fa_desc* d) {
         return fail(MLZC_ERR_INVALID, "flash_attn: q rows must be contiguous f32 on 16-byte boundaries");
     if (quant) {
         // rows of blocks (nb[0] = block bytes, ggml's convention), 4-byte aligned
-        const size_t bb = d->k_type == MLZC_TYPE_Q8_0 ? 34 : 18;
+        const size_t bb = kv_block_bytes(d->k_type);
         if ((uintptr_t)d->k % 4 || (uintptr_t)d->v % 4 || d->k_nb[1] % 4 || d->v_nb[1] % 4 || d->k_nb[2] % 4 ||
             d->v_nb[2] % 4 || d->k_nb[3] % 4 || d->v_nb[3] % 4 || d->k_nb[0] != bb || d->v_nb[0] != bb)
             return fail(MLZC_ERR_INVALID, "flash_attn: quantised K/V rows must be contiguous blocks on 4-byte boundaries");

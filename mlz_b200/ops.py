@@ -20,7 +20,8 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0,
+from ._lib import (FA_MODE_ALIBI, FA_MODE_SOFTCAP, TYPE_F16, TYPE_F32, TYPE_IQ4_NL, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q4_K,
+                   TYPE_Q5_0, TYPE_Q5_1, TYPE_Q6_K, TYPE_Q8_0,
                    FaDesc,
                    MlzcError, TensorView, check, lib)
 
@@ -118,8 +119,9 @@ def _nb(t, esz: int):
 def make_fa_desc(q_ptr, q_nb, k_ptr, k_nb, v_ptr, v_nb, dst_ptr, dst_nb, dims, scale,
                  mask_ptr=None, mask_nb=(0, 0, 0, 0), kv_len_ptr=None, softcap=0.0,
                  alibi=False, max_bias=0.0, kv_type=TYPE_F16) -> FaDesc:
-    """dims = (B, Hq, NQ, Hkv, NKV, D); kv_type: TYPE_F16, or TYPE_Q8_0 / TYPE_Q4_0 for a
-    quantised cache (k_nb / v_nb then in bytes with nb[0] = the block size)."""
+    """dims = (B, Hq, NQ, Hkv, NKV, D); kv_type: TYPE_F16, or a quantised cache type
+    (TYPE_Q8_0, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q5_0, TYPE_Q5_1, TYPE_IQ4_NL; k_nb / v_nb then
+    in bytes with nb[0] = the block size)."""
     B, Hq, NQ, Hkv, NKV, D = dims
     d = FaDesc()
     d.head_dim_k = d.head_dim_v = D
@@ -175,15 +177,17 @@ def flash_attn_dispatch(q, k, v, scale: float, *, kv_len=None, mask=None, softca
     return out
 
 
-KV_BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18}
+# bytes per 32-value block of each quantised KV-cache type (GGUF layouts)
+KV_BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_IQ4_NL: 18}
 
 
 def flash_attn_dispatch_quant(q, k, v, scale: float, kv_type: int, *, kv_len=None, mask=None,
                               softcap: float = 0.0, alibi: bool = False, out=None, workspace=None,
                               stream=None):
     """Flash-attention over a quantised KV cache on device tensors: q (B, Hq, NQ, D) f32;
-    k, v (B, Hkv, L, D/32*block_bytes) uint8 rows of Q8_0 (34-byte) or Q4_0 (18-byte)
-    blocks (any strides with contiguous rows).  Returns out (B, Hq, NQ, D) f32."""
+    k, v (B, Hkv, L, D/32*block_bytes) uint8 rows of blocks of kv_type (Q8_0 34 bytes, Q4_0
+    18, Q4_1 20, Q5_0 22, Q5_1 24, IQ4_NL 18; any strides with contiguous rows).  Returns
+    out (B, Hq, NQ, D) f32."""
     torch = _torch()
     B, Hq, NQ, D = q.shape
     _, Hkv, L, _ = k.shape

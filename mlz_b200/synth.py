@@ -69,18 +69,25 @@ def fa_inputs(g: np.random.Generator, B: int, Hq: int, Hkv: int, L: int, D: int,
     return q, k, v
 
 
-KV_QUANT = {8: (34, 64.0), 2: (18, 4.0)}   # ggml type -> (block bytes, typical |q|)
+# ggml type -> (block bytes, typical |value / d|, offset m / d or None): Q8_0, Q4_0, Q4_1,
+# Q5_0, Q5_1, IQ4_NL
+KV_QUANT = {8: (34, 64.0, None), 2: (18, 4.0, None), 3: (20, 4.0, -7.5), 6: (22, 8.0, None),
+            7: (24, 8.0, -15.5), 20: (18, 60.0, None)}
 
 
 def kv_quant_rows(g: np.random.Generator, shape, D: int, kv_type: int) -> np.ndarray:
-    """Quantised K/V rows (Q8_0 = 8 or Q4_0 = 2): uint8 array of shape + (D/32*block_bytes,),
-    random quants, block scales d = f16(|N(0, 1)| / (typical |q| * sqrt(D))) so that the
-    values have the spread of N(0, 1)/sqrt(D)."""
-    bb, qmag = KV_QUANT[kv_type]
+    """Quantised K/V rows of a KV-cache type of KV_QUANT: uint8 array of shape +
+    (D/32*block_bytes,), random quants (and fifth bits), block scales d = f16(|N(0, 1)| /
+    (typical |value / d| * sqrt(D))) so that the values have the spread of N(0, 1)/sqrt(D);
+    the types with a block minimum (Q4_1, Q5_1) get m = f16(offset * d * (1 + N(0, 0.1)))."""
+    bb, qmag, moff = KV_QUANT[kv_type]
     nb = D // 32
     rows = g.integers(0, 256, size=tuple(shape) + (nb, bb), dtype=np.uint8)
-    d = (np.abs(g.standard_normal(tuple(shape) + (nb, 1), dtype=np.float32)) / (qmag * np.sqrt(D))).astype(np.float16)
-    rows[..., 0:2] = d.view(np.uint8)
+    d32 = np.abs(g.standard_normal(tuple(shape) + (nb, 1), dtype=np.float32)) / (qmag * np.sqrt(D))
+    rows[..., 0:2] = d32.astype(np.float16).view(np.uint8)
+    if moff is not None:
+        jit = 1.0 + 0.1 * g.standard_normal(tuple(shape) + (nb, 1), dtype=np.float32)
+        rows[..., 2:4] = (moff * d32 * jit).astype(np.float16).view(np.uint8)
     return rows.reshape(tuple(shape) + (nb * bb,))
 
 

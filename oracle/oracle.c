@@ -360,31 +360,77 @@ typedef struct {
     float* dst;                     /* f32 */
     size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
     const int32_t* kv_len;          /* per batch element, NULL = n_kv for all */
-    int32_t kv_type;                /* K/V element type: 1 F16, 8 Q8_0, 2 Q4_0 (ggml ids) */
+    int32_t kv_type;                /* K/V element type (ggml ids): 1 F16, 8 Q8_0, 2 Q4_0, 3 Q4_1,
+                                       6 Q5_0, 7 Q5_1, 20 IQ4_NL */
 } ora_fa_t;
 
-/* Element d of a K or V row of type `type` as f32.
- *   F16  : the half at d.
- *   Q8_0 : 34-byte blocks of 32 values (f16 d, 32 int8 q); value d * q in f32 (the
- *          dequant of flash_attn_q8_0_avx512.asm:40-70 and of the gguf decoder).
- *   Q4_0 : 18-byte blocks of 32 values (f16 d, 16 bytes: value i < 16 in the low nibble of
- *          byte i, value i >= 16 in the high nibble of byte i - 16); value d * (q - 8) in f32
- *          (the gguf 0.19.0 decoder, gguf/quants.py Q4_0.dequantize_blocks). */
-static float ora_kv_elem(const char* row, int64_t d, int32_t type) {
-    if (type == 8) {
-        const char* b = row + (d / 32) * 34;
-        uint16_t h;
-        memcpy(&h, b, 2);
-        return ora_f16_to_f32(h) * (float)(int8_t)b[2 + d % 32];
+/* Bytes of one 32-value block of a quantised KV-cache type (ggml ids), 0 for F16. */
+static int64_t ora_kv_block_bytes(int32_t type) {
+    switch (type) {
+        case 8: return 34;   /* Q8_0   */
+        case 2: return 18;   /* Q4_0   */
+        case 3: return 20;   /* Q4_1   */
+        case 6: return 22;   /* Q5_0   */
+        case 7: return 24;   /* Q5_1   */
+        case 20: return 18;  /* IQ4_NL */
+        default: return 0;
     }
-    if (type == 2) {
-        const char* b = row + (d / 32) * 18;
-        uint16_t h;
-        memcpy(&h, b, 2);
-        const int i = (int)(d % 32);
-        const uint8_t byte = (uint8_t)b[2 + (i % 16)];
-        const int q = (i < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
-        return ora_f16_to_f32(h) * (float)q;
+}
+
+/* The 16 values of IQ4_NL's non-linear 4-bit code (the GGUF table, also the LUT of
+ * flash_attn_iq4_nl_avx512.asm:34-35). */
+static const int8_t ora_iq4nl_values[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                            1, 13, 25, 38, 53, 69, 89, 113};
+
+/* One 32-value block of a quantised KV row as f32, in the GGUF element order (value i < 16
+ * from the low nibble of quant byte i, value i >= 16 from the high nibble of byte i - 16;
+ * Q5_x: bit i of the 32-bit qh is value i's fifth bit).  Each value is formed in f32 as the
+ * gguf 0.19.0 decoders (gguf/quants.py) and the reference's DEQUANT_K_DOT_BLOCK macros form it:
+ *   Q8_0  (34 B: f16 d, 32 int8)              d * q
+ *   Q4_0  (18 B: f16 d, 16 B nibbles)         d * (q - 8)      flash_attn_q4_0_avx512.asm
+ *   Q4_1  (20 B: f16 d, f16 m, 16 B nibbles)  d * q + m        flash_attn_q4_1_avx512.asm:7-13
+ *   Q5_0  (22 B: f16 d, u32 qh, 16 B)         d * (q5 - 16)    flash_attn_q5_0_avx512.asm:9-15
+ *   Q5_1  (24 B: f16 d, f16 m, u32 qh, 16 B)  d * q5 + m       flash_attn_q5_1_avx512.asm:7-14
+ *   IQ4_NL (18 B: f16 d, 16 B nibbles)        d * table[q]     flash_attn_iq4_nl_avx512.asm:7-13
+ * (d * q is exact in f32, so d * q + m has one rounding whether or not it is fused.) */
+static void ora_kv_block(const unsigned char* blk, int32_t type, float* o) {
+    const float d = ora_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+    if (type == 8) {
+        for (int i = 0; i < 32; i++) o[i] = d * (float)(int8_t)blk[2 + i];
+        return;
+    }
+    float m = 0.0f;
+    const unsigned char* qs = blk + 2;
+    uint32_t qh = 0;
+    if (type == 3 || type == 7) {
+        m = ora_f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+        qs = blk + 4;
+    }
+    if (type == 6 || type == 7) {
+        const unsigned char* h = type == 6 ? blk + 2 : blk + 4;
+        qh = (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+        qs = h + 4;
+    }
+    for (int i = 0; i < 32; i++) {
+        const int q4 = i < 16 ? (qs[i] & 0x0F) : (qs[i - 16] >> 4);
+        const int q5 = q4 | (int)(((qh >> i) & 1u) << 4);
+        switch (type) {
+            case 2: o[i] = d * (float)(q4 - 8); break;
+            case 3: o[i] = d * (float)q4 + m; break;
+            case 6: o[i] = d * (float)(q5 - 16); break;
+            case 7: o[i] = d * (float)q5 + m; break;
+            default: o[i] = d * (float)ora_iq4nl_values[q4]; break;   /* 20: IQ4_NL */
+        }
+    }
+}
+
+/* Element d of a K or V row of type `type` (1 = F16, or a quantised type above) as f32. */
+static float ora_kv_elem(const char* row, int64_t d, int32_t type) {
+    const int64_t bb = ora_kv_block_bytes(type);
+    if (bb) {
+        float blk[32];
+        ora_kv_block((const unsigned char*)row + (d / 32) * bb, type, blk);
+        return blk[d % 32];
     }
     uint16_t h;
     memcpy(&h, row + 2 * d, 2);
@@ -394,21 +440,9 @@ static float ora_kv_elem(const char* row, int64_t d, int32_t type) {
 /* A whole K/V row of type `type` (dv values) as f32, block by block (the same products as
  * ora_kv_elem, so the same bits). */
 void ora_kv_row(const char* row, int64_t dv, int32_t type, float* out) {
-    if (type == 8 || type == 2) {
-        const int64_t bb = type == 8 ? 34 : 18;
-        for (int64_t b = 0; b < dv / 32; b++) {
-            const unsigned char* blk = (const unsigned char*)row + b * bb;
-            const float d = ora_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
-            float* o = out + 32 * b;
-            if (type == 8) {
-                for (int i = 0; i < 32; i++) o[i] = d * (float)(int8_t)blk[2 + i];
-            } else {
-                for (int i = 0; i < 16; i++) {
-                    o[i] = d * (float)((int)(blk[2 + i] & 0x0F) - 8);
-                    o[16 + i] = d * (float)((int)(blk[2 + i] >> 4) - 8);
-                }
-            }
-        }
+    const int64_t bb = ora_kv_block_bytes(type);
+    if (bb) {
+        for (int64_t b = 0; b < dv / 32; b++) ora_kv_block((const unsigned char*)row + b * bb, type, out + 32 * b);
         return;
     }
     for (int64_t d = 0; d < dv; d++) out[d] = ora_kv_elem(row, d, type);
@@ -428,6 +462,7 @@ void ora_flash_attn(const ora_fa_t* c) {
     const int64_t DK = c->head_dim_k, DV = c->head_dim_v;
     double* s = (double*)malloc(sizeof(double) * (size_t)(c->n_kv > 0 ? c->n_kv : 1));
     double* o = (double*)malloc(sizeof(double) * (size_t)DV);
+    float* row = (float*)malloc(sizeof(float) * (size_t)(DK > DV ? DK : DV));   /* one decoded K / V row */
     for (int64_t ib = 0; ib < c->batch_size; ib++) {
         const int64_t L = c->kv_len ? c->kv_len[ib] : c->n_kv;
         for (int64_t ihq = 0; ihq < c->n_head_q; ihq++) {
@@ -440,7 +475,8 @@ void ora_flash_attn(const ora_fa_t* c) {
                 for (int64_t j = 0; j < L; j++) {
                     const char* kr = (const char*)c->k + j * c->k_nb[1] + ihkv * c->k_nb[2] + ib * c->k_nb[3];
                     double dot = 0.0;
-                    for (int64_t d = 0; d < DK; d++) dot += (double)qr[d] * (double)ora_kv_elem(kr, d, c->kv_type);
+                    ora_kv_row(kr, DK, c->kv_type, row);
+                    for (int64_t d = 0; d < DK; d++) dot += (double)qr[d] * (double)row[d];
                     double sj = dot * (double)c->scale;
                     if (c->mask) {
                         sj += (double)*(const float*)((const char*)c->mask + iq * c->mask_nb[1] + j * c->mask_nb[0]);
@@ -457,7 +493,8 @@ void ora_flash_attn(const ora_fa_t* c) {
                         const double p = exp(s[j] - mx);
                         l += p;
                         const char* vr = (const char*)c->v + j * c->v_nb[1] + ihkv * c->v_nb[2] + ib * c->v_nb[3];
-                        for (int64_t d = 0; d < DV; d++) o[d] += p * (double)ora_kv_elem(vr, d, c->kv_type);
+                        ora_kv_row(vr, DV, c->kv_type, row);
+                        for (int64_t d = 0; d < DV; d++) o[d] += p * (double)row[d];
                     }
                 }
                 for (int64_t d = 0; d < DV; d++) dr[d] = l > 0.0 ? (float)(o[d] / l) : 0.0f;
@@ -466,6 +503,7 @@ void ora_flash_attn(const ora_fa_t* c) {
     }
     free(s);
     free(o);
+    free(row);
 }
 
 /* ========================================================================= */
@@ -882,9 +920,9 @@ static void base_fa_item_avx512(const ora_fa_t* c, int64_t ib, int64_t ihq, int6
 #endif
 
 #if defined(__x86_64__)
-/* The same FA2 loop for quantised K/V (Q8_0, Q4_0): each key / value row is first
- * dequantised to f32 (the DEQUANT_K_DOT_BLOCK / DEQUANT_V_ACCUM_BLOCK steps of
- * flash_attn_q8_0_avx512.asm / flash_attn_q4_0_avx512.asm), then dotted / accumulated. */
+/* The same FA2 loop for quantised K/V (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL): each key /
+ * value row is first dequantised to f32 (the DEQUANT_K_DOT_BLOCK / DEQUANT_V_ACCUM_BLOCK
+ * steps of kernels/x86/flash/flash_attn_<type>_avx512.asm), then dotted / accumulated. */
 __attribute__((target("avx512f,avx512bw,fma")))
 static void base_fa_item_q_avx512(const ora_fa_t* c, int64_t ib, int64_t ihq, int64_t iq) {
     enum { TILE = 64 };

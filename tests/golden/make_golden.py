@@ -6,8 +6,8 @@ they were made).
                        Python decoder (gguf.quants.dequantize), the published GGUF
                        algorithm the reference's Q4_K kernels implement.
 * q6k_gguf.npz      -- Q6_K super-blocks and their dequantisation by the same gguf decoder.
-* kv_gguf.npz       -- Q8_0 and Q4_0 blocks (the quantised KV-cache formats) and their
-                       dequantisation by the same gguf decoder.
+* kv_gguf.npz       -- Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 and IQ4_NL blocks (the quantised
+                       KV-cache formats) and their dequantisation by the same gguf decoder.
 * fa_reference.npz  -- flash-attention decode cases and the outputs of the reference's
                        own flash_attn_quantized (src/simd/flash_attention.cpp:291-410),
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
@@ -78,7 +78,9 @@ def kv_fixture() -> None:
     from gguf import GGMLQuantizationType, quants
     g = np.random.Generator(np.random.PCG64(21))
     out = {}
-    for name, qt, bb in (("q8_0", GGMLQuantizationType.Q8_0, 34), ("q4_0", GGMLQuantizationType.Q4_0, 18)):
+    for name, qt, bb in (("q8_0", GGMLQuantizationType.Q8_0, 34), ("q4_0", GGMLQuantizationType.Q4_0, 18),
+                         ("q4_1", GGMLQuantizationType.Q4_1, 20), ("q5_0", GGMLQuantizationType.Q5_0, 22),
+                         ("q5_1", GGMLQuantizationType.Q5_1, 24), ("iq4_nl", GGMLQuantizationType.IQ4_NL, 18)):
         rows = g.integers(0, 256, size=(6, 4, bb), dtype=np.uint8)
         d = (np.abs(g.standard_normal((6, 4))) * 0.02).astype(np.float16)
         d[0, 0] = np.float16(0.0)
@@ -86,6 +88,14 @@ def kv_fixture() -> None:
         d[2, 2] = np.float16(65504.0)
         d[3, 3] = np.float16(-0.5)
         rows[:, :, 0:2] = d.view(np.uint8).reshape(6, 4, 2)
+        if name in ("q4_1", "q5_1"):
+            # block minimum m: the usual -c * d, plus edge values
+            with np.errstate(over="ignore"):   # the 65504 scale gives an infinite m: kept as an edge case
+                m = (-8.0 * d.astype(np.float32) * (1 + 0.1 * g.standard_normal((6, 4)))).astype(np.float16)
+            m[0, 1] = np.float16(0.0)
+            m[4, 0] = np.float16(-65504.0)
+            m[5, 2] = np.float16(3e-8)
+            rows[:, :, 2:4] = m.view(np.uint8).reshape(6, 4, 2)
         rows = rows.reshape(6, 4 * bb)
         out[name + "_rows"] = rows
         out[name + "_dequant"] = quants.dequantize(rows, qt).astype(np.float32)

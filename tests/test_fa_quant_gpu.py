@@ -1,7 +1,7 @@
-"""GPU: flash-attention decode over a quantised KV cache (Q8_0 and Q4_0 K/V, the branches
-of flash_attn_dispatch at src/simd/flash_attention.cpp:112-248) against the oracle, which
-dequantises every element with the GGUF rule (pinned to the gguf decoder) and runs the
-attention in fp64.  Gate: max |o - o_oracle| / max |o_oracle| <= 1e-3."""
+"""GPU: flash-attention decode over a quantised KV cache (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 and
+IQ4_NL K/V, the branches of flash_attn_dispatch at src/simd/flash_attention.cpp:112-248)
+against the oracle, which dequantises every element with the GGUF rule (pinned to the gguf
+decoder) and runs the attention in fp64.  Gate: max |o - o_oracle| / max |o_oracle| <= 1e-3."""
 import ctypes as C
 
 import numpy as np
@@ -13,7 +13,8 @@ from mlz_b200 import synth
 
 TOL = 1e-3
 pytestmark = pytest.mark.gpu
-TYPES = [(mlz_b200.TYPE_Q8_0, "q8_0"), (mlz_b200.TYPE_Q4_0, "q4_0")]
+TYPES = [(mlz_b200.TYPE_Q8_0, "q8_0"), (mlz_b200.TYPE_Q4_0, "q4_0"), (mlz_b200.TYPE_Q4_1, "q4_1"),
+         (mlz_b200.TYPE_Q5_0, "q5_0"), (mlz_b200.TYPE_Q5_1, "q5_1"), (mlz_b200.TYPE_IQ4_NL, "iq4_nl")]
 
 
 def _case(dev, seed, B, Hq, Hkv, L, D, kv_type, NQ=1, ragged=True):
@@ -104,3 +105,47 @@ def test_quant_gate_rejects_mixed_types_and_misaligned_rows(dev):
     d.v_type = mlz_b200.TYPE_Q8_0
     d.k_nb[1] = 70
     assert mlz_b200.lib().mlzc_flash_attn_workspace_bytes(C.byref(d), C.byref(out)) == -1   # row stride % 4
+
+
+@pytest.mark.parametrize("kv_type,name", TYPES[2:])
+def test_new_types_through_hook_with_host_buffers(dev, kv_type, name):
+    """Q4_1 / Q5_0 / Q5_1 / IQ4_NL caches through the hook body (host buffers, block-size
+    nb[0]), GQA 4:1 with ragged lengths."""
+    B, Hq, Hkv, L, D = 2, 8, 2, 333, 128
+    q, k, v, kl = _case(dev, 810 + kv_type, B, Hq, Hkv, L, D, kv_type)
+    bb = oracle.KV_BLOCK[kv_type][0]
+    out = np.zeros((B, Hq, 1, D), dtype=np.float32)
+    from mlz_b200.ops import _nb
+    desc = mlz_b200.make_fa_desc(q.ctypes.data, _nb(q, 4), k.ctypes.data, (bb,) + _nb(k, 1)[1:], v.ctypes.data,
+                                 (bb,) + _nb(v, 1)[1:], out.ctypes.data, _nb(out, 4), (B, Hq, 1, Hkv, L, D),
+                                 1 / np.sqrt(D), kv_len_ptr=kl.ctypes.data, kv_type=kv_type)
+    assert mlz_b200.ggml_simd_try_flash_attn(desc, 0, 1) == 1
+    want = oracle.flash_attn_q(q, k, v, 1 / np.sqrt(D), kv_type, kv_len=kl)
+    assert oracle.rel_err(out, want) <= TOL
+
+
+@pytest.mark.parametrize("kv_type,name", TYPES[2:])
+def test_new_types_large_minimum_and_all_fifth_bits(dev, kv_type, name):
+    """Blocks whose minimum m dominates the values (Q4_1 / Q5_1: m = -40 d), every fifth bit
+    set (Q5_x: qh = 0xFFFFFFFF) and every code-book entry (IQ4_NL): the minimum, fifth-bit
+    and table paths of both the score and the value side."""
+    import torch
+    B, Hq, Hkv, L, D = 2, 4, 1, 200, 64
+    q, k, v, kl = _case(dev, 830 + kv_type, B, Hq, Hkv, L, D, kv_type)
+    bb = oracle.KV_BLOCK[kv_type][0]
+    for rows in (k, v):
+        r = rows.reshape(B, Hkv, L, D // 32, bb)
+        d = r[..., 0:2].copy().view(np.float16).astype(np.float32)
+        if kv_type in (mlz_b200.TYPE_Q4_1, mlz_b200.TYPE_Q5_1):
+            r[..., 2:4] = (-40.0 * d).astype(np.float16).view(np.uint8)
+        if kv_type in (mlz_b200.TYPE_Q5_0, mlz_b200.TYPE_Q5_1):
+            off = 2 if kv_type == mlz_b200.TYPE_Q5_0 else 4
+            r[..., off:off + 4] = 0xFF
+        if kv_type == mlz_b200.TYPE_IQ4_NL:
+            r[..., 2:] = (np.arange(16, dtype=np.uint8) * 17)[None, None, None, None, :]   # byte i = (i, i)
+    o = mlz_b200.flash_attn_dispatch_quant(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev),
+                                           torch.from_numpy(v).to(dev), 1 / np.sqrt(D), kv_type,
+                                           kv_len=torch.from_numpy(kl).to(dev))
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_q(q, k, v, 1 / np.sqrt(D), kv_type, kv_len=kl)
+    assert oracle.rel_err(o.cpu().numpy(), want) <= TOL

@@ -76,10 +76,12 @@ def test_q6k_known_answer():
                                rtol=1e-12)
 
 
-@pytest.mark.parametrize("name,kv_type", [("q8_0", 8), ("q4_0", 2)])
+@pytest.mark.parametrize("name,kv_type", [("q8_0", 8), ("q4_0", 2), ("q4_1", 3), ("q5_0", 6), ("q5_1", 7),
+                                           ("iq4_nl", 20)])
 def test_kv_dequant_matches_gguf_decoder(golden, name, kv_type):
-    """The quantised KV-cache element rule of the oracle (Q8_0, Q4_0) equals the gguf
-    decoder bit for bit on blocks with edge scales."""
+    """The quantised KV-cache element rule of the oracle (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1,
+    IQ4_NL) equals the gguf decoder bit for bit on blocks with edge scales (and, for Q4_1 /
+    Q5_1, edge block minima)."""
     f = golden("kv_gguf.npz")
     got = oracle.kv_dequant(f[name + "_rows"], 128, kv_type)
     want = f[name + "_dequant"]
@@ -207,3 +209,25 @@ def test_cpu_baselines_agree_with_oracle():
     got = oracle.base_flash_attn(q, k, v, 0.125, kv_len=kl, nth=3)
     want = oracle.flash_attn(q, k, v, 0.125, kv_len=kl)
     assert oracle.rel_err(got, want) < 1e-5
+
+
+@pytest.mark.parametrize("kv_type", [8, 2, 3, 6, 7, 20])
+def test_fa_quant_oracle_equals_numpy_attention_on_decoded_rows(kv_type):
+    """The quantised-KV attention oracle equals a plain numpy fp64 attention over the rows
+    decoded by kv_dequant (the gguf-pinned rule), for every KV-cache type, GQA and ragged."""
+    g = synth.rng(45 + kv_type)
+    B, Hq, Hkv, L, D = 2, 4, 2, 37, 64
+    q = synth.fa_inputs(g, B, Hq, Hkv, L, D)[0]
+    k = synth.kv_quant_rows(g, (B, Hkv, L), D, kv_type)
+    v = synth.kv_quant_rows(g, (B, Hkv, L), D, kv_type)
+    kl = np.array([37, 20], dtype=np.int32)
+    got = oracle.flash_attn_q(q, k, v, 0.125, kv_type, kv_len=kl)
+    kf = oracle.kv_dequant(k, D, kv_type).astype(np.float64)
+    vf = oracle.kv_dequant(v, D, kv_type).astype(np.float64)
+    for b in range(B):
+        for h in range(Hq):
+            hk = h * Hkv // Hq
+            s = kf[b, hk, :kl[b]] @ q[b, h, 0].astype(np.float64) * 0.125
+            p = np.exp(s - s.max())
+            want = (p @ vf[b, hk, :kl[b]]) / p.sum()
+            np.testing.assert_allclose(got[b, h, 0], want, rtol=1e-6, atol=1e-9)
