@@ -18,7 +18,7 @@ Workloads (synthetic seeded inputs of the named shapes; random-init weights):
   c6  Q6_K decode mul_mat on the Llama-3.1-8B shapes of c3, batch N (Q4_K_M files carry
       Q6_K tensors; the reference hook routes them with Q4_K)
   c7  flash-attention decode of c4 over a quantised KV cache (Q8_0; --kv-type q4_0, q4_1,
-      q5_0, q5_1 or iq4_nl for the other block types)
+      q5_0, q5_1 or iq4_nl for the other block types, f32 for an F32 cache)
 
 A step is one pass of the hot path over one batch.  `value` is whole-job throughput with
 inputs resident in HBM; `e2e` is the same metric through the reference-facing plugin
@@ -100,7 +100,7 @@ def parse_args():
 
 DEFAULT_N = {"c1": 8, "c2": 2048, "c3": 4, "c4": 16, "c5": 1, "c6": 4, "c7": 16}
 # c7's KV-cache block types: name -> ggml type id (block layouts in mlz_b200.synth.KV_QUANT)
-C7_KV = {"q8_0": 8, "q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "iq4_nl": 20}
+C7_KV = {"q8_0": 8, "q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "iq4_nl": 20, "f32": 0}
 C7_TYPE = {"kv": "q8_0"}   # set from --kv-type
 DTYPE = {"c1": "f16", "c2": "f16", "c3": "q4_k/f32", "c4": "f16 kv / f32", "c5": "f16", "c6": "q6_k/f32",
          "c7": "q8_0 kv / f32"}
@@ -450,8 +450,9 @@ class C7(Workload):
         self.L = 8192
         self.kv_type = C7_KV[C7_TYPE["kv"]]
         self.dtype = f"{C7_TYPE['kv']} kv / f32"
-        self.bb, self.qmag, self.moff = synth.KV_QUANT[self.kv_type]
-        self.rb = self.D // 32 * self.bb
+        # F32 rows: nb[0] = the 4-byte element, 4 D bytes per row
+        self.bb, self.qmag, self.moff = synth.KV_QUANT[self.kv_type] if self.kv_type else (4, None, None)
+        self.rb = self.D // 32 * self.bb if self.kv_type else 4 * self.D
         s = 1.0 / math.sqrt(self.D)
         self.q = torch.randn((n, self.Hq, 1, self.D), generator=gen, device=dev) * s
         self.k = self._rows(gen, dev)
@@ -472,6 +473,9 @@ class C7(Workload):
         """Random quants; block scales d with the spread of N(0, 1)/sqrt(D) values; block
         minima m = offset * d * (1 + N(0, 0.1)) for the types that carry one."""
         import torch
+        if self.kv_type == 0:
+            v = torch.randn((self.B, self.Hkv, self.L, self.D), generator=gen, device=dev) / math.sqrt(self.D)
+            return v.view(torch.uint8)
         nb, bb = self.D // 32, self.bb
         shape = (self.B, self.Hkv, self.L, nb)
         if self.kv_type == 8:
@@ -638,7 +642,7 @@ class CpuStep:
             self.row_bytes = 256
             if cfg == "c7":
                 self.kv_type = C7_KV[C7_TYPE["kv"]]
-                self.row_bytes = 4 * synth.KV_QUANT[self.kv_type][0]
+                self.row_bytes = 4 * synth.KV_QUANT[self.kv_type][0] if self.kv_type else 512
                 self.k = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, self.kv_type)
                 self.v = synth.kv_quant_rows(g, (self.slots, 8, int(self.kl.max())), 128, self.kv_type)
             kv = C7_TYPE["kv"].upper()

@@ -163,7 +163,8 @@ typedef struct {
     const float* mask;
     float* dst;
     size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
-    int32_t k_type, v_type;   /* both F16, or both one quantised KV type (Q8_0 Q4_0 Q4_1 Q5_0 Q5_1 IQ4_NL) */
+    int32_t k_type, v_type;   /* both F16, both F32 (DK <= 128) or both one quantised KV type
+                                 (Q8_0 Q4_0 Q4_1 Q5_0 Q5_1 IQ4_NL) */
     const int32_t* kv_len;    /* NULL or batch_size entries (device memory for _dev) */
 } mlzc_fa_desc;
 
@@ -182,7 +183,9 @@ int mlzc_flash_attn_workspace_bytes(const mlzc_fa_desc* desc, size_t* out_bytes)
  * GGUF layouts (nb[0] = the block size, as ggml sets it), 4-byte aligned with 4-byte
  * multiple strides.  Element: Q8_0 (34 B) f16 d * int8 q; Q4_0 (18 B) d * (nibble - 8);
  * Q4_1 (20 B) d * nibble + f16 m; Q5_0 (22 B) d * (q5 - 16); Q5_1 (24 B) d * q5 + m, q5 the
- * nibble with its fifth bit from the block's 32-bit qh; IQ4_NL (18 B) d * table[nibble]. */
+ * nibble with its fifth bit from the block's 32-bit qh; IQ4_NL (18 B) d * table[nibble].
+ * F32 K/V (flash_attn_dispatch's F32 branch -> simd_flash_attn_f32_avx512), head_dim 64 or
+ * 128: contiguous f32 rows (nb[0] = 4) on 4-byte boundaries with 4-byte multiple strides. */
 int mlzc_flash_attn_dev(const mlzc_fa_desc* desc, void* workspace, size_t workspace_bytes,
                         void* stream);
 

@@ -76,6 +76,11 @@ using ptx::split_h2;
 template <int TYPE>
 struct KvFormat;
 template <>
+struct KvFormat<0> {   // F32 rows, taken 32 values (128 bytes) at a time; no scale
+    static constexpr int kBlockBytes = 128, kQs = 0, kQh = -1;
+    static constexpr bool kMin = false;
+};
+template <>
 struct KvFormat<8> {   // Q8_0: f16 d, 32 int8; d * q
     static constexpr int kBlockBytes = 34, kQs = 2, kQh = -1;
     static constexpr bool kMin = false;
@@ -120,6 +125,11 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
 __device__ __forceinline__ uint4 lds_v4(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 lds_f2(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
     return v;
 }
 __device__ __forceinline__ float lds_f16(uint32_t a) { return __half2float(__ushort_as_half((unsigned short)lds_u16(a))); }
@@ -342,7 +352,24 @@ fa_quant_kernel(const FaqParams p) {
         for (int b = 0; b < NB; ++b) {
             float th[4] = {0.f, 0.f, 0.f, 0.f}, tl[4] = {0.f, 0.f, 0.f, 0.f};
             const uint32_t o0 = kr0 + b * F::kBlockBytes + F::kQs, o1 = kr1 + b * F::kBlockBytes + F::kQs;
-            if constexpr (TYPE == 8) {
+            if constexpr (TYPE == 0) {
+                // f32 keys as f16 hi + lo: K.Q = Khi.Qhi + Khi.Qlo + Klo.Qhi (the dropped
+                // Klo.Qlo term is ~2^-22 relative)
+#pragma unroll
+                for (int st = 0; st < 2; ++st) {
+                    const uint32_t e0 = o0 + 4 * (16 * st + 2 * q4), e1 = o1 + 4 * (16 * st + 2 * q4);
+                    const float2 k0 = lds_f2(e0), k1 = lds_f2(e1), k2 = lds_f2(e0 + 32), k3 = lds_f2(e1 + 32);
+                    uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+                    split_h2(k0.x, k0.y, h0, l0);
+                    split_h2(k1.x, k1.y, h1, l1);
+                    split_h2(k2.x, k2.y, h2, l2);
+                    split_h2(k3.x, k3.y, h3, l3);
+                    const uint4 qf = lds_v4(qtab_u + (uint32_t)(2 * b + st) * 512);
+                    mma16816(th, h0, h1, h2, h3, qf.x, qf.y);
+                    mma16816(tl, h0, h1, h2, h3, qf.z, qf.w);
+                    mma16816(tl, l0, l1, l2, l3, qf.x, qf.y);
+                }
+            } else if constexpr (TYPE == 8) {
 #pragma unroll
                 for (int st = 0; st < 2; ++st) {
                     const uint32_t a0 = i8x2_to_h2(lds_u16(o0 + 16 * st + 2 * q4));
@@ -395,7 +422,8 @@ fa_quant_kernel(const FaqParams p) {
                     mma16816(tl, hi[0], hi[1], hi[2], hi[3], qf.z, qf.w);
                 }
             }
-            const float d0 = lds_f16(kr0 + b * F::kBlockBytes), d1 = lds_f16(kr1 + b * F::kBlockBytes);
+            const float d0 = TYPE == 0 ? 1.0f : lds_f16(kr0 + b * F::kBlockBytes);
+            const float d1 = TYPE == 0 ? 1.0f : lds_f16(kr1 + b * F::kBlockBytes);
             sacc[0] = fmaf(d0, th[0] + tl[0], sacc[0]);
             sacc[1] = fmaf(d0, th[1] + tl[1], sacc[1]);
             sacc[2] = fmaf(d1, th[2] + tl[2], sacc[2]);
@@ -466,13 +494,30 @@ fa_quant_kernel(const FaqParams p) {
         const uint32_t vd0 = vb + (uint32_t)(kw + g) * RB, vd8 = vd0 + 8 * RB;   // keys g, g + 8 (scales)
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            const float dv0 = lds_f16(vd0 + b * F::kBlockBytes), dv8 = lds_f16(vd8 + b * F::kBlockBytes);
+            const float dv0 = TYPE == 0 ? 1.0f : lds_f16(vd0 + b * F::kBlockBytes);
+            const float dv8 = TYPE == 0 ? 1.0f : lds_f16(vd8 + b * F::kBlockBytes);
             uint32_t h0, l0, h1, l1;
             split_h2(pe[0] * dv0, pe[1] * dv0, h0, l0);   // key g
             split_h2(pe[2] * dv8, pe[3] * dv8, h1, l1);   // key g + 8
             const uint32_t bh0 = movtrans(h0), bh1 = movtrans(h1), bl0 = movtrans(l0), bl1 = movtrans(l1);
             const uint32_t base0 = vk0 + b * F::kBlockBytes + F::kQs + 2 * g, base8 = vk8 + b * F::kBlockBytes + F::kQs + 2 * g;
-            if constexpr (TYPE == 8) {
+            if constexpr (TYPE == 0) {
+                // f32 values as f16 hi + lo: V.P = Vhi.Phi + Vhi.Plo + Vlo.Phi
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const uint32_t e = 4 * (32 * b + 16 * hf + 2 * g);   // dims 2 g, 2 g + 1 of the tile
+                    const float2 va = lds_f2(vk0 + e), vb2 = lds_f2(vk0 + RB + e);   // keys 2 q4, 2 q4 + 1
+                    const float2 vc = lds_f2(vk8 + e), vd = lds_f2(vk8 + RB + e);    // keys 2 q4 + 8, + 9
+                    uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+                    split_h2(va.x, vb2.x, h0, l0);
+                    split_h2(va.y, vb2.y, h1, l1);
+                    split_h2(vc.x, vd.x, h2, l2);
+                    split_h2(vc.y, vd.y, h3, l3);
+                    mma16816(o[2 * b + hf], h0, h1, h2, h3, bh0, bh1);
+                    mma16816(o[2 * b + hf], h0, h1, h2, h3, bl0, bl1);
+                    mma16816(o[2 * b + hf], l0, l1, l2, l3, bh0, bh1);
+                }
+            } else if constexpr (TYPE == 8) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t c00, c01, c80, c81;
@@ -691,7 +736,12 @@ template <int TYPE, bool GEN>
 int faq_dispatch(const FaqPlan& pl, int D, cudaStream_t s) {
     if (D == 64) return faq_launch<64, TYPE, GEN>(pl, s);
     if (D == 128) return faq_launch<128, TYPE, GEN>(pl, s);
-    return faq_launch<256, TYPE, GEN>(pl, s);
+    if constexpr (TYPE == 0) {
+        // f32 rows of 256 dims: two stages of 64-key K and V tiles are 256 KB (the gate declines it)
+        return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: F32 K/V with head_dim %d", D);
+    } else {
+        return faq_launch<256, TYPE, GEN>(pl, s);
+    }
 }
 
 // Widest cp.async piece every row of a tile can be copied with: 16 when a head's rows are
@@ -751,6 +801,7 @@ int launch_flash_attn_quant(int sm_count, const mlzc_fa_desc* d, void* ws, size_
         p.b_base = (int)b0;
         p.nB = (int)std::min<int64_t>(pl.slice, d->batch_size - b0);
         switch (d->k_type) {
+            case MLZC_TYPE_F32: st = gen ? faq_dispatch<0, true>(pl, D, s) : faq_dispatch<0, false>(pl, D, s); break;
             case MLZC_TYPE_Q8_0: st = gen ? faq_dispatch<8, true>(pl, D, s) : faq_dispatch<8, false>(pl, D, s); break;
             case MLZC_TYPE_Q4_0: st = gen ? faq_dispatch<2, true>(pl, D, s) : faq_dispatch<2, false>(pl, D, s); break;
             case MLZC_TYPE_Q4_1: st = gen ? faq_dispatch<3, true>(pl, D, s) : faq_dispatch<3, false>(pl, D, s); break;

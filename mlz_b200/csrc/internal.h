@@ -153,7 +153,8 @@ inline size_t kv_block_bytes(int32_t type) {
 }
 inline size_t fa_row_bytes(int32_t type, int64_t head_dim) {
     const size_t bb = kv_block_bytes(type);
-    return bb ? (size_t)(head_dim / 32) * bb : (size_t)head_dim * 2;
+    if (bb) return (size_t)(head_dim / 32) * bb;
+    return (size_t)head_dim * (type == MLZC_TYPE_F32 ? 4 : 2);
 }
 int launch_flash_attn(const DeviceCtx* c, const mlzc_fa_desc* d, void* ws, size_t ws_bytes,
                       cudaStream_t s);

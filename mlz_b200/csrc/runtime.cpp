@@ -136,14 +136,18 @@ int check_mul_mat_args(int w_type, const void* w, size_t w_row_bytes, int64_t M,
 
 int check_fa_args(const mlzc_fa_desc* d) {
     if (!d) return fail(MLZC_ERR_INVALID, "flash_attn: null descriptor");
-    const bool quant = kv_block_bytes(d->k_type) != 0;
+    // quantised caches and F32 go to the cp.async-ring kernel (rows of 4-byte-aligned pieces)
+    const bool f32 = d->k_type == MLZC_TYPE_F32;
+    const bool quant = kv_block_bytes(d->k_type) != 0 || f32;
     if ((d->k_type != MLZC_TYPE_F16 && !quant) || d->v_type != d->k_type)
         return fail(MLZC_ERR_UNSUPPORTED,
-                    "flash_attn: K/V types %d/%d (both F16, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 or IQ4_NL)", d->k_type,
+                    "flash_attn: K/V types %d/%d (both F16, F32, Q8_0, Q4_0, Q4_1, Q5_0, Q5_1 or IQ4_NL)", d->k_type,
                     d->v_type);
     if (d->head_dim_k != d->head_dim_v) return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: DK != DV");
     if (d->head_dim_k != 64 && d->head_dim_k != 128 && d->head_dim_k != 256)
         return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: head_dim %lld (64, 128, 256 supported)", (long long)d->head_dim_k);
+    if (f32 && d->head_dim_k == 256)
+        return fail(MLZC_ERR_UNSUPPORTED, "flash_attn: F32 K/V with head_dim 256 (64, 128 supported)");
     if (d->n_queries <= 0 || d->n_kv < 0 || d->n_head_q <= 0 || d->n_head_kv <= 0 || d->batch_size <= 0)
         return fail(MLZC_ERR_INVALID, "flash_attn: empty or negative dimension");
     if (d->n_head_kv > d->n_head_q) return fail(MLZC_ERR_INVALID, "flash_attn: more KV heads than query heads");
@@ -154,10 +158,10 @@ int check_fa_args(const mlzc_fa_desc* d) {
         return fail(MLZC_ERR_INVALID, "flash_attn: q rows must be contiguous f32 on 16-byte boundaries");
     if (quant) {
         // rows of blocks (nb[0] = block bytes, ggml's convention), 4-byte aligned
-        const size_t bb = kv_block_bytes(d->k_type);
+        const size_t bb = f32 ? 4 : kv_block_bytes(d->k_type);   // nb[0]: block (or element) bytes
         if ((uintptr_t)d->k % 4 || (uintptr_t)d->v % 4 || d->k_nb[1] % 4 || d->v_nb[1] % 4 || d->k_nb[2] % 4 ||
             d->v_nb[2] % 4 || d->k_nb[3] % 4 || d->v_nb[3] % 4 || d->k_nb[0] != bb || d->v_nb[0] != bb)
-            return fail(MLZC_ERR_INVALID, "flash_attn: quantised K/V rows must be contiguous blocks on 4-byte boundaries");
+            return fail(MLZC_ERR_INVALID, "flash_attn: quantised / F32 K/V rows must be contiguous on 4-byte boundaries");
     } else if ((uintptr_t)d->k % 16 || (uintptr_t)d->v % 16 || d->k_nb[1] % 16 || d->v_nb[1] % 16 ||
                d->k_nb[2] % 16 || d->v_nb[2] % 16 || d->k_nb[3] % 16 || d->v_nb[3] % 16 || d->k_nb[0] != 2 ||
                d->v_nb[0] != 2) {

@@ -178,7 +178,9 @@ def flash_attn_dispatch(q, k, v, scale: float, *, kv_len=None, mask=None, softca
 
 
 # bytes per 32-value block of each quantised KV-cache type (GGUF layouts)
-KV_BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_IQ4_NL: 18}
+# (F32 rows: nb[0] is the 4-byte element)
+KV_BLOCK_BYTES = {TYPE_Q8_0: 34, TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q5_0: 22, TYPE_Q5_1: 24, TYPE_IQ4_NL: 18,
+                  TYPE_F32: 4}
 
 
 def flash_attn_dispatch_quant(q, k, v, scale: float, kv_type: int, *, kv_len=None, mask=None,
@@ -186,8 +188,8 @@ def flash_attn_dispatch_quant(q, k, v, scale: float, kv_type: int, *, kv_len=Non
                               stream=None):
     """Flash-attention over a quantised KV cache on device tensors: q (B, Hq, NQ, D) f32;
     k, v (B, Hkv, L, D/32*block_bytes) uint8 rows of blocks of kv_type (Q8_0 34 bytes, Q4_0
-    18, Q4_1 20, Q5_0 22, Q5_1 24, IQ4_NL 18; any strides with contiguous rows).  Returns
-    out (B, Hq, NQ, D) f32."""
+    18, Q4_1 20, Q5_0 22, Q5_1 24, IQ4_NL 18), or (B, Hkv, L, 4 D) bytes of f32 rows for
+    TYPE_F32 (D <= 128); any strides with contiguous rows.  Returns out (B, Hq, NQ, D) f32."""
     torch = _torch()
     B, Hq, NQ, D = q.shape
     _, Hkv, L, _ = k.shape

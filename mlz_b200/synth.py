@@ -76,10 +76,14 @@ KV_QUANT = {8: (34, 64.0, None), 2: (18, 4.0, None), 3: (20, 4.0, -7.5), 6: (22,
 
 
 def kv_quant_rows(g: np.random.Generator, shape, D: int, kv_type: int) -> np.ndarray:
-    """Quantised K/V rows of a KV-cache type of KV_QUANT: uint8 array of shape +
-    (D/32*block_bytes,), random quants (and fifth bits), block scales d = f16(|N(0, 1)| /
+    """Quantised K/V rows of a KV-cache type of KV_QUANT (or F32 rows, kv_type 0, of N(0, 1)/
+    sqrt(D) values): uint8 array of shape + (D/32*block_bytes,), random quants (and fifth bits),
+    block scales d = f16(|N(0, 1)| /
     (typical |value / d| * sqrt(D))) so that the values have the spread of N(0, 1)/sqrt(D);
     the types with a block minimum (Q4_1, Q5_1) get m = f16(offset * d * (1 + N(0, 0.1)))."""
+    if kv_type == 0:   # F32 rows: the values themselves, as bytes
+        v = (g.standard_normal(tuple(shape) + (D,), dtype=np.float32) / np.sqrt(D)).astype(np.float32)
+        return v.view(np.uint8)
     bb, qmag, moff = KV_QUANT[kv_type]
     nb = D // 32
     rows = g.integers(0, 256, size=tuple(shape) + (nb, bb), dtype=np.uint8)

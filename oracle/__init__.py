@@ -312,9 +312,9 @@ KV_BLOCK = {8: (34, 32), 2: (18, 32), 3: (20, 32), 6: (22, 32), 7: (24, 32), 20:
 def flash_attn_q(q, k_blocks, v_blocks, scale, kv_type, mask=None, kv_len=None, softcap=0.0,
                  max_bias=0.0, mode=0) -> np.ndarray:
     """Exact decode attention over a quantised KV cache (kv_type 8 = Q8_0, 2 = Q4_0, 3 = Q4_1,
-    6 = Q5_0, 7 = Q5_1, 20 = IQ4_NL): k/v_blocks: (B, Hkv, NKV, D/32*block_bytes) uint8 rows
-    of blocks; every row is dequantised with GGUF's rule (ora_kv_row) and the attention runs
-    in fp64."""
+    6 = Q5_0, 7 = Q5_1, 20 = IQ4_NL) or an F32 one (kv_type 0): k/v_blocks: (B, Hkv, NKV,
+    row_bytes) uint8 rows (blocks, or D f32 values); every row is decoded with GGUF's rule
+    (ora_kv_row) and the attention runs in fp64."""
     q = np.ascontiguousarray(q, dtype=np.float32)
     k_blocks = np.ascontiguousarray(k_blocks, dtype=np.uint8)
     v_blocks = np.ascontiguousarray(v_blocks, dtype=np.uint8)

@@ -360,8 +360,8 @@ typedef struct {
     float* dst;                     /* f32 */
     size_t q_nb[4], k_nb[4], v_nb[4], mask_nb[4], dst_nb[4];
     const int32_t* kv_len;          /* per batch element, NULL = n_kv for all */
-    int32_t kv_type;                /* K/V element type (ggml ids): 1 F16, 8 Q8_0, 2 Q4_0, 3 Q4_1,
-                                       6 Q5_0, 7 Q5_1, 20 IQ4_NL */
+    int32_t kv_type;                /* K/V element type (ggml ids): 0 F32, 1 F16, 8 Q8_0, 2 Q4_0,
+                                       3 Q4_1, 6 Q5_0, 7 Q5_1, 20 IQ4_NL */
 } ora_fa_t;
 
 /* Bytes of one 32-value block of a quantised KV-cache type (ggml ids), 0 for F16. */
@@ -424,13 +424,19 @@ static void ora_kv_block(const unsigned char* blk, int32_t type, float* o) {
     }
 }
 
-/* Element d of a K or V row of type `type` (1 = F16, or a quantised type above) as f32. */
+/* Element d of a K or V row of type `type` (0 = F32, 1 = F16, or a quantised type above) as
+ * f32. */
 static float ora_kv_elem(const char* row, int64_t d, int32_t type) {
     const int64_t bb = ora_kv_block_bytes(type);
     if (bb) {
         float blk[32];
         ora_kv_block((const unsigned char*)row + (d / 32) * bb, type, blk);
         return blk[d % 32];
+    }
+    if (type == 0) {
+        float f;
+        memcpy(&f, row + 4 * d, 4);
+        return f;
     }
     uint16_t h;
     memcpy(&h, row + 2 * d, 2);

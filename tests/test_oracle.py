@@ -211,10 +211,11 @@ def test_cpu_baselines_agree_with_oracle():
     assert oracle.rel_err(got, want) < 1e-5
 
 
-@pytest.mark.parametrize("kv_type", [8, 2, 3, 6, 7, 20])
+@pytest.mark.parametrize("kv_type", [8, 2, 3, 6, 7, 20, 0])
 def test_fa_quant_oracle_equals_numpy_attention_on_decoded_rows(kv_type):
     """The quantised-KV attention oracle equals a plain numpy fp64 attention over the rows
-    decoded by kv_dequant (the gguf-pinned rule), for every KV-cache type, GQA and ragged."""
+    decoded by kv_dequant (the gguf-pinned rule), for every KV-cache type (and F32 rows),
+    GQA and ragged."""
     g = synth.rng(45 + kv_type)
     B, Hq, Hkv, L, D = 2, 4, 2, 37, 64
     q = synth.fa_inputs(g, B, Hq, Hkv, L, D)[0]
