@@ -16,6 +16,9 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <type_traits>
 
 #include "internal.h"
 #include "peer.h"
@@ -226,6 +229,25 @@ gemv_scalar_kernel(const char* __restrict__ W, size_t w_rs, int64_t M, int64_t K
 // to keep its loads in flight: measured on B200 (us per call, KW = 8 / one warp per 2 rows):
 // 8192 x 28672 68.3 / 73.5, 28672 x 8192 65.0 / 74.6 (7.2 TB/s of weights).
 
+// SM count of the current device (queried once per device).
+int sm_count_cached() {
+    static std::atomic<int> cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 148;
+    }
+    int v = cached[dev].load(std::memory_order_relaxed);
+    if (!v) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+            cudaGetLastError();
+            v = 148;
+        }
+        cached[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
 template <class WT, int NB, bool PEER = false>
 int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, size_t x_cs,
                int ncols, char* y, size_t y_cs, cudaStream_t s, const PeerView& pv = PeerView{}) {
@@ -237,14 +259,45 @@ int launch_vec(const char* w, size_t w_rs, int64_t M, int64_t K, const char* x, 
     const int kw = chunks >= (int64_t)32 * U * 8 ? 8 : chunks >= (int64_t)32 * U * 4 ? 4 : chunks >= (int64_t)32 * U * 2 ? 2 : 1;
     const int64_t rows_per_cta = (int64_t)(kWarps / kw) * ROWS;
     const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
-    auto go = [&](auto kern) {
-        return launch_pdl(kern, dim3(grid), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs, ncols, y, y_cs, early, pv);
+    auto go = [&](auto kern, unsigned g) {
+        return launch_pdl(kern, dim3(g), dim3(kThreads), 0, s, w, w_rs, M, K, x, x_cs, ncols, y, y_cs, early, pv);
     };
     cudaError_t e;
-    if (kw == 8) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 8, PEER>);
-    else if (kw == 4) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 4, PEER>);
-    else if (kw == 2) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 2, PEER>);
-    else e = go(gemv_vec_kernel<WT, NB, ROWS, U, 1, PEER>);
+    if constexpr (NB == 1 && std::is_same<WT, WF16>::value) {
+        // Matrices of fewer than ~16 CTAs per SM at the shape above (C1's 8192 x 3072, the row
+        // shards of the sharded FFN): 4 rows per group, 2 loads in flight, and the KW that
+        // brings the grid nearest ~3.5 CTAs per SM.  Swept on B200 over ROWS {1, 2, 4} x
+        // U {2, 3, 4, 6, 8} x KW {1, 2, 4, 8} (us per call, graph-replayed, weights rotated
+        // past L2; this shape / the one above): 8192 x 3072 8.1 / 10.1, 3584 x 8192 9.9 /
+        // 10.4, 2048 x 28672 18.1 / 20.7; at 7168 x 8192 and above the shape above wins.
+        const int64_t sms = sm_count_cached();
+        if ((int64_t)grid < 16 * sms) {
+            int best_kw = 0;
+            int64_t best_grid = 0;
+            for (int k2 = 1; k2 <= 8; k2 *= 2) {
+                if (chunks < (int64_t)64 * k2) break;   // every warp one full 2-chunk step
+                const int64_t g2 = (M + (int64_t)(kWarps / k2) * 4 - 1) / ((int64_t)(kWarps / k2) * 4);
+                if (!best_kw || std::llabs(2 * g2 - 7 * sms) < std::llabs(2 * best_grid - 7 * sms)) {
+                    best_kw = k2;
+                    best_grid = g2;
+                }
+            }
+            if (best_kw && 2 * best_grid >= 5 * sms) {
+                const unsigned g2 = (unsigned)best_grid;
+                if (best_kw == 8) e = go(gemv_vec_kernel<WT, 1, 4, 2, 8, PEER>, g2);
+                else if (best_kw == 4) e = go(gemv_vec_kernel<WT, 1, 4, 2, 4, PEER>, g2);
+                else if (best_kw == 2) e = go(gemv_vec_kernel<WT, 1, 4, 2, 2, PEER>, g2);
+                else e = go(gemv_vec_kernel<WT, 1, 4, 2, 1, PEER>, g2);
+                MLZC_CUDA_TRY(e);
+                count_launch();
+                return MLZC_OK;
+            }
+        }
+    }
+    if (kw == 8) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 8, PEER>, grid);
+    else if (kw == 4) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 4, PEER>, grid);
+    else if (kw == 2) e = go(gemv_vec_kernel<WT, NB, ROWS, U, 2, PEER>, grid);
+    else e = go(gemv_vec_kernel<WT, NB, ROWS, U, 1, PEER>, grid);
     MLZC_CUDA_TRY(e);
     count_launch();
     return MLZC_OK;

@@ -54,6 +54,21 @@ def test_f16_edge_shapes(dev, M, K, N):
     assert oracle.rel_err(y, oracle.mul_mat_f16(w.view(np.uint16), x)) <= TOL
 
 
+@pytest.mark.parametrize("M,K", [(16576, 512), (8192, 3072), (3584, 8192), (2048, 28672), (2050, 28672),
+                                 (1024, 28672)])
+def test_f16_decode_gemv_launch_shapes(dev, M, K):
+    """One activation column through every launch shape of the decode GEMV: 4 rows per warp
+    group with 1, 2, 4 and 8 warps splitting K (the shapes whose grid would be small:
+    16576 x 512, C1's 8192 x 3072, the 8- and 4-GPU shards of the 70B FFN), a row count
+    that is not a multiple of 4, and the 2-row shape (1024 x 28672); NaN guard columns
+    around Y must stay NaN."""
+    g = synth.rng(900 + M % 97 + K % 89)
+    w = synth.f16_weights(g, M, K)
+    x = synth.f32_acts(g, 1, K)
+    y = _run(dev, w, x, x_pad=4, y_pad=8)
+    assert oracle.rel_err(y, oracle.mul_mat_f16(w.view(np.uint16), x)) <= TOL
+
+
 @pytest.mark.parametrize("M,K,N", [(256, 512, 1), (100, 36, 3), (64, 4096, 8), (7, 5, 2), (100, 8192, 3)])
 def test_f32_weights(dev, M, K, N):
     g = synth.rng(200 + M + N)
