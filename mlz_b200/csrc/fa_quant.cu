@@ -690,11 +690,17 @@ int faq_plan(const mlzc_fa_desc* d, int sm_count, FaqPlan* out) {
     p.HR = p.n_hidx * p.n_rgroups;
     pl.slice = (int)std::min<int64_t>(d->batch_size, 65535);
     const int tiles = std::max(1, (p.n_kv + kQTile - 1) / kQTile);
-    // Splits of 4..64 tiles, sized for ~8 CTAs per SM over the launch if every sequence had
+    // Splits of 4..64 tiles, sized for ~T CTAs per SM over the launch if every sequence had
     // n_kv keys: ragged batches then still fill several waves (CTAs past a sequence's end
-    // exit at once), and the partial records stay a few percent of the K/V bytes.
+    // exit at once), and the partial records stay a few percent of the K/V bytes.  T per
+    // type, measured on B200 over T in {2 .. 32} on the C7 batch (us per call, chosen T / 8):
+    // Q4_0 12 (44.5 / 53.2), Q5_1 12 (66.7 / 82.5), F32 6 (157 / 163); Q8_0, Q4_1, Q5_0 and
+    // IQ4_NL 8 (12 was level for Q8_0 and Q5_0, 9-15 % slower for Q4_1 and IQ4_NL).
     const int64_t segs = (int64_t)pl.slice * p.HR;
-    const int64_t want = (int64_t)tiles * segs / std::max<int64_t>(1, 8LL * sm_count);
+    const int64_t T = (d->k_type == MLZC_TYPE_Q4_0 || d->k_type == MLZC_TYPE_Q5_1) ? 12
+                      : d->k_type == MLZC_TYPE_F32                                 ? 6
+                                                                                   : 8;
+    const int64_t want = (int64_t)tiles * segs / std::max<int64_t>(1, T * sm_count);
     p.tiles_per_split = (int)std::min<int64_t>(std::max<int64_t>(4, want), 64);
     p.tiles_per_split = std::min(p.tiles_per_split, tiles);
     p.splits = (tiles + p.tiles_per_split - 1) / p.tiles_per_split;

@@ -181,10 +181,17 @@ int launch_gemv_f16_mma(const void* w, size_t w_row_bytes, int64_t M, int64_t K,
     char* yc = reinterpret_cast<char*>(y);
     // measured on B200 (8192 x 3072, us for U = 2 / 3 / 4 chunks in flight per warp): N = 2
     // 10.6 / 9.7 / 10.5, N = 4 10.9 / 10.0 / 10.2, N = 8 11.4 / 10.8 / 10.4; 16-row CTAs beat
-    // 32-row ones; beyond 16 columns the tcgen05 GEMM is faster
-    if (N <= 4) return launch_sk<1, 1, 3>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+    // 32-row ones up to 8 columns; beyond 16 columns the tcgen05 GEMM is faster.  A later
+    // sweep of MT {1, 2, 4} x U {2, 3, 4, 6} (graph-replayed, weights rotated past L2) kept
+    // those and found U = 4 better for N <= 4 on matrices from ~40 M weights (14336 x 4096,
+    // N = 4: 22.6 vs 24.3 us) and MT = 2, U = 4 for 9..16 columns (N = 16: 12.8 vs 13.3 us
+    // on 8192 x 3072, 28.7 vs 31.9 on 14336 x 4096).
+    if (N <= 4) {
+        if (M * K >= (int64_t)40 << 20) return launch_sk<1, 1, 4>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+        return launch_sk<1, 1, 3>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+    }
     if (N <= 8) return launch_sk<1, 1, 4>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
-    return launch_sk<2, 2, 2>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
+    return launch_sk<2, 2, 4>(wc, w_row_bytes, M, K, xc, x_col_bytes, N, yc, y_col_bytes, s);
 }
 
 }  // namespace mlzc
