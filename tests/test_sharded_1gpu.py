@@ -19,7 +19,9 @@ def comm(dev):
     c.destroy()
 
 
-CASES = [(4096, 1024, 1), (1024, 512, 33), (2048, 1024, 256), (516, 256, 5)]
+# (3584 x 8192 and 2050 x 28672 at one column take the fused decode GEMV's 4-row launch
+# shapes, with 4 and 8 warps splitting K, as the 70B FFN's row shards on 8 and 4 GPUs do)
+CASES = [(4096, 1024, 1), (1024, 512, 33), (2048, 1024, 256), (516, 256, 5), (3584, 8192, 1), (2050, 28672, 1)]
 
 
 def test_single_rank_equals_unsharded(dev, comm):
