@@ -30,11 +30,12 @@ def main(out_path: str) -> None:
     res = {"rank": rank, "cases": []}
     try:
         # small shapes (host-generated), then the Llama-3-70B FFN shapes at full size
-        # (gate/up 28672x8192 at N = 1, down 8192x28672 at N = 256; generated on the
+        # (gate/up 28672x8192 at N = 1, down 8192x28672 at N = 1 and 256; generated on the
         # device from one seed on every rank, so every rank holds the same full W)
         for (kind, M, K, N) in [("f16", 1024, 512, 1), ("f16", 2048, 1024, 4), ("f16", 512, 768, 33),
                                 ("f16", 1024, 256, 256), ("f16", 520, 256, 5), ("q4k", 1024, 1024, 1),
-                                ("q4k", 512, 512, 16), ("f16", 28672, 8192, 1), ("f16", 8192, 28672, 256)]:
+                                ("q4k", 512, 512, 16), ("f16", 28672, 8192, 1), ("f16", 8192, 28672, 1),
+                                ("f16", 8192, 28672, 256)]:
             g = synth.rng(5000 + M + K + N)
             m_loc = M // world
             if M * K > (1 << 26):
