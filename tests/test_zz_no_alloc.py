@@ -100,3 +100,34 @@ def test_noalloc_rejects_calls_beyond_its_scratch(dev):
     st = mlz_b200.lib().mlzc_flash_attn_dev_noalloc(C.byref(d), None)
     assert st == -4  # MLZC_ERR_NOMEM, before anything is launched
     assert "fixed scratch" in mlz_b200.last_error()
+
+
+@pytest.mark.parametrize("kv_type", [mlz_b200.TYPE_Q8_0, mlz_b200.TYPE_Q5_1, mlz_b200.TYPE_F32])
+def test_noalloc_quantised_and_f32_caches(dev, kv_type):
+    """Quantised (Q8_0, Q5_1) and F32 KV caches take the same scratch for their split
+    records: two consecutive calls of each equal the workspace entry point's result."""
+    import torch
+    L = mlz_b200.lib()
+    B, Hq, Hkv, Lmax, D = 4, 8, 2, 1500, 128
+    g = synth.rng(960 + kv_type)
+    q = torch.from_numpy(synth.fa_inputs(g, B, Hq, Hkv, 1, D)[0]).to(dev)
+    k = torch.from_numpy(synth.kv_quant_rows(g, (B, Hkv, Lmax), D, kv_type)).to(dev)
+    v = torch.from_numpy(synth.kv_quant_rows(g, (B, Hkv, Lmax), D, kv_type)).to(dev)
+    kl = torch.from_numpy(synth.kv_lengths(g, B, 1, Lmax)).to(dev)
+    bb = mlz_b200.ops.KV_BLOCK_BYTES[kv_type]
+    outs = [torch.full((B, Hq, 1, D), float("nan"), device=dev) for _ in range(2)]
+    descs = [mlz_b200.make_fa_desc(q.data_ptr(), _nb(q, 4), k.data_ptr(), (bb,) + _nb(k, 1)[1:], v.data_ptr(),
+                                   (bb,) + _nb(v, 1)[1:], o.data_ptr(), _nb(o, 4), (B, Hq, 1, Hkv, Lmax, D),
+                                   1.0 / np.sqrt(D), kv_len_ptr=kl.data_ptr(), kv_type=kv_type) for o in outs]
+    wsb = C.c_size_t(0)
+    mlz_b200.check(L.mlzc_flash_attn_workspace_bytes(C.byref(descs[0]), C.byref(wsb)))
+    assert 0 < wsb.value <= 16 << 20
+    ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        mlz_b200.check(L.mlzc_flash_attn_dev(C.byref(descs[0]), ws.data_ptr(), wsb.value, stream))
+        mlz_b200.check(L.mlzc_flash_attn_dev_noalloc(C.byref(descs[1]), stream))
+        torch.cuda.synchronize()
+        a, b = outs[0].cpu().numpy(), outs[1].cpu().numpy()
+        assert np.isfinite(b).all()
+        assert np.max(np.abs(a - b)) / max(np.max(np.abs(a)), 1e-30) <= 1e-3
