@@ -1,29 +1,39 @@
-// fa_quant.cu -- flash-attention decode over a quantised KV cache (Q8_0 or Q4_0 K and V).
+// fa_quant.cu -- flash-attention decode over a quantised KV cache (Q8_0, Q4_0, Q4_1, Q5_0,
+// Q5_1 or IQ4_NL K and V) or an F32 one.
 //
-// Replaces the quantised-KV branches of flash_attn_dispatch (src/simd/flash_attention.cpp
-// :112-248: simd_flash_attn_q8_0_avx512 / _q4_0_avx512, i.e. the FA2 skeleton
-// flash_attn_fa2_skeleton_avx512.inc with the DEQUANT_K_DOT_BLOCK / DEQUANT_V_ACCUM_BLOCK
-// macros of kernels/x86/flash/flash_attn_q8_0_avx512.asm and flash_attn_q4_0_avx512.asm).
-// Element d of a row: Q8_0 (34-byte blocks of 32) = f16 d * int8 q; Q4_0 (18-byte blocks of
-// 32) = f16 d * (nibble - 8), values 0-15 in the low nibbles, 16-31 in the high ones.  The
-// score order is the F16 kernel's: s = <q * scale, k> + mask, softcap, + ALiBi.
+// Replaces the quantised-KV and F32 branches of flash_attn_dispatch
+// (src/simd/flash_attention.cpp:112-248: simd_flash_attn_<type>_avx512, i.e. the FA2
+// skeleton flash_attn_fa2_skeleton_avx512.inc with the DEQUANT_K_DOT_BLOCK /
+// DEQUANT_V_ACCUM_BLOCK macros of kernels/x86/flash/flash_attn_<type>_avx512.asm).
+// Element d of a row, per 32-value block (GGUF layouts; values 0-15 in the low nibbles,
+// 16-31 in the high ones; Q5_x: bit d of the 32-bit qh is value d's fifth bit):
+//   Q8_0 (34 B)  f16 d * int8 q            Q4_0 (18 B)   d * (nibble - 8)
+//   Q4_1 (20 B)  d * nibble + f16 m        Q5_0 (22 B)   d * (q5 - 16)
+//   Q5_1 (24 B)  d * q5 + m                IQ4_NL (18 B) d * code_book[nibble]
+//   F32          the value itself (head_dim 64 or 128)
+// The score order is the F16 kernel's: s = <q * scale, k> + mask, softcap, + ALiBi.
 //
-// Design (split-K flash decoding on the tensor cores; the rows are 136 / 72 bytes for
-// D = 128, not 16-byte multiples, so no TMA map describes them):
+// Design (split-K flash decoding on the tensor cores; the rows are 72-136 bytes for D = 128,
+// not 16-byte multiples, so no TMA map describes them):
 //   - a CTA (four warps) owns one segment -- one sequence, one KV head, up to 8 query rows
 //     sharing it (GQA packing, as the F16 kernel) -- and one contiguous range of up to
 //     tiles_per_split 64-key tiles (grid.x = splits; CTAs past a sequence's end only write
 //     an empty record);
-//   - the raw K and V rows of each tile stream into a 3-stage shared-memory ring with
+//   - the raw K and V rows of each tile stream into a 2-stage shared-memory ring with
 //     cp.async (16-byte chunks when a head's rows are contiguous, else 8- or 4-byte
 //     pieces per row; rows past the sequence's end are zero-filled);
 //   - warp w owns keys 16 w .. 16 w + 15 of every tile, with its own online softmax.
 //     Scores S^T = K . Q^T and the update O^T += V^T . P^T run on mma.sync m16n8k16 (keys
 //     on M for S, dims on M for O, up to 8 query rows on N), Q and P split into f16 hi + lo
-//     as in the F16 kernel.  The quantised values enter as exact f16 (int8 or nibble - 8,
-//     one LOP3 + PRMT + HSUB2 per pair) and the f16 block scales d are applied in f32: per
-//     key and 32-dim block on the score partial sums, and per key and block on P before
-//     the V^T . P^T step -- the reference's own order (q . (d k) as (q . k) d per block);
+//     as in the F16 kernel.  The quantised values enter as exact f16 integers (int8, or a
+//     nibble with its fifth bit OR-ed into the mantissa, minus the type's offset: one LOP3
+//     + PRMT + HSUB2 / HFMA2 per pair; IQ4_NL through a shared-memory table from a byte to
+//     the f16 pair of its two code-book values) and the f16 block scales d are applied in
+//     f32: per key and 32-dim block on the score partial sums, and per key and block on P
+//     before the V^T . P^T step -- the reference's own order (q . (d k) as (q . k) d per
+//     block).  A block minimum m adds m * (the block's sum of the scaled query) to a score
+//     and sum_keys p * m to every dim of the block of O (kept per lane, rescaled with O,
+//     added at the end).  F32 values are split into f16 hi + lo like Q and P;
 //   - at the end the four warps' (max, sum, O) states are merged through shared memory into
 //     one partial record per row and a combine kernel merges a segment's records in split
 //     order (results repeat bit for bit).
