@@ -268,8 +268,11 @@ int mlzc_mul_mat_sharded_workspace_bytes(mlzc_comm comm, int w_type, int64_t M_t
 /* Row-sharded mul_mat: this rank holds rows [r*M_total/G, (r+1)*M_total/G) of W
  * (w_shard, M_total % G == 0) and computes that slice of Y; the slices are all-gathered
  * so that every rank ends with the full Y (ggml layout, M_total rows).  No counterpart
- * in the reference (it has no multi-GPU path); it composes mlzc_mul_mat_dev with an
- * NCCL all-gather on `stream`. */
+ * in the reference (it has no multi-GPU path).  The slices travel through the ranks'
+ * exchange regions in peer memory over NVLink (the decode GEMV and the prefill GEMM store
+ * their outputs straight into every rank's slot; a wait kernel then signals, waits and
+ * gathers), or through an NCCL all-gather on `stream` where the peer regions could not be
+ * set up.  Every rank makes the same calls in the same order. */
 int mlzc_mul_mat_sharded_dev(mlzc_comm comm, int w_type, const void* w_shard,
                              size_t w_row_bytes, int64_t M_total, int64_t K,
                              const float* x, size_t x_col_bytes, int64_t N,
