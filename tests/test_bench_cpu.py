@@ -39,3 +39,19 @@ def test_workload_names_agree_between_arms():
         assert bench.workload_name(cfg, n, 1).startswith(cfg)
         assert bench.metric_name(cfg, n, 1)
     assert "sum L = " in bench.workload_name("c4", 16, 1)
+
+
+def test_c7_reference_arm_per_kv_type():
+    """The reference arm of c7 times the same KV-cache type as the GPU arm (--kv-type) and
+    names it in the metric, the workload and the dtype."""
+    probe = r"""
+import runpy, sys
+sys.argv = ["bench.py", "--impl", "reference", "--config", "c7", "--kv-type", "q5_1", "--steps", "1",
+            "--warmup", "0", "--cpu-seconds", "0.1"]
+runpy.run_path("bench.py", run_name="__main__")
+"""
+    out = subprocess.run([sys.executable, "-c", probe], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][0])
+    assert "Q5_1 KV" in d["metric"] and "Q5_1 KV cache" in d["config"]["workload"]
+    assert d["dtype"] == "q5_1 kv / f32" and d["value"] > 0
