@@ -170,10 +170,11 @@ __device__ __forceinline__ uint32_t nib_to_h2(uint32_t u, uint32_t hb) {
         return h2_bits(__hfma2(bits_h2((u & 0xFFF0FFF0u) | hb), k, c));
     }
 }
-// Fifth bits of a pair: bit s0 of x to bit t, bit s1 of y to bit t + 16.
-__device__ __forceinline__ uint32_t bits2(uint32_t x, int s0, uint32_t y, int s1, int t) {
-    return (((x >> s0) & 1u) << t) | (((y >> s1) & 1u) << (t + 16));
-}
+// Fifth bits of one key's pair: bits s, s + 1 of h to bits 4 and 20 (low nibbles) or 8 and
+// 24 (high nibbles).  v * (2^4 + 2^19) puts bit 0 of v at 4 and bit 1 at 20 (and copies at 19
+// and 5 that the mask drops); likewise 2^8 + 2^23 for 8 and 24.
+__device__ __forceinline__ uint32_t fifth_lo(uint32_t h, int s) { return (((h >> s) & 3u) * 0x80010u) & 0x100010u; }
+__device__ __forceinline__ uint32_t fifth_hi(uint32_t h, int s) { return (((h >> s) & 3u) * 0x800100u) & 0x1000100u; }
 // The 32-bit qh of a block at a 2-byte-aligned shared address.
 __device__ __forceinline__ uint32_t lds_qh(uint32_t a) { return __byte_perm(lds_u16(a), lds_u16(a + 2), 0x5410); }
 // IQ4_NL: the f16 pair (value of the low nibble, value of the high nibble) of byte x, from
@@ -409,10 +410,10 @@ fa_quant_kernel(const FaqParams p) {
                         // fifth bits of this lane's values: bits 2 q4 + {0, 1, 8, 9, 16, 17, 24, 25}
                         const uint32_t h0 = lds_qh(kr0 + b * F::kBlockBytes + F::kQh) >> (2 * q4);
                         const uint32_t h1 = lds_qh(kr1 + b * F::kBlockBytes + F::kQh) >> (2 * q4);
-                        hl[0] = bits2(h0, 0, h0, 1, 4); hl[1] = bits2(h1, 0, h1, 1, 4);
-                        hl[2] = bits2(h0, 8, h0, 9, 4); hl[3] = bits2(h1, 8, h1, 9, 4);
-                        hh[0] = bits2(h0, 16, h0, 17, 8); hh[1] = bits2(h1, 16, h1, 17, 8);
-                        hh[2] = bits2(h0, 24, h0, 25, 8); hh[3] = bits2(h1, 24, h1, 25, 8);
+                        hl[0] = fifth_lo(h0, 0); hl[1] = fifth_lo(h1, 0);
+                        hl[2] = fifth_lo(h0, 8); hl[3] = fifth_lo(h1, 8);
+                        hh[0] = fifth_hi(h0, 16); hh[1] = fifth_hi(h1, 16);
+                        hh[2] = fifth_hi(h0, 24); hh[3] = fifth_hi(h1, 24);
                     }
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -566,10 +567,14 @@ fa_quant_kernel(const FaqParams p) {
                         const uint32_t qb = lds_qh(vk0 + RB + b * F::kBlockBytes + F::kQh) >> (2 * g);
                         const uint32_t qc = lds_qh(vk8 + b * F::kBlockBytes + F::kQh) >> (2 * g);
                         const uint32_t qd = lds_qh(vk8 + RB + b * F::kBlockBytes + F::kQh) >> (2 * g);
-                        hl[0] = bits2(qa, 0, qb, 0, 4); hl[1] = bits2(qa, 1, qb, 1, 4);
-                        hl[2] = bits2(qc, 0, qd, 0, 4); hl[3] = bits2(qc, 1, qd, 1, 4);
-                        hh[0] = bits2(qa, 16, qb, 16, 8); hh[1] = bits2(qa, 17, qb, 17, 8);
-                        hh[2] = bits2(qc, 16, qd, 16, 8); hh[3] = bits2(qc, 17, qd, 17, 8);
+                        // byte 0 (bits 2 g, 2 g + 1) and byte 2 (16 + 2 g, 17 + 2 g) of two keys' qh
+                        // side by side: bit j of key A's byte at j, of key B's at 16 + j
+                        const uint32_t zab = __byte_perm(qa, qb, 0x5410u), zcd = __byte_perm(qc, qd, 0x5410u);
+                        const uint32_t zab2 = __byte_perm(qa, qb, 0x7632u), zcd2 = __byte_perm(qc, qd, 0x7632u);
+                        hl[0] = (zab & 0x00010001u) << 4; hl[1] = (zab & 0x00020002u) << 3;
+                        hl[2] = (zcd & 0x00010001u) << 4; hl[3] = (zcd & 0x00020002u) << 3;
+                        hh[0] = (zab2 & 0x00010001u) << 8; hh[1] = (zab2 & 0x00020002u) << 7;
+                        hh[2] = (zcd2 & 0x00010001u) << 8; hh[3] = (zcd2 & 0x00020002u) << 7;
                     }
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
