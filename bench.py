@@ -1091,9 +1091,9 @@ def run_e2e(w, a, world, value_dev):
         kl = torch.from_numpy(w.kv_len_np).pin_memory()
         o = torch.empty(w.out.shape, dtype=torch.float32).pin_memory()
         nb = lambda t, e: tuple(s * e for s in t.stride()[::-1])
-        if isinstance(w, C7):   # rows of 34-byte Q8_0 blocks (nb[0] = block bytes)
-            kv_nb = lambda t: (34,) + nb(t, 1)[1:]
-            kv_type = mlz_b200.TYPE_Q8_0
+        if isinstance(w, C7):   # rows of the KV type's blocks (nb[0] = block or element bytes)
+            kv_nb = lambda t: (w.bb,) + nb(t, 1)[1:]
+            kv_type = w.kv_type
         else:
             kv_nb = lambda t: nb(t, 2)
             kv_type = mlz_b200.TYPE_F16
