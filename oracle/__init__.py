@@ -77,6 +77,7 @@ def ref() -> C.CDLL:
         _ref = C.CDLL(_REF)
         _ref.mlzref_config_size.restype = C.c_size_t
         _ref.mlzref_flash_attn_f16.argtypes = [C.c_void_p]
+        _ref.mlzref_flash_attn_f32.argtypes = [C.c_void_p]
         _ref.simd_matmul_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                          C.c_size_t, C.c_size_t, C.c_int, C.c_int]
         _ref.simd_matmul_f16.argtypes = _ref.simd_matmul_f32.argtypes
@@ -356,11 +357,16 @@ def base_flash_attn_q(q, k_blocks, v_blocks, scale, kv_type, kv_len=None, nth: i
 
 
 def ref_flash_attn(q, k_bits, v_bits, scale, mask=None, softcap=0.0, max_bias=0.0,
-                   mode=0) -> np.ndarray:
-    """Run the reference's own flash_attn_quantized (oracle/_ref) on F16 K/V."""
+                   mode=0, f32_kv: bool = False) -> np.ndarray:
+    """Run the reference's own flash_attn_quantized (oracle/_ref) on F16 K/V (f16 bit
+    patterns), or on F32 K/V arrays with f32_kv=True."""
     q = np.ascontiguousarray(q, dtype=np.float32)
-    k_bits = np.ascontiguousarray(k_bits.view(np.uint16))
-    v_bits = np.ascontiguousarray(v_bits.view(np.uint16))
+    if f32_kv:
+        k_bits = np.ascontiguousarray(k_bits, dtype=np.float32)
+        v_bits = np.ascontiguousarray(v_bits, dtype=np.float32)
+    else:
+        k_bits = np.ascontiguousarray(k_bits.view(np.uint16))
+        v_bits = np.ascontiguousarray(v_bits.view(np.uint16))
     B, Hq, NQ, D = q.shape
     _, Hkv, NKV, DV = v_bits.shape
     out = np.zeros((B, Hq, NQ, DV), dtype=np.float32)
@@ -381,10 +387,13 @@ def ref_flash_attn(q, k_bits, v_bits, scale, mask=None, softcap=0.0, max_bias=0.
         # (src/simd/flash_attention.cpp:352); hand it the transposed strides so that
         # it reads the same element the skeleton's iq*nb1 + j*nb0 does.
         c.mask_nb[0], c.mask_nb[1] = nb[1], nb[0]
-    c.k_type, c.v_type = 1, 1
+    c.k_type = c.v_type = 0 if f32_kv else 1
     c.ith, c.nth = 0, 1
     assert C.sizeof(RefFAConfig) == ref().mlzref_config_size()
-    ref().mlzref_flash_attn_f16(C.byref(c))
+    if f32_kv:
+        ref().mlzref_flash_attn_f32(C.byref(c))
+    else:
+        ref().mlzref_flash_attn_f16(C.byref(c))
     return out
 
 

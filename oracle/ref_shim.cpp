@@ -13,7 +13,8 @@
 // :291-410, whose K dot product is a ggml_vec_dot_t) to F16 keys and an f32 query:
 // "from_float" copies the query unchanged and "vec_dot" is an f16 x f32 dot, so the
 // reference loop computes exactly the F16-KV attention of its F16 assembly kernel
-// (flash_attn_f16_avx512.asm:46-82: f16 K widened to f32, f32 Q).
+// (flash_attn_f16_avx512.asm:46-82: f16 K widened to f32, f32 Q); an f32 x f32 "vec_dot"
+// does the same for F32 K/V (its F32 value branch).
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -87,6 +88,23 @@ static void mlzref_vec_dot_f16_f32(int n, float* s, size_t, const void* vx, size
 // Run the reference's flash_attn_quantized on F16 K/V with an f32 query.
 void mlzref_flash_attn_f16(const flash_attn_config_t* cfg) {
     flash_attn_quantized(cfg, mlzref_vec_dot_f16_f32, mlzref_from_float_copy,
+                         sizeof(float) * (size_t)cfg->head_dim_k);
+}
+
+// The f32 x f32 dot of ggml's F32 vec_dot (k ascending, one float accumulator).
+static void mlzref_vec_dot_f32_f32(int n, float* s, size_t, const void* vx, size_t,
+                                   const void* vy, size_t, int) {
+    const float* k = (const float*)vx;
+    const float* q = (const float*)vy;
+    float acc = 0.0f;
+    for (int i = 0; i < n; i++) acc += k[i] * q[i];
+    *s = acc;
+}
+
+// Run the reference's flash_attn_quantized on F32 K/V (its F32 value branch,
+// flash_attention.cpp:391-393) with an f32 query.
+void mlzref_flash_attn_f32(const flash_attn_config_t* cfg) {
+    flash_attn_quantized(cfg, mlzref_vec_dot_f32_f32, mlzref_from_float_copy,
                          sizeof(float) * (size_t)cfg->head_dim_k);
 }
 

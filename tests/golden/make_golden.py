@@ -11,6 +11,8 @@ they were made).
 * fa_reference.npz  -- flash-attention decode cases and the outputs of the reference's
                        own flash_attn_quantized (src/simd/flash_attention.cpp:291-410),
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
+* fa_f32_reference.npz -- the same for F32 K/V (the reference's F32 value branch, fed
+                       through an f32 x f32 dot).
 * matmul_reference.npz -- tiny row-major matmuls through the reference's simd_matmul_f32
                        scalar path (src/simd/simd_matmul.cpp:196-223).
 * matmul_f16_reference.npz -- tiny F16 matmuls through the reference's own F16 GEMM,
@@ -137,6 +139,37 @@ def fa_fixture() -> None:
     np.savez_compressed(os.path.join(HERE, "fa_reference.npz"), **cases)
 
 
+def fa_f32_fixture() -> None:
+    """F32 K/V cases through the reference's flash_attn_quantized (its F32 value branch)."""
+    g = np.random.Generator(np.random.PCG64(12))
+    cases = {}
+    specs = [
+        ("gqa4_l70_d64", 1, 8, 2, 70, 64, 1, False, 0.0, False),
+        ("gqa4_l65_d128_mask", 1, 8, 2, 65, 128, 1, True, 0.0, False),
+        ("gqa2_l64_d64_softcap", 1, 4, 2, 64, 64, 1, False, 30.0, False),
+        ("gqa4_l33_d128_alibi", 1, 8, 2, 33, 128, 1, False, 0.0, True),
+        ("gqa4_nq3_l40_d64", 1, 8, 2, 40, 64, 3, True, 0.0, False),
+    ]
+    for name, B, Hq, Hkv, L, D, NQ, use_mask, softcap, alibi in specs:
+        s = 1.0 / np.sqrt(D)
+        q = (g.standard_normal((B, Hq, NQ, D)) * s * 4).astype(np.float32)
+        k = (g.standard_normal((B, Hkv, L, D)) * s * 4).astype(np.float32)
+        v = (g.standard_normal((B, Hkv, L, D)) * s).astype(np.float32)
+        mask = None
+        if use_mask:
+            mask = (g.standard_normal((NQ, L)) * 0.5).astype(np.float32)
+            mask[:, ::7] = -np.inf
+        mode = (oracle.FA_MODE_SOFTCAP if softcap else 0) | (oracle.FA_MODE_ALIBI if alibi else 0)
+        out = oracle.ref_flash_attn(q, k, v, float(s), mask=mask, softcap=softcap, mode=mode, f32_kv=True)
+        assert oracle.ref_stub_hits() == 0
+        cases[name + "__q"], cases[name + "__k"], cases[name + "__v"] = q, k, v
+        if mask is not None:
+            cases[name + "__mask"] = mask
+        cases[name + "__meta"] = np.array([softcap, 1.0 if alibi else 0.0, s], dtype=np.float64)
+        cases[name + "__out"] = out
+    np.savez_compressed(os.path.join(HERE, "fa_f32_reference.npz"), **cases)
+
+
 def matmul_fixture() -> None:
     g = np.random.Generator(np.random.PCG64(13))
     cases = {}
@@ -181,6 +214,7 @@ if __name__ == "__main__":
     q6k_fixture()
     kv_fixture()
     fa_fixture()
+    fa_f32_fixture()
     matmul_fixture()
     matmul_f16_fixture()
     print("fixtures written to", HERE)

@@ -185,3 +185,22 @@ def test_f32_large_values_keep_fp32_accuracy(dev):
     torch.cuda.synchronize()
     want = oracle.flash_attn_q(q, k, v, 1 / np.sqrt(D), mlz_b200.TYPE_F32, kv_len=kl)
     assert oracle.rel_err(o.cpu().numpy(), want) <= 1e-4
+
+
+@pytest.mark.parametrize("case", ["gqa4_l70_d64", "gqa4_l65_d128_mask", "gqa2_l64_d64_softcap",
+                                  "gqa4_l33_d128_alibi", "gqa4_nq3_l40_d64"])
+def test_f32_reference_fixtures(dev, golden, case):
+    """F32 K/V against the reference's own flash_attn_quantized outputs (its F32 value
+    branch; mask, softcap, ALiBi, n_q > 1), within 1e-4."""
+    import torch
+    f = golden("fa_f32_reference.npz")
+    q, k, v = f[case + "__q"], f[case + "__k"], f[case + "__v"]
+    softcap, alibi, scale = f[case + "__meta"]
+    mask = f[case + "__mask"] if (case + "__mask") in f.files else None
+    o = mlz_b200.flash_attn_dispatch_quant(torch.from_numpy(q).to(dev), torch.from_numpy(k.view(np.uint8)).to(dev),
+                                           torch.from_numpy(v.view(np.uint8)).to(dev), float(scale),
+                                           mlz_b200.TYPE_F32,
+                                           mask=torch.from_numpy(mask).to(dev) if mask is not None else None,
+                                           softcap=float(softcap), alibi=bool(alibi))
+    torch.cuda.synchronize()
+    assert oracle.rel_err(o.cpu().numpy(), f[case + "__out"]) <= 1e-4

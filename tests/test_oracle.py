@@ -232,3 +232,18 @@ def test_fa_quant_oracle_equals_numpy_attention_on_decoded_rows(kv_type):
             p = np.exp(s - s.max())
             want = (p @ vf[b, hk, :kl[b]]) / p.sum()
             np.testing.assert_allclose(got[b, h, 0], want, rtol=1e-6, atol=1e-9)
+
+
+@pytest.mark.parametrize("case", ["gqa4_l70_d64", "gqa4_l65_d128_mask", "gqa2_l64_d64_softcap",
+                                  "gqa4_l33_d128_alibi", "gqa4_nq3_l40_d64"])
+def test_fa_oracle_f32_kv_matches_reference_outputs(golden, case):
+    """F32 K/V: the oracle's attention (kv_type 0) equals the reference's own
+    flash_attn_quantized run on the same f32 rows (its F32 value branch), to f32 rounding."""
+    f = golden("fa_f32_reference.npz")
+    q, k, v = f[case + "__q"], f[case + "__k"], f[case + "__v"]
+    softcap, alibi, scale = f[case + "__meta"]
+    mask = f[case + "__mask"] if (case + "__mask") in f.files else None
+    mode = (oracle.FA_MODE_SOFTCAP if softcap else 0) | (oracle.FA_MODE_ALIBI if alibi else 0)
+    got = oracle.flash_attn_q(q, k.view(np.uint8), v.view(np.uint8), float(scale), 0, mask=mask,
+                              softcap=float(softcap), mode=mode)
+    assert oracle.rel_err(f[case + "__out"], got) < 2e-5
