@@ -78,6 +78,7 @@ def ref() -> C.CDLL:
         _ref.mlzref_config_size.restype = C.c_size_t
         _ref.mlzref_flash_attn_f16.argtypes = [C.c_void_p]
         _ref.mlzref_flash_attn_f32.argtypes = [C.c_void_p]
+        _ref.mlzref_quantize_row_q8k.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         _ref.simd_matmul_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                          C.c_size_t, C.c_size_t, C.c_int, C.c_int]
         _ref.simd_matmul_f16.argtypes = _ref.simd_matmul_f32.argtypes
@@ -394,6 +395,15 @@ def ref_flash_attn(q, k_bits, v_bits, scale, mask=None, softcap=0.0, max_bias=0.
         ref().mlzref_flash_attn_f32(C.byref(c))
     else:
         ref().mlzref_flash_attn_f16(C.byref(c))
+    return out
+
+
+def ref_quantize_q8k(x: np.ndarray) -> np.ndarray:
+    """The reference's own quantize_row_q8_k_reference (src/simd/ggml_simd_hook.cpp:109-148,
+    compiled into oracle/_ref) on one row of K f32 values: (K/256 * 292,) uint8."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.shape[0] // QK_K * Q8K_BYTES, dtype=np.uint8)
+    ref().mlzref_quantize_row_q8k(_p(x), _p(out), int(x.shape[0]))
     return out
 
 

@@ -13,6 +13,9 @@ they were made).
                        compiled from source into oracle/_ref, fed F16 K/V and an f32 query.
 * fa_f32_reference.npz -- the same for F32 K/V (the reference's F32 value branch, fed
                        through an f32 x f32 dot).
+* q8k_reference.npz  -- F32 rows and their Q8_K blocks from the reference's own
+                       quantize_row_q8_k_reference (src/simd/ggml_simd_hook.cpp:109-148),
+                       the hook compiled in place against minimal ggml declarations.
 * matmul_reference.npz -- tiny row-major matmuls through the reference's simd_matmul_f32
                        scalar path (src/simd/simd_matmul.cpp:196-223).
 * matmul_f16_reference.npz -- tiny F16 matmuls through the reference's own F16 GEMM,
@@ -170,6 +173,26 @@ def fa_f32_fixture() -> None:
     np.savez_compressed(os.path.join(HERE, "fa_f32_reference.npz"), **cases)
 
 
+def q8k_fixture() -> None:
+    """Rows quantised by the reference's own quantize_row_q8_k_reference (ggml_simd_hook.cpp
+    :109-148) through oracle/_ref, with edge blocks: all zero, tiny values, huge values of
+    both signs, exact halves after scaling (ties of the rounding) and a lone extreme."""
+    g = np.random.Generator(np.random.PCG64(31))
+    K = 2048
+    rows = g.standard_normal((6, K)).astype(np.float32)
+    rows[0, :256] = 0.0
+    rows[1, :256] *= np.float32(1e-30)
+    rows[1, 256:512] = np.where(np.arange(256) % 2, 1e20, -3e19).astype(np.float32)
+    rows[2, :256] = (np.round(rows[2, :256] * 4) / 4).astype(np.float32)
+    rows[2, 256:512] = np.float32(0.5) * (np.arange(256) % 7 - 3).astype(np.float32)
+    rows[3, 512:768] = 0.0
+    rows[3, 700] = np.float32(-7.0)
+    rows[4] *= np.float32(1000.0)
+    out = np.stack([oracle.ref_quantize_q8k(r) for r in rows])
+    assert oracle.ref_stub_hits() == 0
+    np.savez_compressed(os.path.join(HERE, "q8k_reference.npz"), x=rows, q8k=out)
+
+
 def matmul_fixture() -> None:
     g = np.random.Generator(np.random.PCG64(13))
     cases = {}
@@ -215,6 +238,7 @@ if __name__ == "__main__":
     kv_fixture()
     fa_fixture()
     fa_f32_fixture()
+    q8k_fixture()
     matmul_fixture()
     matmul_f16_fixture()
     print("fixtures written to", HERE)

@@ -247,3 +247,12 @@ def test_fa_oracle_f32_kv_matches_reference_outputs(golden, case):
     got = oracle.flash_attn_q(q, k.view(np.uint8), v.view(np.uint8), float(scale), 0, mask=mask,
                               softcap=float(softcap), mode=mode)
     assert oracle.rel_err(f[case + "__out"], got) < 2e-5
+
+
+def test_q8k_oracle_matches_reference_quantiser(golden):
+    """The oracle's Q8_K restatement equals the reference's own quantize_row_q8_k_reference
+    (src/simd/ggml_simd_hook.cpp:109-148, compiled from the reference tree) bit for bit,
+    edge blocks included (zeros, tiny and huge values, rounding ties)."""
+    f = golden("q8k_reference.npz")
+    got = np.stack([oracle.quantize_q8k(r) for r in f["x"]]).view(np.uint8).reshape(f["q8k"].shape)
+    assert np.array_equal(got, f["q8k"])

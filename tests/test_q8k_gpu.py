@@ -50,3 +50,12 @@ def test_q8k_rejects_ragged_k(dev):
     x = torch.zeros((1, 300), device=dev)
     with pytest.raises(mlz_b200.MlzcError):
         mlz_b200.quantize_q8k(x, out=torch.zeros((1, 292), dtype=torch.uint8, device=dev))
+
+
+def test_q8k_matches_reference_quantiser_fixture(dev, golden):
+    """The GPU quantiser against blocks produced by the reference's own
+    quantize_row_q8_k_reference (ggml_simd_hook.cpp:109-148): bit-identical."""
+    import torch
+    f = golden("q8k_reference.npz")
+    got = mlz_b200.quantize_q8k(torch.from_numpy(f["x"]).to(dev)).cpu().numpy()
+    assert np.array_equal(got.view(np.uint8).reshape(f["q8k"].shape), f["q8k"])
