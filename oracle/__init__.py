@@ -79,6 +79,8 @@ def ref() -> C.CDLL:
         _ref.mlzref_flash_attn_f16.argtypes = [C.c_void_p]
         _ref.mlzref_flash_attn_f32.argtypes = [C.c_void_p]
         _ref.mlzref_quantize_row_q8k.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        _ref.mlzref_try_mul_mat.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.c_int64, C.c_int64, C.c_void_p,
+                                            C.c_int64, C.c_void_p, C.c_int]
         _ref.simd_matmul_f32.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                          C.c_size_t, C.c_size_t, C.c_int, C.c_int]
         _ref.simd_matmul_f16.argtypes = _ref.simd_matmul_f32.argtypes
@@ -405,6 +407,19 @@ def ref_quantize_q8k(x: np.ndarray) -> np.ndarray:
     out = np.zeros(x.shape[0] // QK_K * Q8K_BYTES, dtype=np.uint8)
     ref().mlzref_quantize_row_q8k(_p(x), _p(out), int(x.shape[0]))
     return out
+
+
+def ref_try_mul_mat(w: np.ndarray, x: np.ndarray, w_type: int, nth: int = 1):
+    """The reference's own hook, ggml_simd_try_mul_mat (src/simd/ggml_simd_hook.cpp:153-315,
+    compiled into oracle/_ref), on W (M, K) of w_type (0 = F32, 1 = F16 bit patterns) and X
+    (N, K) f32, for thread indices 0..nth-1 in turn.  Returns (handled, Y (N, M))."""
+    w = np.ascontiguousarray(w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = w.shape
+    N = x.shape[0]
+    y = np.zeros((N, M), dtype=np.float32)
+    r = ref().mlzref_try_mul_mat(w_type, _p(w), w.strides[0], M, K, _p(x), N, _p(y), nth)
+    return int(r), y
 
 
 def ref_matmul_f32_small(a: np.ndarray, b: np.ndarray) -> np.ndarray:

@@ -16,6 +16,8 @@ they were made).
 * q8k_reference.npz  -- F32 rows and their Q8_K blocks from the reference's own
                        quantize_row_q8_k_reference (src/simd/ggml_simd_hook.cpp:109-148),
                        the hook compiled in place against minimal ggml declarations.
+* hook_reference.npz -- one-column MUL_MAT nodes through the reference's own hook,
+                       ggml_simd_try_mul_mat (its F32 branch; F16 weights are declined).
 * matmul_reference.npz -- tiny row-major matmuls through the reference's simd_matmul_f32
                        scalar path (src/simd/simd_matmul.cpp:196-223).
 * matmul_f16_reference.npz -- tiny F16 matmuls through the reference's own F16 GEMM,
@@ -193,6 +195,28 @@ def q8k_fixture() -> None:
     np.savez_compressed(os.path.join(HERE, "q8k_reference.npz"), x=rows, q8k=out)
 
 
+def hook_fixture() -> None:
+    """One-column MUL_MAT nodes through the reference's own hook, ggml_simd_try_mul_mat
+    (src/simd/ggml_simd_hook.cpp:153-315, compiled in place), for F32 weights (handled: its
+    F32 branch, simd_matmul_f32 on the scalar path below M*N*K = 512) with 1 and 3 thread
+    indices, and F16 weights (declined: 0, upstream computes them)."""
+    g = np.random.Generator(np.random.PCG64(41))
+    out = {}
+    for i, (M, K) in enumerate([(8, 32), (12, 40), (3, 160)]):
+        w = g.standard_normal((M, K)).astype(np.float32)
+        x = g.standard_normal((1, K)).astype(np.float32)
+        for nth in (1, 3):
+            r, y = oracle.ref_try_mul_mat(w, x, 0, nth)
+            assert r == 1 and oracle.ref_stub_hits() == 0
+            out[f"f32_{i}_nth{nth}__y"] = y
+        out[f"f32_{i}__w"], out[f"f32_{i}__x"] = w, x
+    w16 = g.standard_normal((8, 32)).astype(np.float16)
+    x16 = g.standard_normal((1, 32)).astype(np.float32)
+    r, _ = oracle.ref_try_mul_mat(w16.view(np.uint16), x16, 1, 1)
+    out["f16__handled"] = np.array([r], dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "hook_reference.npz"), **out)
+
+
 def matmul_fixture() -> None:
     g = np.random.Generator(np.random.PCG64(13))
     cases = {}
@@ -239,6 +263,7 @@ if __name__ == "__main__":
     fa_fixture()
     fa_f32_fixture()
     q8k_fixture()
+    hook_fixture()
     matmul_fixture()
     matmul_f16_fixture()
     print("fixtures written to", HERE)

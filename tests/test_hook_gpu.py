@@ -91,3 +91,17 @@ def test_weight_handle_host_call(dev):
     y = h.mul_mat(x)
     h.free()
     assert oracle.rel_err(y, oracle.mul_mat_f16(w.view(np.uint16), x)) <= 1e-3
+
+
+@pytest.mark.parametrize("nth", [1, 3])
+def test_f32_node_matches_reference_hook(dev, golden, nth):
+    """The same one-column F32 nodes the reference's own ggml_simd_try_mul_mat computed
+    (its F32 branch, compiled from source): this hook returns 1 on every thread and the
+    same values to fp32 rounding."""
+    f = golden("hook_reference.npz")
+    for i in range(3):
+        w, x = f[f"f32_{i}__w"], f[f"f32_{i}__x"]
+        y = np.full((1, w.shape[0]), np.nan, dtype=np.float32)
+        s0, s1, d = _views(w, x, y, mlz_b200.TYPE_F32)
+        assert [mlz_b200.ggml_simd_try_mul_mat(s0, s1, d, t, nth) for t in range(nth)] == [1] * nth
+        assert oracle.rel_err(y, f[f"f32_{i}_nth{nth}__y"]) < 1e-5

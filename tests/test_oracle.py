@@ -256,3 +256,16 @@ def test_q8k_oracle_matches_reference_quantiser(golden):
     f = golden("q8k_reference.npz")
     got = np.stack([oracle.quantize_q8k(r) for r in f["x"]]).view(np.uint8).reshape(f["q8k"].shape)
     assert np.array_equal(got, f["q8k"])
+
+
+def test_f32_oracle_matches_reference_hook(golden):
+    """One-column F32-weight nodes through the reference's own ggml_simd_try_mul_mat (with 1
+    and 3 thread indices): the oracle's F32 product agrees to fp32 rounding; the reference
+    declines F16 weights (returns 0) -- this library's hook takes them (a superset)."""
+    f = golden("hook_reference.npz")
+    for i in range(3):
+        w, x = f[f"f32_{i}__w"], f[f"f32_{i}__x"]
+        want = oracle.mul_mat_f32(w, x)
+        for nth in (1, 3):
+            assert oracle.rel_err(f[f"f32_{i}_nth{nth}__y"], want) < 1e-6
+    assert int(f["f16__handled"][0]) == 0
